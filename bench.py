@@ -1,0 +1,540 @@
+#!/usr/bin/env python
+"""Benchmark of the B200-native low-precision path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl kab|reference]
+
+Workloads (synthetic, seeded; BASELINE.json's configurations):
+  w4a4     config 4: NVFP4 W4A4 linear with bias, X [8192, 8192] x W [28672, 8192]^T: the
+           per-token NVFP4 producer of X plus the block-scaled tcgen05 GEMM with its fused
+           dequant / bias epilogue (default once the GEMM is built). At N > 1 the GEMM is
+           column-sharded over the ranks and the bf16 output all-gathered over NVLink.
+  nvfp4_producer  config 4's activation producer alone (HBM-bound).
+  mxfp8_producer  config 3's fused SiLU(gate) * up -> MXFP8 producer (HBM-bound).
+  compare  the comparator on a config-4-sized bf16 output pair (HBM-bound).
+
+``value`` is the whole-job throughput with inputs resident in HBM, timed with CUDA events
+over exactly K steps between barriers, the max over ranks; ``e2e`` is the same metric through
+the public Python API with host buffers (pinned host -> device copies of the step's inputs
+and a device -> host read of its result inside the timed region). ``roofline`` covers the
+dominant kernel (its launches timed with events on the launching stream); ``cpu_baseline``
+the CPU oracle on a bounded sample on this host's cores. ``--impl reference`` times the
+reference's CPU path (the oracle port: the reference is Python and does not travel) on the
+host cores for the same workload and prints its own line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "kernel-agent_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "scaled-GEMM TFLOPS & % block-scaled tensor peak; quantize GB/s & % HBM"
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+TRAFFIC_FILE = ROOT / "profiles" / "traffic.json"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks() -> tuple[dict, str]:
+    if PEAKS_FILE.exists():
+        return json.loads(PEAKS_FILE.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ------------------------------------------------------------------ distributed plumbing
+
+
+class Dist:
+    def __init__(self) -> None:
+        import torch
+
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.torch = torch
+        if self.world > 1:
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.dist = dist
+        else:
+            self.dist = None
+
+    def barrier(self) -> None:
+        if self.dist is not None:
+            self.dist.barrier()
+
+    def max(self, v: float) -> float:
+        if self.dist is None:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self) -> None:
+        if self.dist is not None:
+            self.dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ clocks
+
+
+class Clocks:
+    """nvidia-smi samples of the SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(",") for r in out.strip().splitlines() if r.strip()]
+        sm, mx, reasons, power = [], [], set(), []
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+                power.append(float(r[3]))
+                for name, val in zip(names, r[5:9]):
+                    if val.strip().lower() == "active":
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [s for s, p in zip(sm, power) if p > 0.5 * max(power)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baselines (oracle)
+
+
+def _cpu_worker(args):
+    """One chunk of the CPU oracle's work (runs in a spawned process)."""
+    kind, payload = args
+    import numpy as np  # noqa: F401
+
+    sys.path.insert(0, str(ROOT))
+    from oracle import quant as oq
+
+    t0 = time.perf_counter()
+    if kind == "nvfp4":
+        oq.quantize_fp4_activations(payload, "nvfp4", "token")
+    elif kind == "mxfp8_silu":
+        g, u = payload
+        oq.quantize_mxfp8(oq.silu_mul(g, u))
+    elif kind == "w4a4":
+        x, codes, scales, ts, bias = payload
+        oq.fp4_w4a4_linear(x, codes, scales, ts, bias)
+    elif kind == "compare":
+        from oracle import compare as ocmp
+
+        a, b = payload
+        ocmp.compare_tensors("y", a, b, "bf16", tier="near-lossless-fp4a")
+    return time.perf_counter() - t0
+
+
+def cpu_rate(kind: str, chunks: list, units: float, budget_s: float, processes: int) -> tuple[float, int]:
+    """Throughput (units per second) of the oracle over ``chunks`` (each worth units /
+    len(chunks)), repeated until ``budget_s`` of wall time, on ``processes`` spawned workers."""
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    done = 0.0
+    t0 = time.perf_counter()
+    with ctx.Pool(processes) as pool:
+        pool.map(_cpu_worker, [(kind, chunks[0])] * processes)  # warm the workers' imports
+        t0 = time.perf_counter()
+        while True:
+            pool.map(_cpu_worker, [(kind, c) for c in chunks])
+            done += units
+            if time.perf_counter() - t0 >= budget_s:
+                break
+    return done / (time.perf_counter() - t0), processes
+
+
+# ------------------------------------------------------------------ workloads
+
+
+class Workload:
+    name = ""
+    unit = ""
+    dtype = ""
+    scaling = "weak"
+    config: dict = {}
+
+    def setup(self, dev, world, rank):
+        raise NotImplementedError
+
+    def step(self):
+        """One pass of the hot path on device-resident inputs; returns the number of this
+        library's kernel launches."""
+        raise NotImplementedError
+
+    def e2e_step(self):
+        """One pass through the public API with host buffers (copies included)."""
+        raise NotImplementedError
+
+
+class Nvfp4Producer(Workload):
+    name = "nvfp4_producer"
+    unit = "GB/s"
+    dtype = "bf16->nvfp4"
+
+    def setup(self, dev, world, rank):
+        import torch
+
+        from kernel_agent_b200 import workloads
+        from kernel_agent_b200.kernels import producers
+
+        self.torch, self.producers = torch, producers
+        self.m, self.k = 8192, 8192
+        x, _, _ = workloads.config4(seed=0, device="cuda", n=128)
+        self.x = x.to(dev)
+        self.bytes = self.m * self.k * 2 + self.m * self.k // 2 + self.m * self.k // 16 + 4 * self.m
+        self.units = self.bytes / 1e9  # GB per step
+        self.kernel = "quant_fp4_kernel"
+        self.kernel_bytes = self.bytes
+        self.x_host = self.x.cpu().pin_memory()
+        self.h2d = self.x.numel() * 2
+        self.d2h = self.m * self.k // 2 + self.m * self.k // 16 + 4 * self.m
+        q, s, o = producers.quantize_rows_fp4(self.x, swizzle=True)
+        self.out_host = [t.cpu().pin_memory() for t in (q, s.view(torch.uint8), o)]
+        self.config = {"workload": "config 4 NVFP4 activation producer (per-token outer, swizzled scales)",
+                       "rows": self.m, "k": self.k, "l2": "inputs larger than L2 (134 MB per step)"}
+
+    def step(self):
+        self.producers.quantize_rows_fp4(self.x, swizzle=True)
+        return 1
+
+    def e2e_step(self):
+        x = self.x_host.to(self.x.device, non_blocking=True)
+        q, s, o = self.producers.quantize_rows_fp4(x, swizzle=True)
+        for host, t in zip(self.out_host, (q, s.view(self.torch.uint8), o)):
+            host.copy_(t, non_blocking=True)
+        return 1
+
+    def cpu_baseline(self):
+        import numpy as np
+
+        rows = 64
+        x = self.x[:rows].float().cpu().numpy()
+        chunks = [x]
+        gb = rows * self.k * (2 + 0.5 + 1 / 16) / 1e9
+        rate, cores = cpu_rate("nvfp4", chunks, gb, 10.0, 1)
+        return {"value": rate, "unit": "GB/s", "cores": cores, "kind": "port",
+                "sample": f"oracle quantize_fp4_activations on {rows} x {self.k} rows, repeated ~10 s"}
+
+    def reference(self, steps, warmup):
+        rows = 256
+        x = self.x[:rows].float().cpu().numpy()
+        procs = os.cpu_count() or 1
+        chunks = [x[i::procs] for i in range(procs)]
+        gb = rows * self.k * (2 + 0.5 + 1 / 16) / 1e9
+        rate, cores = cpu_rate("nvfp4", chunks, gb, 2.0 * max(steps, 1), procs)
+        return rate, cores, f"oracle NVFP4 producer on {rows} x {self.k} rows per step, {procs} processes"
+
+
+class Mxfp8Producer(Workload):
+    name = "mxfp8_producer"
+    unit = "GB/s"
+    dtype = "bf16->mxfp8"
+
+    def setup(self, dev, world, rank):
+        import torch
+
+        from kernel_agent_b200 import workloads
+        from kernel_agent_b200.kernels import producers
+
+        self.torch, self.producers = torch, producers
+        g, u, _ = workloads.config3(seed=0, device="cuda", h=128)
+        self.g, self.u = g.to(dev), u.to(dev)
+        m, f = g.shape
+        self.m, self.f = m, f
+        self.bytes = 2 * m * f * 2 + m * f + m * f // 32
+        self.units = self.bytes / 1e9
+        self.kernel = "quant_mxfp8_kernel"
+        self.kernel_bytes = self.bytes
+        self.h2d = 2 * m * f * 2
+        self.d2h = m * f + m * f // 32
+        self.g_host, self.u_host = self.g.cpu().pin_memory(), self.u.cpu().pin_memory()
+        self.out_host = [torch.empty(m * f, dtype=torch.uint8).pin_memory(),
+                         torch.empty(m * f // 32, dtype=torch.uint8).pin_memory()]
+        self.config = {"workload": "config 3 fused SiLU(gate)*up -> MXFP8 producer (swizzled scales)",
+                       "rows": m, "k": f, "l2": "inputs larger than L2 (235 MB per step)"}
+
+    def step(self):
+        self.producers.silu_mul_fp8(self.g, self.u, mx=True, blocked=True)
+        return 1
+
+    def e2e_step(self):
+        g = self.g_host.to(self.g.device, non_blocking=True)
+        u = self.u_host.to(self.g.device, non_blocking=True)
+        q, s = self.producers.silu_mul_fp8(g, u, mx=True, blocked=True)
+        self.out_host[0].copy_(q.view(self.torch.uint8).reshape(-1), non_blocking=True)
+        self.out_host[1].copy_(s.reshape(-1), non_blocking=True)
+        return 1
+
+    def cpu_baseline(self):
+        rows = 16
+        g = self.g[:rows].float().cpu().numpy()
+        u = self.u[:rows].float().cpu().numpy()
+        gb = rows * self.f * (4 + 1 + 1 / 32) / 1e9
+        rate, cores = cpu_rate("mxfp8_silu", [(g, u)], gb, 10.0, 1)
+        return {"value": rate, "unit": "GB/s", "cores": cores, "kind": "port",
+                "sample": f"oracle silu_mul + quantize_mxfp8 on {rows} x {self.f}, repeated ~10 s"}
+
+    def reference(self, steps, warmup):
+        rows = 64
+        procs = os.cpu_count() or 1
+        g = self.g[:rows].float().cpu().numpy()
+        u = self.u[:rows].float().cpu().numpy()
+        chunks = [(g[i::procs], u[i::procs]) for i in range(procs)]
+        gb = rows * self.f * (4 + 1 + 1 / 32) / 1e9
+        rate, cores = cpu_rate("mxfp8_silu", chunks, gb, 2.0 * max(steps, 1), procs)
+        return rate, cores, f"oracle SiLU*up + MXFP8 on {rows} x {self.f} per step, {procs} processes"
+
+
+class Compare(Workload):
+    name = "compare"
+    unit = "GB/s"
+    dtype = "bf16"
+
+    def setup(self, dev, world, rank):
+        import torch
+
+        from kernel_agent_b200.kernels import compare
+
+        self.torch, self.compare = torch, compare
+        g = torch.Generator(device="cuda").manual_seed(0)
+        shape = (8192, 28672)
+        self.ref = torch.randn(*shape, generator=g, device="cuda").to(torch.bfloat16).to(dev)
+        self.new = (self.ref.float() * (1 + 0.01 * torch.randn(*shape, generator=g, device="cuda"))).to(torch.bfloat16)
+        n = self.ref.numel()
+        self.bytes = 2 * n * 2  # one read of each (exact tier)
+        self.units = self.bytes / 1e9
+        self.kernel = "compare_kernel"
+        self.kernel_bytes = self.bytes
+        self.h2d = 0
+        self.d2h = 0
+        self.config = {"workload": "comparator, exact tier, bf16 [8192, 28672] pair (config-4 output)",
+                       "l2": "inputs larger than L2 (940 MB per step)"}
+
+    def step(self):
+        self.compare.compare_tensors("y", self.ref, self.new)
+        return 2
+
+    def e2e_step(self):
+        self.compare.compare_tensors("y", self.ref, self.new)
+        return 2
+
+    def cpu_baseline(self):
+        a = self.ref[:256].float().cpu().numpy()
+        b = self.new[:256].float().cpu().numpy()
+        gb = a.size * 4 / 1e9
+        rate, cores = cpu_rate("compare", [(a, b)], gb, 10.0, 1)
+        return {"value": rate, "unit": "GB/s", "cores": cores, "kind": "port",
+                "sample": "oracle compare_tensors on 256 rows of the pair, repeated ~10 s"}
+
+    def reference(self, steps, warmup):
+        procs = os.cpu_count() or 1
+        a = self.ref[:1024].float().cpu().numpy()
+        b = self.new[:1024].float().cpu().numpy()
+        chunks = [(a[i::procs], b[i::procs]) for i in range(procs)]
+        gb = a.size * 4 / 1e9
+        rate, cores = cpu_rate("compare", chunks, gb, 2.0 * max(steps, 1), procs)
+        return rate, cores, f"oracle compare_tensors on 1024 rows per step, {procs} processes"
+
+
+WORKLOADS = {w.name: w for w in (Nvfp4Producer, Mxfp8Producer, Compare)}
+DEFAULT = "nvfp4_producer"
+
+
+def load_w4a4():
+    try:
+        from kernel_agent_b200.bench_w4a4 import W4A4Linear
+    except ImportError:
+        return None
+    return W4A4Linear
+
+
+# ------------------------------------------------------------------ timing
+
+
+def timed(fn, steps: int, torch):
+    """(total ms of `steps` calls on the current stream, launches) with CUDA events."""
+    launches = 0
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(steps):
+        launches += fn()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end), launches
+
+
+def kernel_ms(fn, steps: int, torch) -> float:
+    """Average device time of one call of `fn` (one dominant launch), events around each."""
+    evs = []
+    for _ in range(steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs) / steps
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("kab", "reference"), default="kab")
+    ap.add_argument("--workload", default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    W4A4 = load_w4a4()
+    workloads = dict(WORKLOADS)
+    if W4A4 is not None:
+        workloads[W4A4.name] = W4A4
+    name = args.workload or (W4A4.name if W4A4 is not None else DEFAULT)
+    if name not in workloads:
+        print(json.dumps({"error": f"unknown workload {name}", "known": sorted(workloads)}))
+        return 2
+
+    dist = Dist()
+    torch = dist.torch
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    wl = workloads[name]()
+
+    if args.impl == "reference":
+        if dist.rank != 0:
+            dist.close()
+            return 0
+        wl.setup(dev, 1, 0)
+        t0 = time.perf_counter()
+        rate, cores, sample = wl.reference(args.steps, args.warmup)
+        line = {
+            "impl": "reference", "metric": METRIC, "value": rate, "unit": wl.unit,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": None, "higher_is_better": True, "scaling": wl.scaling,
+            "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded)",
+            "config": wl.config,
+            "cpu_baseline": {"value": rate, "unit": wl.unit, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": rate, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": round(time.perf_counter() - t0, 1),
+        }
+        print(json.dumps(line))
+        dist.close()
+        return 0
+
+    wl.setup(dev, dist.world, dist.rank)
+    for _ in range(args.warmup):
+        wl.step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = Clocks(dist.local)
+    clocks.start()
+    time.sleep(0.3)
+    dist.barrier()
+    total_ms, launches = timed(wl.step, args.steps, torch)
+    dist.barrier()
+    k_ms = kernel_ms(getattr(wl, "dominant", wl.step), args.steps, torch)
+    clk = clocks.stop()
+    total_ms = dist.max(total_ms)
+    k_ms = dist.max(k_ms)
+    ms_per_step = total_ms / args.steps
+    value = wl.units * dist.world / (ms_per_step / 1e3) if wl.scaling == "weak" else wl.units / (ms_per_step / 1e3)
+
+    # end to end through the public API with host buffers
+    for _ in range(2):
+        wl.e2e_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e2e_ms, _ = timed(wl.e2e_step, max(3, args.steps // 2), torch)
+    e2e_ms = dist.max(e2e_ms) / max(3, args.steps // 2)
+    e2e_value = wl.units * dist.world / (e2e_ms / 1e3) if wl.scaling == "weak" else wl.units / (e2e_ms / 1e3)
+
+    pk, pk_kind = peaks()
+    if wl.unit == "GB/s":
+        achieved = wl.kernel_bytes / (k_ms / 1e3) / 1e9
+        peak = pk["hbm_gbs"]
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_kind": f"{pk_kind} copy bandwidth"}
+    else:
+        achieved = wl.kernel_flops / (k_ms / 1e3) / 1e12
+        peak, peak_kind = wl.tensor_peak(pk, pk_kind)
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "peak_kind": peak_kind}
+    roof["kernel"] = wl.kernel
+    roof["kernel_ms"] = k_ms
+    traffic = None
+    if TRAFFIC_FILE.exists():
+        traffic = json.loads(TRAFFIC_FILE.read_text()).get(f"{wl.kernel} {wl.name}")
+    roof["traffic"] = traffic
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        cpu = wl.cpu_baseline()
+    line = {
+        "metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
+        "dtype": wl.dtype, "data": "synthetic (seeded)", "config": wl.config,
+        "roofline": roof, "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d,
+                "d2h_bytes_per_step": wl.d2h},
+        "gpu_launches": launches, "clocks": clk,
+    }
+    if dist.rank == 0:
+        print(json.dumps(line))
+    closer = getattr(wl, "close", None)
+    if closer is not None:
+        closer()
+    dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,215 @@
+/*
+ * kab.h: the C ABI of the B200-native low-precision library (libkab.so).
+ *
+ * It replaces the numeric core of kernel-agent's low-precision path: the quantisers and
+ * scaled linears of src/kernel_agent/kernels/quant.py, the research blockwise / FP8
+ * attention math of docs/research-scripts/fp8-sm120/fp8lib.py, and the element loop of the
+ * comparator src/kernel_agent/kernels/compare.py:631-790. Each entry point below names the
+ * reference function it stands in for.
+ *
+ * Conventions
+ *  - Plain device pointers, element counts and strides (in elements); matrices are
+ *    row-major with a leading dimension `ld*` >= their width. Outputs are contiguous.
+ *  - `stream` is a cudaStream_t passed as void* (NULL: the legacy default stream). Every
+ *    call is asynchronous on it: no host synchronisation, no allocation, so the calls can
+ *    be captured in a CUDA graph.
+ *  - The return value is a KAB_* status. On failure kab_last_error() gives the reason
+ *    (thread-local). Arguments are validated before any launch.
+ *  - Floating-point inputs are fp32, bf16 or fp16 (KAB_F32 / KAB_BF16 / KAB_F16).
+ *  - FP8 codes are e4m3fn bytes, MX scales e8m0 bytes (exponent + 127), NVFP4 block scales
+ *    e4m3fn bytes, FP4 codes two e2m1 per byte with the even element in the low nibble.
+ *  - "Swizzled" scales use the 128 x 4 blocked layout of cuBLASLt (quant.py:540-564,
+ *    mx_scale_offset): rows padded to 128, columns to 4, blocks of 512 bytes; the caller
+ *    provides a zeroed buffer of that padded size when padding exists.
+ */
+#ifndef KAB_H_
+#define KAB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+
+#define KAB_OK 0
+#define KAB_EINVAL 1       /* an argument is out of range, misaligned or null */
+#define KAB_EUNSUPPORTED 2 /* no sm_100 device, or a shape this build does not handle */
+#define KAB_ECUDA 3        /* the CUDA runtime reported an error (launch, attribute, ...) */
+#define KAB_ETIMEOUT 4     /* a device-side wait gave up (see kab_device_status) */
+
+#define KAB_F32 0
+#define KAB_BF16 1
+#define KAB_F16 2
+
+/* The message of the last failing call on this thread ("" when none). */
+const char* kab_last_error(void);
+/* The library's ABI version (KAB_ABI_VERSION). */
+int kab_abi_version(void);
+#define KAB_ABI_VERSION 1
+/* KAB_OK when `device` is an sm_100 GPU this build runs on. */
+int kab_device_check(int device);
+/* Error bits kernels raised on the current device since the last clear (1: a wait timed
+ * out, 2: an index check failed); synchronises the stream. `clear` resets them. */
+int kab_device_status(unsigned* bits, int clear, void* stream);
+
+/* ------------------------------------------------------------------ producers */
+
+/* Per-row INT8: scale = amax * fp32(1/127) (1 for a zero row), codes round(v / scale) to
+ * nearest even clamped to +-127. smooth_mode 0: v = x; 1: v = x / smooth[col]
+ * (activations, quant.py:823-839 quantize_int8_activations); 2: v = x * smooth[col]
+ * (weights, quant.py:794-813 quantize_int8). k % 8 == 0, 16-byte aligned rows. */
+int kab_quant_rows_int8(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                        const float* smooth, int smooth_mode, int8_t* q, float* scale,
+                        void* stream);
+
+/* Per-row FP8 e4m3: scale = amax / 448 (1 for a zero row), codes (v / scale) clamped to
+ * +-448, nearest even (quant.py:361-377 quantize_fp8_activations, quant.py:101-119
+ * quantize_fp8). With `up` non-null the row is silu(x) * up in x's dtype, and `h` (nullable,
+ * x's dtype, [rows, k]) receives it (triton_fp8_producers.py:136-147). */
+int kab_quant_rows_fp8(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                       const void* up, int64_t ldu, uint8_t* q, float* scale, void* h,
+                       void* stream);
+
+/* FP8 per 1 x group along rows (group 32, 64 or 128): scale = amax / 448, 0 -> 1, scales
+ * fp32 [rows, k / group] (fp8lib.py:22-27 fq_groups). */
+int kab_quant_groups_fp8(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                         int group, uint8_t* q, float* scales, void* stream);
+
+/* FP8 per 128 x 128 block of a weight [n, k]: scales fp32 [n / 128, k / 128]
+ * (fp8lib.py:35-39 fq_block). */
+int kab_quant_blocks_fp8(const void* w, int dtype, int64_t n, int64_t k, int64_t ldw,
+                         uint8_t* q, float* scales, void* stream);
+
+/* MXFP8: per block of 32 along rows, e = the rule's exponent (rule 0: ceil
+ * 2^ceil(log2(amax / 448)), 1: floor, the OCP rule), codes (v / 2^e) clamped to +-448,
+ * scale byte e + 127, row-major [rows, k / 32] or swizzled (quant.py:479-526
+ * mx_scale_exponents / quantize_mxfp8). `up`, `h`: the fused SiLU * up producer. */
+int kab_quant_mxfp8(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                    const void* up, int64_t ldu, int rule, uint8_t* q, uint8_t* scales,
+                    int swizzle, void* h, void* stream);
+
+#define KAB_NVFP4 0
+#define KAB_MXFP4 1
+#define KAB_FP4_TOKEN 0  /* activations, outer scale per row */
+#define KAB_FP4_TENSOR 1 /* activations, one outer scale per call (from *amax) */
+#define KAB_FP4_WEIGHT 2 /* a weight with its tensor scale *tensor_scale */
+
+/* FP4 activations (quant.py:1056-1107 quantize_fp4_activations) or weights (quant.py:217-272
+ * quantize_fp4): codes [rows, k / 2], block scales [rows, k / block] row-major or swizzled,
+ * outer fp32 [rows] (nullable). mode KAB_FP4_TENSOR reads the call's amax from *amax
+ * (kab_amax); KAB_FP4_WEIGHT reads *tensor_scale (kab_fp4_tensor_scale). `up`, `h`: the
+ * fused SiLU * up producer (triton_fp4_producers.py:297-328). */
+int kab_quant_fp4(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                  const void* up, int64_t ldu, int fmt, int mode, const float* amax,
+                  const float* tensor_scale, uint8_t* q, uint8_t* scales, int swizzle,
+                  float* outer, void* h, void* stream);
+
+/* NaN-keeping max |x| of a [rows, k] matrix into *out, which must hold 0 (or a smaller
+ * value to fold in) before the call. */
+int kab_amax(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, float* out,
+             void* stream);
+
+/* The NVFP4 weight tensor scale fp32(double(*amax) / 2688), 1 for 0 (quant.py:253-254). */
+int kab_fp4_tensor_scale(const float* amax, float* tensor_scale, void* stream);
+
+/* The unbiased exponents (int32, clamped to [-127, 127], -127 for 0) of block maxima
+ * amax[n] under rule 0 (ceil) or 1 (floor) (quant.py:479-495 mx_scale_exponents). */
+int kab_mx_exponents(const float* amax, int64_t n, int rule, int32_t* out, void* stream);
+
+/* [rows, cols] scale bytes into the swizzled layout (quant.py:550-564 swizzle_mx_scales,
+ * 1176-1182 swizzle_fp4_scales); `out` is zeroed by the caller where padding exists. */
+int kab_swizzle_scales(const uint8_t* scales, int64_t rows, int64_t cols, uint8_t* out,
+                       void* stream);
+
+/* Exact fp32 e2m1 * block scale [rows, k] of FP4 codes (quant.py:1110-1114 fp4_values). */
+int kab_fp4_values(const uint8_t* codes, const uint8_t* scales, int64_t rows, int64_t k,
+                   int fmt, float* out, void* stream);
+
+/* ------------------------------------------------------------------ comparator */
+
+/* Count slots of KabCompareResult.count */
+#define KAB_CMP_NAN_REF 0
+#define KAB_CMP_NAN_NEW 1
+#define KAB_CMP_NAN_DIFF 2
+#define KAB_CMP_PINF_REF 3
+#define KAB_CMP_PINF_NEW 4
+#define KAB_CMP_PINF_DIFF 5
+#define KAB_CMP_NINF_REF 6
+#define KAB_CMP_NINF_NEW 7
+#define KAB_CMP_NINF_DIFF 8
+#define KAB_CMP_FINITE 9
+#define KAB_CMP_MISMATCH 10
+#define KAB_CMP_NCOUNT 11
+/* Sum slots (float64, over the finite elements of ref; RR over both-finite (ref, alt)) */
+#define KAB_CMP_SUM_AA 0
+#define KAB_CMP_SUM_BB 1
+#define KAB_CMP_SUM_AB 2
+#define KAB_CMP_SUM_DD 3
+#define KAB_CMP_SUM_D 4
+#define KAB_CMP_SUM_RR 5
+#define KAB_CMP_NSUM 6
+/* Max slots (fp32): |a - b|, |a - b| / allowed, the element ratio */
+#define KAB_CMP_MAX_D 0
+#define KAB_CMP_MAX_RATIO 1
+#define KAB_CMP_MAX_ELEMENT 2
+#define KAB_CMP_NMAX 3
+
+typedef struct KabCompareResult {
+  long long count[KAB_CMP_NCOUNT];
+  double sum[KAB_CMP_NSUM];
+  float max[KAB_CMP_NMAX];
+  float pad_;
+} KabCompareResult;
+
+/* One pass of compare_tensors' element loop (compare.py:684-739) over `n` elements of
+ * ref / new (and rerounded when has_rerounded). With a = ref[i], b = new[i], d = |a - b|
+ * in fp32 and the reference's roundings:
+ *   allowed = atol + rtol * |a|                      (compare.py:698)
+ *   alt_bound:    allowed = max(allowed, alt_atol + alt_rtol * |a|)    (699-700)
+ *   widen_mode 1: allowed += widen_scalar; 2: allowed += widen_channel[i % channels] (713)
+ *   element_mode 1: den = element_first + element_rtol * |a|;
+ *                2: den = element_atol * element_scale[i % channels] + element_rtol * |a| (739)
+ * `vector` selects 16-byte loads (ref / new / rerounded 16-byte aligned). */
+typedef struct KabCompareParams {
+  const void* ref;
+  const void* new_;
+  const void* rerounded;
+  int64_t n;
+  int64_t channels;
+  int dtype;
+  int has_rerounded;
+  int vector;
+  int alt_bound;
+  float atol, rtol;
+  float alt_atol, alt_rtol;
+  int widen_mode;
+  float widen_scalar;
+  const float* widen_channel;
+  int element_mode;
+  float element_first, element_atol, element_rtol;
+  const float* element_scale;
+} KabCompareParams;
+
+/* Bytes of scratch kab_compare needs (device memory the caller provides). */
+size_t kab_compare_scratch_bytes(int64_t n);
+/* The element loop into *result (device). `scratch`: kab_compare_scratch_bytes(n) bytes. */
+int kab_compare(const KabCompareParams* params, void* scratch, size_t scratch_bytes,
+                KabCompareResult* result, void* stream);
+
+/* Per-channel RMS over the last dimension (compare.py:582-589 _channels): rms[c] =
+ * sqrt(mean over rows of v^2) with v = x (non-finite as 0) or, with `alt` non-null,
+ * v = alt - x where both are finite (compare.py:622-625). Scratch:
+ * kab_channel_rms_scratch_bytes(rows, channels) bytes. */
+size_t kab_channel_rms_scratch_bytes(int64_t rows, int64_t channels);
+int kab_channel_rms(const void* x, const void* alt, int dtype, int64_t rows,
+                    int64_t channels, float* rms, void* scratch, size_t scratch_bytes,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KAB_H_ */

@@ -1,0 +1,190 @@
+// The comparator's element loop (kernel-agent src/kernel_agent/kernels/compare.py:684-739)
+// as one fused reduction over (ref, new[, rerounded]): positions of NaN / +inf / -inf in
+// each, the finite count, the mismatch count `diff > allowed`, the largest `diff / allowed`,
+// the element ratio of the reduced tiers, and float64 sums of a^2, b^2, ab, d^2, d and
+// (alt - ref)^2. Element-wise arithmetic is the reference's fp32 with explicit roundings
+// (allowed = atol + rtol * |a| in two roundings, never an FMA), so counts and maxima equal
+// torch's on the CPU bit for bit; the sums are float64 (more accurate than torch's fp32).
+//
+// Each block writes one partial into caller-provided scratch; a one-block kernel then adds
+// the partials in index order, so the result does not depend on scheduling.
+#pragma once
+
+#include "kab_common.cuh"
+
+namespace kab {
+
+struct CmpPartial {
+  long long cnt[KAB_CMP_NCOUNT];
+  double sum[KAB_CMP_NSUM];
+  float mx[KAB_CMP_NMAX];
+  float pad[1];
+};
+
+__device__ __forceinline__ void warp_sum_partial(CmpPartial& p) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int i = 0; i < KAB_CMP_NCOUNT; ++i) p.cnt[i] += __shfl_xor_sync(0xffffffffu, p.cnt[i], o);
+#pragma unroll
+    for (int i = 0; i < KAB_CMP_NSUM; ++i) p.sum[i] += __shfl_xor_sync(0xffffffffu, p.sum[i], o);
+#pragma unroll
+    for (int i = 0; i < KAB_CMP_NMAX; ++i) p.mx[i] = amax_merge(p.mx[i], __shfl_xor_sync(0xffffffffu, p.mx[i], o));
+  }
+}
+
+// Block reduction of a partial into shared memory slot 0 (fixed order: warp by warp).
+__device__ __forceinline__ void block_sum_partial(CmpPartial& p, CmpPartial* sm) {
+  warp_sum_partial(p);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) sm[warp] = p;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    CmpPartial t = sm[0];
+    for (int w = 1; w < nw; ++w) {
+      for (int i = 0; i < KAB_CMP_NCOUNT; ++i) t.cnt[i] += sm[w].cnt[i];
+      for (int i = 0; i < KAB_CMP_NSUM; ++i) t.sum[i] += sm[w].sum[i];
+      for (int i = 0; i < KAB_CMP_NMAX; ++i) t.mx[i] = amax_merge(t.mx[i], sm[w].mx[i]);
+    }
+    sm[0] = t;
+  }
+  __syncthreads();
+}
+
+template <int T>
+__device__ __forceinline__ void cmp_element(const KabCompareParams& P, float a, float b,
+                                            float alt, int64_t i, CmpPartial& p) {
+  const bool an = a != a, bn = b != b;
+  const bool ap = a == INFINITY, bp = b == INFINITY, am = a == -INFINITY, bm = b == -INFINITY;
+  p.cnt[KAB_CMP_NAN_REF] += an; p.cnt[KAB_CMP_NAN_NEW] += bn; p.cnt[KAB_CMP_NAN_DIFF] += an != bn;
+  p.cnt[KAB_CMP_PINF_REF] += ap; p.cnt[KAB_CMP_PINF_NEW] += bp; p.cnt[KAB_CMP_PINF_DIFF] += ap != bp;
+  p.cnt[KAB_CMP_NINF_REF] += am; p.cnt[KAB_CMP_NINF_NEW] += bm; p.cnt[KAB_CMP_NINF_DIFF] += am != bm;
+  if (P.has_rerounded) {  // compare.py:622-624: diff where both ref and alt are finite
+    const bool both = isfinite(a) && isfinite(alt);
+    const float r = both ? __fsub_rn(alt, a) : 0.0f;
+    p.sum[KAB_CMP_SUM_RR] += static_cast<double>(r) * r;
+  }
+  if (!isfinite(a)) return;  // compare.py:690-693: the finite elements of the reference
+  p.cnt[KAB_CMP_FINITE] += 1;
+  const float d = fabsf(__fsub_rn(a, b));
+  const float aa = fabsf(a);
+  p.sum[KAB_CMP_SUM_AA] += static_cast<double>(a) * a;
+  p.sum[KAB_CMP_SUM_BB] += static_cast<double>(b) * b;
+  p.sum[KAB_CMP_SUM_AB] += static_cast<double>(a) * b;
+  p.sum[KAB_CMP_SUM_DD] += static_cast<double>(d) * d;
+  p.sum[KAB_CMP_SUM_D] += d;
+  p.mx[KAB_CMP_MAX_D] = amax_merge(p.mx[KAB_CMP_MAX_D], d);
+  // compare.py:698: atol + rtol * |a| (fp32, two roundings)
+  float allowed = __fadd_rn(P.atol, __fmul_rn(P.rtol, aa));
+  if (P.alt_bound) allowed = fmaxf(allowed, __fadd_rn(P.alt_atol, __fmul_rn(P.alt_rtol, aa)));
+  if (P.widen_mode == 1) allowed = __fadd_rn(allowed, P.widen_scalar);
+  else if (P.widen_mode == 2) allowed = __fadd_rn(allowed, __ldg(P.widen_channel + i % P.channels));
+  p.cnt[KAB_CMP_MISMATCH] += d > allowed;
+  // compare.py:716: diff / allowed.clamp_min(1e-30)
+  p.mx[KAB_CMP_MAX_RATIO] = amax_merge(p.mx[KAB_CMP_MAX_RATIO], __fdiv_rn(d, fmaxf(allowed, 1e-30f)));
+  if (P.element_mode != 0) {  // compare.py:739: diff / (e_atol * scale + e_rtol * |a|)
+    const float first = P.element_mode == 1 ? P.element_first
+                                            : __fmul_rn(P.element_atol, __ldg(P.element_scale + i % P.channels));
+    const float den = __fadd_rn(first, __fmul_rn(P.element_rtol, aa));
+    p.mx[KAB_CMP_MAX_ELEMENT] = amax_merge(p.mx[KAB_CMP_MAX_ELEMENT], __fdiv_rn(d, den));
+  }
+}
+
+template <int T>
+__global__ void __launch_bounds__(256)
+compare_kernel(KabCompareParams P, CmpPartial* __restrict__ partials) {
+  __shared__ CmpPartial sm[8];
+  CmpPartial p;
+#pragma unroll
+  for (int i = 0; i < KAB_CMP_NCOUNT; ++i) p.cnt[i] = 0;
+#pragma unroll
+  for (int i = 0; i < KAB_CMP_NSUM; ++i) p.sum[i] = 0.0;
+#pragma unroll
+  for (int i = 0; i < KAB_CMP_NMAX; ++i) p.mx[i] = 0.0f;
+  const int64_t n = P.n;
+  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if (P.vector) {  // 8 elements per thread per step (16-byte loads of 2-byte types)
+    const int64_t nv = n >> 3;
+    for (int64_t c = tid; c < nv; c += stride) {
+      float a[8], b[8], r[8];
+      load8<T>(P.ref, c * 8, a);
+      load8<T>(P.new_, c * 8, b);
+      if (P.has_rerounded) load8<T>(P.rerounded, c * 8, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cmp_element<T>(P, a[j], b[j], P.has_rerounded ? r[j] : 0.0f, c * 8 + j, p);
+    }
+    for (int64_t i = nv * 8 + tid; i < n; i += stride)
+      cmp_element<T>(P, load_elem<T>(P.ref, i), load_elem<T>(P.new_, i),
+                     P.has_rerounded ? load_elem<T>(P.rerounded, i) : 0.0f, i, p);
+  } else {
+    for (int64_t i = tid; i < n; i += stride)
+      cmp_element<T>(P, load_elem<T>(P.ref, i), load_elem<T>(P.new_, i),
+                     P.has_rerounded ? load_elem<T>(P.rerounded, i) : 0.0f, i, p);
+  }
+  block_sum_partial(p, sm);
+  if (threadIdx.x == 0) partials[blockIdx.x] = sm[0];
+}
+
+// Adds `count` partials in index order into *out (one block).
+__global__ void __launch_bounds__(256)
+compare_finalize_kernel(const CmpPartial* __restrict__ partials, int count, KabCompareResult* out) {
+  __shared__ CmpPartial sm[8];
+  CmpPartial p;
+#pragma unroll
+  for (int i = 0; i < KAB_CMP_NCOUNT; ++i) p.cnt[i] = 0;
+#pragma unroll
+  for (int i = 0; i < KAB_CMP_NSUM; ++i) p.sum[i] = 0.0;
+#pragma unroll
+  for (int i = 0; i < KAB_CMP_NMAX; ++i) p.mx[i] = 0.0f;
+  for (int b = threadIdx.x; b < count; b += blockDim.x) {
+    const CmpPartial& q = partials[b];
+    for (int i = 0; i < KAB_CMP_NCOUNT; ++i) p.cnt[i] += q.cnt[i];
+    for (int i = 0; i < KAB_CMP_NSUM; ++i) p.sum[i] += q.sum[i];
+    for (int i = 0; i < KAB_CMP_NMAX; ++i) p.mx[i] = amax_merge(p.mx[i], q.mx[i]);
+  }
+  block_sum_partial(p, sm);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < KAB_CMP_NCOUNT; ++i) out->count[i] = sm[0].cnt[i];
+    for (int i = 0; i < KAB_CMP_NSUM; ++i) out->sum[i] = sm[0].sum[i];
+    for (int i = 0; i < KAB_CMP_NMAX; ++i) out->max[i] = sm[0].mx[i];
+  }
+}
+
+// Per-channel (last dimension) float64 sums of squares of x (non-finite as 0) or of
+// (alt - x) where both are finite, over `rows` rows of `channels`: compare.py:582-589 and
+// 622-625. Grid (ceil(channels / 256), chunks); partial [chunk, channel] sums.
+template <int T>
+__global__ void __launch_bounds__(256)
+channel_sumsq_kernel(const void* __restrict__ x, const void* __restrict__ alt, int64_t rows,
+                     int64_t channels, int64_t rows_per_chunk, double* __restrict__ partial) {
+  const int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (c >= channels) return;
+  const int64_t r0 = blockIdx.y * rows_per_chunk;
+  const int64_t r1 = r0 + rows_per_chunk < rows ? r0 + rows_per_chunk : rows;
+  double s = 0.0;
+  for (int64_t r = r0; r < r1; ++r) {
+    const float a = load_elem<T>(x, r * channels + c);
+    float v;
+    if (alt != nullptr) {
+      const float b = load_elem<T>(alt, r * channels + c);
+      v = (isfinite(a) && isfinite(b)) ? __fsub_rn(b, a) : 0.0f;
+    } else {
+      v = isfinite(a) ? a : 0.0f;
+    }
+    s += static_cast<double>(v) * v;
+  }
+  partial[blockIdx.y * channels + c] = s;
+}
+
+// rms[c] = sqrt(fp32(sum over chunks / rows)) (a mean then a square root in fp32).
+__global__ void channel_rms_kernel(const double* __restrict__ partial, int64_t chunks,
+                                   int64_t rows, int64_t channels, float* __restrict__ rms) {
+  const int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (c >= channels) return;
+  double s = 0.0;
+  for (int64_t k = 0; k < chunks; ++k) s += partial[k * channels + c];
+  rms[c] = __fsqrt_rn(static_cast<float>(s / static_cast<double>(rows)));
+}
+
+}  // namespace kab

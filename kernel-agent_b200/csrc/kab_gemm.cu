@@ -1,0 +1,17 @@
+// Scaled GEMMs on tcgen05: device status word of this translation unit.
+#include "kab_host.h"
+
+namespace kab {
+__device__ unsigned g_gemm_status = 0;
+
+unsigned gemm_device_status(bool clear, cudaStream_t stream) {
+  unsigned v = 0;
+  cudaMemcpyFromSymbolAsync(&v, g_gemm_status, sizeof v, 0, cudaMemcpyDeviceToHost, stream);
+  cudaStreamSynchronize(stream);
+  if (clear) {
+    const unsigned zero = 0;
+    cudaMemcpyToSymbolAsync(g_gemm_status, &zero, sizeof zero, 0, cudaMemcpyHostToDevice, stream);
+  }
+  return v;
+}
+}  // namespace kab

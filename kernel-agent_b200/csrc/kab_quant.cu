@@ -1,0 +1,288 @@
+// extern "C" entry points of the quantise producers (quant.cuh): argument checks, launch
+// shapes and template dispatch.
+#include "kab_host.h"
+#include "quant.cuh"
+
+namespace kab {
+namespace {
+
+constexpr int64_t kMaxRegChunks = 16;  // chunks of 8 a thread keeps in registers
+
+// Threads per row and chunks per thread for a row of `nchunks` chunks of 8.
+void row_shape(int64_t nchunks, int& threads, int& maxc) {
+  threads = nchunks <= 128 ? 128 : 256;
+  const int64_t per = (nchunks + threads - 1) / threads;
+  maxc = per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : per <= 8 ? 8 : per <= 16 ? 16 : 0;
+}
+
+int grid_for(int64_t work_items, int threads) {
+  const int64_t blocks = (work_items + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+  return static_cast<int>(blocks < 1 ? 1 : (blocks > cap ? cap : blocks));
+}
+
+template <int T, int OUT, int SMOOTH, bool SILU>
+void launch_rows(int maxc, dim3 grid, int threads, cudaStream_t s, const void* x, int64_t ldx,
+                 const void* up, int64_t ldu, int64_t k, const float* smooth, void* q,
+                 float* scale, void* h) {
+#define KAB_ROWS(MC) quant_rows_kernel<T, MC, OUT, SMOOTH, SILU><<<grid, threads, 0, s>>>(x, ldx, up, ldu, k, smooth, q, scale, h)
+  switch (maxc) {
+    case 1: KAB_ROWS(1); break;
+    case 2: KAB_ROWS(2); break;
+    case 4: KAB_ROWS(4); break;
+    case 8: KAB_ROWS(8); break;
+    case 16: KAB_ROWS(16); break;
+    default: KAB_ROWS(0); break;
+  }
+#undef KAB_ROWS
+}
+
+int check_matrix(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, const char* name) {
+  KAB_REQUIRE(valid_dtype(dtype), "%s: unknown dtype %d", name, dtype);
+  KAB_REQUIRE(rows >= 0 && k >= 0, "%s: negative shape [%lld, %lld]", name, (long long)rows, (long long)k);
+  KAB_REQUIRE(rows == 0 || x != nullptr, "%s is null", name);
+  KAB_REQUIRE(ldx >= k, "%s: leading dimension %lld < width %lld", name, (long long)ldx, (long long)k);
+  KAB_REQUIRE(k % 8 == 0, "%s: width %lld is not a multiple of 8", name, (long long)k);
+  KAB_REQUIRE(ldx % 8 == 0, "%s: leading dimension %lld is not a multiple of 8", name, (long long)ldx);
+  KAB_REQUIRE(aligned(x, 16), "%s is not 16-byte aligned", name);
+  return KAB_OK;
+}
+
+template <int T, int FMT, int MODE, bool SILU>
+void launch_fp4(int maxc, unsigned rows, int threads, cudaStream_t s, const void* x, int64_t ldx,
+                const void* up, int64_t ldu, int64_t nrows, int64_t k, const float* amax,
+                const float* ts, int swizzle, uint8_t* q, uint8_t* scales, float* outer, void* h) {
+#define KAB_FP4(MC) quant_fp4_kernel<T, MC, FMT, MODE, SILU><<<rows, threads, 0, s>>>(x, ldx, up, ldu, nrows, k, amax, ts, swizzle, q, scales, outer, h)
+  switch (maxc) {
+    case 1: KAB_FP4(1); break;
+    case 2: KAB_FP4(2); break;
+    case 4: KAB_FP4(4); break;
+    case 8: KAB_FP4(8); break;
+    default: KAB_FP4(16); break;
+  }
+#undef KAB_FP4
+}
+template <int T, bool SILU>
+void launch_fp4_fmt(int fmt, int mode, int maxc, unsigned rows, int threads, cudaStream_t s,
+                    const void* x, int64_t ldx, const void* up, int64_t ldu, int64_t nrows,
+                    int64_t k, const float* amax, const float* ts, int swizzle, uint8_t* q,
+                    uint8_t* scales, float* outer, void* h) {
+#define KAB_FP4M(F, M) launch_fp4<T, F, M, SILU>(maxc, rows, threads, s, x, ldx, up, ldu, nrows, k, amax, ts, swizzle, q, scales, outer, h)
+  if (fmt == KAB_NVFP4) {
+    if (mode == KAB_FP4_TOKEN) KAB_FP4M(0, 0);
+    else if (mode == KAB_FP4_TENSOR) KAB_FP4M(0, 1);
+    else KAB_FP4M(0, 2);
+  } else {
+    if (mode == KAB_FP4_WEIGHT) KAB_FP4M(1, 2);
+    else KAB_FP4M(1, 0);
+  }
+#undef KAB_FP4M
+}
+}  // namespace
+}  // namespace kab
+
+using namespace kab;
+
+extern "C" {
+
+int kab_quant_rows_int8(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                        const float* smooth, int smooth_mode, int8_t* q, float* scale,
+                        void* stream) {
+  if (int e = check_matrix(x, dtype, rows, k, ldx, "x")) return e;
+  KAB_REQUIRE(smooth_mode >= 0 && smooth_mode <= 2, "smooth_mode %d not in 0..2", smooth_mode);
+  KAB_REQUIRE(smooth_mode == 0 || (smooth != nullptr && aligned(smooth, 16)),
+              "smooth factors are null or not 16-byte aligned");
+  KAB_REQUIRE(rows == 0 || (q != nullptr && scale != nullptr && aligned(q, 8)), "outputs are null or misaligned");
+  if (rows == 0) return KAB_OK;
+  int threads, maxc;
+  row_shape(k / 8, threads, maxc);
+  const cudaStream_t s = as_stream(stream);
+  const dim3 grid(static_cast<unsigned>(rows));
+#define KAB_INT8(TT, SM) launch_rows<TT, 0, SM, false>(maxc, grid, threads, s, x, ldx, nullptr, 0, k, smooth, q, scale, nullptr)
+#define KAB_INT8_SM(TT) \
+  if (smooth_mode == 0) KAB_INT8(TT, 0); else if (smooth_mode == 1) KAB_INT8(TT, 1); else KAB_INT8(TT, 2)
+  if (dtype == KAB_BF16) { KAB_INT8_SM(kBF16); }
+  else if (dtype == KAB_F16) { KAB_INT8_SM(kF16); }
+  else { KAB_INT8_SM(kF32); }
+#undef KAB_INT8_SM
+#undef KAB_INT8
+  return check_launch("kab_quant_rows_int8");
+}
+
+int kab_quant_rows_fp8(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                       const void* up, int64_t ldu, uint8_t* q, float* scale, void* h,
+                       void* stream) {
+  if (int e = check_matrix(x, dtype, rows, k, ldx, "x")) return e;
+  if (up != nullptr) {
+    if (int e = check_matrix(up, dtype, rows, k, ldu, "up")) return e;
+    KAB_REQUIRE(dtype != KAB_F32, "the fused SiLU * up producer takes bf16 or fp16");
+  }
+  KAB_REQUIRE(h == nullptr || aligned(h, 16), "h is not 16-byte aligned");
+  KAB_REQUIRE(rows == 0 || (q != nullptr && scale != nullptr && aligned(q, 8)), "outputs are null or misaligned");
+  if (rows == 0) return KAB_OK;
+  int threads, maxc;
+  row_shape(k / 8, threads, maxc);
+  const cudaStream_t s = as_stream(stream);
+  const dim3 grid(static_cast<unsigned>(rows));
+  if (up != nullptr) {
+    if (dtype == KAB_BF16) launch_rows<kBF16, 1, 0, true>(maxc, grid, threads, s, x, ldx, up, ldu, k, nullptr, q, scale, h);
+    else launch_rows<kF16, 1, 0, true>(maxc, grid, threads, s, x, ldx, up, ldu, k, nullptr, q, scale, h);
+  } else {
+    if (dtype == KAB_BF16) launch_rows<kBF16, 1, 0, false>(maxc, grid, threads, s, x, ldx, nullptr, 0, k, nullptr, q, scale, nullptr);
+    else if (dtype == KAB_F16) launch_rows<kF16, 1, 0, false>(maxc, grid, threads, s, x, ldx, nullptr, 0, k, nullptr, q, scale, nullptr);
+    else launch_rows<kF32, 1, 0, false>(maxc, grid, threads, s, x, ldx, nullptr, 0, k, nullptr, q, scale, nullptr);
+  }
+  return check_launch("kab_quant_rows_fp8");
+}
+
+int kab_quant_groups_fp8(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                         int group, uint8_t* q, float* scales, void* stream) {
+  if (int e = check_matrix(x, dtype, rows, k, ldx, "x")) return e;
+  KAB_REQUIRE(group == 32 || group == 64 || group == 128, "group %d is not 32, 64 or 128", group);
+  KAB_REQUIRE(k % group == 0, "width %lld is not a multiple of the group %d", (long long)k, group);
+  KAB_REQUIRE(rows == 0 || (q != nullptr && scales != nullptr && aligned(q, 8)), "outputs are null or misaligned");
+  if (rows == 0 || k == 0) return KAB_OK;
+  const int threads = 256;
+  const int grid = grid_for(rows * (k / 8), threads);
+  const cudaStream_t s = as_stream(stream);
+#define KAB_GROUPS(TT)                                                                          \
+  if (group == 32) quant_groups_kernel<TT, 4><<<grid, threads, 0, s>>>(x, ldx, rows, k, q, scales); \
+  else if (group == 64) quant_groups_kernel<TT, 8><<<grid, threads, 0, s>>>(x, ldx, rows, k, q, scales); \
+  else quant_groups_kernel<TT, 16><<<grid, threads, 0, s>>>(x, ldx, rows, k, q, scales)
+  if (dtype == KAB_BF16) { KAB_GROUPS(kBF16); }
+  else if (dtype == KAB_F16) { KAB_GROUPS(kF16); }
+  else { KAB_GROUPS(kF32); }
+#undef KAB_GROUPS
+  return check_launch("kab_quant_groups_fp8");
+}
+
+int kab_quant_blocks_fp8(const void* w, int dtype, int64_t n, int64_t k, int64_t ldw,
+                         uint8_t* q, float* scales, void* stream) {
+  if (int e = check_matrix(w, dtype, n, k, ldw, "w")) return e;
+  KAB_REQUIRE(n % 128 == 0 && k % 128 == 0, "weight [%lld, %lld] is not whole 128 x 128 blocks",
+              (long long)n, (long long)k);
+  KAB_REQUIRE(n == 0 || (q != nullptr && scales != nullptr && aligned(q, 8)), "outputs are null or misaligned");
+  if (n == 0 || k == 0) return KAB_OK;
+  const dim3 grid(static_cast<unsigned>(k / 128), static_cast<unsigned>(n / 128));
+  const cudaStream_t s = as_stream(stream);
+  if (dtype == KAB_BF16) quant_blocks128_kernel<kBF16><<<grid, 256, 0, s>>>(w, ldw, k, q, scales);
+  else if (dtype == KAB_F16) quant_blocks128_kernel<kF16><<<grid, 256, 0, s>>>(w, ldw, k, q, scales);
+  else quant_blocks128_kernel<kF32><<<grid, 256, 0, s>>>(w, ldw, k, q, scales);
+  return check_launch("kab_quant_blocks_fp8");
+}
+
+int kab_quant_mxfp8(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                    const void* up, int64_t ldu, int rule, uint8_t* q, uint8_t* scales,
+                    int swizzle, void* h, void* stream) {
+  if (int e = check_matrix(x, dtype, rows, k, ldx, "x")) return e;
+  KAB_REQUIRE(k % 32 == 0, "width %lld is not a multiple of the MXFP8 block (32)", (long long)k);
+  KAB_REQUIRE(rule == 0 || rule == 1, "rule %d is not 0 (ceil) or 1 (floor)", rule);
+  if (up != nullptr) {
+    if (int e = check_matrix(up, dtype, rows, k, ldu, "up")) return e;
+    KAB_REQUIRE(dtype != KAB_F32, "the fused SiLU * up producer takes bf16 or fp16");
+  }
+  KAB_REQUIRE(h == nullptr || aligned(h, 16), "h is not 16-byte aligned");
+  KAB_REQUIRE(rows == 0 || (q != nullptr && scales != nullptr && aligned(q, 8)), "outputs are null or misaligned");
+  if (rows == 0 || k == 0) return KAB_OK;
+  const int threads = 256;
+  const int grid = grid_for(rows * (k / 8), threads);
+  const cudaStream_t s = as_stream(stream);
+  if (up != nullptr) {
+    if (dtype == KAB_BF16) quant_mxfp8_kernel<kBF16, true><<<grid, threads, 0, s>>>(x, ldx, up, ldu, rows, k, rule, swizzle, q, scales, h);
+    else quant_mxfp8_kernel<kF16, true><<<grid, threads, 0, s>>>(x, ldx, up, ldu, rows, k, rule, swizzle, q, scales, h);
+  } else {
+    if (dtype == KAB_BF16) quant_mxfp8_kernel<kBF16, false><<<grid, threads, 0, s>>>(x, ldx, nullptr, 0, rows, k, rule, swizzle, q, scales, nullptr);
+    else if (dtype == KAB_F16) quant_mxfp8_kernel<kF16, false><<<grid, threads, 0, s>>>(x, ldx, nullptr, 0, rows, k, rule, swizzle, q, scales, nullptr);
+    else quant_mxfp8_kernel<kF32, false><<<grid, threads, 0, s>>>(x, ldx, nullptr, 0, rows, k, rule, swizzle, q, scales, nullptr);
+  }
+  return check_launch("kab_quant_mxfp8");
+}
+
+
+int kab_quant_fp4(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                  const void* up, int64_t ldu, int fmt, int mode, const float* amax,
+                  const float* tensor_scale, uint8_t* q, uint8_t* scales, int swizzle,
+                  float* outer, void* h, void* stream) {
+  if (int e = check_matrix(x, dtype, rows, k, ldx, "x")) return e;
+  KAB_REQUIRE(fmt == KAB_NVFP4 || fmt == KAB_MXFP4, "fmt %d is not NVFP4 (0) or MXFP4 (1)", fmt);
+  KAB_REQUIRE(mode >= 0 && mode <= 2, "mode %d not in 0..2", mode);
+  const int block = fmt == KAB_NVFP4 ? 16 : 32;
+  KAB_REQUIRE(k % block == 0, "width %lld is not a multiple of the block (%d)", (long long)k, block);
+  KAB_REQUIRE(!(fmt == KAB_NVFP4 && mode == KAB_FP4_TENSOR && amax == nullptr), "amax is null");
+  KAB_REQUIRE(!(fmt == KAB_NVFP4 && mode == KAB_FP4_WEIGHT && tensor_scale == nullptr), "tensor_scale is null");
+  KAB_REQUIRE(k / 8 <= 256 * 16, "width %lld exceeds the register-resident row (32768)", (long long)k);
+  if (up != nullptr) {
+    if (int e = check_matrix(up, dtype, rows, k, ldu, "up")) return e;
+    KAB_REQUIRE(dtype != KAB_F32, "the fused SiLU * up producer takes bf16 or fp16");
+  }
+  KAB_REQUIRE(h == nullptr || aligned(h, 16), "h is not 16-byte aligned");
+  KAB_REQUIRE(rows == 0 || (q != nullptr && scales != nullptr && aligned(q, 4)), "outputs are null or misaligned");
+  if (rows == 0 || k == 0) return KAB_OK;
+  int threads, maxc;
+  row_shape(k / 8, threads, maxc);
+  const cudaStream_t s = as_stream(stream);
+  const unsigned grid = static_cast<unsigned>(rows);
+  if (up != nullptr) {
+    if (dtype == KAB_BF16) launch_fp4_fmt<kBF16, true>(fmt, mode, maxc, grid, threads, s, x, ldx, up, ldu, rows, k, amax, tensor_scale, swizzle, q, scales, outer, h);
+    else launch_fp4_fmt<kF16, true>(fmt, mode, maxc, grid, threads, s, x, ldx, up, ldu, rows, k, amax, tensor_scale, swizzle, q, scales, outer, h);
+  } else {
+    if (dtype == KAB_BF16) launch_fp4_fmt<kBF16, false>(fmt, mode, maxc, grid, threads, s, x, ldx, nullptr, 0, rows, k, amax, tensor_scale, swizzle, q, scales, outer, nullptr);
+    else if (dtype == KAB_F16) launch_fp4_fmt<kF16, false>(fmt, mode, maxc, grid, threads, s, x, ldx, nullptr, 0, rows, k, amax, tensor_scale, swizzle, q, scales, outer, nullptr);
+    else launch_fp4_fmt<kF32, false>(fmt, mode, maxc, grid, threads, s, x, ldx, nullptr, 0, rows, k, amax, tensor_scale, swizzle, q, scales, outer, nullptr);
+  }
+  return check_launch("kab_quant_fp4");
+}
+
+int kab_amax(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, float* out,
+             void* stream) {
+  KAB_REQUIRE(valid_dtype(dtype), "unknown dtype %d", dtype);
+  KAB_REQUIRE(rows >= 0 && k >= 0 && ldx >= k, "bad shape");
+  KAB_REQUIRE(out != nullptr && (rows * k == 0 || x != nullptr), "null pointer");
+  if (rows * k == 0) return KAB_OK;
+  const int threads = 256;
+  const int grid = grid_for(rows * k / 8 + 1, threads);
+  const cudaStream_t s = as_stream(stream);
+  if (dtype == KAB_BF16) amax_kernel<kBF16><<<grid, threads, 0, s>>>(x, ldx, rows, k, out);
+  else if (dtype == KAB_F16) amax_kernel<kF16><<<grid, threads, 0, s>>>(x, ldx, rows, k, out);
+  else amax_kernel<kF32><<<grid, threads, 0, s>>>(x, ldx, rows, k, out);
+  return check_launch("kab_amax");
+}
+
+int kab_fp4_tensor_scale(const float* amax, float* tensor_scale, void* stream) {
+  KAB_REQUIRE(amax != nullptr && tensor_scale != nullptr, "null pointer");
+  fp4_tensor_scale_kernel<<<1, 1, 0, as_stream(stream)>>>(amax, tensor_scale);
+  return check_launch("kab_fp4_tensor_scale");
+}
+
+int kab_mx_exponents(const float* amax, int64_t n, int rule, int32_t* out, void* stream) {
+  KAB_REQUIRE(rule == 0 || rule == 1, "rule %d is not 0 (ceil) or 1 (floor)", rule);
+  KAB_REQUIRE(n >= 0, "negative count");
+  if (n == 0) return KAB_OK;
+  KAB_REQUIRE(amax != nullptr && out != nullptr, "null pointer");
+  mx_exponents_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(amax, n, rule, out);
+  return check_launch("kab_mx_exponents");
+}
+
+int kab_swizzle_scales(const uint8_t* scales, int64_t rows, int64_t cols, uint8_t* out,
+                       void* stream) {
+  KAB_REQUIRE(rows >= 0 && cols >= 0, "negative shape");
+  if (rows * cols == 0) return KAB_OK;
+  KAB_REQUIRE(scales != nullptr && out != nullptr, "null pointer");
+  const int grid = grid_for(rows * cols, 256);
+  swizzle_scales_kernel<<<grid, 256, 0, as_stream(stream)>>>(scales, rows, cols, out);
+  return check_launch("kab_swizzle_scales");
+}
+
+int kab_fp4_values(const uint8_t* codes, const uint8_t* scales, int64_t rows, int64_t k,
+                   int fmt, float* out, void* stream) {
+  KAB_REQUIRE(fmt == KAB_NVFP4 || fmt == KAB_MXFP4, "fmt %d is not NVFP4 (0) or MXFP4 (1)", fmt);
+  const int block = fmt == KAB_NVFP4 ? 16 : 32;
+  KAB_REQUIRE(rows >= 0 && k >= 0 && k % block == 0, "bad shape [%lld, %lld]", (long long)rows, (long long)k);
+  if (rows * k == 0) return KAB_OK;
+  KAB_REQUIRE(codes != nullptr && scales != nullptr && out != nullptr, "null pointer");
+  const int grid = grid_for(rows * k, 256);
+  fp4_values_kernel<<<grid, 256, 0, as_stream(stream)>>>(codes, scales, rows, k, fmt, out);
+  return check_launch("kab_fp4_values");
+}
+
+}  // extern "C"

@@ -1,0 +1,504 @@
+// Activation / weight quantise producers: HBM-bound, one pass over the input.
+//
+//  * per-row INT8 / FP8 (per token or per output channel), optionally fused with
+//    SiLU(gate) * up (FP8) or a SmoothQuant divisor / multiplier (INT8);
+//  * 1 x G groups and B x B blocks of FP8 (the blockwise recipe);
+//  * MXFP8 (e4m3 + e8m0 per 32), optionally fused with SiLU(gate) * up;
+//  * NVFP4 (e2m1 + e4m3 per 16 + fp32 outer / tensor scale) and MXFP4 (e2m1 + e8m0 per 32),
+//    activations and weights, optionally fused with SiLU(gate) * up;
+//  * the global amax of a matrix (NVFP4 tensor scales).
+//
+// Rows are read with 16-byte vector loads (8 elements per thread per chunk) and kept in
+// registers between the reduction and the conversion, so HBM sees one read of the input
+// and one write of the codes. Every rounding follows kernel-agent's
+// src/kernel_agent/kernels/quant.py (line numbers at each function).
+#pragma once
+
+#include "kab_common.cuh"
+
+namespace kab {
+
+constexpr float kInt8Step = 0.007874015718698502f;     // fp32(1 / 127), quant.py:764
+constexpr float kNvfp4OuterStep = 0.00037202381645329297f;  // fp32(1 / 2688), quant.py:1033
+constexpr float kFp8Max = 448.0f;
+
+// ------------------------------------------------------------------ SiLU(gate) * up
+
+// F.silu(g) * u with the rounding points of eager (triton_fp8_producers.py:136-147): the
+// SiLU rounded to the input dtype, the product rounded to it again. `expf` is CUDA's.
+template <int T>
+__device__ __forceinline__ float round_to_input(float f) {
+  if constexpr (T == kBF16) return round_bf16(f);
+  else if constexpr (T == kF16) return __half2float(__float2half_rn(f));
+  else return f;
+}
+template <int T>
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  const float a = round_to_input<T>(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+  return round_to_input<T>(__fmul_rn(a, u));
+}
+
+// Optional write of the producer's own output h (the input dtype), for checking.
+template <int T>
+__device__ __forceinline__ void store_h8(void* h, int64_t i, const float (&v)[8]) {
+  if constexpr (T == kF32) {
+    float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(h) + i);
+    p[0] = make_float4(v[0], v[1], v[2], v[3]);
+    p[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint16_t lo, hi;
+      if constexpr (T == kBF16) { lo = f32_to_bf16_bits(v[2 * j]); hi = f32_to_bf16_bits(v[2 * j + 1]); }
+      else { lo = f32_to_f16_bits(v[2 * j]); hi = f32_to_f16_bits(v[2 * j + 1]); }
+      w[j] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<char*>(h) + i * 2) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// Loads a chunk of 8 producer values: x itself, or silu(x) * up.
+template <int T, bool SILU>
+__device__ __forceinline__ void load_producer8(const void* x, const void* up, int64_t ix,
+                                               int64_t iu, float (&v)[8]) {
+  load8<T>(x, ix, v);
+  if constexpr (SILU) {
+    float u[8];
+    load8<T>(up, iu, u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = silu_mul<T>(v[j], u[j]);
+  }
+}
+
+// ------------------------------------------------------------------ MX exponent rules
+
+// frexp of an fp32 value as (ex, mantissa == 0.5): q = m * 2^ex, m in [0.5, 1); 0, inf and
+// NaN give ex = 0 with m != 0.5 (glibc's and torch's frexp).
+__device__ __forceinline__ void frexp_parts(float q, int& ex, bool& half) {
+  const uint32_t u = __float_as_uint(q) & 0x7FFFFFFFu;
+  const uint32_t E = u >> 23, f = u & 0x7FFFFFu;
+  if (u == 0 || E == 0xFF) { ex = 0; half = false; return; }
+  if (E == 0) {  // subnormal: q = f * 2^-149
+    const int p = 31 - __clz(f);
+    ex = p - 148;
+    half = (f & (f - 1)) == 0;
+    return;
+  }
+  ex = static_cast<int>(E) - 126;
+  half = f == 0;
+}
+// 2^e as fp32 (0 below 2^-149, inf from 2^128 on): torch.pow(2.0, e.double()).float().
+__device__ __forceinline__ float pow2f(int e) {
+  if (e >= 128) return __uint_as_float(0x7F800000u);
+  if (e >= -126) return __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+  if (e >= -149) return __uint_as_float(1u << (e + 149));
+  return 0.0f;
+}
+// quant.py:479-495 mx_scale_exponents for one block maximum (rule 0: ceil, 1: floor).
+__device__ __forceinline__ int mx_exponent(float a, int rule) {
+  int e;
+  if (rule == 1) {
+    int ex; bool half;
+    frexp_parts(a, ex, half);
+    e = ex - 1 - 8;
+  } else {
+    int ex; bool half;
+    frexp_parts(__fdiv_rn(a, kFp8Max), ex, half);
+    e = ex - (half ? 1 : 0);
+    e += (a > __fmul_rn(kFp8Max, pow2f(e))) ? 1 : 0;
+  }
+  if (!(a > 0.0f)) e = -127;
+  return e < -127 ? -127 : (e > 127 ? 127 : e);
+}
+// quant.py:1092-1099 (activations, MXFP4): e = ex - 3 + (m > 0.75) from frexp(bmax).
+__device__ __forceinline__ int mxfp4_act_exponent(float bmax) {
+  const uint32_t u = __float_as_uint(bmax) & 0x7FFFFFFFu;
+  int ex; bool half;
+  frexp_parts(bmax, ex, half);
+  // m > 0.75 <=> the normalised mantissa 1.f > 1.5 <=> the top fraction bit set with more
+  // bits below it, on the normalised significand
+  bool over;
+  const uint32_t E = u >> 23, f = u & 0x7FFFFFu;
+  if (u == 0 || E == 0xFF) over = false;                      // m is 0 / inf / NaN
+  else if (E != 0) over = f > 0x400000u;                      // 1.f > 1.5
+  else { const int p = 31 - __clz(f); const uint32_t g = f << (23 - p); over = (g & 0x7FFFFFu) > 0x400000u; }
+  int e = ex - 3 + (over ? 1 : 0);
+  if (!(bmax > 0.0f)) e = -127;
+  return e < -127 ? -127 : (e > 127 ? 127 : e);
+}
+// quant.py:258-261 (weights, MXFP4): ceil(log2(bmax / 6)) from frexp(bmax / 6).
+__device__ __forceinline__ int mxfp4_weight_exponent(float bmax) {
+  int ex; bool half;
+  frexp_parts(__fdiv_rn(bmax, 6.0f), ex, half);
+  int e = ex - (half ? 1 : 0);
+  if (!(bmax > 0.0f)) e = -127;
+  return e < -127 ? -127 : (e > 127 ? 127 : e);
+}
+
+// ------------------------------------------------------------------ per-row INT8 / FP8
+
+// MAXC: chunks of 8 elements each thread keeps in registers (0: reread the row).
+// OUT 0: INT8 (SMOOTH 0 none, 1 divide: activations, 2 multiply: weights); 1: FP8.
+template <int T, int MAXC, int OUT, int SMOOTH, bool SILU>
+__global__ void __launch_bounds__(256)
+quant_rows_kernel(const void* __restrict__ x, int64_t ldx, const void* __restrict__ up,
+                  int64_t ldu, int64_t k, const float* __restrict__ smooth,
+                  void* __restrict__ q, float* __restrict__ scale, void* __restrict__ h) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int64_t nchunks = k >> 3;
+  const int64_t xo = row * ldx, uo = row * ldu;
+  auto value8 = [&](int64_t c, float (&v)[8]) {
+    load_producer8<T, SILU>(x, up, xo + c * 8, uo + c * 8, v);
+    if constexpr (SMOOTH != 0) {
+      const float4* sp = reinterpret_cast<const float4*>(smooth + c * 8);
+      const float4 s0 = __ldg(sp), s1 = __ldg(sp + 1);
+      const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = SMOOTH == 1 ? __fdiv_rn(v[j], s[j]) : __fmul_rn(v[j], s[j]);
+    }
+  };
+  float cache[MAXC > 0 ? MAXC : 1][8];
+  float amax = 0.0f;
+  if constexpr (MAXC > 0) {
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) {
+      const int64_t ci = threadIdx.x + static_cast<int64_t>(c) * blockDim.x;
+      if (ci < nchunks) {
+        value8(ci, cache[c]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = amax_step(amax, cache[c][j]);
+      }
+    }
+  } else {
+    for (int64_t ci = threadIdx.x; ci < nchunks; ci += blockDim.x) {
+      float v[8];
+      value8(ci, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = amax_step(amax, v[j]);
+    }
+  }
+  amax = block_amax(amax, red);
+  float sc;
+  if constexpr (OUT == 0) sc = amax > 0.0f ? __fmul_rn(amax, kInt8Step) : 1.0f;   // quant.py:777-780
+  else sc = amax > 0.0f ? __fdiv_rn(amax, kFp8Max) : 1.0f;                        // quant.py:374-375
+  if (threadIdx.x == 0) scale[row] = sc;
+  auto emit = [&](int64_t ci, float (&v)[8]) {
+    if (h != nullptr) store_h8<T>(h, row * k + ci * 8, v);
+    if constexpr (OUT == 0) {  // quant.py:770-774: round(v / scale) to nearest even, ±127
+      uint32_t w[2] = {0, 0};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float r = clamp_keep_nan(rintf(__fdiv_rn(v[j], sc)), -127.0f, 127.0f);
+        const uint32_t b = static_cast<uint8_t>(static_cast<int8_t>(__float2int_rn(r)));
+        w[j >> 2] |= b << (8 * (j & 3));
+      }
+      *reinterpret_cast<uint2*>(reinterpret_cast<int8_t*>(q) + row * k + ci * 8) = make_uint2(w[0], w[1]);
+    } else {  // quant.py:376: (v / scale).clamp(±448) to e4m3
+      uint32_t w[2];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = clamp_keep_nan(__fdiv_rn(v[2 * j], sc), -kFp8Max, kFp8Max);
+        const float b = clamp_keep_nan(__fdiv_rn(v[2 * j + 1], sc), -kFp8Max, kFp8Max);
+        const uint32_t p = e4m3_pair(a, b);
+        if (j & 1) w[j >> 1] |= p << 16; else w[j >> 1] = p;
+      }
+      *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(q) + row * k + ci * 8) = make_uint2(w[0], w[1]);
+    }
+  };
+  if constexpr (MAXC > 0) {
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) {
+      const int64_t ci = threadIdx.x + static_cast<int64_t>(c) * blockDim.x;
+      if (ci < nchunks) emit(ci, cache[c]);
+    }
+  } else {
+    for (int64_t ci = threadIdx.x; ci < nchunks; ci += blockDim.x) {
+      float v[8];
+      value8(ci, v);
+      emit(ci, v);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ FP8 1 x G groups
+
+// fp8lib.py:22-27 fq_groups: scale = amax / 448 per group (0 -> 1), codes e4m3(v / scale).
+// LANES = G / 8 threads share a group (G = 32, 64 or 128).
+template <int T, int LANES>
+__global__ void __launch_bounds__(256)
+quant_groups_kernel(const void* __restrict__ x, int64_t ldx, int64_t rows, int64_t k,
+                    uint8_t* __restrict__ q, float* __restrict__ scales) {
+  const int64_t chunks_per_row = k >> 3;
+  const int64_t total = rows * chunks_per_row;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+       c - (threadIdx.x & 31) < total; c += stride) {
+    const bool live = c < total;
+    const int64_t row = live ? c / chunks_per_row : 0, j = live ? c % chunks_per_row : 0;
+    float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (live) load8<T>(x, row * ldx + j * 8, v);
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = amax_step(amax, v[i]);
+#pragma unroll
+    for (int o = LANES / 2; o > 0; o >>= 1) amax = amax_merge(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    float s = __fdiv_rn(amax, kFp8Max);
+    s = s > 0.0f ? s : 1.0f;  // fp8lib.py:17-18 _safe
+    if (!live) continue;
+    uint32_t w[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = clamp_keep_nan(__fdiv_rn(v[2 * i], s), -kFp8Max, kFp8Max);
+      const float b = clamp_keep_nan(__fdiv_rn(v[2 * i + 1], s), -kFp8Max, kFp8Max);
+      const uint32_t p = e4m3_pair(a, b);
+      if (i & 1) w[i >> 1] |= p << 16; else w[i >> 1] = p;
+    }
+    *reinterpret_cast<uint2*>(q + row * k + j * 8) = make_uint2(w[0], w[1]);
+    if ((j % LANES) == 0) scales[row * (k / (LANES * 8)) + j / LANES] = s;
+  }
+}
+
+// ------------------------------------------------------------------ FP8 B x B blocks
+
+// fp8lib.py:35-39 fq_block: one scale per 128 x 128 tile of a weight [N, K]; one CTA of
+// 256 threads per tile, 64 elements per thread in registers.
+template <int T>
+__global__ void __launch_bounds__(256)
+quant_blocks128_kernel(const void* __restrict__ w, int64_t ldw, int64_t k,
+                       uint8_t* __restrict__ q, float* __restrict__ scales) {
+  __shared__ float red[32];
+  const int64_t nb = blockIdx.y, kb = blockIdx.x;
+  float v[8][8];
+  float amax = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {  // 2048 chunks of 8: row = idx / 16, column chunk = idx % 16
+    const int idx = threadIdx.x + c * 256;
+    const int64_t r = nb * 128 + (idx >> 4), col = kb * 128 + (idx & 15) * 8;
+    load8<T>(w, r * ldw + col, v[c]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = amax_step(amax, v[c][j]);
+  }
+  amax = block_amax(amax, red);
+  float s = __fdiv_rn(amax, kFp8Max);
+  s = s > 0.0f ? s : 1.0f;
+  if (threadIdx.x == 0) scales[nb * (k / 128) + kb] = s;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const int idx = threadIdx.x + c * 256;
+    const int64_t r = nb * 128 + (idx >> 4), col = kb * 128 + (idx & 15) * 8;
+    uint32_t wd[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = clamp_keep_nan(__fdiv_rn(v[c][2 * i], s), -kFp8Max, kFp8Max);
+      const float b = clamp_keep_nan(__fdiv_rn(v[c][2 * i + 1], s), -kFp8Max, kFp8Max);
+      const uint32_t p = e4m3_pair(a, b);
+      if (i & 1) wd[i >> 1] |= p << 16; else wd[i >> 1] = p;
+    }
+    *reinterpret_cast<uint2*>(q + r * k + col) = make_uint2(wd[0], wd[1]);
+  }
+}
+
+// ------------------------------------------------------------------ MXFP8
+
+// quant.py:506-526 quantize_mxfp8 (and the fused SiLU * up producer): 4 lanes hold one
+// block of 32; scale byte e + 127 row-major [rows, K / 32] or in the swizzled layout.
+template <int T, bool SILU>
+__global__ void __launch_bounds__(256)
+quant_mxfp8_kernel(const void* __restrict__ x, int64_t ldx, const void* __restrict__ up,
+                   int64_t ldu, int64_t rows, int64_t k, int rule, int swizzle,
+                   uint8_t* __restrict__ q, uint8_t* __restrict__ scales, void* __restrict__ h) {
+  const int64_t cpr = k >> 3;
+  const int64_t total = rows * cpr;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t cols = k >> 5;
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+       c - (threadIdx.x & 31) < total; c += stride) {
+    const bool live = c < total;
+    const int64_t row = live ? c / cpr : 0, j = live ? c % cpr : 0;
+    float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (live) load_producer8<T, SILU>(x, up, row * ldx + j * 8, row * ldu + j * 8, v);
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = amax_step(amax, v[i]);
+    amax = amax_merge(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = amax_merge(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    if (!live) continue;
+    const int e = mx_exponent(amax, rule);
+    const float inv = pow2_neg(e);  // x / 2^e == x * 2^-e exactly
+    if (SILU && h != nullptr) store_h8<T>(h, row * k + j * 8, v);
+    uint32_t w[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = clamp_keep_nan(__fmul_rn(v[2 * i], inv), -kFp8Max, kFp8Max);
+      const float b = clamp_keep_nan(__fmul_rn(v[2 * i + 1], inv), -kFp8Max, kFp8Max);
+      const uint32_t p = e4m3_pair(a, b);
+      if (i & 1) w[i >> 1] |= p << 16; else w[i >> 1] = p;
+    }
+    *reinterpret_cast<uint2*>(q + row * k + j * 8) = make_uint2(w[0], w[1]);
+    if ((j & 3) == 0) {
+      const int64_t col = j >> 2;
+      const int64_t off = swizzle ? scale_offset_swizzled(row, col, cols) : row * cols + col;
+      scales[off] = static_cast<uint8_t>(e + 127);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ NVFP4 / MXFP4
+
+// FMT 0: NVFP4 (16 per e4m3 scale), 1: MXFP4 (32 per e8m0 scale).
+// MODE 0: activations per token (outer from the row's amax), 1: activations with one amax
+// per call (*amax_in), 2: weights (tensor scale *ts_in; quant.py:217-272).
+// One CTA per row; MAXC chunks of 8 per thread in registers.
+template <int T, int MAXC, int FMT, int MODE, bool SILU>
+__global__ void __launch_bounds__(256)
+quant_fp4_kernel(const void* __restrict__ x, int64_t ldx, const void* __restrict__ up,
+                 int64_t ldu, int64_t rows, int64_t k, const float* __restrict__ amax_in,
+                 const float* __restrict__ ts_in, int swizzle, uint8_t* __restrict__ q,
+                 uint8_t* __restrict__ scales, float* __restrict__ outer_out,
+                 void* __restrict__ h) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int64_t nchunks = k >> 3;
+  constexpr int BLOCK = FMT == 0 ? 16 : 32;
+  constexpr int LANES = BLOCK / 8;
+  const int64_t cols = k / BLOCK;
+  float cache[MAXC][8];
+  float amax = 0.0f;
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    const int64_t ci = threadIdx.x + static_cast<int64_t>(c) * blockDim.x;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) cache[c][j] = 0.0f;
+    if (ci < nchunks) {
+      load_producer8<T, SILU>(x, up, row * ldx + ci * 8, row * ldu + ci * 8, cache[c]);
+      if (SILU && h != nullptr) store_h8<T>(h, row * k + ci * 8, cache[c]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = amax_step(amax, cache[c][j]);
+    }
+  }
+  float s_outer = 1.0f;  // outer (activations) or tensor scale (weights)
+  if constexpr (FMT == 0) {
+    if constexpr (MODE == 0) {
+      amax = block_amax(amax, red);
+      s_outer = amax > 0.0f ? __fmul_rn(amax, kNvfp4OuterStep) : 1.0f;  // quant.py:1104
+    } else if constexpr (MODE == 1) {
+      const float a = *amax_in;
+      s_outer = a > 0.0f ? __fmul_rn(a, kNvfp4OuterStep) : 1.0f;
+    } else {
+      s_outer = *ts_in;
+    }
+  }
+  if (threadIdx.x == 0 && outer_out != nullptr) outer_out[row] = s_outer;
+  const float div6 = __fmul_rn(s_outer, 6.0f);  // fp32(outer * 6), fp32(6 * tensor_scale)
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    const int64_t ci = threadIdx.x + static_cast<int64_t>(c) * blockDim.x;
+    float bmax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bmax = amax_step(bmax, cache[c][j]);
+#pragma unroll
+    for (int o = LANES / 2; o > 0; o >>= 1) bmax = amax_merge(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+    if (ci >= nchunks) continue;
+    uint32_t sbyte;
+    float step;
+    bool clamp_min = false;
+    if constexpr (FMT == 0) {
+      const float ratio = __fdiv_rn(bmax, div6);
+      sbyte = e4m3_byte(min_keep_nan(ratio, 448.0f));
+      step = __fmul_rn(e4m3_value(static_cast<uint8_t>(sbyte)), s_outer);
+      clamp_min = MODE == 2;  // weights divide by step.clamp_min(1e-38) (quant.py:265)
+    } else {
+      const int e = MODE == 2 ? mxfp4_weight_exponent(bmax) : mxfp4_act_exponent(bmax);
+      sbyte = static_cast<uint32_t>(e + 127);
+      step = e8m0_value(static_cast<uint8_t>(sbyte));
+      clamp_min = MODE == 2;
+    }
+    const float div = (clamp_min && step < 1e-38f) ? 1e-38f : step;
+    uint32_t packed = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint32_t code = 0;
+      if (step > 0.0f) code = e2m1_code(clamp_keep_nan(__fdiv_rn(cache[c][j], div), -6.0f, 6.0f));
+      packed |= code << (4 * j);
+    }
+    *reinterpret_cast<uint32_t*>(q + row * (k >> 1) + ci * 4) = packed;
+    if ((ci % LANES) == 0) {
+      const int64_t col = ci / LANES;
+      const int64_t off = swizzle ? scale_offset_swizzled(row, col, cols) : row * cols + col;
+      scales[off] = static_cast<uint8_t>(sbyte);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ global amax
+
+// NaN-keeping max |x| of a [rows, k] matrix into *out (which holds 0 before the launch):
+// non-negative floats order like their bits, and a NaN (0x7FC00000) beats +inf.
+template <int T>
+__global__ void __launch_bounds__(256)
+amax_kernel(const void* __restrict__ x, int64_t ldx, int64_t rows, int64_t k, float* out) {
+  __shared__ float red[32];
+  float amax = 0.0f;
+  const int64_t total = rows * k;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / k, c = i % k;
+    amax = amax_step(amax, load_elem<T>(x, r * ldx + c));
+  }
+  amax = block_amax(amax, red);
+  if (threadIdx.x == 0) {
+    const uint32_t bits = amax != amax ? 0x7FC00000u : __float_as_uint(amax);
+    atomicMax(reinterpret_cast<unsigned int*>(out), bits);
+  }
+}
+
+// tensor_scale = fp32(double(amax) / (6 * 448)), 1 for a zero amax (quant.py:253-254).
+__global__ void fp4_tensor_scale_kernel(const float* amax, float* ts) {
+  const float a = *amax;
+  *ts = a > 0.0f ? __double2float_rn(static_cast<double>(a) / 2688.0) : 1.0f;
+}
+
+// quant.py:479-495 mx_scale_exponents over a vector of block maxima.
+__global__ void mx_exponents_kernel(const float* __restrict__ amax, int64_t n, int rule,
+                                    int* __restrict__ out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = mx_exponent(amax[i], rule);
+}
+
+// ------------------------------------------------------------------ layout helpers
+
+// quant.py:550-564: [rows, cols] bytes -> the flat 128 x 4 blocked layout (padding written
+// as 0 by the caller's zeroed buffer).
+__global__ void swizzle_scales_kernel(const uint8_t* __restrict__ s, int64_t rows, int64_t cols,
+                                      uint8_t* __restrict__ out) {
+  const int64_t total = rows * cols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols, c = i % cols;
+    out[scale_offset_swizzled(r, c, cols)] = s[i];
+  }
+}
+
+// Exact fp32 values e2m1 * block scale [rows, K] of packed FP4 codes (quant.py:1110-1114).
+__global__ void fp4_values_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales,
+                                  int64_t rows, int64_t k, int fmt, float* __restrict__ out) {
+  const int block = fmt == 0 ? 16 : 32;
+  const int64_t total = rows * k;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / k, c = i % k;
+    const uint8_t byte = codes[r * (k >> 1) + (c >> 1)];
+    const uint32_t code = (c & 1) ? (byte >> 4) : (byte & 0xF);
+    const uint32_t idx = code & 7;
+    const float mag = idx <= 4 ? 0.5f * static_cast<float>(idx) : static_cast<float>(idx - 2) + (idx == 7 ? 1.0f : 0.0f);
+    const float v = (code & 8) ? -mag : mag;
+    const uint8_t sb = scales[r * (k / block) + c / block];
+    const float s = fmt == 0 ? e4m3_value(sb) : e8m0_value(sb);
+    out[i] = __fmul_rn(v, s);
+  }
+}
+
+}  // namespace kab

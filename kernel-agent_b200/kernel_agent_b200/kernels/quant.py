@@ -1,0 +1,391 @@
+"""GPU drop-in for ``kernel_agent.kernels.quant`` (kernel-agent 0.1.0,
+``src/kernel_agent/kernels/quant.py``): the same names, arguments, return tuples, dtypes and
+errors, computed by ``libkab.so`` on an sm_100a GPU.
+
+Every function takes CUDA tensors (a CPU tensor raises ``ValueError("CUDA tensor
+required")``: there is no CPU fallback) and returns new contiguous tensors on the input's
+device, allocated through torch's caching allocator on the current stream (no host
+synchronisation on the quantise paths, so they can be captured in a CUDA graph). Codes and
+scales are bit for bit the reference's; the linears' outputs are the block-scaled fp32
+products of the same codes (the tensor core's accumulation order) with the reference's
+epilogue roundings.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Any
+
+import torch
+
+from .. import _native as nat
+
+# ------------------------------------------------------------------ constants (quant.py)
+
+#: Largest finite value of each FP8 format (quant.py:98).
+FP8_MAX = {torch.float8_e4m3fn: 448.0, torch.float8_e5m2: 57344.0}
+#: e2m1 magnitudes of codes 0..7 (quant.py:189-190).
+E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+FP4_MAX = 6.0
+#: Block-scaled FP4 formats (quant.py:194-197).
+FP4_FORMATS: dict[str, tuple[int, torch.dtype]] = {
+    "nvfp4": (16, torch.float8_e4m3fn),
+    "mxfp4": (32, torch.float8_e8m0fnu),
+}
+#: MXFP8 block and scale rules (quant.py:464-474).
+MX_BLOCK = 32
+MX_RULES = ("ceil", "floor")
+MX_SATURATION_SLACK = 2.0**-10
+#: INT8 (quant.py:760-767).
+INT8_MAX = 127.0
+INT8_STEP = float(torch.tensor(1.0 / 127.0, dtype=torch.float32))
+#: NVFP4 outer-scale step and granularities (quant.py:1033-1039).
+NVFP4_OUTER_STEP = float(torch.tensor(1.0 / (FP4_MAX * 448.0), dtype=torch.float32))
+FP4_GRANULARITIES = ("token", "tensor")
+#: The NVFP4 scale-rule bounds (quant.py:1291-1296).
+NVFP4_ROUNDING_RATIO = FP4_MAX * (1 + 2.0**-4)
+FP4_SATURATION_SLACK = 2.0**-10
+E4M3_MIN_NORMAL = 2.0**-6
+NVFP4_STRESS_RATIOS = (
+    *(1.1125 * 2.0**e for e in range(-6, 8)),
+    *((k + 0.7) * 2.0**-9 for k in range(1, 6)),
+)
+#: The reference records torch._int_mm failures per device here (quant.py:851); this
+#: package's INT8 GEMM is its own tcgen05 kernel and never falls back, so it stays empty.
+INT_MM_FAILED: dict[tuple[str, str], str] = {}
+
+_E4M3 = torch.float8_e4m3fn
+_E8M0 = torch.float8_e8m0fnu
+_RULE = {"ceil": 0, "floor": 1}
+
+
+def _sig(value: float, digits: int = 4) -> float:
+    return float(f"{value:.{digits}g}") if math.isfinite(value) else value
+
+
+def _rows(x: torch.Tensor) -> torch.Tensor:
+    """``x.reshape(-1, K)`` with unit stride along K and 16-byte aligned rows."""
+    x2 = x.detach().reshape(-1, x.shape[-1]) if x.dim() != 2 else x.detach()
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    return x2
+
+
+def _stream(t: torch.Tensor) -> int:
+    return nat.stream_of(t)
+
+
+def _input(x: torch.Tensor) -> torch.Tensor:
+    """A floating-point input the kernels read (fp32, bf16 or fp16)."""
+    if x.dtype not in nat.DTYPES:
+        x = x.float()
+    return x
+
+
+def _amax(x2: torch.Tensor) -> torch.Tensor:
+    """NaN-keeping max |x| (0-d fp32 on the device)."""
+    out = torch.zeros((), dtype=torch.float32, device=x2.device)
+    nat.call("kab_amax", x2.data_ptr(), nat.dtype_code(x2), x2.shape[0], x2.shape[1], x2.stride(0),
+             out.data_ptr(), _stream(x2))
+    return out
+
+
+def _require_finite(x2: torch.Tensor) -> None:
+    """quant.py:114-115: non-finite weights are refused (one device-to-host read)."""
+    if x2.numel() and not math.isfinite(float(_amax(x2))):
+        raise ValueError("the weight has non-finite values")
+
+
+# ------------------------------------------------------------------ FP8 per token / channel
+
+
+def quantize_fp8(
+    weight: torch.Tensor, dtype: torch.dtype = torch.float8_e4m3fn
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """quant.py:101-119: ``(q, scale)`` of a 2-D weight ``[out, in]``, one scale ``amax /
+    448`` per output channel (1 for a zero row), e4m3 codes to nearest even."""
+    if weight.dim() != 2:
+        raise ValueError(f"expected a 2-D weight [out, in], got shape {tuple(weight.shape)}")
+    if dtype not in FP8_MAX:
+        raise ValueError(f"unsupported FP8 dtype {dtype}")
+    if dtype != _E4M3:
+        raise ValueError(f"unsupported FP8 dtype {dtype} (this build quantises to float8_e4m3fn)")
+    nat.require_cuda(weight)
+    w = _rows(_input(weight))
+    _require_finite(w)
+    return _fp8_rows(w)
+
+
+def _fp8_rows(x2: torch.Tensor, up: torch.Tensor | None = None, h: torch.Tensor | None = None):
+    m, k = x2.shape
+    q = torch.empty(m, k, dtype=_E4M3, device=x2.device)
+    s = torch.empty(m, dtype=torch.float32, device=x2.device)
+    if m:
+        nat.call("kab_quant_rows_fp8", x2.data_ptr(), nat.dtype_code(x2), m, k, x2.stride(0),
+                 nat.ptr(up), 0 if up is None else up.stride(0), q.data_ptr(), s.data_ptr(),
+                 nat.ptr(h), _stream(x2))
+    return q, s
+
+
+def quantize_fp8_activations(
+    x: torch.Tensor, dtype: torch.dtype = torch.float8_e4m3fn
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """quant.py:361-377: ``(q [tokens, in], scale [tokens])``, per token ``amax / 448``."""
+    if dtype not in FP8_MAX:
+        raise ValueError(f"unsupported FP8 dtype {dtype}")
+    if dtype != _E4M3:
+        raise ValueError(f"unsupported FP8 dtype {dtype} (this build quantises to float8_e4m3fn)")
+    nat.require_cuda(x)
+    return _fp8_rows(_rows(_input(x)))
+
+
+def dequantize_fp8(q: torch.Tensor, scale: torch.Tensor, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """quant.py:122-126: ``q * scale[:, None]`` (fp32 product, one rounding to ``dtype``)."""
+    nat.require_cuda(q, scale)
+    return (q.float() * scale.float()[:, None]).to(dtype)
+
+
+# ------------------------------------------------------------------ INT8
+
+
+def _smooth_of(smooth: torch.Tensor | None, k: int, device: torch.device) -> torch.Tensor | None:
+    """quant.py:783-791."""
+    if smooth is None:
+        return None
+    s = smooth.detach().float().to(device).reshape(-1).contiguous()
+    if s.numel() != k:
+        raise ValueError(f"expected {k} smoothing factors (one per input channel), got {s.numel()}")
+    lo = _amax((-s).clamp_min(0).reshape(1, -1))  # > 0 when some factor is negative
+    if not math.isfinite(float(_amax(s.reshape(1, -1)))) or float(lo) > 0 or bool((s == 0).any()):
+        raise ValueError("smoothing factors must be finite and positive")
+    return s
+
+
+def _int8_rows(x2: torch.Tensor, smooth: torch.Tensor | None, mode: int):
+    m, k = x2.shape
+    q = torch.empty(m, k, dtype=torch.int8, device=x2.device)
+    s = torch.empty(m, dtype=torch.float32, device=x2.device)
+    if m:
+        nat.call("kab_quant_rows_int8", x2.data_ptr(), nat.dtype_code(x2), m, k, x2.stride(0),
+                 nat.ptr(smooth), mode if smooth is not None else 0, q.data_ptr(), s.data_ptr(),
+                 _stream(x2))
+    return q, s
+
+
+def quantize_int8(weight: torch.Tensor, smooth: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """quant.py:794-813: per-output-channel int8 ``(q, scale)``, ``scale = amax * INT8_STEP``
+    (1 for a zero row), codes ``round(w / scale)`` to nearest even, clamped to ±127; with
+    ``smooth`` the weight is ``weight * smooth[None, :]``."""
+    if weight.dim() != 2:
+        raise ValueError(f"expected a 2-D weight [out, in], got shape {tuple(weight.shape)}")
+    nat.require_cuda(weight)
+    w = _rows(_input(weight))
+    _require_finite(w)
+    s = _smooth_of(smooth, w.shape[1], w.device)
+    return _int8_rows(w, s, 2)
+
+
+def quantize_int8_activations(x: torch.Tensor, smooth: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """quant.py:823-839: per-token int8 ``(q [tokens, in], scale [tokens])`` of ``x`` (of ``x /
+    smooth`` with SmoothQuant factors)."""
+    nat.require_cuda(x)
+    x2 = _rows(_input(x))
+    s = _smooth_of(smooth, x2.shape[1], x2.device)
+    return _int8_rows(x2, s, 1)
+
+
+def dequantize_int8(q: torch.Tensor, scale: torch.Tensor, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """quant.py:816-820."""
+    nat.require_cuda(q, scale)
+    return (q.float() * scale.float()[:, None]).to(dtype)
+
+
+# ------------------------------------------------------------------ MXFP8
+
+
+def mx_scale_exponents(amax: torch.Tensor, rule: str = "ceil") -> torch.Tensor:
+    """quant.py:479-495: the unbiased exponents (int32) of blocks with maxima ``amax``."""
+    if rule not in MX_RULES:
+        raise ValueError(f"unknown MXFP8 scale rule {rule!r} (one of {', '.join(MX_RULES)})")
+    nat.require_cuda(amax)
+    a = amax.detach().float().reshape(-1).contiguous()
+    out = torch.empty(a.shape, dtype=torch.int32, device=a.device)
+    if a.numel():
+        nat.call("kab_mx_exponents", a.data_ptr(), a.numel(), _RULE[rule], out.data_ptr(), _stream(a))
+    return out.reshape(amax.shape)
+
+
+def mx_scale_values(scales: torch.Tensor) -> torch.Tensor:
+    """quant.py:498-503."""
+    if scales.dtype == torch.uint8:
+        scales = scales.view(_E8M0)
+    return scales.float()
+
+
+def _mx_outputs(m: int, k: int, device, swizzle: bool):
+    cols = k // MX_BLOCK
+    if swizzle:
+        size = -(-m // 128) * 128 * (-(-cols // 4)) * 4
+        pad = m % 128 != 0 or cols % 4 != 0
+        s = (torch.zeros if pad else torch.empty)(size, dtype=torch.uint8, device=device)
+    else:
+        s = torch.empty(m, cols, dtype=torch.uint8, device=device)
+    return torch.empty(m, k, dtype=_E4M3, device=device), s
+
+
+def _mxfp8(x2, rule: str, up=None, swizzle=False, h=None):
+    m, k = x2.shape
+    q, s = _mx_outputs(m, k, x2.device, swizzle)
+    if m and k:
+        nat.call("kab_quant_mxfp8", x2.data_ptr(), nat.dtype_code(x2), m, k, x2.stride(0),
+                 nat.ptr(up), 0 if up is None else up.stride(0), _RULE[rule], q.data_ptr(),
+                 s.data_ptr(), int(swizzle), nat.ptr(h), _stream(x2))
+    return q, s
+
+
+def quantize_mxfp8(x: torch.Tensor, rule: str = "ceil") -> tuple[torch.Tensor, torch.Tensor]:
+    """quant.py:506-526: ``(codes e4m3 [rows, K], scales e8m0 [rows, K / 32])`` (unswizzled)."""
+    k = x.shape[-1]
+    if k % MX_BLOCK:
+        raise ValueError(f"the last dimension {k} is not a multiple of the MXFP8 block (32)")
+    if rule not in MX_RULES:
+        raise ValueError(f"unknown MXFP8 scale rule {rule!r} (one of {', '.join(MX_RULES)})")
+    nat.require_cuda(x)
+    q, s = _mxfp8(_rows(_input(x)), rule)
+    return q, s.view(_E8M0)
+
+
+def dequantize_mxfp8(codes: torch.Tensor, scales: torch.Tensor, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """quant.py:529-537."""
+    nat.require_cuda(codes, scales)
+    rows, k = codes.shape
+    values = codes.float().reshape(rows, k // MX_BLOCK, MX_BLOCK)
+    step = mx_scale_values(scales).reshape(rows, k // MX_BLOCK, 1)
+    return (values * step).reshape(rows, k).to(dtype)
+
+
+def mx_scale_offset(row: Any, col: Any, cols: int) -> Any:
+    """quant.py:540-547: offset of scale ``[row, col]`` in the swizzled layout (ints or
+    integer tensors)."""
+    blocks_per_row = -(-cols // 4)
+    block = (row // 128) * blocks_per_row + col // 4
+    return block * 512 + (row % 32) * 16 + ((row % 128) // 32) * 4 + col % 4
+
+
+def _swizzle(s: torch.Tensor) -> torch.Tensor:
+    rows, cols = s.shape
+    nrb, ncb = -(-rows // 128), -(-cols // 4)
+    out = torch.zeros(nrb * 128 * ncb * 4, dtype=torch.uint8, device=s.device)
+    if rows and cols:
+        s = s.contiguous()
+        nat.call("kab_swizzle_scales", s.data_ptr(), rows, cols, out.data_ptr(), _stream(s))
+    return out
+
+
+def swizzle_mx_scales(scales: torch.Tensor) -> torch.Tensor:
+    """quant.py:550-564: ``[rows, K / 32]`` e8m0 / uint8 scales -> the flat 128 x 4 layout."""
+    s = scales.view(torch.uint8) if scales.dtype == _E8M0 else scales
+    if s.dtype != torch.uint8 or s.dim() != 2:
+        raise ValueError(f"expected [rows, K / 32] e8m0 / uint8 scales, got {s.dtype} {s.shape}")
+    nat.require_cuda(s)
+    return _swizzle(s).view(_E8M0)
+
+
+def swizzle_fp4_scales(scales: torch.Tensor) -> torch.Tensor:
+    """quant.py:1176-1182: FP4 block scales -> the flat 128 x 4 layout, in their dtype."""
+    nat.require_cuda(scales)
+    return _swizzle(scales.view(torch.uint8)).view(scales.dtype)
+
+
+# ------------------------------------------------------------------ FP4
+
+
+def fp4_values(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """quant.py:1110-1114: exact fp32 ``e2m1 * block scale`` ``[rows, K]``."""
+    nat.require_cuda(codes, scales)
+    rows, half = codes.shape
+    k = 2 * half
+    fmt = nat.KAB_NVFP4 if scales.dtype in (_E4M3, torch.uint8) and k // max(scales.shape[1], 1) == 16 else nat.KAB_MXFP4
+    out = torch.empty(rows, k, dtype=torch.float32, device=codes.device)
+    if rows and k:
+        c, s = codes.contiguous(), scales.contiguous().view(torch.uint8)
+        nat.call("kab_fp4_values", c.data_ptr(), s.data_ptr(), rows, k, fmt, out.data_ptr(), _stream(c))
+    return out
+
+
+def _fp4(x2, fmt: str, mode: int, amax=None, ts=None, up=None, swizzle=False, h=None):
+    block, scale_dtype = FP4_FORMATS[fmt]
+    m, k = x2.shape
+    cols = k // block
+    q = torch.empty(m, k // 2, dtype=torch.uint8, device=x2.device)
+    if swizzle:
+        size = -(-m // 128) * 128 * (-(-cols // 4)) * 4
+        pad = m % 128 != 0 or cols % 4 != 0
+        s = (torch.zeros if pad else torch.empty)(size, dtype=torch.uint8, device=x2.device)
+    else:
+        s = torch.empty(m, cols, dtype=torch.uint8, device=x2.device)
+    outer = torch.empty(m, dtype=torch.float32, device=x2.device)
+    if m and k:
+        nat.call("kab_quant_fp4", x2.data_ptr(), nat.dtype_code(x2), m, k, x2.stride(0), nat.ptr(up),
+                 0 if up is None else up.stride(0), nat.KAB_NVFP4 if fmt == "nvfp4" else nat.KAB_MXFP4,
+                 mode, nat.ptr(amax), nat.ptr(ts), q.data_ptr(), s.data_ptr(), int(swizzle),
+                 outer.data_ptr(), nat.ptr(h), _stream(x2))
+    elif m:
+        outer.fill_(1.0)
+    return q, s.view(scale_dtype), outer
+
+
+def quantize_fp4(
+    weight: torch.Tensor, fmt: str = "nvfp4", unbiased: bool = False
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """quant.py:217-272: ``(codes [out, in / 2], scales [out, in / block], tensor_scale)``;
+    NVFP4 ``tensor_scale = amax / (6 * 448)`` (a 0-d fp32 tensor), MXFP4 1."""
+    if weight.dim() != 2:
+        raise ValueError(f"expected a 2-D weight [out, in], got shape {tuple(weight.shape)}")
+    if fmt not in FP4_FORMATS:
+        raise ValueError(f"unknown FP4 format {fmt!r} (one of {', '.join(FP4_FORMATS)})")
+    block, _ = FP4_FORMATS[fmt]
+    rows, cols = weight.shape
+    if cols % block:
+        raise ValueError(f"in_features {cols} is not a multiple of the {fmt} block ({block})")
+    if unbiased:
+        raise NotImplementedError("quantize_fp4(unbiased=True): the bias correction is not built yet")
+    nat.require_cuda(weight)
+    w = _rows(_input(weight))
+    amax = _amax(w)
+    if w.numel() and not math.isfinite(float(amax)):
+        raise ValueError("the weight has non-finite values")
+    if fmt == "nvfp4":
+        ts = torch.empty((), dtype=torch.float32, device=w.device)
+        nat.call("kab_fp4_tensor_scale", amax.data_ptr(), ts.data_ptr(), _stream(w))
+    else:
+        ts = torch.ones((), dtype=torch.float32, device=w.device)
+    q, s, _ = _fp4(w, fmt, nat.KAB_FP4_WEIGHT, ts=ts)
+    return q, s, ts
+
+
+def quantize_fp4_activations(
+    x: torch.Tensor, fmt: str = "nvfp4", granularity: str = "token"
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """quant.py:1056-1107: ``(codes [rows, K / 2], scales [rows, K / block], outer [rows])``."""
+    if fmt not in FP4_FORMATS:
+        raise ValueError(f"unknown FP4 format {fmt!r} (one of {', '.join(FP4_FORMATS)})")
+    if granularity not in FP4_GRANULARITIES:
+        raise ValueError(f"unknown granularity {granularity!r} ({', '.join(FP4_GRANULARITIES)})")
+    block, _ = FP4_FORMATS[fmt]
+    k = x.shape[-1]
+    if k % block:
+        raise ValueError(f"the last dimension {k} is not a multiple of the {fmt} block ({block})")
+    nat.require_cuda(x)
+    x2 = _rows(_input(x))
+    if fmt == "nvfp4" and granularity == "tensor":
+        return _fp4(x2, fmt, nat.KAB_FP4_TENSOR, amax=_amax(x2))
+    return _fp4(x2, fmt, nat.KAB_FP4_TOKEN)
+
+
+def dequantize_fp4(codes, scales, tensor_scale, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """quant.py:275-294: ``e2m1 * scale * tensor_scale`` in fp32, one rounding to ``dtype``."""
+    v = fp4_values(codes, scales)
+    ts = torch.as_tensor(tensor_scale, dtype=torch.float32, device=v.device)
+    ts = ts.reshape(()) if ts.numel() == 1 else ts.reshape(-1, 1)
+    return (v * ts).to(dtype)
