@@ -128,6 +128,42 @@ int kab_swizzle_scales(const uint8_t* scales, int64_t rows, int64_t cols, uint8_
 int kab_fp4_values(const uint8_t* codes, const uint8_t* scales, int64_t rows, int64_t k,
                    int fmt, float* out, void* stream);
 
+/* ------------------------------------------------------------------ scaled GEMMs (tcgen05) */
+
+/* A [m, k] and B [n, k] are K-major (row-major, K contiguous; B is an nn.Linear weight),
+ * 16-byte aligned, with k * (bytes per element) a positive multiple of 128. The output
+ * [m, ldo] (ldo >= n, a multiple of 8) is bf16 / fp16 / fp32 (out_dtype); `bias` (nullable,
+ * [n], bias_dtype) is added in the epilogue. One persistent CTA per SM. */
+
+/* int8 x int8 -> exact int32 (kind::i8). With acc_out non-null: the raw int32 products
+ * [m, ldo] (quant.py:854-885 int8_matmul); else out = acc * a_scale[m] * b_scale[n]
+ * (+ bias) in fp32, one rounding (quant.py:901-923 int8_w8a8_linear's epilogue). */
+int kab_gemm_i8(const int8_t* a, const int8_t* b, int64_t m, int64_t n, int64_t k,
+                const float* a_scale, const float* b_scale, const void* bias, int bias_dtype,
+                void* out, int out_dtype, int64_t ldo, int32_t* acc_out, void* stream);
+
+/* e4m3 x e4m3 -> fp32 (kind::f8f6f4); out = acc * a_scale[m] * b_scale[n] (+ bias)
+ * (quant.py:390-417 fp8_w8a8_linear, torch._scaled_mm with row-wise scales). */
+int kab_gemm_f8(const uint8_t* a, const uint8_t* b, int64_t m, int64_t n, int64_t k,
+                const float* a_scale, const float* b_scale, const void* bias, int bias_dtype,
+                void* out, int out_dtype, int64_t ldo, void* stream);
+
+/* MXFP8: e4m3 with e8m0 scales per 32 along K on both operands (swizzled layout), applied
+ * by the tensor core (kind::mxf8f6f4.block_scale); out = round(acc) (+ bias) in out_dtype
+ * (quant.py:581-620 mxfp8_linear, F.scaled_mm BlockWise1x32 then + bias). n % 128 == 0. */
+int kab_gemm_mxf8(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf,
+                  int64_t m, int64_t n, int64_t k, const void* bias, int bias_dtype, void* out,
+                  int out_dtype, int64_t ldo, void* stream);
+
+/* NVFP4 W4A4: packed e2m1 A [m, k/2], B [n, k/2] with e4m3 scales per 16 (swizzled), applied
+ * by the tensor core (kind::mxf4nvf4.block_scale.scale_vec::4X), fp32 accumulation;
+ * out = acc * (a_outer[m] * b_scale[0 or n]) (+ bias) in fp32, one rounding
+ * (quant.py:1201-1257 fp4_w4a4_linear). k % 256 == 0, n % 128 == 0. */
+int kab_gemm_nvf4(const uint8_t* a, const uint8_t* a_sf, const float* a_outer, const uint8_t* b,
+                  const uint8_t* b_sf, const float* b_scale, int b_scale_per_col, int64_t m,
+                  int64_t n, int64_t k, const void* bias, int bias_dtype, void* out,
+                  int out_dtype, int64_t ldo, void* stream);
+
 /* ------------------------------------------------------------------ comparator */
 
 /* Count slots of KabCompareResult.count */

@@ -1,8 +1,13 @@
-// Scaled GEMMs on tcgen05: device status word of this translation unit.
+// extern "C" entry points of the scaled GEMMs (gemm.cuh): argument checks, TMA tensor maps,
+// the persistent launch, and this translation unit's device status word.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "gemm.cuh"
 #include "kab_host.h"
 
 namespace kab {
-__device__ unsigned g_gemm_status = 0;
 
 unsigned gemm_device_status(bool clear, cudaStream_t stream) {
   unsigned v = 0;
@@ -11,7 +16,174 @@ unsigned gemm_device_status(bool clear, cudaStream_t stream) {
   if (clear) {
     const unsigned zero = 0;
     cudaMemcpyToSymbolAsync(g_gemm_status, &zero, sizeof zero, 0, cudaMemcpyHostToDevice, stream);
+    cudaStreamSynchronize(stream);
   }
   return v;
 }
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// A 2-D byte matrix [rows, cols_bytes] (row stride ld_bytes) read in boxes of
+// [box_rows, 128 bytes] with the 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols_bytes, uint64_t ld_bytes,
+             uint32_t box_rows, const char* name) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(KAB_EUNSUPPORTED, "cuTensorMapEncodeTiled is unavailable (driver too old?)");
+  cuuint64_t dims[2] = {cols_bytes, rows};
+  cuuint64_t strides[1] = {ld_bytes};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KAB_EINVAL, "tensor map of %s failed (CUresult %d)", name, static_cast<int>(r));
+  return KAB_OK;
+}
+
+template <int KIND, int BN, int STAGES, int OUT>
+int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, cudaStream_t s) {
+  using L = GemmLayout<BN, STAGES, KIND>;
+  auto kernel = gemm_kernel<KIND, BN, STAGES, OUT>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem) != cudaSuccess)
+      return fail(KAB_ECUDA, "cannot set %d bytes of shared memory", L::kSmem);
+    configured[dev] = true;
+  }
+  const int tiles = g.m_tiles * g.n_tiles;
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kernel<<<grid, 192, L::kSmem, s>>>(ma, mb, g);
+  return check_launch("gemm kernel");
+}
+
+template <int KIND, int BN>
+int launch_out(int out_dtype, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, cudaStream_t s) {
+  constexpr int STAGES = BN == 256 ? 4 : 6;
+  if (out_dtype == KAB_BF16) return launch_one<KIND, BN, STAGES, KAB_BF16>(ma, mb, g, s);
+  if (out_dtype == KAB_F16) return launch_one<KIND, BN, STAGES, KAB_F16>(ma, mb, g, s);
+  return launch_one<KIND, BN, STAGES, KAB_F32>(ma, mb, g, s);
+}
+
+// Common checks and launch: a [m, k_bytes] and b [n, k_bytes] K-major byte matrices.
+template <int KIND>
+int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, GemmArgs g, int out_dtype,
+        cudaStream_t s) {
+  KAB_REQUIRE(m >= 0 && n >= 0 && k_bytes >= 0, "negative shape");
+  if (m == 0 || n == 0) return KAB_OK;
+  KAB_REQUIRE(a != nullptr && b != nullptr, "operand is null");
+  KAB_REQUIRE(aligned(a, 16) && aligned(b, 16), "operands must be 16-byte aligned");
+  KAB_REQUIRE(k_bytes > 0 && k_bytes % 128 == 0,
+              "K must be a positive multiple of 128 bytes per row (128 int8 / e4m3, 256 e2m1); got %lld bytes",
+              (long long)k_bytes);
+  KAB_REQUIRE(out_dtype == KAB_BF16 || out_dtype == KAB_F16 || out_dtype == KAB_F32, "unknown out dtype %d", out_dtype);
+  KAB_REQUIRE(g.out != nullptr || g.acc_out != nullptr, "output is null");
+  KAB_REQUIRE(g.ldo >= n && g.ldo % 8 == 0, "ldo %lld must be >= n and a multiple of 8", (long long)g.ldo);
+  KAB_REQUIRE((g.out == nullptr || aligned(g.out, 16)) && (g.acc_out == nullptr || aligned(g.acc_out, 16)),
+              "output must be 16-byte aligned");
+  KAB_REQUIRE(m <= (int64_t(1) << 30) && n <= (int64_t(1) << 30), "shape too large");
+  const int bn = (n % 256 == 0 || !GemmTraits<KIND>::kScaled) && n >= 256 ? 256 : 128;
+  if (GemmTraits<KIND>::kScaled)
+    KAB_REQUIRE(n % 128 == 0, "block-scaled GEMMs need N a multiple of 128 (got %lld)", (long long)n);
+  g.m = m;
+  g.n = n;
+  g.k_stages = static_cast<int>(k_bytes / 128);
+  g.m_tiles = static_cast<int>((m + 127) / 128);
+  g.n_tiles = static_cast<int>((n + bn - 1) / bn);
+  CUtensorMap ma, mb;
+  if (int e = make_map(&ma, a, m, k_bytes, k_bytes, 128, "A")) return e;
+  if (int e = make_map(&mb, b, n, k_bytes, k_bytes, bn, "B")) return e;
+  if (bn == 256) return launch_out<KIND, 256>(out_dtype, ma, mb, g, s);
+  return launch_out<KIND, 128>(out_dtype, ma, mb, g, s);
+}
+
+GemmArgs args_of(const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo) {
+  GemmArgs g{};
+  g.bias = bias;
+  g.bias_dtype = bias_dtype;
+  g.out = out;
+  g.out_dtype = out_dtype;
+  g.ldo = ldo;
+  return g;
+}
+
+}  // namespace
 }  // namespace kab
+
+using namespace kab;
+
+extern "C" {
+
+int kab_gemm_i8(const int8_t* a, const int8_t* b, int64_t m, int64_t n, int64_t k, const float* a_scale,
+                const float* b_scale, const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo,
+                int32_t* acc_out, void* stream) {
+  GemmArgs g = args_of(bias, bias_dtype, out, out_dtype, ldo);
+  g.acc_out = acc_out;
+  g.a_scale = a_scale;
+  g.b_scale = b_scale;
+  if (acc_out == nullptr)
+    KAB_REQUIRE(a_scale != nullptr && b_scale != nullptr, "scales are null");
+  else
+    g.out = nullptr;
+  KAB_REQUIRE(bias == nullptr || valid_dtype(bias_dtype), "unknown bias dtype %d", bias_dtype);
+  return run<0>(a, b, m, n, k, g, acc_out != nullptr ? KAB_BF16 : out_dtype, as_stream(stream));
+}
+
+int kab_gemm_f8(const uint8_t* a, const uint8_t* b, int64_t m, int64_t n, int64_t k, const float* a_scale,
+                const float* b_scale, const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo,
+                void* stream) {
+  GemmArgs g = args_of(bias, bias_dtype, out, out_dtype, ldo);
+  g.a_scale = a_scale;
+  g.b_scale = b_scale;
+  KAB_REQUIRE(a_scale != nullptr && b_scale != nullptr, "scales are null");
+  KAB_REQUIRE(bias == nullptr || valid_dtype(bias_dtype), "unknown bias dtype %d", bias_dtype);
+  return run<1>(a, b, m, n, k, g, out_dtype, as_stream(stream));
+}
+
+int kab_gemm_mxf8(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf, int64_t m,
+                  int64_t n, int64_t k, const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo,
+                  void* stream) {
+  GemmArgs g = args_of(bias, bias_dtype, out, out_dtype, ldo);
+  KAB_REQUIRE(a_sf != nullptr && b_sf != nullptr && aligned(a_sf, 16) && aligned(b_sf, 16),
+              "block scales are null or not 16-byte aligned");
+  KAB_REQUIRE(bias == nullptr || valid_dtype(bias_dtype), "unknown bias dtype %d", bias_dtype);
+  g.sfa = a_sf;
+  g.sfb = b_sf;
+  g.sfa_ncb = g.sfb_ncb = (k / 32 + 3) / 4;
+  return run<2>(a, b, m, n, k, g, out_dtype, as_stream(stream));
+}
+
+int kab_gemm_nvf4(const uint8_t* a, const uint8_t* a_sf, const float* a_outer, const uint8_t* b,
+                  const uint8_t* b_sf, const float* b_scale, int b_scale_per_col, int64_t m, int64_t n, int64_t k,
+                  const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo, void* stream) {
+  GemmArgs g = args_of(bias, bias_dtype, out, out_dtype, ldo);
+  KAB_REQUIRE(a_sf != nullptr && b_sf != nullptr && aligned(a_sf, 16) && aligned(b_sf, 16),
+              "block scales are null or not 16-byte aligned");
+  KAB_REQUIRE(a_outer != nullptr && b_scale != nullptr, "outer / tensor scales are null");
+  KAB_REQUIRE(k % 2 == 0, "K must be even");
+  KAB_REQUIRE(bias == nullptr || valid_dtype(bias_dtype), "unknown bias dtype %d", bias_dtype);
+  g.sfa = a_sf;
+  g.sfb = b_sf;
+  g.sfa_ncb = g.sfb_ncb = (k / 16 + 3) / 4;
+  g.a_scale = a_outer;
+  g.b_scale = b_scale;
+  g.b_scale_per_col = b_scale_per_col;
+  return run<3>(a, b, m, n, k / 2, g, out_dtype, as_stream(stream));
+}
+
+}  // extern "C"

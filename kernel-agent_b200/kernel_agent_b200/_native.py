@@ -69,6 +69,14 @@ _SIGNATURES: dict[str, list] = {
     "kab_mx_exponents": [c_void_p, c_int64, c_int, c_void_p, c_void_p],
     "kab_swizzle_scales": [c_void_p, c_int64, c_int64, c_void_p, c_void_p],
     "kab_fp4_values": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_void_p, c_void_p],
+    "kab_gemm_i8": [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int,
+                    c_void_p, c_int, c_int64, c_void_p, c_void_p],
+    "kab_gemm_f8": [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int,
+                    c_void_p, c_int, c_int64, c_void_p],
+    "kab_gemm_mxf8": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int,
+                      c_void_p, c_int, c_int64, c_void_p],
+    "kab_gemm_nvf4": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64,
+                      c_int64, c_void_p, c_int, c_void_p, c_int, c_int64, c_void_p],
     "kab_compare_scratch_bytes": [c_int64],
     "kab_compare": [POINTER(KabCompareParams), c_void_p, c_size_t, c_void_p, c_void_p],
     "kab_channel_rms_scratch_bytes": [c_int64, c_int64],

@@ -19,6 +19,7 @@ from typing import Any
 import torch
 
 from .. import _native as nat
+from . import gemm
 
 # ------------------------------------------------------------------ constants (quant.py)
 
@@ -389,3 +390,132 @@ def dequantize_fp4(codes, scales, tensor_scale, dtype: torch.dtype = torch.bfloa
     ts = torch.as_tensor(tensor_scale, dtype=torch.float32, device=v.device)
     ts = ts.reshape(()) if ts.numel() == 1 else ts.reshape(-1, 1)
     return (v * ts).to(dtype)
+
+
+# ------------------------------------------------------------------ linears (tcgen05 GEMMs)
+
+
+def int8_matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """quant.py:854-885: exact int32 ``a [M, K] @ b [N, K]ᵀ`` (tcgen05 kind::i8)."""
+    if a.dtype != torch.int8 or b.dtype != torch.int8 or a.dim() != 2 or b.dim() != 2:
+        raise ValueError("int8_matmul takes 2-D int8 a [M, K] and b [N, K]")
+    if a.shape[1] != b.shape[1]:
+        raise ValueError(f"K differs: a {tuple(a.shape)}, b {tuple(b.shape)}")
+    nat.require_cuda(a)
+    b = b.to(a.device)
+    if a.shape[0] == 0:
+        return torch.zeros(0, b.shape[0], dtype=torch.int32, device=a.device)
+    return gemm.int8(a, b)
+
+
+def _linear_out(y: torch.Tensor, x: torch.Tensor, n: int) -> torch.Tensor:
+    if y.dtype != x.dtype:
+        y = y.to(x.dtype)
+    return y.reshape(*x.shape[:-1], n)
+
+
+def int8_w8a8_linear(
+    x: torch.Tensor,
+    q: torch.Tensor,
+    scale: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    *,
+    smooth: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """quant.py:901-923: per-token int8 activations, exact int32 products (tcgen05 kind::i8),
+    ``acc * x_scale[m] * w_scale[n] (+ bias)`` in fp32 with one rounding to ``x``'s dtype:
+    bit for bit the reference's result."""
+    nat.require_cuda(x, q)
+    xq, xs = quantize_int8_activations(x, smooth)
+    y = gemm.int8(xq, q, xs, scale, bias, out_dtype=x.dtype)
+    return _linear_out(y, x, q.shape[0])
+
+
+def fp8_w8a8_linear(
+    x: torch.Tensor,
+    q: torch.Tensor,
+    scale: torch.Tensor,
+    bias: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """quant.py:390-417: per-token e4m3 activations, e4m3 weight per channel, fp32
+    accumulation (tcgen05 kind::f8f6f4), both scales and the bias in the epilogue."""
+    nat.require_cuda(x, q)
+    xq, xs = quantize_fp8_activations(x, q.dtype)
+    y = gemm.fp8(xq, q, xs, scale, bias, out_dtype=x.dtype)
+    return _linear_out(y, x, q.shape[0])
+
+
+def _swizzled(scales: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
+    """Block scales in the swizzled layout: as given when already flat (1-D), else swizzled."""
+    s = scales.view(torch.uint8) if scales.dtype != torch.uint8 else scales
+    if s.dim() == 1:
+        need = -(-rows // 128) * 128 * (-(-cols // 4)) * 4
+        if s.numel() != need:
+            raise ValueError(f"swizzled scales have {s.numel()} bytes, expected {need}")
+        return s.contiguous()
+    if tuple(s.shape) != (rows, cols):
+        raise ValueError(f"expected scales [{rows}, {cols}], got {tuple(s.shape)}")
+    return _swizzle(s)
+
+
+def mxfp8_linear(
+    x: torch.Tensor,
+    q: torch.Tensor,
+    scales: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    *,
+    rule: str = "ceil",
+) -> torch.Tensor:
+    """quant.py:581-620: ``x`` quantised to MXFP8 (scales written swizzled), the block-scaled
+    GEMM (tcgen05 kind::mxf8f6f4, e8m0 per 32 on both operands) with a bf16 result, ``+ bias``
+    in bf16, then ``x``'s dtype. ``scales``: the weight's ``[N, K / 32]`` (or already
+    swizzled, flat)."""
+    nat.require_cuda(x, q)
+    k = x.shape[-1]
+    if k % MX_BLOCK:
+        raise ValueError(f"the last dimension {k} is not a multiple of the MXFP8 block (32)")
+    xq, xs = _mxfp8(_rows(_input(x)), rule, swizzle=True)
+    ws = _swizzled(scales, q.shape[0], k // MX_BLOCK)
+    y = gemm.mxf8(xq, xs, q, ws, bias, out_dtype=torch.bfloat16)
+    return _linear_out(y, x, q.shape[0])
+
+
+def fp4_w4a4_linear(
+    x: torch.Tensor,
+    codes: torch.Tensor,
+    scales: torch.Tensor,
+    tensor_scale: torch.Tensor | float,
+    bias: torch.Tensor | None = None,
+    *,
+    fmt: str = "nvfp4",
+    granularity: str = "token",
+    rotate: int | None = None,
+    unbiased: bool = False,
+) -> torch.Tensor:
+    """quant.py:1201-1257: ``x`` quantised to NVFP4 per call (block scales written swizzled,
+    outer scale per token or per call), the block-scaled GEMM (tcgen05 kind::mxf4nvf4, e4m3
+    scales per 16 applied by the tensor core, fp32 accumulation), then ``acc * (outer[m] *
+    tensor_scale) (+ bias)`` in fp32 and one rounding to ``x``'s dtype. ``scales``: the
+    weight's ``[N, K / 16]`` (or already swizzled, flat)."""
+    if fmt not in FP4_FORMATS:
+        raise ValueError(f"unknown FP4 format {fmt!r} (one of {', '.join(FP4_FORMATS)})")
+    if granularity not in FP4_GRANULARITIES:
+        raise ValueError(f"unknown granularity {granularity!r} ({', '.join(FP4_GRANULARITIES)})")
+    if fmt != "nvfp4":
+        raise NotImplementedError("fp4_w4a4_linear: MXFP4 (kind::mxf4) is not built yet; use nvfp4")
+    if rotate or unbiased:
+        raise NotImplementedError("fp4_w4a4_linear: rotate / unbiased are not built yet")
+    nat.require_cuda(x, codes)
+    k = x.shape[-1]
+    if k % 16:
+        raise ValueError(f"the last dimension {k} is not a multiple of the nvfp4 block (16)")
+    x2 = _rows(_input(x))
+    mode = nat.KAB_FP4_TENSOR if granularity == "tensor" else nat.KAB_FP4_TOKEN
+    amax = _amax(x2) if granularity == "tensor" else None
+    xq, xs, outer = _fp4(x2, "nvfp4", mode, amax=amax, swizzle=True)
+    n = codes.shape[0]
+    ws = _swizzled(scales, n, k // 16)
+    ts = torch.as_tensor(tensor_scale, dtype=torch.float32, device=x2.device)
+    y = gemm.nvf4(xq, xs.view(torch.uint8), outer, codes, ws, ts, bias,
+                  out_dtype=x.dtype if x.dtype in (torch.bfloat16, torch.float16, torch.float32) else torch.float32)
+    return _linear_out(y, x, n)

@@ -1,0 +1,192 @@
+"""The tcgen05 scaled GEMMs against the oracle: int8 products and the W8A8 INT8 linear bit
+for bit; FP8 / MXFP8 / NVFP4 linears within the bf16 tolerances the comparator applies
+(atol = rtol = 2e-2, relative L2 <= 0.02, cosine >= 0.999) and, tighter, within one bf16
+step of the float64-accumulated oracle on >= 99 % of the outputs."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import np_bf16_bits, np_bytes, np_values, ulp_distance_bf16
+from oracle import quant as oq
+from oracle.formats import bf16_to_f32, f32_to_bf16
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def kq():
+    from kernel_agent_b200.kernels import quant
+
+    return quant
+
+
+def rand_i8(g, *shape):
+    return torch.randint(-127, 128, shape, generator=g, dtype=torch.int8)
+
+
+def diagnose(got: np.ndarray, want: np.ndarray) -> str:
+    """A short description of how an integer product differs (layout bugs show as patterns)."""
+    bad = got != want
+    lines = [f"mismatch {bad.mean():.4f} of {bad.size}"]
+    idx = np.argwhere(bad)[:6]
+    for i, j in idx:
+        lines.append(f"  [{i},{j}] got {got[i, j]} want {want[i, j]}")
+    # which reference row / column does each output row / column equal?
+    for i in range(min(4, got.shape[0])):
+        hits = [r for r in range(want.shape[0]) if np.array_equal(got[i], want[r])]
+        lines.append(f"  row {i} equals reference rows {hits[:4]}")
+    for j in range(min(4, got.shape[1])):
+        hits = [c for c in range(want.shape[1]) if np.array_equal(got[:, j], want[:, c])]
+        lines.append(f"  col {j} equals reference cols {hits[:4]}")
+    lines.append(f"  got[0,:8] {got[0, :8].tolist()}")
+    lines.append(f"  want[0,:8] {want[0, :8].tolist()}")
+    return "\n".join(lines)
+
+
+def close_bf16(y: torch.Tensor, want_f32: np.ndarray, label: str) -> None:
+    got = np_values(y).astype(np.float64)
+    ref = want_f32.astype(np.float64)
+    diff = np.abs(got - ref)
+    allowed = 2e-2 + 2e-2 * np.abs(ref)
+    mism = float((diff > allowed).mean())
+    rel = float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
+    cos = float((got.ravel() @ ref.ravel()) / max(np.linalg.norm(got) * np.linalg.norm(ref), 1e-30))
+    ulps = ulp_distance_bf16(np_bf16_bits(y).reshape(-1), f32_to_bf16(want_f32).reshape(-1))
+    msg = f"{label}: mismatch {mism:.2e} rel_l2 {rel:.3e} cos {cos:.7f} same {np.mean(ulps == 0):.4f} max ulps {ulps.max()}"
+    assert mism <= 1e-3 and rel <= 0.02 and cos >= 0.999, msg
+    assert float(np.mean(ulps <= 1)) >= 0.99, msg
+
+
+def test_int8_products_layout():
+    g = torch.Generator().manual_seed(0)
+    a = rand_i8(g, 128, 128)
+    b = rand_i8(g, 256, 128)
+    from kernel_agent_b200.kernels import quant
+
+    got = quant.int8_matmul(a.to(DEV), b.to(DEV)).cpu().numpy()
+    want = oq.int8_matmul(a.numpy(), b.numpy())
+    assert np.array_equal(got, want), diagnose(got, want)
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 128, 8), (5, 3000, 24), (17, 4096, 40), (128, 1024, 1024),
+                                   (300, 512, 520), (1000, 256, 4096), (2, 4096, 3)])
+def test_int8_matmul_exact(kq, m, k, n):
+    g = torch.Generator().manual_seed(m * 7 + n)
+    a, b = rand_i8(g, m, k), rand_i8(g, n, k)
+    got = kq.int8_matmul(a.to(DEV), b.to(DEV))
+    assert got.dtype == torch.int32 and tuple(got.shape) == (m, n)
+    want = oq.int8_matmul(a.numpy(), b.numpy())
+    g2 = got.cpu().numpy()
+    assert np.array_equal(g2, want), diagnose(g2, want)
+    worst = torch.full((2, 4096), 127, dtype=torch.int8, device=DEV)
+    assert int(kq.int8_matmul(worst, -worst)[0, 0]) == -4096 * 127 * 127
+
+
+def test_int8_w8a8_linear_bit_exact_config1_and_golden(kq, golden):
+    from kernel_agent_b200 import workloads
+
+    x, w, b = workloads.config1(seed=0)
+    q, s = kq.quantize_int8(w.to(DEV))
+    y = kq.int8_w8a8_linear(x.to(DEV), q, s, b.to(DEV))
+    want = oq.int8_w8a8_linear(np_values(x), np_bytes(q).view(np.int8), s.cpu().numpy(), np_values(b))
+    assert y.dtype == torch.bfloat16 and np.array_equal(np_bf16_bits(y), want)
+    g = golden
+    xg = torch.from_numpy(g["int8_x"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    wq = torch.from_numpy(g["int8_wq"]).to(DEV)
+    ws = torch.from_numpy(g["int8_ws"]).to(DEV)
+    bg = torch.from_numpy(g["int8_bias"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    y = kq.int8_w8a8_linear(xg, wq, ws, bg)
+    assert np.array_equal(np_bf16_bits(y), g["int8_y"])  # the reference's own output bits
+    # [..., K] inputs keep their leading shape; fp32 activations give fp32 outputs
+    x3 = torch.randn(3, 7, 1024, generator=torch.Generator().manual_seed(1))
+    y3 = kq.int8_w8a8_linear(x3.to(DEV), q, s)
+    want3 = oq.int8_w8a8_linear(x3.numpy(), np_bytes(q).view(np.int8), s.cpu().numpy(), None, out_dtype="f32")
+    assert y3.shape == (3, 7, 1024) and np.array_equal(y3.reshape(21, -1).cpu().numpy(), want3)
+
+
+@pytest.mark.parametrize("m,k,n", [(128, 1024, 1024), (33, 512, 384), (2048, 1024, 3072)])
+def test_fp8_w8a8_linear(kq, m, k, n):
+    g = torch.Generator().manual_seed(m + k)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16)
+    q, s = kq.quantize_fp8(w.to(DEV))
+    y = kq.fp8_w8a8_linear(x.to(DEV), q, s, b.to(DEV))
+    xq, xs = oq.quantize_fp8_activations(np_values(x))
+    from oracle.formats import e4m3_to_f32
+
+    acc = e4m3_to_f32(xq).astype(np.float64) @ e4m3_to_f32(np_bytes(q)).astype(np.float64).T
+    want = ((acc.astype(np.float32) * xs[:, None]).astype(np.float32) * s.cpu().numpy()[None, :]).astype(np.float32)
+    want = (want + np_values(b)[None, :]).astype(np.float32)
+    close_bf16(y, want, f"fp8 {m}x{k}x{n}")
+    golden_like = oq.fp8_w8a8_linear(np_values(x), np_bytes(q), s.cpu().numpy(), np_values(b), out_dtype="f32")
+    close_bf16(y, golden_like, "fp8 vs dequant-matmul")
+
+
+@pytest.mark.parametrize("m,k,n", [(44, 256, 128), (300, 1024, 512), (4096, 14336, 256)])
+def test_mxfp8_linear(kq, m, k, n, golden):
+    g = torch.Generator().manual_seed(m)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.015).to(torch.bfloat16)
+    b = torch.randn(n, generator=g).to(torch.bfloat16)
+    q, s = kq.quantize_mxfp8(w.to(DEV))
+    y = kq.mxfp8_linear(x.to(DEV), q, s, b.to(DEV))
+    rows = slice(0, min(m, 256))
+    xq, xs = oq.quantize_mxfp8(np_values(x[rows]))
+    acc = oq.mxfp8_linear_codes(xq, xs, np_bytes(q), np_bytes(s), None, out_dtype="f32")
+    want = (bf16_to_f32(f32_to_bf16(acc)) + np_values(b)[None, :]).astype(np.float32)
+    close_bf16(y[rows], want, f"mxfp8 {m}x{k}x{n}")
+    gg = golden
+    xl = torch.from_numpy(gg["mxl_x"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    wq = torch.from_numpy(gg["mxl_wq"]).view(torch.float8_e4m3fn).to(DEV)
+    ws = torch.from_numpy(gg["mxl_ws"]).view(torch.float8_e8m0fnu).to(DEV)
+    wb = torch.from_numpy(gg["mxl_bias"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    yl = kq.mxfp8_linear(xl, wq, ws, wb)
+    ul = ulp_distance_bf16(np_bf16_bits(yl).reshape(-1), gg["mxl_y"].reshape(-1))
+    assert float(np.mean(ul <= 1)) >= 0.99 and ul.max() <= 4
+
+
+@pytest.mark.parametrize("m,k,n", [(48, 256, 128), (200, 1024, 384), (1024, 8192, 512)])
+def test_fp4_w4a4_linear(kq, m, k, n, golden):
+    g = torch.Generator().manual_seed(n)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.01).to(torch.bfloat16)
+    b = (torch.randn(n, generator=g) * 0.05).to(torch.bfloat16)
+    q, s, ts = kq.quantize_fp4(w.to(DEV))
+    y = kq.fp4_w4a4_linear(x.to(DEV), q, s, ts, b.to(DEV))
+    rows = slice(0, min(m, 128))
+    want = oq.fp4_w4a4_linear(np_values(x[rows]), np_bytes(q), np_bytes(s), float(ts), np_values(b), out_dtype="f32")
+    close_bf16(y[rows], want, f"nvfp4 {m}x{k}x{n}")
+    gg = golden
+    xg = torch.from_numpy(gg["w4a4_x"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    qg = torch.from_numpy(gg["w4a4_q"]).to(DEV)
+    sg = torch.from_numpy(gg["w4a4_s"]).view(torch.float8_e4m3fn).to(DEV)
+    tg = torch.tensor(float(gg["w4a4_ts"]), device=DEV)
+    bg = torch.from_numpy(gg["w4a4_bias"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    yg = kq.fp4_w4a4_linear(xg, qg, sg, tg, bg)
+    ul = ulp_distance_bf16(np_bf16_bits(yg).reshape(-1), gg["w4a4_y"].reshape(-1))
+    assert float(np.mean(ul <= 1)) >= 0.99 and ul.max() <= 4, (np.mean(ul == 0), ul.max())
+
+
+def test_fp4_config4_row_sample(kq):
+    """Config 4's shapes (K = 8192, N = 28672 sliced to 1024 output channels for the oracle)."""
+    from kernel_agent_b200 import workloads
+
+    x, w, b = workloads.config4(seed=0, device="cpu", n=1024)
+    q, s, ts = kq.quantize_fp4(w.to(DEV))
+    y = kq.fp4_w4a4_linear(x.to(DEV), q, s, ts, b.to(DEV))
+    rows = [0, 1, 2, 8191]
+    want = oq.fp4_w4a4_linear(np_values(x[rows]), np_bytes(q), np_bytes(s), float(ts), np_values(b), out_dtype="f32")
+    close_bf16(y[rows], want, "config 4 rows")
+    y2 = kq.fp4_w4a4_linear(x.to(DEV), q, s, ts, b.to(DEV))
+    assert torch.equal(y, y2)  # deterministic
+
+
+def test_gemm_status_clean():
+    from kernel_agent_b200 import _native
+
+    assert _native.device_status() == 0

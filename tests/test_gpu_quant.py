@@ -226,6 +226,8 @@ def test_mxfp4_and_fp4_weights_golden(kq, golden):
 @pytest.mark.parametrize("rows,k", [(1, 16), (33, 64), (257, 1024), (64, 8192), (3, 32768)])
 @pytest.mark.parametrize("fmt", ["nvfp4", "mxfp4"])
 def test_fp4_random(kq, rows, k, fmt):
+    if k % kq.FP4_FORMATS[fmt][0]:
+        pytest.skip("K is not a whole number of this format's blocks")
     x = torch.cat([gen(rows * 5 + k, (rows, k), spread=20), edge_rows(k)])
     for gran in (("token", "tensor") if fmt == "nvfp4" else ("token",)):
         q, s, o = kq.quantize_fp4_activations(x.to(DEV), fmt, gran)
