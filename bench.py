@@ -43,6 +43,7 @@ for _p in (str(ROOT), str(ROOT / "kernel-agent_b200")):
 METRIC = "scaled-GEMM TFLOPS & % block-scaled tensor peak; quantize GB/s & % HBM"
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 TRAFFIC_FILE = ROOT / "profiles" / "traffic.json"
+SHAPE: tuple[int, int, int] | None = None  # (M, K, N) override of the w4a4 workload
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -381,16 +382,165 @@ class Compare(Workload):
         return rate, cores, f"oracle compare_tensors on 1024 rows per step, {procs} processes"
 
 
-WORKLOADS = {w.name: w for w in (Nvfp4Producer, Mxfp8Producer, Compare)}
-DEFAULT = "nvfp4_producer"
+class W4A4Linear(Workload):
+    """Config 4: y = fp4_w4a4_linear(x, W) with bias, W [28672, 8192] NVFP4 (tensor scale from
+    the whole weight), X [8192, 8192] quantised per token on every step. At N ranks each rank
+    holds N / world output channels of W and the bf16 outputs are all-gathered (NCCL)."""
+
+    name = "w4a4"
+    unit = "TFLOP/s"
+    dtype = "nvfp4 (e2m1 x e2m1, e4m3 / fp32 scales) -> bf16"
+    scaling = "strong"
+
+    def setup(self, dev, world, rank):
+        import torch
+
+        from kernel_agent_b200 import workloads
+        from kernel_agent_b200.kernels import gemm, producers, quant
+
+        self.torch, self.gemm, self.producers, self.quant = torch, gemm, producers, quant
+        m, k, n = SHAPE or (8192, 8192, 28672)
+        self.m, self.k, self.n, self.world, self.rank = m, k, n, world, rank
+        x, w, b = workloads.config4(seed=0, device="cuda", m=m, k=k, n=n)
+        self.x, self.bias_full = x.to(dev), b.to(dev)
+        codes, scales, ts = quant.quantize_fp4(w.to(dev))  # build-time: one tensor scale for all of W
+        del w
+        ns = n // world
+        rows = slice(rank * ns, (rank + 1) * ns)
+        self.ns = ns
+        self.wq = codes[rows].contiguous()
+        self.ws = quant.swizzle_fp4_scales(scales[rows].contiguous()).view(torch.uint8)
+        self.ts = ts
+        self.bias = self.bias_full[rows].contiguous()
+        self.w_unswizzled = (codes, scales)
+        self.out_local = torch.empty(m, ns, dtype=torch.bfloat16, device=dev)
+        self.out = torch.empty(m, n, dtype=torch.bfloat16, device=dev) if world > 1 else self.out_local
+        self.gathered = torch.empty(world, m, ns, dtype=torch.bfloat16, device=dev) if world > 1 else None
+        self.flops = 2.0 * m * n * k
+        self.units = self.flops / 1e12
+        self.kernel = "gemm_kernel<KIND=3 nvf4>"
+        self.kernel_flops = 2.0 * m * ns * k
+        self.h2d = m * k * 2
+        self.d2h = m * n * 2
+        self.x_host = self.x.cpu().pin_memory()
+        self.y_host = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+        self.config = {
+            "workload": "config 4: W4A4 NVFP4 linear with bias, X [8192, 8192] x W [28672, 8192]^T -> bf16",
+            "m": m, "k": k, "n": n, "step": "NVFP4 activation producer + tcgen05 mxf4nvf4 GEMM with fused epilogue"
+            + (" + NCCL all-gather of the column shards" if world > 1 else ""),
+            "parallelism": f"column-sharded over {world} GPU(s)" if world > 1 else "1 GPU",
+            "l2": "inputs larger than L2 (W codes 117 MB, X 134 MB, output 470 MB per step)",
+        }
+
+    def _gemm(self, xq, xs, outer):
+        return self.gemm.nvf4(xq, xs.view(self.torch.uint8), outer, self.wq, self.ws, self.ts, self.bias,
+                              out=self.out_local)
+
+    def step(self):
+        xq, xs, outer = self.producers.quantize_rows_fp4(self.x, swizzle=True)
+        self._gemm(xq, xs, outer)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(self.gathered, self.out_local)
+            self.out.view(self.m, self.world, self.ns).copy_(self.gathered.permute(1, 0, 2))
+        return 2
+
+    def dominant(self):
+        if not hasattr(self, "_xq"):
+            self._xq = self.producers.quantize_rows_fp4(self.x, swizzle=True)
+        self._gemm(*self._xq)
+        return 1
+
+    def e2e_step(self):
+        x = self.x_host.to(self.x.device, non_blocking=True)
+        y = self.quant.fp4_w4a4_linear(x, self.wq, self.ws, self.ts, self.bias) if self.world == 1 else None
+        if self.world > 1:
+            xq, xs, outer = self.producers.quantize_rows_fp4(x, swizzle=True)
+            self._gemm(xq, xs, outer)
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(self.gathered, self.out_local)
+            self.out.view(self.m, self.world, self.ns).copy_(self.gathered.permute(1, 0, 2))
+            y = self.out
+        self.y_host.copy_(y, non_blocking=True)
+        return 2
+
+    def tensor_peak(self, pk, pk_kind):
+        """The dense NVFP4 tensor peak as 4 x the measured bf16 GEMM burst (B200: 9 vs 2.25
+        PFLOP/s nominal dense)."""
+        return 4.0 * pk["bf16_tflops"], f"4 x {pk_kind} bf16 burst ({pk['bf16_tflops']:.0f} TFLOP/s): NVFP4 dense"
+
+    def library_bar(self):
+        """cuBLASLt's NVFP4 GEMM (torch F.scaled_mm, BlockWise1x16) on the same codes: TFLOP/s."""
+        torch = self.torch
+        import torch.nn.functional as F
+
+        try:
+            xq, xs, outer = self.producers.quantize_rows_fp4(self.x, swizzle=True)
+            a = xq.view(torch.float4_e2m1fn_x2)
+            b = self.wq.view(torch.float4_e2m1fn_x2).t()
+            kw = dict(scale_a=xs, scale_recipe_a=F.ScalingType.BlockWise1x16,
+                      scale_b=self.ws.view(torch.float8_e4m3fn), scale_recipe_b=F.ScalingType.BlockWise1x16,
+                      swizzle_a=F.SwizzleType.SWIZZLE_32_4_4, swizzle_b=F.SwizzleType.SWIZZLE_32_4_4,
+                      output_dtype=torch.float32)
+            for _ in range(3):
+                F.scaled_mm(a, b, **kw)
+            ms, _ = timed(lambda: (F.scaled_mm(a, b, **kw), 1)[1], 10, torch)
+            return {"cublaslt_nvfp4_tflops": 2.0 * self.m * self.ns * self.k / (ms / 10 / 1e3) / 1e12,
+                    "what": "F.scaled_mm BlockWise1x16 NVFP4, fp32 out, same codes (no epilogue)"}
+        except Exception as exc:  # a torch without the NVFP4 path
+            return {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+
+    def _cpu_sample(self, rows: int, cols: int):
+        import numpy as np
+
+        codes, scales = self.w_unswizzled
+        x = self.x[:rows].float().cpu().numpy()
+        wq = codes[:cols].cpu().numpy()
+        ws = scales[:cols].view(self.torch.uint8).cpu().numpy()
+        b = self.bias_full[:cols].float().cpu().numpy()
+        return x, wq, ws, float(self.ts), b
+
+    def cpu_baseline(self):
+        import time as _t
+
+        sys.path.insert(0, str(ROOT))
+        from oracle import quant as oq
+
+        rows, cols = 32, 4096
+        x, wq, ws, ts, b = self._cpu_sample(rows, cols)
+        flops = 2.0 * rows * cols * self.k
+        t0 = _t.perf_counter()
+        reps = 0
+        while _t.perf_counter() - t0 < 10.0:
+            oq.fp4_w4a4_linear(x, wq, ws, ts, b)
+            reps += 1
+        rate = flops * reps / (_t.perf_counter() - t0) / 1e12
+        return {"value": rate, "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port",
+                "sample": f"oracle fp4_w4a4_linear (float64 BLAS matmul, all threads) on {rows} rows x "
+                          f"{cols} output channels x K {self.k}, repeated ~10 s"}
+
+    def reference(self, steps, warmup):
+        import time as _t
+
+        sys.path.insert(0, str(ROOT))
+        from oracle import quant as oq
+
+        rows, cols = 64, 4096
+        x, wq, ws, ts, b = self._cpu_sample(rows, cols)
+        flops = 2.0 * rows * cols * self.k
+        for _ in range(max(1, warmup // 3)):
+            oq.fp4_w4a4_linear(x, wq, ws, ts, b)
+        t0 = _t.perf_counter()
+        for _ in range(steps):
+            oq.fp4_w4a4_linear(x, wq, ws, ts, b)
+        rate = flops * steps / (_t.perf_counter() - t0) / 1e12
+        return rate, os.cpu_count() or 1, f"oracle fp4_w4a4_linear on {rows} rows x {cols} output channels per step"
 
 
-def load_w4a4():
-    try:
-        from kernel_agent_b200.bench_w4a4 import W4A4Linear
-    except ImportError:
-        return None
-    return W4A4Linear
+WORKLOADS = {w.name: w for w in (W4A4Linear, Nvfp4Producer, Mxfp8Producer, Compare)}
+DEFAULT = "w4a4"
 
 
 # ------------------------------------------------------------------ timing
@@ -430,14 +580,17 @@ def main() -> int:
     ap.add_argument("--impl", choices=("kab", "reference"), default="kab")
     ap.add_argument("--workload", default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shape", default=None,
+                    help="M,N,K of the w4a4 workload (a smaller case for profiling; default config 4)")
     args = ap.parse_args()
+    global SHAPE
+    if args.shape:
+        m_, n_, k_ = (int(v) for v in args.shape.split(","))
+        SHAPE = (m_, k_, n_)
     args.warmup = max(args.warmup, 3)
 
-    W4A4 = load_w4a4()
     workloads = dict(WORKLOADS)
-    if W4A4 is not None:
-        workloads[W4A4.name] = W4A4
-    name = args.workload or (W4A4.name if W4A4 is not None else DEFAULT)
+    name = args.workload or DEFAULT
     if name not in workloads:
         print(json.dumps({"error": f"unknown workload {name}", "known": sorted(workloads)}))
         return 2
@@ -514,6 +667,7 @@ def main() -> int:
         traffic = json.loads(TRAFFIC_FILE.read_text()).get(f"{wl.kernel} {wl.name}")
     roof["traffic"] = traffic
 
+    library = wl.library_bar() if hasattr(wl, "library_bar") else None
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         cpu = wl.cpu_baseline()
@@ -527,6 +681,8 @@ def main() -> int:
                 "d2h_bytes_per_step": wl.d2h},
         "gpu_launches": launches, "clocks": clk,
     }
+    if library is not None:
+        line["library_bar"] = library
     if dist.rank == 0:
         print(json.dumps(line))
     closer = getattr(wl, "close", None)

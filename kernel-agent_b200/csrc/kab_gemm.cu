@@ -98,8 +98,6 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
               "output must be 16-byte aligned");
   KAB_REQUIRE(m <= (int64_t(1) << 30) && n <= (int64_t(1) << 30), "shape too large");
   const int bn = (n % 256 == 0 || !GemmTraits<KIND>::kScaled) && n >= 256 ? 256 : 128;
-  if (GemmTraits<KIND>::kScaled)
-    KAB_REQUIRE(n % 128 == 0, "block-scaled GEMMs need N a multiple of 128 (got %lld)", (long long)n);
   g.m = m;
   g.n = n;
   g.k_stages = static_cast<int>(k_bytes / 128);

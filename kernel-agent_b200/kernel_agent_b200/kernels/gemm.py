@@ -89,14 +89,15 @@ def mxf8(a: torch.Tensor, a_sf_swizzled: torch.Tensor, b: torch.Tensor, b_sf_swi
     core; the result in ``out_dtype``, then ``+ bias`` in that dtype. K % 128 == 0, N % 128 == 0."""
     _bind()
     m, n, k = a.shape[0], b.shape[0], a.shape[1]
-    if k % 128 or n % 128:
-        raise ValueError(f"the MXFP8 GEMM needs K and N multiples of 128 (got K {k}, N {n})")
+    if k % 128:
+        raise ValueError(f"the MXFP8 GEMM needs K a multiple of 128 (got {k})")
     odt, code = _out_code(out_dtype)
-    out = torch.empty(m, n, dtype=odt, device=a.device)
+    ldo = n + (-n % 8)
+    out = torch.empty(m, ldo, dtype=odt, device=a.device)
     bb, bcode = _bias(bias, n, a.device)
     nat.call("kab_gemm_mxf8", a.contiguous().data_ptr(), a_sf_swizzled.data_ptr(), b.contiguous().data_ptr(),
-             b_sf_swizzled.data_ptr(), m, n, k, nat.ptr(bb), bcode, out.data_ptr(), code, n, nat.stream_of(a))
-    return out
+             b_sf_swizzled.data_ptr(), m, n, k, nat.ptr(bb), bcode, out.data_ptr(), code, ldo, nat.stream_of(a))
+    return out[:, :n] if ldo != n else out
 
 
 def nvf4(a: torch.Tensor, a_sf_swizzled: torch.Tensor, a_outer: torch.Tensor, b: torch.Tensor,
@@ -108,11 +109,13 @@ def nvf4(a: torch.Tensor, a_sf_swizzled: torch.Tensor, a_outer: torch.Tensor, b:
     ``[M, N]`` destination (a column block of a wider buffer: its row stride is used)."""
     _bind()
     m, n, k = a.shape[0], b.shape[0], 2 * a.shape[1]
-    if k % 256 or n % 128:
-        raise ValueError(f"the NVFP4 GEMM needs K a multiple of 256 and N of 128 (got K {k}, N {n})")
+    if k % 256:
+        raise ValueError(f"the NVFP4 GEMM needs K a multiple of 256 (got {k})")
     odt, code = _out_code(out_dtype)
     if out is None:
-        out = torch.empty(m, n, dtype=odt, device=a.device)
+        ldo = n + (-n % 8)
+        full = torch.empty(m, ldo, dtype=odt, device=a.device)
+        out = full[:, :n]
     elif out.shape != (m, n) or out.stride(1) != 1 or out.dtype != odt:
         raise ValueError("out must be [M, N] with unit column stride in the output dtype")
     bb, bcode = _bias(bias, n, a.device)
