@@ -61,6 +61,17 @@ def close_bf16(y: torch.Tensor, want_f32: np.ndarray, label: str) -> None:
     assert float(np.mean(ulps <= 1)) >= 0.99, msg
 
 
+def close_bf16_tol(y: torch.Tensor, want_f32: np.ndarray, label: str) -> None:
+    """The comparator's exact-tier bf16 checks (atol = rtol = 2e-2, <= 0.1 % outside, relative
+    L2 <= 0.02, cosine >= 0.999)."""
+    got = np_values(y).astype(np.float64)
+    ref = want_f32.astype(np.float64)
+    mism = float((np.abs(got - ref) > 2e-2 + 2e-2 * np.abs(ref)).mean())
+    rel = float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
+    cos = float((got.ravel() @ ref.ravel()) / max(np.linalg.norm(got) * np.linalg.norm(ref), 1e-30))
+    assert mism <= 1e-3 and rel <= 0.02 and cos >= 0.999, (label, mism, rel, cos)
+
+
 def test_int8_products_layout():
     g = torch.Generator().manual_seed(0)
     a = rand_i8(g, 128, 128)
@@ -146,8 +157,9 @@ def test_mxfp8_linear(kq, m, k, n, golden):
     ws = torch.from_numpy(gg["mxl_ws"]).view(torch.float8_e8m0fnu).to(DEV)
     wb = torch.from_numpy(gg["mxl_bias"].view(np.int16)).view(torch.bfloat16).to(DEV)
     yl = kq.mxfp8_linear(xl, wq, ws, wb)
-    ul = ulp_distance_bf16(np_bf16_bits(yl).reshape(-1), gg["mxl_y"].reshape(-1))
-    assert float(np.mean(ul <= 1)) >= 0.99 and ul.max() <= 4
+    # the golden output is the reference's CPU path (one rounding after the bias); the GPU
+    # path it mirrors rounds the GEMM to bf16 before the bias: the comparator's tolerance
+    close_bf16_tol(yl, bf16_to_f32(gg["mxl_y"]), "mxfp8 golden")
 
 
 @pytest.mark.parametrize("m,k,n", [(48, 256, 128), (200, 1024, 384), (1024, 8192, 512)])
