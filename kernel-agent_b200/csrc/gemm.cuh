@@ -45,47 +45,50 @@ struct GemmArgs {
 template <int KIND>
 struct GemmTraits {
   static constexpr bool kScaled = KIND >= 2;
-  // bytes of block scales per 128 rows per k-step (128 bytes of K per row)
-  static constexpr int kSfBytes = KIND == 3 ? 2048 : (KIND == 2 ? 512 : 0);
-  // TMEM columns of block scales per k-step for A (B: twice as many per 256 rows)
-  static constexpr int kSfColsA = KIND == 3 ? 16 : (KIND == 2 ? 4 : 0);
 };
 
-template <int BN, int STAGES, int KIND>
+// Output element types of the epilogue (KAB_BF16 / KAB_F16 / KAB_F32, or the raw int32
+// products of KIND 0).
+constexpr int kOutI32 = 7;
+__host__ __device__ constexpr int out_bytes(int out) { return out == KAB_F32 || out == kOutI32 ? 4 : 2; }
+
+// BKB: bytes of K per row per pipeline stage (128: 128-byte swizzle, 64: 64-byte swizzle);
+// each stage holds BKB / 32 MMAs (32 bytes of K each).
+template <int KIND, int BN, int BKB, int OUT>
 struct GemmLayout {
   static constexpr int kBM = 128;
-  static constexpr int kABytes = kBM * 128;
-  static constexpr int kBBytes = BN * 128;
-  static constexpr int kSfaBytes = GemmTraits<KIND>::kSfBytes;
-  static constexpr int kSfbBytes = GemmTraits<KIND>::kSfBytes * (BN / 128);
+  static constexpr int kKSteps = BKB / 32;
+  static constexpr bool kScaled = KIND >= 2;
+  static constexpr int kABytes = kBM * BKB;
+  static constexpr int kBBytes = BN * BKB;
+  // block scales per 128 rows per stage: NVFP4 one 512-byte chunk per MMA (K = 64), MXFP8 one
+  // chunk per 4 MMAs (K = 128: the stage)
+  static constexpr int kSfaBytes = KIND == 3 ? 512 * kKSteps : (KIND == 2 ? 512 : 0);
+  static constexpr int kSfbBytes = kSfaBytes * (BN / 128);
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
-  static constexpr int kAccBufs = GemmTraits<KIND>::kScaled ? (BN == 256 ? 1 : 2) : 2;
+  // TMEM columns of block scales per stage: each 512-byte chunk (32 rows of 16 bytes: row
+  // r % 32 holds rows {r, r + 32, r + 64, r + 96}) lands in 4 columns of every lane quarter,
+  // lane l holding chunk row l (the layout tcgen05.cp.32x128b.warpx4 makes); the
+  // scale-factor warps write it with tcgen05.st, each into its own quarter.
+  static constexpr int kSfaCols = KIND == 3 ? 4 * kKSteps : (KIND == 2 ? 4 : 0);
+  static constexpr int kSfbCols = kSfaCols * (BN / 128);
+  static constexpr int kSfColsPerStage = kSfaCols + kSfbCols;
+  static constexpr int kThreads = kScaled ? 320 : 192;
+  static constexpr int kAccBufs = kScaled ? 1 : 2;
   static constexpr int kSfCol = kAccBufs * BN;
-  static constexpr int kSfColsPerStage = GemmTraits<KIND>::kSfColsA * (1 + BN / 128);
-  static constexpr int kBarriers = 2 * STAGES + 2 * kAccBufs + 1;
-  static constexpr int kSmem = 1024 + STAGES * kStageBytes + kBarriers * 8 + 16;
-  static_assert(kSfCol + STAGES * kSfColsPerStage <= 512, "TMEM overflow");
+  // epilogue staging: 4 warps x 2 buffers x [32 rows, 32 columns]
+  static constexpr int kStageOutBytes = 32 * 32 * out_bytes(OUT);
+  static constexpr int kStagingBytes = 4 * 2 * kStageOutBytes;
+  static constexpr int kSmemLimit = 232448;
+  static constexpr int kFixed = 1024 + kStagingBytes + 320;
+  static constexpr int kStagesFit = (kSmemLimit - kFixed) / kStageBytes;
+  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+  static constexpr int kBarriers = 3 * kStages + 2 * kAccBufs + 1;
+  static constexpr int kSmem = 1024 + kStages * kStageBytes + kStagingBytes + kBarriers * 8 + 16;
+  static_assert(kStages >= 2, "shared memory does not fit two stages");
+  static_assert(kSfCol + kStages * kSfColsPerStage <= 512, "TMEM overflow");
+  static_assert(kSmem <= kSmemLimit, "shared memory overflow");
 };
-
-template <int OUT>
-__device__ __forceinline__ void store32(void* out, int64_t off, const float (&y)[32]) {
-  if constexpr (OUT == KAB_F32) {
-    float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + off);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) p[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
-  } else {
-    uint32_t w[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint16_t lo = OUT == KAB_BF16 ? f32_to_bf16_bits(y[2 * i]) : f32_to_f16_bits(y[2 * i]);
-      const uint16_t hi = OUT == KAB_BF16 ? f32_to_bf16_bits(y[2 * i + 1]) : f32_to_f16_bits(y[2 * i + 1]);
-      w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
-    }
-    uint4* p = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + off);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) p[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-  }
-}
 
 __device__ __forceinline__ float load_bias(const void* bias, int dtype, int64_t i) {
   if (dtype == KAB_BF16) return __bfloat162float(__ldg(reinterpret_cast<const __nv_bfloat16*>(bias) + i));
@@ -101,68 +104,74 @@ __device__ __forceinline__ float round_out(float f) {
   else return f;
 }
 
-template <int KIND, int BN, int OUT>
-__device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, const uint32_t (&r)[32], int64_t row,
-                                               int64_t col0) {
-  float y[32];
-  if constexpr (KIND == 0 || KIND == 1) {
+// The epilogue of 32 accumulator columns of one row: y[i] in fp32 (or raw int32 bits).
+// `sa`: this row's scale (token scale, or NVFP4 outer scale); `cs` / `cb`: lane i holds the
+// column scale / bias of column col0 + i (broadcast by shuffles).
+template <int KIND, int OUT>
+__device__ __forceinline__ void epilogue_math(const GemmArgs& g, const uint32_t (&r)[32], float sa, float cs,
+                                              float cb, uint32_t (&y)[32]) {
+  const bool bias = g.bias != nullptr;
+  if constexpr (OUT == kOutI32) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) y[i] = r[i];
+  } else if constexpr (KIND == 0 || KIND == 1) {
     // quant.py:920-922: acc.float() * xs[m] * sw[n] (+ bias), left to right in fp32
-    const float sa = row < g.m ? __ldg(g.a_scale + row) : 0.0f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const float acc = KIND == 0 ? __int2float_rn(static_cast<int>(r[i])) : __uint_as_float(r[i]);
-      const int64_t c = col0 + i;
-      const float sb = c < g.n ? __ldg(g.b_scale + c) : 0.0f;
+      const float sb = __shfl_sync(0xffffffffu, cs, i);
+      const float bi = __shfl_sync(0xffffffffu, cb, i);
       float v = __fmul_rn(__fmul_rn(acc, sa), sb);
-      if (g.bias != nullptr && c < g.n) v = __fadd_rn(v, load_bias(g.bias, g.bias_dtype, c));
-      y[i] = v;
+      if (bias) v = __fadd_rn(v, bi);
+      y[i] = __float_as_uint(v);
     }
   } else if constexpr (KIND == 2) {
     // quant.py:602-614: F.scaled_mm's output in the output dtype, then + bias in that dtype
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      const int64_t c = col0 + i;
+      const float bi = __shfl_sync(0xffffffffu, cb, i);
       float v = round_out<OUT>(__uint_as_float(r[i]));
-      if (g.bias != nullptr && c < g.n) v = __fadd_rn(v, load_bias(g.bias, g.bias_dtype, c));
-      y[i] = v;
+      if (bias) v = __fadd_rn(v, bi);
+      y[i] = __float_as_uint(v);
     }
   } else {
     // quant.py:1254-1256: acc * (outer[m] * ts) (+ bias.float())
-    const float outer = row < g.m ? __ldg(g.a_scale + row) : 0.0f;
-    const float ts0 = g.b_scale_per_col ? 0.0f : __ldg(g.b_scale);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      const int64_t c = col0 + i;
-      const float ts = g.b_scale_per_col ? (c < g.n ? __ldg(g.b_scale + c) : 0.0f) : ts0;
-      float v = __fmul_rn(__uint_as_float(r[i]), __fmul_rn(outer, ts));
-      if (g.bias != nullptr && c < g.n) v = __fadd_rn(v, load_bias(g.bias, g.bias_dtype, c));
-      y[i] = v;
-    }
-  }
-  if (row >= g.m) return;
-  if (col0 + 32 <= g.n) {
-    store32<OUT>(g.out, row * g.ldo + col0, y);
-  } else {
-    for (int i = 0; i < 32 && col0 + i < g.n; ++i) {
-      const int64_t o = row * g.ldo + col0 + i;
-      if constexpr (OUT == KAB_F32) reinterpret_cast<float*>(g.out)[o] = y[i];
-      else if constexpr (OUT == KAB_BF16) reinterpret_cast<uint16_t*>(g.out)[o] = f32_to_bf16_bits(y[i]);
-      else reinterpret_cast<uint16_t*>(g.out)[o] = f32_to_f16_bits(y[i]);
+      const float ts = __shfl_sync(0xffffffffu, cs, i);
+      const float bi = __shfl_sync(0xffffffffu, cb, i);
+      float v = __fmul_rn(__uint_as_float(r[i]), __fmul_rn(sa, ts));
+      if (bias) v = __fadd_rn(v, bi);
+      y[i] = __float_as_uint(v);
     }
   }
 }
 
-__device__ __forceinline__ void store_acc32(const GemmArgs& g, const uint32_t (&r)[32], int64_t row, int64_t col0) {
-  if (row >= g.m) return;
-  int32_t* p = g.acc_out + row * g.ldo + col0;
-  if (col0 + 32 <= g.n) {
-    int4* q = reinterpret_cast<int4*>(p);
+// Writes one row of 32 outputs (this lane's row) into a [32 rows, 32 columns] staging tile.
+template <int OUT>
+__device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const uint32_t (&y)[32]) {
+  if constexpr (out_bytes(OUT) == 4) {
+    uint4* p = reinterpret_cast<uint4*>(buf + lane * 128);
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      q[i] = make_int4(static_cast<int>(r[4 * i]), static_cast<int>(r[4 * i + 1]), static_cast<int>(r[4 * i + 2]),
-                       static_cast<int>(r[4 * i + 3]));
+    for (int i = 0; i < 8; ++i) {
+      const int j = (i + lane) & 7;  // rotate the 16-byte chunks: fewer bank conflicts
+      p[j] = make_uint4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+    }
   } else {
-    for (int i = 0; i < 32 && col0 + i < g.n; ++i) p[i] = static_cast<int>(r[i]);
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float a = __uint_as_float(y[2 * i]), b = __uint_as_float(y[2 * i + 1]);
+      const uint16_t lo = OUT == KAB_BF16 ? f32_to_bf16_bits(a) : f32_to_f16_bits(a);
+      const uint16_t hi = OUT == KAB_BF16 ? f32_to_bf16_bits(b) : f32_to_f16_bits(b);
+      w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+    }
+    uint4* p = reinterpret_cast<uint4*>(buf + lane * 64);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int j = (i + lane) & 3;
+      p[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+    }
   }
 }
 
@@ -178,32 +187,45 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
   nt = r / gm;
 }
 
-template <int KIND, int BN, int STAGES, int OUT>
-__global__ void __launch_bounds__(192, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, GemmArgs g) {
-  using L = GemmLayout<BN, STAGES, KIND>;
+template <int KIND, int BN, int BKB, int OUT>
+__global__ void __launch_bounds__(GemmLayout<KIND, BN, BKB, OUT>::kThreads, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+            const __grid_constant__ CUtensorMap tma_out, GemmArgs g) {
+  using L = GemmLayout<KIND, BN, BKB, OUT>;
+  constexpr int STAGES = L::kStages;
+  constexpr int KS = L::kKSteps;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * L::kABytes;
   uint8_t* sSFA = sB + STAGES * L::kBBytes;
   uint8_t* sSFB = sSFA + STAGES * L::kSfaBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sSFB + STAGES * L::kSfbBytes);
+  uint8_t* sOut = sSFB + STAGES * L::kSfbBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + L::kStagingBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
-  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* sf_full = bars + 2 * STAGES;  // scale factors of stage s are in TMEM (4 arrivals)
+  uint64_t* acc_full = bars + 3 * STAGES;
   uint64_t* acc_empty = acc_full + L::kAccBufs;
   uint64_t* drain = acc_empty + L::kAccBufs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+      tc::mbar_init(&sf_full[s], 4);
+    }
     for (int b = 0; b < L::kAccBufs; ++b) { tc::mbar_init(&acc_full[b], 1); tc::mbar_init(&acc_empty[b], 4); }
     tc::mbar_init(drain, 1);
     tc::fence_barrier_init();
   }
-  if (warp == 0 && lane == 0) { tc::prefetch_tensormap(&tma_a); tc::prefetch_tensormap(&tma_b); }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tensormap(&tma_a);
+    tc::prefetch_tensormap(&tma_b);
+    tc::prefetch_tensormap(&tma_out);
+  }
   if (warp == 1) { tc::tmem_alloc(tmem_slot, 512); tc::tmem_relinquish(); }
   tc::fence_before_sync();
   __syncthreads();
@@ -226,14 +248,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         for (int kb = 0; kb < g.k_stages; ++kb) {
           if (!tc::mbar_wait(&empty[s], ph ^ 1u)) { ok = false; break; }
           tc::mbar_arrive_expect_tx(&full[s], kTx);
-          tc::tma_load_2d(&tma_a, &full[s], sA + s * L::kABytes, kb * 128, mt * 128);
-          tc::tma_load_2d(&tma_b, &full[s], sB + s * L::kBBytes, kb * 128, nt * BN);
-          if constexpr (KIND == 3) {
-            tc::bulk_load(sSFA + s * L::kSfaBytes, g.sfa + (mt * g.sfa_ncb + 4 * kb) * 512, 2048, &full[s]);
+          tc::tma_load_2d(&tma_a, &full[s], sA + s * L::kABytes, kb * BKB, mt * 128);
+          tc::tma_load_2d(&tma_b, &full[s], sB + s * L::kBBytes, kb * BKB, nt * BN);
+          if constexpr (KIND == 3) {  // KS chunks of 512 bytes per 128 rows: contiguous
+            tc::bulk_load(sSFA + s * L::kSfaBytes, g.sfa + (mt * g.sfa_ncb + KS * kb) * 512, L::kSfaBytes, &full[s]);
 #pragma unroll
             for (int h = 0; h < BN / 128; ++h)
-              tc::bulk_load(sSFB + s * L::kSfbBytes + h * 2048,
-                            g.sfb + ((nt * (BN / 128) + h) * g.sfb_ncb + 4 * kb) * 512, 2048, &full[s]);
+              tc::bulk_load(sSFB + s * L::kSfbBytes + h * L::kSfaBytes,
+                            g.sfb + ((nt * (BN / 128) + h) * g.sfb_ncb + KS * kb) * 512, L::kSfaBytes, &full[s]);
           } else if constexpr (KIND == 2) {
             tc::bulk_load(sSFA + s * L::kSfaBytes, g.sfa + (mt * g.sfa_ncb + kb) * 512, 512, &full[s]);
 #pragma unroll
@@ -263,34 +285,29 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         const uint32_t d = tmem + ab * BN;
         for (int kb = 0; kb < g.k_stages; ++kb) {
           if (!tc::mbar_wait(&full[s], ph)) { ok = false; break; }
-          tc::fence_after_sync();
-          const uint64_t adesc = tc::desc_sw128(tc::smem_u32(sA + s * L::kABytes));
-          const uint64_t bdesc = tc::desc_sw128(tc::smem_u32(sB + s * L::kBBytes));
-          const uint32_t sf = tmem + L::kSfCol + s * L::kSfColsPerStage;
-          if constexpr (KIND == 3) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              tc::cp_sf(sf + j * 4, tc::desc_sf(tc::smem_u32(sSFA + s * L::kSfaBytes + j * 512)));
-#pragma unroll
-              for (int h = 0; h < BN / 128; ++h)
-                tc::cp_sf(sf + 16 + j * (4 * (BN / 128)) + h * 4,
-                          tc::desc_sf(tc::smem_u32(sSFB + s * L::kSfbBytes + h * 2048 + j * 512)));
-            }
-          } else if constexpr (KIND == 2) {
-            tc::cp_sf(sf, tc::desc_sf(tc::smem_u32(sSFA + s * L::kSfaBytes)));
-#pragma unroll
-            for (int h = 0; h < BN / 128; ++h)
-              tc::cp_sf(sf + 4 + h * 4, tc::desc_sf(tc::smem_u32(sSFB + s * L::kSfbBytes + h * 512)));
+          if constexpr (L::kScaled) {
+            if (!tc::mbar_wait(&sf_full[s], ph)) { ok = false; break; }
           }
+          tc::fence_after_sync();
+          const uint32_t abase = tc::smem_u32(sA + s * L::kABytes);
+          const uint32_t bbase = tc::smem_u32(sB + s * L::kBBytes);
+          const uint64_t adesc = BKB == 128 ? tc::desc_sw128(abase) : tc::desc_sw64(abase);
+          const uint64_t bdesc = BKB == 128 ? tc::desc_sw128(bbase) : tc::desc_sw64(bbase);
+          const uint32_t sf = tmem + L::kSfCol + s * L::kSfColsPerStage;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+          for (int j = 0; j < KS; ++j) {
             const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
             const uint64_t a = adesc + static_cast<uint64_t>(2 * j);  // +32 bytes of K
             const uint64_t b = bdesc + static_cast<uint64_t>(2 * j);
-            if constexpr (KIND == 0) tc::mma_i8(d, a, b, tc::idesc_i8(128, BN), acc);
-            else if constexpr (KIND == 1) tc::mma_f8(d, a, b, tc::idesc_f8(128, BN), acc);
-            else if constexpr (KIND == 2) tc::mma_mxf8(d, a, b, tc::idesc_mxf8(128, BN, j), sf, sf + 4, acc);
-            else tc::mma_nvf4(d, a, b, tc::idesc_nvf4(128, BN), sf + j * 4, sf + 16 + j * (4 * (BN / 128)), acc);
+            if constexpr (KIND == 0) {
+              tc::mma_i8(d, a, b, tc::idesc_i8(128, BN), acc);
+            } else if constexpr (KIND == 1) {
+              tc::mma_f8(d, a, b, tc::idesc_f8(128, BN), acc);
+            } else if constexpr (KIND == 2) {  // one scale byte per row per MMA (sf_id = j)
+              tc::mma_mxf8(d, a, b, tc::idesc_mxf8(128, BN, j), sf, sf + L::kSfaCols, acc);
+            } else {  // this MMA's chunk: 4 columns for A, 4 per 128 rows of B
+              tc::mma_nvf4(d, a, b, tc::idesc_nvf4(128, BN), sf + 4 * j, sf + L::kSfaCols + 4 * (BN / 128) * j, acc);
+            }
           }
           tc::commit(&empty[s]);
           if (++s == STAGES) { s = 0; ph ^= 1u; }
@@ -303,11 +320,50 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       if (!tc::mbar_wait(drain, 0)) ok = false;
       if (!ok) atomicOr(&g_gemm_status, kDevTimeout);
     }
+  } else if (warp >= 6) {  // ----------------------------------------------- scale-factor warps
+    if constexpr (L::kScaled) {
+      const int q = warp & 3;
+      const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        for (int kb = 0; kb < g.k_stages; ++kb) {
+          if (!tc::mbar_wait(&full[s], ph)) { ok = false; break; }
+          const uint32_t col = tmem + lane_base + L::kSfCol + s * L::kSfColsPerStage;
+          const uint8_t* ca = sSFA + s * L::kSfaBytes + lane * 16;
+          const uint8_t* cb = sSFB + s * L::kSfbBytes + lane * 16;
+          if constexpr (KIND == 3) {  // MMA j: A chunk j at +4 j, B chunks (j, h) at +4 (BN/128) j + 4 h
+#pragma unroll
+            for (int j = 0; j < KS; ++j) {
+              tc::tmem_st4(col + 4 * j, *reinterpret_cast<const uint4*>(ca + j * 512));
+#pragma unroll
+              for (int h = 0; h < BN / 128; ++h)
+                tc::tmem_st4(col + L::kSfaCols + 4 * (BN / 128) * j + 4 * h,
+                             *reinterpret_cast<const uint4*>(cb + h * L::kSfaBytes + j * 512));
+            }
+          } else {  // one chunk per 128 rows covers the stage's 4 MMAs
+            tc::tmem_st4(col, *reinterpret_cast<const uint4*>(ca));
+#pragma unroll
+            for (int h = 0; h < BN / 128; ++h)
+              tc::tmem_st4(col + L::kSfaCols + 4 * h, *reinterpret_cast<const uint4*>(cb + h * 512));
+          }
+          tc::tmem_st_wait();
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&sf_full[s]);
+          if (++s == STAGES) { s = 0; ph ^= 1u; }
+        }
+      }
+      if (!ok && lane == 0) atomicOr(&g_gemm_status, kDevTimeout);
+    }
   } else {  // ------------------------------------------------------------- epilogue warps
     const int quarter = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(32 * quarter) << 16;
+    uint8_t* stage0 = sOut + (warp - 2) * 2 * L::kStageOutBytes;
     int ab = 0;
     uint32_t aph = 0;
+    int chunk = 0;  // chunks this warp has staged (selects the staging buffer)
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int mt, nt;
       tile_coords(t, g.m_tiles, g.n_tiles, mt, nt);
@@ -316,21 +372,57 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         break;
       }
       tc::fence_after_sync();
-      const int64_t row = static_cast<int64_t>(mt) * 128 + 32 * quarter + lane;
-#pragma unroll 1
+      const int row0 = mt * 128 + 32 * quarter;
+      const int64_t row = static_cast<int64_t>(row0) + lane;
+      const uint32_t tbase = tmem + lane_base + ab * BN;
+      // this tile's row scale and (lane i of chunk c) column scale / bias, loaded once
+      float sa = 0.0f;
+      if constexpr (KIND != 2 && OUT != kOutI32) sa = row < g.m ? __ldg(g.a_scale + row) : 0.0f;
+      float cs[BN / 32], cbv[BN / 32];
+#pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tc::tmem_ld32(tmem + lane_base + ab * BN + c * 32, r);
-        tc::tmem_ld_wait();
-        const int64_t col0 = static_cast<int64_t>(nt) * BN + c * 32;
-        if (KIND == 0 && g.acc_out != nullptr) store_acc32(g, r, row, col0);
-        else epilogue_chunk<KIND, BN, OUT>(g, r, row, col0);
+        const int64_t col = static_cast<int64_t>(nt) * BN + c * 32 + lane;
+        cs[c] = 0.0f;
+        cbv[c] = 0.0f;
+        if constexpr (OUT != kOutI32) {
+          if constexpr (KIND == 0 || KIND == 1) cs[c] = col < g.n ? __ldg(g.b_scale + col) : 0.0f;
+          if constexpr (KIND == 3) cs[c] = g.b_scale_per_col ? (col < g.n ? __ldg(g.b_scale + col) : 0.0f) : __ldg(g.b_scale);
+          if (g.bias != nullptr && col < g.n) cbv[c] = load_bias(g.bias, g.bias_dtype, col);
+        }
       }
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&acc_empty[ab]);
+      uint32_t r[32];
+      tc::tmem_ld32(tbase, r);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t y[32];
+        const int64_t col0 = static_cast<int64_t>(nt) * BN + c * 32;
+        epilogue_math<KIND, OUT>(g, r, sa, cs[c], cbv[c], y);
+        if (c + 1 < BN / 32) {
+          tc::tmem_ld32(tbase + (c + 1) * 32, r);
+        } else {  // the accumulator is read: hand it back to the MMA warp
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&acc_empty[ab]);
+        }
+        uint8_t* buf = stage0 + (chunk & 1) * L::kStageOutBytes;
+        if (chunk >= 2) {  // the store two chunks ago has finished reading this buffer
+          if (lane == 0) tc::bulk_wait_read<1>();
+          __syncwarp();
+        }
+        stage_row<OUT>(buf, lane, y);
+        tc::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          tc::tma_store_2d(&tma_out, buf, static_cast<int>(col0), row0);
+          tc::bulk_commit();
+        }
+        ++chunk;
+        if (c + 1 < BN / 32) tc::tmem_ld_wait();
+      }
       if (++ab == L::kAccBufs) { ab = 0; aph ^= 1u; }
     }
+    if (lane == 0) tc::bulk_wait_all();
   }
   tc::fence_before_sync();
   __syncthreads();

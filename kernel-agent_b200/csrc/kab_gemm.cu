@@ -38,26 +38,47 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // A 2-D byte matrix [rows, cols_bytes] (row stride ld_bytes) read in boxes of
-// [box_rows, 128 bytes] with the 128-byte swizzle.
+// [box_rows, box_bytes] with the swizzle of that row width (128 or 64 bytes).
 int make_map(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols_bytes, uint64_t ld_bytes,
-             uint32_t box_rows, const char* name) {
+             uint32_t box_rows, uint32_t box_bytes, const char* name) {
   auto fn = encode_fn();
   if (fn == nullptr) return fail(KAB_EUNSUPPORTED, "cuTensorMapEncodeTiled is unavailable (driver too old?)");
   cuuint64_t dims[2] = {cols_bytes, rows};
   cuuint64_t strides[1] = {ld_bytes};
-  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t box[2] = {box_bytes, box_rows};
   cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(KAB_EINVAL, "tensor map of %s failed (CUresult %d)", name, static_cast<int>(r));
   return KAB_OK;
 }
 
-template <int KIND, int BN, int STAGES, int OUT>
-int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, cudaStream_t s) {
-  using L = GemmLayout<BN, STAGES, KIND>;
-  auto kernel = gemm_kernel<KIND, BN, STAGES, OUT>;
+// The output [m, n] (row stride ldo elements) written in [32, 32] boxes by TMA stores.
+int make_out_map(CUtensorMap* map, void* ptr, int out, uint64_t m, uint64_t n, uint64_t ldo) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(KAB_EUNSUPPORTED, "cuTensorMapEncodeTiled is unavailable (driver too old?)");
+  const CUtensorMapDataType dt = out == KAB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : out == KAB_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                 : out == KAB_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                  : CU_TENSOR_MAP_DATA_TYPE_INT32;
+  cuuint64_t dims[2] = {n, m};
+  cuuint64_t strides[1] = {ldo * static_cast<uint64_t>(out_bytes(out))};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, dt, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KAB_EINVAL, "tensor map of the output failed (CUresult %d)", static_cast<int>(r));
+  return KAB_OK;
+}
+
+template <int KIND, int BN, int BKB, int OUT>
+int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const GemmArgs& g,
+               cudaStream_t s) {
+  using L = GemmLayout<KIND, BN, BKB, OUT>;
+  auto kernel = gemm_kernel<KIND, BN, BKB, OUT>;
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -68,16 +89,20 @@ int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, 
   }
   const int tiles = g.m_tiles * g.n_tiles;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kernel<<<grid, 192, L::kSmem, s>>>(ma, mb, g);
+  kernel<<<grid, L::kThreads, L::kSmem, s>>>(ma, mb, mo, g);
   return check_launch("gemm kernel");
 }
 
 template <int KIND, int BN>
-int launch_out(int out_dtype, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, cudaStream_t s) {
-  constexpr int STAGES = BN == 256 ? 4 : 6;
-  if (out_dtype == KAB_BF16) return launch_one<KIND, BN, STAGES, KAB_BF16>(ma, mb, g, s);
-  if (out_dtype == KAB_F16) return launch_one<KIND, BN, STAGES, KAB_F16>(ma, mb, g, s);
-  return launch_one<KIND, BN, STAGES, KAB_F32>(ma, mb, g, s);
+int launch_out(int out, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const GemmArgs& g,
+               cudaStream_t s) {
+  constexpr int BKB = KIND == 3 ? 64 : 128;
+  if constexpr (KIND == 0) {
+    if (out == kOutI32) return launch_one<KIND, BN, BKB, kOutI32>(ma, mb, mo, g, s);
+  }
+  if (out == KAB_BF16) return launch_one<KIND, BN, BKB, KAB_BF16>(ma, mb, mo, g, s);
+  if (out == KAB_F16) return launch_one<KIND, BN, BKB, KAB_F16>(ma, mb, mo, g, s);
+  return launch_one<KIND, BN, BKB, KAB_F32>(ma, mb, mo, g, s);
 }
 
 // Common checks and launch: a [m, k_bytes] and b [n, k_bytes] K-major byte matrices.
@@ -88,26 +113,29 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
   if (m == 0 || n == 0) return KAB_OK;
   KAB_REQUIRE(a != nullptr && b != nullptr, "operand is null");
   KAB_REQUIRE(aligned(a, 16) && aligned(b, 16), "operands must be 16-byte aligned");
-  KAB_REQUIRE(k_bytes > 0 && k_bytes % 128 == 0,
-              "K must be a positive multiple of 128 bytes per row (128 int8 / e4m3, 256 e2m1); got %lld bytes",
-              (long long)k_bytes);
-  KAB_REQUIRE(out_dtype == KAB_BF16 || out_dtype == KAB_F16 || out_dtype == KAB_F32, "unknown out dtype %d", out_dtype);
-  KAB_REQUIRE(g.out != nullptr || g.acc_out != nullptr, "output is null");
+  const int bkb = KIND == 3 ? 64 : 128;
+  KAB_REQUIRE(k_bytes > 0 && k_bytes % bkb == 0,
+              "K must be a positive multiple of %d bytes per row (128 int8 / e4m3, 256 e2m1); got %lld bytes",
+              bkb, (long long)k_bytes);
+  KAB_REQUIRE(out_dtype == KAB_BF16 || out_dtype == KAB_F16 || out_dtype == KAB_F32 || out_dtype == kOutI32,
+              "unknown out dtype %d", out_dtype);
+  void* out = out_dtype == kOutI32 ? static_cast<void*>(g.acc_out) : g.out;
+  KAB_REQUIRE(out != nullptr, "output is null");
   KAB_REQUIRE(g.ldo >= n && g.ldo % 8 == 0, "ldo %lld must be >= n and a multiple of 8", (long long)g.ldo);
-  KAB_REQUIRE((g.out == nullptr || aligned(g.out, 16)) && (g.acc_out == nullptr || aligned(g.acc_out, 16)),
-              "output must be 16-byte aligned");
+  KAB_REQUIRE(aligned(out, 16), "output must be 16-byte aligned");
   KAB_REQUIRE(m <= (int64_t(1) << 30) && n <= (int64_t(1) << 30), "shape too large");
   const int bn = (n % 256 == 0 || !GemmTraits<KIND>::kScaled) && n >= 256 ? 256 : 128;
   g.m = m;
   g.n = n;
-  g.k_stages = static_cast<int>(k_bytes / 128);
+  g.k_stages = static_cast<int>(k_bytes / bkb);
   g.m_tiles = static_cast<int>((m + 127) / 128);
   g.n_tiles = static_cast<int>((n + bn - 1) / bn);
-  CUtensorMap ma, mb;
-  if (int e = make_map(&ma, a, m, k_bytes, k_bytes, 128, "A")) return e;
-  if (int e = make_map(&mb, b, n, k_bytes, k_bytes, bn, "B")) return e;
-  if (bn == 256) return launch_out<KIND, 256>(out_dtype, ma, mb, g, s);
-  return launch_out<KIND, 128>(out_dtype, ma, mb, g, s);
+  CUtensorMap ma, mb, mo;
+  if (int e = make_map(&ma, a, m, k_bytes, k_bytes, 128, bkb, "A")) return e;
+  if (int e = make_map(&mb, b, n, k_bytes, k_bytes, bn, bkb, "B")) return e;
+  if (int e = make_out_map(&mo, out, out_dtype, m, n, g.ldo)) return e;
+  if (bn == 256) return launch_out<KIND, 256>(out_dtype, ma, mb, mo, g, s);
+  return launch_out<KIND, 128>(out_dtype, ma, mb, mo, g, s);
 }
 
 GemmArgs args_of(const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo) {
@@ -139,7 +167,7 @@ int kab_gemm_i8(const int8_t* a, const int8_t* b, int64_t m, int64_t n, int64_t 
   else
     g.out = nullptr;
   KAB_REQUIRE(bias == nullptr || valid_dtype(bias_dtype), "unknown bias dtype %d", bias_dtype);
-  return run<0>(a, b, m, n, k, g, acc_out != nullptr ? KAB_BF16 : out_dtype, as_stream(stream));
+  return run<0>(a, b, m, n, k, g, acc_out != nullptr ? kOutI32 : out_dtype, as_stream(stream));
 }
 
 int kab_gemm_f8(const uint8_t* a, const uint8_t* b, int64_t m, int64_t n, int64_t k, const float* a_scale,
