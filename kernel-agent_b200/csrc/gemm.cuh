@@ -8,9 +8,10 @@
 //   KIND 3  kind::mxf4nvf4  e2m1 x e2m1 with e4m3 scales per 16 applied by the tensor core;
 //                            epilogue acc * (outer[m] * ts[n or one]) (+ bias)
 //
-// One persistent CTA per SM (192 threads): warp 0 issues the TMA loads (one thread), warp 1
-// the MMAs (one thread) and owns the TMEM allocation, warps 2-5 drain the accumulator
-// (tcgen05.ld, one TMEM lane = one output row per thread). Output tiles are 128 x BN; the
+// One persistent CTA per SM: warp 0 issues the TMA loads (one thread), warp 1 the MMAs (one
+// thread) and owns the TMEM allocation, warps 2-9 drain the accumulator (tcgen05.ld, one TMEM
+// lane = one output row per thread; two warps per lane quarter, each taking half the columns),
+// and for the block-scaled kinds warps 10-13 move the scale factors into TMEM. Output tiles are 128 x BN; the
 // operand ring holds STAGES k-steps of 128 bytes of K per row (128 int8 / e4m3 elements, 256
 // e2m1). Block scales arrive in cuBLASLt's 128 x 4 blocked layout (quant.py:540-564), whose
 // 512-byte chunks are exactly the 32 x 128-bit sources tcgen05.cp expects; they are copied
@@ -73,12 +74,13 @@ struct GemmLayout {
   static constexpr int kSfaCols = KIND == 3 ? 4 * kKSteps : (KIND == 2 ? 4 : 0);
   static constexpr int kSfbCols = kSfaCols * (BN / 128);
   static constexpr int kSfColsPerStage = kSfaCols + kSfbCols;
-  static constexpr int kThreads = kScaled ? 320 : 192;
+  static constexpr int kEpiWarps = 8;  // two per TMEM lane quarter
+  static constexpr int kThreads = 32 * (2 + kEpiWarps + (kScaled ? 4 : 0));
   static constexpr int kAccBufs = kScaled ? 1 : 2;
   static constexpr int kSfCol = kAccBufs * BN;
-  // epilogue staging: 4 warps x 2 buffers x [32 rows, 32 columns]
+  // epilogue staging: 8 warps x 2 buffers x [32 rows, 32 columns]
   static constexpr int kStageOutBytes = 32 * 32 * out_bytes(OUT);
-  static constexpr int kStagingBytes = 4 * 2 * kStageOutBytes;
+  static constexpr int kStagingBytes = kEpiWarps * 2 * kStageOutBytes;
   static constexpr int kSmemLimit = 232448;
   static constexpr int kFixed = 1024 + kStagingBytes + 320;
   static constexpr int kStagesFit = (kSmemLimit - kFixed) / kStageBytes;
@@ -158,13 +160,17 @@ __device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const uint32_t
       p[j] = make_uint4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
     }
   } else {
-    uint32_t w[16];
+    uint32_t w[16];  // round to nearest even, two per conversion instruction
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const float a = __uint_as_float(y[2 * i]), b = __uint_as_float(y[2 * i + 1]);
-      const uint16_t lo = OUT == KAB_BF16 ? f32_to_bf16_bits(a) : f32_to_f16_bits(a);
-      const uint16_t hi = OUT == KAB_BF16 ? f32_to_bf16_bits(b) : f32_to_f16_bits(b);
-      w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+      if constexpr (OUT == KAB_BF16) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        w[i] = *reinterpret_cast<const uint32_t*>(&h);
+      } else {
+        const __half2 h = __floats2half2_rn(a, b);
+        w[i] = *reinterpret_cast<const uint32_t*>(&h);
+      }
     }
     uint4* p = reinterpret_cast<uint4*>(buf + lane * 64);
 #pragma unroll
@@ -217,7 +223,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       tc::mbar_init(&empty[s], 1);
       tc::mbar_init(&sf_full[s], 4);
     }
-    for (int b = 0; b < L::kAccBufs; ++b) { tc::mbar_init(&acc_full[b], 1); tc::mbar_init(&acc_empty[b], 4); }
+    for (int b = 0; b < L::kAccBufs; ++b) { tc::mbar_init(&acc_full[b], 1); tc::mbar_init(&acc_empty[b], L::kEpiWarps); }
     tc::mbar_init(drain, 1);
     tc::fence_barrier_init();
   }
@@ -320,7 +326,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       if (!tc::mbar_wait(drain, 0)) ok = false;
       if (!ok) atomicOr(&g_gemm_status, kDevTimeout);
     }
-  } else if (warp >= 6) {  // ----------------------------------------------- scale-factor warps
+  } else if (warp >= 2 + L::kEpiWarps) {  // ---------------------------------- scale-factor warps
     if constexpr (L::kScaled) {
       const int q = warp & 3;
       const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
@@ -358,7 +364,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       if (!ok && lane == 0) atomicOr(&g_gemm_status, kDevTimeout);
     }
   } else {  // ------------------------------------------------------------- epilogue warps
+    // warps 2..9: lane quarter = warp % 4 (the quarter a warp may read), column half = (warp - 2) / 4
+    constexpr int HC = BN / 64;  // 32-column chunks per warp per tile
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const uint32_t lane_base = static_cast<uint32_t>(32 * quarter) << 16;
     uint8_t* stage0 = sOut + (warp - 2) * 2 * L::kStageOutBytes;
     int ab = 0;
@@ -374,14 +383,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       tc::fence_after_sync();
       const int row0 = mt * 128 + 32 * quarter;
       const int64_t row = static_cast<int64_t>(row0) + lane;
-      const uint32_t tbase = tmem + lane_base + ab * BN;
+      const int colh = nt * BN + half * (BN / 2);
+      const uint32_t tbase = tmem + lane_base + ab * BN + half * (BN / 2);
       // this tile's row scale and (lane i of chunk c) column scale / bias, loaded once
       float sa = 0.0f;
       if constexpr (KIND != 2 && OUT != kOutI32) sa = row < g.m ? __ldg(g.a_scale + row) : 0.0f;
-      float cs[BN / 32], cbv[BN / 32];
+      float cs[HC], cbv[HC];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        const int64_t col = static_cast<int64_t>(nt) * BN + c * 32 + lane;
+      for (int c = 0; c < HC; ++c) {
+        const int64_t col = static_cast<int64_t>(colh) + c * 32 + lane;
         cs[c] = 0.0f;
         cbv[c] = 0.0f;
         if constexpr (OUT != kOutI32) {
@@ -394,13 +404,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       tc::tmem_ld32(tbase, r);
       tc::tmem_ld_wait();
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < HC; ++c) {
         uint32_t y[32];
-        const int64_t col0 = static_cast<int64_t>(nt) * BN + c * 32;
         epilogue_math<KIND, OUT>(g, r, sa, cs[c], cbv[c], y);
-        if (c + 1 < BN / 32) {
+        if (c + 1 < HC) {
           tc::tmem_ld32(tbase + (c + 1) * 32, r);
-        } else {  // the accumulator is read: hand it back to the MMA warp
+        } else {  // this warp's columns are read: hand the accumulator back to the MMA warp
           tc::fence_before_sync();
           __syncwarp();
           if (lane == 0) tc::mbar_arrive(&acc_empty[ab]);
@@ -414,11 +423,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         tc::fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
-          tc::tma_store_2d(&tma_out, buf, static_cast<int>(col0), row0);
+          tc::tma_store_2d(&tma_out, buf, colh + c * 32, row0);
           tc::bulk_commit();
         }
         ++chunk;
-        if (c + 1 < BN / 32) tc::tmem_ld_wait();
+        if (c + 1 < HC) tc::tmem_ld_wait();
       }
       if (++ab == L::kAccBufs) { ab = 0; aph ^= 1u; }
     }
