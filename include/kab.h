@@ -234,6 +234,17 @@ size_t kab_compare_scratch_bytes(int64_t n);
 /* The element loop into *result (device). `scratch`: kab_compare_scratch_bytes(n) bytes. */
 int kab_compare(const KabCompareParams* params, void* scratch, size_t scratch_bytes,
                 KabCompareResult* result, void* stream);
+/* kab_compare without caller scratch: the per-block partials live in a static device array
+ * of the library (1024 slots of 152 bytes per device; enough for any `n` on a device of up to
+ * 256 SMs, KAB_EINVAL beyond that). No counterpart in the reference, whose comparator runs in
+ * PyTorch: it exists for callers that cannot allocate device memory when they check a result
+ * (a harness judging a candidate that has just exhausted HBM, a host binding without a device
+ * allocator). It allocates nothing; nothing must start at zero (each block overwrites its slot;
+ * every field of *result is written). Results are bit-identical to kab_compare's. Calls overlapping on
+ * one device share the array and race: order them on one stream. The first call on each device
+ * looks up the array's address (cudaGetSymbolAddress, which may load the module); make it
+ * before capturing a stream. */
+int kab_compare_noalloc(const KabCompareParams* params, KabCompareResult* result, void* stream);
 
 /* Per-channel RMS over the last dimension (compare.py:582-589 _channels): rms[c] =
  * sqrt(mean over rows of v^2) with v = x (non-finite as 0) or, with `alt` non-null,

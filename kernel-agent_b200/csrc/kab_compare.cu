@@ -1,4 +1,7 @@
 // extern "C" entry points of the comparator (compare.cuh).
+#include <mutex>
+#include <vector>
+
 #include "compare.cuh"
 #include "kab_host.h"
 
@@ -13,6 +16,33 @@ int compare_grid(int64_t n) {
   return static_cast<int>(g);
 }
 constexpr int64_t kChannelChunkRows = 64;
+
+// The per-block partials of kab_compare_noalloc. compare_grid caps the grid at 4 blocks per
+// SM, so these 1024 slots (152 KB per device) serve any element count on devices of up to
+// 256 SMs (a B200 uses at most 592). Every launched block overwrites its own slot before the
+// finalize kernel reads it: nothing here has to start at zero, and nothing is cleared.
+constexpr int kStaticPartials = 1024;
+static __device__ __align__(256) CmpPartial g_compare_partials[kStaticPartials];
+
+// The device address of g_compare_partials on the current device, looked up once per device
+// (cudaGetSymbolAddress, which may load the module on that device).
+int static_partials(CmpPartial** out) {
+  static std::mutex mu;
+  static std::vector<CmpPartial*> cache;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(KAB_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(mu);
+  if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1, nullptr);
+  if (cache[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_compare_partials);
+    if (e != cudaSuccess) return fail(KAB_ECUDA, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    cache[dev] = static_cast<CmpPartial*>(p);
+  }
+  *out = cache[dev];
+  return KAB_OK;
+}
 }  // namespace
 }  // namespace kab
 
@@ -52,6 +82,26 @@ int kab_compare(const KabCompareParams* params, void* scratch, size_t scratch_by
   if (int e = check_launch("kab_compare")) return e;
   compare_finalize_kernel<<<1, 256, 0, s>>>(partials, grid, result);
   return check_launch("kab_compare finalize");
+}
+
+// kab_compare with its partials in g_compare_partials instead of caller scratch. For callers
+// that cannot allocate device memory at the point of the check: a harness judging a candidate
+// that has just filled HBM (an out-of-memory candidate still gets its verdict), or a host
+// binding with no device allocator of its own. It allocates and frees nothing, and adds no
+// code path: the same kernels run, through kab_compare, on the same grid, so the result is
+// bit-identical to kab_compare's. Calls that overlap on one device (two streams, two host
+// threads) share the slots and race: order them on one stream.
+int kab_compare_noalloc(const KabCompareParams* params, KabCompareResult* result, void* stream) {
+  KAB_REQUIRE(params != nullptr && result != nullptr, "null pointer");
+  KAB_REQUIRE(params->n >= 0, "negative element count");
+  const int grid = compare_grid(params->n);
+  KAB_REQUIRE(grid <= kStaticPartials,
+              "kab_compare_noalloc: %d blocks need %d partial slots, the static scratch holds %d "
+              "(a device of more than %d SMs); use kab_compare with caller scratch",
+              grid, grid, kStaticPartials, kStaticPartials / 4);
+  CmpPartial* partials = nullptr;
+  if (int e = static_partials(&partials)) return e;
+  return kab_compare(params, partials, sizeof(CmpPartial) * kStaticPartials, result, stream);
 }
 
 size_t kab_channel_rms_scratch_bytes(int64_t rows, int64_t channels) {

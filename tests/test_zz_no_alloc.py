@@ -1,0 +1,118 @@
+"""kab_compare_noalloc (the comparator with its partials in the library's static device array)
+against kab_compare (caller scratch), both through the C-ABI: bit-identical results on two
+calls in a row with different sizes, and no device memory taken by the calls themselves.
+
+The file name sorts last, so a full session runs these tests after every other one (the
+static array then starts with whatever earlier launches left in it); they also pass alone."""
+
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def nat():
+    from kernel_agent_b200 import _native
+
+    _native.load()
+    return _native
+
+
+def params_for(nat, ref, new, rer=None, atol=1e-2, rtol=1e-2):
+    p = nat.KabCompareParams()
+    p.ref, p.new_ = ref.data_ptr(), new.data_ptr()
+    p.rerounded = rer.data_ptr() if rer is not None else None
+    p.n, p.channels = ref.numel(), ref.shape[-1]
+    p.dtype = nat.dtype_code(ref)
+    p.has_rerounded = int(rer is not None)
+    p.vector = int(all(t is None or t.data_ptr() % 16 == 0 for t in (ref, new, rer)))
+    p.atol, p.rtol = atol, rtol
+    return p
+
+
+def result_bytes(nat, out: torch.Tensor) -> bytes:
+    """The result's fields as bytes (the struct's tail padding is never written)."""
+    torch.cuda.synchronize()
+    res = nat.KabCompareResult.from_buffer_copy(bytes(out.cpu().numpy().tobytes()))
+    end = nat.KabCompareResult.max.offset + ctypes.sizeof(res.max)
+    return bytes(res)[:end]
+
+
+def with_scratch(nat, p, stream) -> bytes:
+    n = int(nat.query("kab_compare_scratch_bytes", p.n))
+    scratch = torch.empty(max(n, 16), dtype=torch.uint8, device=DEV)
+    out = torch.empty(ctypes.sizeof(nat.KabCompareResult), dtype=torch.uint8, device=DEV)
+    nat.call("kab_compare", ctypes.byref(p), scratch.data_ptr(), scratch.numel(), out.data_ptr(), stream)
+    return result_bytes(nat, out)
+
+
+def without_scratch(nat, p, out, stream) -> bytes:
+    nat.call("kab_compare_noalloc", ctypes.byref(p), out.data_ptr(), stream)
+    return result_bytes(nat, out)
+
+
+def case(seed, rows, cols, dtype, specials=True, with_rer=False):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    ref = torch.randn(rows, cols, generator=g)
+    new = ref + 0.02 * torch.randn(rows, cols, generator=g)
+    if specials:
+        flat_r, flat_n = ref.view(-1), new.view(-1)
+        idx = torch.randint(0, ref.numel(), (64,), generator=g)
+        flat_n[idx[:16]] = float("nan")
+        flat_r[idx[16:24]] = float("inf")
+        flat_n[idx[16:20]] = float("inf")
+        flat_n[idx[24:32]] = -float("inf")
+    rer = (ref + 0.005 * torch.randn(rows, cols, generator=g)) if with_rer else None
+    to = lambda t: None if t is None else t.to(dtype).to(DEV).contiguous()  # noqa: E731
+    return to(ref), to(new), to(rer)
+
+
+def test_noalloc_matches_kab_compare_on_consecutive_calls(nat):
+    stream = torch.cuda.current_stream().cuda_stream
+    out = torch.empty(ctypes.sizeof(nat.KabCompareResult), dtype=torch.uint8, device=DEV)
+    # a large call (grid at its SM cap), then a small one that leaves most slots stale, then a
+    # mid-size fp32 one with a rerounded tensor
+    cases = [case(1, 4096, 1536, torch.bfloat16), case(2, 7, 129, torch.float16),
+             case(3, 1000, 300, torch.float32, with_rer=True)]
+    for ref, new, rer in cases:
+        p = params_for(nat, ref, new, rer)
+        want = with_scratch(nat, p, stream)
+        first = without_scratch(nat, p, out, stream)
+        second = without_scratch(nat, p, out, stream)
+        assert first == want and second == want, (ref.shape, ref.dtype)
+        res = nat.KabCompareResult.from_buffer_copy(want.ljust(ctypes.sizeof(nat.KabCompareResult), b"\0"))
+        assert sum(res.count) > 0  # the planted NaN / inf entries were counted
+
+
+def test_noalloc_takes_no_device_memory(nat):
+    stream = torch.cuda.current_stream().cuda_stream
+    ref, new, _ = case(4, 2048, 2048, torch.bfloat16)
+    p = params_for(nat, ref, new)
+    out = torch.empty(ctypes.sizeof(nat.KabCompareResult), dtype=torch.uint8, device=DEV)
+    without_scratch(nat, p, out, stream)  # the first call on this device does the set-up
+    torch.cuda.synchronize()
+    alloc0 = torch.cuda.memory_allocated()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        nat.call("kab_compare_noalloc", ctypes.byref(p), out.data_ptr(), stream)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert torch.cuda.memory_allocated() == alloc0
+    assert free1 == free0
+
+
+def test_noalloc_rejects_bad_arguments(nat):
+    out = torch.empty(ctypes.sizeof(nat.KabCompareResult), dtype=torch.uint8, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    p = nat.KabCompareParams()
+    p.n = -1
+    with pytest.raises(ValueError, match="negative"):
+        nat.call("kab_compare_noalloc", ctypes.byref(p), out.data_ptr(), stream)
+    with pytest.raises(ValueError, match="null"):
+        nat.call("kab_compare_noalloc", None, out.data_ptr(), stream)
