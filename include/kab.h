@@ -148,6 +148,16 @@ int kab_gemm_f8(const uint8_t* a, const uint8_t* b, int64_t m, int64_t n, int64_
                 const float* a_scale, const float* b_scale, const void* bias, int bias_dtype,
                 void* out, int out_dtype, int64_t ldo, void* stream);
 
+/* Blockwise FP8: e4m3 A [m, k] with fp32 scales a_scale [m, k / 128] (1 x 128 groups), e4m3
+ * B [n, k] with fp32 scales b_scale [n / 128, k / 128] (128 x 128 blocks); out = sum over
+ * 128-wide K steps of (partial * a_scale[m, kb]) * b_scale[n / 128, kb] in fp32 (+ bias), one
+ * rounding to out_dtype (docs/research-scripts/fp8-sm120/gemm_bench.py:39-68, the promotion
+ * of the blockwise recipe; F.scaled_mm BlockWise1x128 / BlockWise128x128 on the GPU).
+ * k % 128 == 0, n % 128 == 0. */
+int kab_gemm_f8_blockwise(const uint8_t* a, const float* a_scale, const uint8_t* b,
+                          const float* b_scale, int64_t m, int64_t n, int64_t k, const void* bias,
+                          int bias_dtype, void* out, int out_dtype, int64_t ldo, void* stream);
+
 /* MXFP8: e4m3 with e8m0 scales per 32 along K on both operands (swizzled layout), applied
  * by the tensor core (kind::mxf8f6f4.block_scale); out = round(acc) (+ bias) in out_dtype
  * (quant.py:581-620 mxfp8_linear, F.scaled_mm BlockWise1x32 then + bias). n % 128 == 0. */

@@ -5,6 +5,7 @@
 #include <mutex>
 
 #include "gemm.cuh"
+#include "gemm_blockwise.cuh"
 #include "kab_host.h"
 
 namespace kab {
@@ -138,6 +139,25 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
   return launch_out<KIND, 128>(out_dtype, ma, mb, mo, g, s);
 }
 
+template <int OUT>
+int launch_blockwise(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const BlockwiseArgs& g,
+                     cudaStream_t s) {
+  using L = BlockwiseLayout<OUT>;
+  auto kernel = gemm_blockwise_kernel<OUT>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem) != cudaSuccess)
+      return fail(KAB_ECUDA, "cannot set %d bytes of shared memory", L::kSmem);
+    configured[dev] = true;
+  }
+  const int tiles = g.m_tiles * g.n_tiles;
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kernel<<<grid, L::kThreads, L::kSmem, s>>>(ma, mb, mo, g);
+  return check_launch("blockwise gemm kernel");
+}
+
 GemmArgs args_of(const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo) {
   GemmArgs g{};
   g.bias = bias;
@@ -210,6 +230,42 @@ int kab_gemm_nvf4(const uint8_t* a, const uint8_t* a_sf, const float* a_outer, c
   g.b_scale = b_scale;
   g.b_scale_per_col = b_scale_per_col;
   return run<3>(a, b, m, n, k / 2, g, out_dtype, as_stream(stream));
+}
+
+int kab_gemm_f8_blockwise(const uint8_t* a, const float* a_scale, const uint8_t* b, const float* b_scale,
+                          int64_t m, int64_t n, int64_t k, const void* bias, int bias_dtype, void* out,
+                          int out_dtype, int64_t ldo, void* stream) {
+  KAB_REQUIRE(m >= 0 && n >= 0 && k >= 0, "negative shape");
+  if (m == 0 || n == 0) return KAB_OK;
+  KAB_REQUIRE(a != nullptr && b != nullptr && a_scale != nullptr && b_scale != nullptr,
+              "operand or scale is null");
+  KAB_REQUIRE(aligned(a, 16) && aligned(b, 16), "operands must be 16-byte aligned");
+  KAB_REQUIRE(k > 0 && k % 128 == 0, "K (%lld) must be a positive multiple of 128 (the scale group)", (long long)k);
+  KAB_REQUIRE(n % 128 == 0, "N (%lld) must be a multiple of 128 (the weight block)", (long long)n);
+  KAB_REQUIRE(out_dtype == KAB_BF16 || out_dtype == KAB_F16 || out_dtype == KAB_F32, "unknown out dtype %d",
+              out_dtype);
+  KAB_REQUIRE(bias == nullptr || valid_dtype(bias_dtype), "unknown bias dtype %d", bias_dtype);
+  KAB_REQUIRE(out != nullptr && aligned(out, 16), "output is null or not 16-byte aligned");
+  KAB_REQUIRE(ldo >= n && ldo % 8 == 0, "ldo %lld must be >= n and a multiple of 8", (long long)ldo);
+  KAB_REQUIRE(m <= (int64_t(1) << 30) && n <= (int64_t(1) << 30), "shape too large");
+  BlockwiseArgs g{};
+  g.m = m;
+  g.n = n;
+  g.k_blocks = static_cast<int>(k / 128);
+  g.m_tiles = static_cast<int>((m + 127) / 128);
+  g.n_tiles = static_cast<int>(n / 128);
+  g.sa = a_scale;
+  g.sb = b_scale;
+  g.bias = bias;
+  g.bias_dtype = bias_dtype;
+  CUtensorMap ma, mb, mo;
+  if (int e = make_map(&ma, a, m, k, k, 128, 128, "A")) return e;
+  if (int e = make_map(&mb, b, n, k, k, 128, 128, "B")) return e;
+  if (int e = make_out_map(&mo, out, out_dtype, m, n, ldo)) return e;
+  const cudaStream_t s = as_stream(stream);
+  if (out_dtype == KAB_BF16) return launch_blockwise<KAB_BF16>(ma, mb, mo, g, s);
+  if (out_dtype == KAB_F16) return launch_blockwise<KAB_F16>(ma, mb, mo, g, s);
+  return launch_blockwise<KAB_F32>(ma, mb, mo, g, s);
 }
 
 }  // extern "C"

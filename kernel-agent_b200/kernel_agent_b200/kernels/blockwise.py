@@ -57,3 +57,23 @@ def quantize_fp8_blocks(weight: torch.Tensor, block: int = GROUP) -> tuple[torch
         nat.call("kab_quant_blocks_fp8", w.data_ptr(), nat.dtype_code(w), n, k, w.stride(0),
                  codes.data_ptr(), scales.data_ptr(), nat.stream_of(w))
     return codes, scales
+
+
+def fp8_blockwise_linear(x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor, bias=None,
+                         out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """``x [..., K] @ Wᵀ`` with W given as blockwise FP8 (``codes [N, K]`` e4m3, ``scales
+    [N/128, K/128]`` fp32 from :func:`quantize_fp8_blocks`): ``x`` is quantised per 1 x 128
+    group, the tcgen05 GEMM promotes each 128-wide K step in fp32 (gemm_bench.py:39-68), then
+    ``+ bias`` and one rounding to ``out_dtype`` (default ``x.dtype``). Returns ``[..., N]``."""
+    from . import gemm
+
+    if codes.dim() != 2:
+        raise ValueError(f"expected 2-D codes [out, in], got shape {tuple(codes.shape)}")
+    n, k = codes.shape
+    if x.shape[-1] != k:
+        raise ValueError(f"x has {x.shape[-1]} input features, the weight {k}")
+    nat.require_cuda(x, codes, scales)
+    lead = x.shape[:-1]
+    xq, xs = quantize_fp8_groups(x.reshape(-1, k))
+    y = gemm.fp8_blockwise(xq, xs, codes, scales, bias=bias, out_dtype=out_dtype or x.dtype)
+    return y.reshape(*lead, n)

@@ -128,3 +128,30 @@ def nvf4(a: torch.Tensor, a_sf_swizzled: torch.Tensor, a_outer: torch.Tensor, b:
              ts.data_ptr(), per_col, m, n, k, nat.ptr(bb), bcode, out.data_ptr(), code, out.stride(0),
              nat.stream_of(a))
     return out
+
+
+def fp8_blockwise(a: torch.Tensor, a_scale: torch.Tensor, b: torch.Tensor, b_scale: torch.Tensor, bias=None,
+                  out_dtype=torch.bfloat16) -> torch.Tensor:
+    """Blockwise FP8 ``a [M, K] @ b [N, K]ᵀ``: ``a_scale [M, K/128]`` per 1 x 128 group,
+    ``b_scale [N/128, K/128]`` per 128 x 128 block, promoted per 128-wide K step in fp32
+    (+ bias), one rounding to ``out_dtype``. K % 128 == 0, N % 128 == 0."""
+    _bind()
+    m, k = a.shape
+    n = b.shape[0]
+    if b.shape[1] != k:
+        raise ValueError(f"K mismatch: a has {k}, b has {b.shape[1]}")
+    if k % 128 or n % 128:
+        raise ValueError(f"the blockwise GEMM needs K and N multiples of 128 (got K={k}, N={n})")
+    if tuple(a_scale.shape) != (m, k // 128) or tuple(b_scale.shape) != (n // 128, k // 128):
+        raise ValueError(f"scales {tuple(a_scale.shape)} / {tuple(b_scale.shape)} do not match "
+                         f"[{m}, {k // 128}] / [{n // 128}, {k // 128}]")
+    odt, code = _out_code(out_dtype)
+    ldo = n + (-n % 8)
+    out = torch.empty(m, ldo, dtype=odt, device=a.device)
+    bb, bcode = _bias(bias, n, a.device)
+    sa = a_scale.float().contiguous()
+    sb = b_scale.float().to(a.device).contiguous()
+    nat.call("kab_gemm_f8_blockwise", a.contiguous().view(torch.uint8).data_ptr(), sa.data_ptr(),
+             b.contiguous().view(torch.uint8).data_ptr(), sb.data_ptr(), m, n, k, nat.ptr(bb), bcode,
+             out.data_ptr(), code, ldo, nat.stream_of(a))
+    return out[:, :n] if ldo != n else out

@@ -198,6 +198,64 @@ def test_fp4_config4_row_sample(kq):
     assert torch.equal(y, y2)  # deterministic
 
 
+@pytest.fixture(scope="module")
+def kb():
+    from kernel_agent_b200.kernels import blockwise
+
+    return blockwise
+
+
+@pytest.mark.parametrize("m", [1, 16, 2048, 200])
+def test_fp8_blockwise_linear_config2(kb, m):
+    """Config 2 (K = 1024, N = 3072, M in {1, 16, 2048}, plus a ragged M): against the oracle's
+    per-128-K promotion of the same codes, and against the fp32 fake-quant matmul."""
+    from kernel_agent_b200 import workloads
+    from oracle import fp8lib
+
+    x, w = workloads.config2(m, seed=m)
+    bias = (torch.randn(3072, generator=torch.Generator().manual_seed(1)) * 0.1).to(torch.bfloat16)
+    wq, ws = kb.quantize_fp8_blocks(w.to(DEV))
+    for b in (None, bias):
+        y = kb.fp8_blockwise_linear(x.to(DEV), wq, ws, None if b is None else b.to(DEV))
+        assert y.shape == (m, 3072) and y.dtype == torch.bfloat16
+        rows = slice(0, min(m, 64))
+        xq, xs = fp8lib.quantize_fp8_groups(np_values(x[rows]), 128)
+        want = fp8lib.fp8_blockwise_gemm(xq, xs, np_bytes(wq), ws.cpu().numpy(),
+                                         None if b is None else np_values(b), out_dtype="f32")
+        close_bf16(y[rows], want, f"blockwise m={m} bias={b is not None}")
+    fq = fp8lib.e4m3_to_f32(xq).astype(np.float64) * np.repeat(xs, 128, axis=1)
+    wfq = fp8lib.e4m3_to_f32(np_bytes(wq)).astype(np.float64) * np.repeat(np.repeat(ws.cpu().numpy(), 128, 0), 128, 1)
+    dq = (fq @ wfq.T + np_values(bias)[None, :]).astype(np.float32)
+    close_bf16_tol(y[rows], dq, "blockwise vs dequant-matmul")
+
+
+def test_fp8_blockwise_golden(kb, golden):
+    """The reference research script's fake-quant tensors (fq_groups / fq_block): the GEMM of
+    our codes equals their fp32 matmul within the bf16 tolerance."""
+    g = golden
+    xb = torch.from_numpy(g["bw_x"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    wb = torch.from_numpy(g["bw_w"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    wq, ws = kb.quantize_fp8_blocks(wb)
+    y = kb.fp8_blockwise_linear(xb, wq, ws)
+    want = (g["bw_x_fq"].astype(np.float64) @ g["bw_w_fq"].astype(np.float64).T).astype(np.float32)
+    close_bf16_tol(y, want, "blockwise golden")
+    y32 = kb.fp8_blockwise_linear(xb, wq, ws, out_dtype=torch.float32)
+    rel = np.linalg.norm(y32.cpu().numpy() - want) / np.linalg.norm(want)
+    assert rel < 1e-5, rel  # fp32 out: only the fp32 partial / promotion roundings differ
+
+
+def test_fp8_blockwise_rejects_bad_shapes(kb):
+    x = torch.randn(4, 200, device=DEV).to(torch.bfloat16)
+    with pytest.raises(ValueError):
+        kb.quantize_fp8_groups(x)
+    from kernel_agent_b200.kernels import gemm
+
+    a = torch.zeros(4, 256, dtype=torch.uint8, device=DEV).view(torch.float8_e4m3fn)
+    b = torch.zeros(200, 256, dtype=torch.uint8, device=DEV).view(torch.float8_e4m3fn)
+    with pytest.raises(ValueError, match="multiples of 128"):
+        gemm.fp8_blockwise(a, torch.ones(4, 2, device=DEV), b, torch.ones(2, 2, device=DEV))
+
+
 def test_gemm_status_clean():
     from kernel_agent_b200 import _native
 
