@@ -11,6 +11,7 @@ Workloads (synthetic, seeded; BASELINE.json's configurations):
   nvfp4_producer  config 4's activation producer alone (HBM-bound).
   mxfp8_producer  config 3's fused SiLU(gate) * up -> MXFP8 producer (HBM-bound).
   compare  the comparator on a config-4-sized bf16 output pair (HBM-bound).
+  fp8_blockwise  config 2: 1x128 FP8 producer + blockwise-scaled tcgen05 GEMM (M = 2048).
 
 ``value`` is the whole-job throughput with inputs resident in HBM, timed with CUDA events
 over exactly K steps between barriers, the max over ranks; ``e2e`` is the same metric through
@@ -399,22 +400,23 @@ class W4A4Linear(Workload):
         import torch
 
         from kernel_agent_b200 import workloads
-        from kernel_agent_b200.kernels import gemm, producers, quant
+        from kernel_agent_b200.kernels import gemm, producers, quant, sharded
 
-        self.torch, self.gemm, self.producers, self.quant = torch, gemm, producers, quant
+        self.torch, self.gemm, self.producers, self.quant, self.sharded = torch, gemm, producers, quant, sharded
         m, k, n = SHAPE or (8192, 8192, 28672)
         self.m, self.k, self.n, self.world, self.rank = m, k, n, world, rank
-        x, w, b = workloads.config4(seed=0, device="cuda", m=m, k=k, n=n)
+        x, w, b = workloads.config4(seed=0, device="cuda", m=m, k=k, n=n)  # the same on every rank
         self.x, self.bias_full = x.to(dev), b.to(dev)
-        codes, scales, ts = quant.quantize_fp4(w.to(dev))  # build-time: one tensor scale for all of W
+        cols = sharded.shard_columns(n, world, rank)
+        ns = cols.stop - cols.start
+        # build time: this rank's rows of W, with the whole weight's tensor scale (all-reduced amax)
+        codes, scales, ts = sharded.quantize_fp4_weight_shard(w[cols].to(dev))
         del w
-        ns = n // world
-        rows = slice(rank * ns, (rank + 1) * ns)
         self.ns = ns
-        self.wq = codes[rows].contiguous()
-        self.ws = quant.swizzle_fp4_scales(scales[rows].contiguous()).view(torch.uint8)
+        self.wq = codes
+        self.ws = quant.swizzle_fp4_scales(scales).view(torch.uint8)
         self.ts = ts
-        self.bias = self.bias_full[rows].contiguous()
+        self.bias = self.bias_full[cols].contiguous()
         self.w_unswizzled = (codes, scales)
         self.out_local = torch.empty(m, ns, dtype=torch.bfloat16, device=dev)
         self.out = torch.empty(m, n, dtype=torch.bfloat16, device=dev) if world > 1 else self.out_local
@@ -443,10 +445,7 @@ class W4A4Linear(Workload):
         xq, xs, outer = self.producers.quantize_rows_fp4(self.x, swizzle=True)
         self._gemm(xq, xs, outer)
         if self.world > 1:
-            import torch.distributed as dist
-
-            dist.all_gather_into_tensor(self.gathered, self.out_local)
-            self.out.view(self.m, self.world, self.ns).copy_(self.gathered.permute(1, 0, 2))
+            self.sharded.gather_columns(self.out_local, out=self.out, staging=self.gathered)
         return 2
 
     def dominant(self):
@@ -457,15 +456,11 @@ class W4A4Linear(Workload):
 
     def e2e_step(self):
         x = self.x_host.to(self.x.device, non_blocking=True)
-        y = self.quant.fp4_w4a4_linear(x, self.wq, self.ws, self.ts, self.bias) if self.world == 1 else None
-        if self.world > 1:
-            xq, xs, outer = self.producers.quantize_rows_fp4(x, swizzle=True)
-            self._gemm(xq, xs, outer)
-            import torch.distributed as dist
-
-            dist.all_gather_into_tensor(self.gathered, self.out_local)
-            self.out.view(self.m, self.world, self.ns).copy_(self.gathered.permute(1, 0, 2))
-            y = self.out
+        if self.world == 1:
+            y = self.quant.fp4_w4a4_linear(x, self.wq, self.ws, self.ts, self.bias)
+        else:
+            y = self.sharded.fp4_w4a4_linear_sharded(x, self.wq, self.ws, self.ts, self.bias,
+                                                     out_local=self.out_local, out=self.out, staging=self.gathered)
         self.y_host.copy_(y, non_blocking=True)
         return 2
 
@@ -542,7 +537,146 @@ class W4A4Linear(Workload):
         return rate, os.cpu_count() or 1, f"oracle fp4_w4a4_linear on {rows} rows x {cols} output channels per step"
 
 
-WORKLOADS = {w.name: w for w in (W4A4Linear, Nvfp4Producer, Mxfp8Producer, Compare)}
+class Fp8Blockwise(Workload):
+    """Config 2: y = fp8_blockwise_linear(x, W): x [M, 1024] quantised per 1 x 128 group on
+    every step, W [3072, 1024] with 128 x 128 block scales (build time), promoted per
+    128-wide K step; bf16 out. M = 2048 (the tensor-bound case) unless --shape says otherwise.
+    The step is a few microseconds, so the K timed steps run as one CUDA graph, step i on
+    input copy i % copies: the copies together are larger than L2, so each step reads HBM."""
+
+    name = "fp8_blockwise"
+    graph = True
+    unit = "TFLOP/s"
+    dtype = "e4m3 x e4m3 (fp32 1x128 / 128x128 scales) -> bf16"
+    scaling = "weak"
+
+    def setup(self, dev, world, rank):
+        import torch
+
+        from kernel_agent_b200 import workloads
+        from kernel_agent_b200.kernels import blockwise, gemm
+
+        self.torch, self.blockwise, self.gemm = torch, blockwise, gemm
+        m, k, n = SHAPE or (2048, 1024, 3072)
+        self.m, self.k, self.n = m, k, n
+        x, w = workloads.config2(m, seed=0, device="cuda", k=k, n=n)
+        self.x = x.to(dev)
+        self.wq, self.ws = blockwise.quantize_fp8_blocks(w.to(dev))
+        per_step = m * k * 2 + m * k + n * k + m * n * 2  # x, its codes, W codes, y
+        self.copies = max(2, -(-(256 << 20) // per_step))
+        self.xs_ = [self.x.clone() for _ in range(self.copies)]
+        self.ws_ = [(self.wq.clone(), self.ws.clone()) for _ in range(self.copies)]
+        self.xq_ = [blockwise.quantize_fp8_groups(t) for t in self.xs_]
+        self.flops = 2.0 * m * n * k
+        self.units = self.flops / 1e12
+        self.kernel = "gemm_blockwise_kernel"
+        self.kernel_flops = self.flops
+        self.h2d = m * k * 2
+        self.d2h = m * n * 2
+        self.x_host = self.x.cpu().pin_memory()
+        self.y_host = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+        self.config = {
+            "workload": f"config 2: blockwise FP8 linear, X [{m}, {k}] x W [{n}, {k}]^T -> bf16",
+            "m": m, "k": k, "n": n,
+            "step": "1x128 FP8 activation producer + tcgen05 f8f6f4 GEMM with per-128-K fp32 promotion",
+            "parallelism": "replicas",
+            "l2": f"inputs larger than L2: step i uses copy i % {self.copies} of X and W ({self.copies} x "
+                  f"{per_step / 2**20:.1f} MB)",
+            "launch": "the K timed steps are one CUDA graph (2 kernels per step)",
+        }
+
+    def step_at(self, i):
+        j = i % self.copies
+        xq, xs = self.blockwise.quantize_fp8_groups(self.xs_[j])
+        wq, ws = self.ws_[j]
+        self.gemm.fp8_blockwise(xq, xs, wq, ws)
+        return 2
+
+    def dominant_at(self, i):
+        j = i % self.copies
+        xq, xs = self.xq_[j]
+        wq, ws = self.ws_[j]
+        self.gemm.fp8_blockwise(xq, xs, wq, ws)
+        return 1
+
+    def step(self):
+        return self.step_at(0)
+
+    def e2e_step(self):
+        x = self.x_host.to(self.x.device, non_blocking=True)
+        y = self.blockwise.fp8_blockwise_linear(x, self.wq, self.ws)
+        self.y_host.copy_(y, non_blocking=True)
+        return 2
+
+    def tensor_peak(self, pk, pk_kind):
+        return 2.0 * pk["bf16_tflops"], f"2 x {pk_kind} bf16 burst ({pk['bf16_tflops']:.0f} TFLOP/s): FP8 dense"
+
+    def library_bar(self):
+        """cuBLASLt's blockwise FP8 GEMM (F.scaled_mm BlockWise1x128 x BlockWise128x128)."""
+        torch = self.torch
+        import torch.nn.functional as F
+
+        xq, xs = self.blockwise.quantize_fp8_groups(self.x)
+        b = self.wq.t()
+        errors = []
+        # the scale layouts torch may ask for: row-major, or outer-dim-major (transposed)
+        for sa, sb in ((xs.t().contiguous().t(), self.ws), (xs, self.ws), (xs.t().contiguous().t(), self.ws.t()),
+                       (xs, self.ws.t())):
+            kw = dict(scale_a=sa, scale_recipe_a=F.ScalingType.BlockWise1x128, scale_b=sb,
+                      scale_recipe_b=F.ScalingType.BlockWise128x128, output_dtype=torch.bfloat16)
+            try:
+                for _ in range(3):
+                    F.scaled_mm(xq, b, **kw)
+                ms, _ = timed(lambda: (F.scaled_mm(xq, b, **kw), 1)[1], 20, torch)
+            except Exception as exc:
+                errors.append(f"{type(exc).__name__}: {exc}"[:120])
+                continue
+            return {"cublaslt_blockwise_tflops": self.flops / (ms / 20 / 1e3) / 1e12,
+                    "what": "F.scaled_mm BlockWise1x128 x BlockWise128x128, bf16 out, same codes, L2 warm"}
+        return {"unavailable": " | ".join(errors)[:400]}
+
+    def _cpu_case(self, rows):
+        import numpy as np
+
+        sys.path.insert(0, str(ROOT))
+        from oracle import fp8lib
+
+        x = self.x[:rows].float().cpu().numpy()
+        wq = self.wq.view(self.torch.uint8).cpu().numpy()
+        ws = self.ws.cpu().numpy()
+        return fp8lib, x, wq, ws
+
+    def cpu_baseline(self):
+        import time as _t
+
+        rows = 64
+        fp8lib, x, wq, ws = self._cpu_case(rows)
+        t0 = _t.perf_counter()
+        reps = 0
+        while _t.perf_counter() - t0 < 10.0:
+            xq, xs = fp8lib.quantize_fp8_groups(x, 128)
+            fp8lib.fp8_blockwise_gemm(xq, xs, wq, ws)
+            reps += 1
+        rate = 2.0 * rows * self.n * self.k * reps / (_t.perf_counter() - t0) / 1e12
+        return {"value": rate, "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port",
+                "sample": f"oracle fq_groups + blockwise GEMM (float64 BLAS per K step, all threads) on "
+                          f"{rows} rows x {self.n} x K {self.k}, repeated ~10 s"}
+
+    def reference(self, steps, warmup):
+        import time as _t
+
+        rows = 128
+        fp8lib, x, wq, ws = self._cpu_case(rows)
+        for _ in range(max(1, warmup // 3)):
+            fp8lib.fp8_blockwise_gemm(*fp8lib.quantize_fp8_groups(x, 128), wq, ws)
+        t0 = _t.perf_counter()
+        for _ in range(steps):
+            fp8lib.fp8_blockwise_gemm(*fp8lib.quantize_fp8_groups(x, 128), wq, ws)
+        rate = 2.0 * rows * self.n * self.k * steps / (_t.perf_counter() - t0) / 1e12
+        return rate, os.cpu_count() or 1, f"oracle blockwise FP8 linear on {rows} rows per step"
+
+
+WORKLOADS = {w.name: w for w in (W4A4Linear, Nvfp4Producer, Mxfp8Producer, Compare, Fp8Blockwise)}
 DEFAULT = "w4a4"
 
 
@@ -560,6 +694,27 @@ def timed(fn, steps: int, torch):
     end.record()
     torch.cuda.synchronize()
     return start.elapsed_time(end), launches
+
+
+def as_graph(fn, torch):
+    """`fn` captured once into a CUDA graph; the returned callable replays it and returns the
+    launch count the captured call reported."""
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        fn()  # first call outside capture (lazy set-up)
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        launches = fn()
+
+    def replay():
+        graph.replay()
+        return launches
+
+    replay.graph = graph
+    return replay
 
 
 def kernel_ms(fn, steps: int, torch) -> float:
@@ -584,7 +739,7 @@ def main() -> int:
     ap.add_argument("--workload", default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--shape", default=None,
-                    help="M,N,K of the w4a4 workload (a smaller case for profiling; default config 4)")
+                    help="M,N,K of the w4a4 / fp8_blockwise workload (default: the config's shape)")
     args = ap.parse_args()
     global SHAPE
     if args.shape:
@@ -629,14 +784,28 @@ def main() -> int:
     for _ in range(args.warmup):
         wl.step()
     torch.cuda.synchronize()
+    graphed = getattr(wl, "graph", False)
+    if graphed:
+        # launch-bound steps: the K timed steps (and K dominant launches) are one CUDA graph,
+        # each step on its own copy of the inputs (the copies together exceed L2)
+        k_steps = args.steps
+        steps_graph = as_graph(lambda: sum(wl.step_at(i) for i in range(k_steps)), torch)
+        dom_graph = as_graph(lambda: sum(wl.dominant_at(i) for i in range(k_steps)), torch)
+        steps_graph()
+        torch.cuda.synchronize()
     dist.barrier()
     clocks = Clocks(dist.local)
     clocks.start()
     time.sleep(0.3)
     dist.barrier()
-    total_ms, launches = timed(wl.step, args.steps, torch)
-    dist.barrier()
-    k_ms = kernel_ms(getattr(wl, "dominant", wl.step), args.steps, torch)
+    if graphed:
+        total_ms, launches = timed(steps_graph, 1, torch)
+        dist.barrier()
+        k_ms = kernel_ms(dom_graph, 1, torch) / args.steps
+    else:
+        total_ms, launches = timed(wl.step, args.steps, torch)
+        dist.barrier()
+        k_ms = kernel_ms(getattr(wl, "dominant", wl.step), args.steps, torch)
     clk = clocks.stop()
     total_ms = dist.max(total_ms)
     k_ms = dist.max(k_ms)

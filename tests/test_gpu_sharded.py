@@ -1,0 +1,19 @@
+"""The column-sharded W4A4 linear over NCCL on two GPUs: each rank's shard quantised with the
+all-reduced tensor scale equals the slice of the unsharded quantisation bit for bit, and the
+gathered output equals the one-GPU linear. Skipped with fewer than two GPUs."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from test_sharded import run_ranks
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_w4a4_sharded_matches_one_gpu():
+    for same_codes, same_ts, same_y, max_diff in run_ranks("w4a4_body", world=2, backend="nccl", timeout=300):
+        assert same_codes and same_ts
+        assert same_y, max_diff
