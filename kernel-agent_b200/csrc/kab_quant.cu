@@ -15,6 +15,14 @@ void row_shape(int64_t nchunks, int& threads, int& maxc) {
   maxc = per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : per <= 8 ? 8 : per <= 16 ? 16 : 0;
 }
 
+// One row per grid x index, chunks of 8 along the row over grid y blocks of `threads`
+// (a multiple of 32 that covers a short row in one block).
+void chunk_grid(int64_t rows, int64_t k, int& threads, dim3& grid) {
+  const int64_t chunks = k / 8;
+  threads = chunks >= 256 ? 256 : static_cast<int>((chunks + 31) / 32 * 32);
+  grid = dim3(static_cast<unsigned>(rows), static_cast<unsigned>((chunks + threads - 1) / threads));
+}
+
 int grid_for(int64_t work_items, int threads) {
   const int64_t blocks = (work_items + threads - 1) / threads;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
@@ -142,13 +150,15 @@ int kab_quant_groups_fp8(const void* x, int dtype, int64_t rows, int64_t k, int6
   KAB_REQUIRE(k % group == 0, "width %lld is not a multiple of the group %d", (long long)k, group);
   KAB_REQUIRE(rows == 0 || (q != nullptr && scales != nullptr && aligned(q, 8)), "outputs are null or misaligned");
   if (rows == 0 || k == 0) return KAB_OK;
-  const int threads = 256;
-  const int grid = grid_for(rows * (k / 8), threads);
+  KAB_REQUIRE(rows < (int64_t(1) << 31), "too many rows (%lld)", (long long)rows);
+  int threads;
+  dim3 grid;
+  chunk_grid(rows, k, threads, grid);
   const cudaStream_t s = as_stream(stream);
 #define KAB_GROUPS(TT)                                                                          \
-  if (group == 32) quant_groups_kernel<TT, 4><<<grid, threads, 0, s>>>(x, ldx, rows, k, q, scales); \
-  else if (group == 64) quant_groups_kernel<TT, 8><<<grid, threads, 0, s>>>(x, ldx, rows, k, q, scales); \
-  else quant_groups_kernel<TT, 16><<<grid, threads, 0, s>>>(x, ldx, rows, k, q, scales)
+  if (group == 32) quant_groups_kernel<TT, 4><<<grid, threads, 0, s>>>(x, ldx, k, q, scales); \
+  else if (group == 64) quant_groups_kernel<TT, 8><<<grid, threads, 0, s>>>(x, ldx, k, q, scales); \
+  else quant_groups_kernel<TT, 16><<<grid, threads, 0, s>>>(x, ldx, k, q, scales)
   if (dtype == KAB_BF16) { KAB_GROUPS(kBF16); }
   else if (dtype == KAB_F16) { KAB_GROUPS(kF16); }
   else { KAB_GROUPS(kF32); }
@@ -184,16 +194,18 @@ int kab_quant_mxfp8(const void* x, int dtype, int64_t rows, int64_t k, int64_t l
   KAB_REQUIRE(h == nullptr || aligned(h, 16), "h is not 16-byte aligned");
   KAB_REQUIRE(rows == 0 || (q != nullptr && scales != nullptr && aligned(q, 8)), "outputs are null or misaligned");
   if (rows == 0 || k == 0) return KAB_OK;
-  const int threads = 256;
-  const int grid = grid_for(rows * (k / 8), threads);
+  KAB_REQUIRE(rows < (int64_t(1) << 31), "too many rows (%lld)", (long long)rows);
+  int threads;
+  dim3 grid;
+  chunk_grid(rows, k, threads, grid);
   const cudaStream_t s = as_stream(stream);
   if (up != nullptr) {
-    if (dtype == KAB_BF16) quant_mxfp8_kernel<kBF16, true><<<grid, threads, 0, s>>>(x, ldx, up, ldu, rows, k, rule, swizzle, q, scales, h);
-    else quant_mxfp8_kernel<kF16, true><<<grid, threads, 0, s>>>(x, ldx, up, ldu, rows, k, rule, swizzle, q, scales, h);
+    if (dtype == KAB_BF16) quant_mxfp8_kernel<kBF16, true><<<grid, threads, 0, s>>>(x, ldx, up, ldu, k, rule, swizzle, q, scales, h);
+    else quant_mxfp8_kernel<kF16, true><<<grid, threads, 0, s>>>(x, ldx, up, ldu, k, rule, swizzle, q, scales, h);
   } else {
-    if (dtype == KAB_BF16) quant_mxfp8_kernel<kBF16, false><<<grid, threads, 0, s>>>(x, ldx, nullptr, 0, rows, k, rule, swizzle, q, scales, nullptr);
-    else if (dtype == KAB_F16) quant_mxfp8_kernel<kF16, false><<<grid, threads, 0, s>>>(x, ldx, nullptr, 0, rows, k, rule, swizzle, q, scales, nullptr);
-    else quant_mxfp8_kernel<kF32, false><<<grid, threads, 0, s>>>(x, ldx, nullptr, 0, rows, k, rule, swizzle, q, scales, nullptr);
+    if (dtype == KAB_BF16) quant_mxfp8_kernel<kBF16, false><<<grid, threads, 0, s>>>(x, ldx, nullptr, 0, k, rule, swizzle, q, scales, nullptr);
+    else if (dtype == KAB_F16) quant_mxfp8_kernel<kF16, false><<<grid, threads, 0, s>>>(x, ldx, nullptr, 0, k, rule, swizzle, q, scales, nullptr);
+    else quant_mxfp8_kernel<kF32, false><<<grid, threads, 0, s>>>(x, ldx, nullptr, 0, k, rule, swizzle, q, scales, nullptr);
   }
   return check_launch("kab_quant_mxfp8");
 }

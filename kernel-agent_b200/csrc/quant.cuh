@@ -71,6 +71,93 @@ __device__ __forceinline__ void load_producer8(const void* x, const void* up, in
   }
 }
 
+// ------------------------------------------------------------------ quotients by one divisor
+
+// The codes here (int8 rint, e4m3 and e2m1 round-to-nearest-even, each saturating) are step
+// functions of the IEEE quotient RN(v / s) whose steps sit at "short" floats: the rounding
+// boundaries (k + 1/2 for int8, the e4m3 and e2m1 midpoints) have at most 8, 4 and 3
+// significant bits, so their low LOW = 16, 19, 21 mantissa bits are zero. With y = RN(1 / s)
+// (__frcp_rn), RN(v * y) is within 3 units in the last place of RN(v / s) (three relative
+// roundings of 2^-24 each), so both give the same code unless the product lies within 8 units
+// of a short float. Only then (about 17 quotients in 2^LOW) does the thread recompute its
+// quotients with the IEEE division __fdiv_rn. The reciprocal path is taken only where y is a
+// normal float, |s| in [2^-125, 2^125]; other divisors always divide.
+struct Divisor {
+  float s, y;
+  bool fast;
+  __device__ __forceinline__ explicit Divisor(float s_) : s(s_) {
+    const float a = fabsf(s_);
+    fast = a >= 2.350988701644575e-38f && a <= 4.253529586511731e+37f;
+    y = fast ? __frcp_rn(s_) : 0.0f;
+  }
+};
+template <int LOW>
+__device__ __forceinline__ bool near_short(float q) {
+  return ((__float_as_uint(q) + 8u) & ((1u << LOW) - 1u)) <= 16u;
+}
+template <int LOW, int N>
+__device__ __forceinline__ void quotients(const float (&v)[N], const Divisor& d, float (&q)[N]) {
+  bool slow = !d.fast;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    q[i] = __fmul_rn(v[i], d.y);
+    slow |= near_short<LOW>(q[i]);
+  }
+  if (slow) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) q[i] = __fdiv_rn(v[i], d.s);
+  }
+}
+constexpr int kLowInt8 = 16, kLowE4m3 = 19, kLowE2m1 = 21;
+
+// Eight e4m3fn codes of quotients (cvt.rn.satfinite: +-inf and finite overflow to +-448, NaN
+// stays NaN: the reference's clamp(+-448) then cast), element 0 in the low byte.
+__device__ __forceinline__ uint2 e4m3x8(const float (&q)[8]) {
+  const uint32_t w0 = e4m3_pair(q[0], q[1]) | (static_cast<uint32_t>(e4m3_pair(q[2], q[3])) << 16);
+  const uint32_t w1 = e4m3_pair(q[4], q[5]) | (static_cast<uint32_t>(e4m3_pair(q[6], q[7])) << 16);
+  return make_uint2(w0, w1);
+}
+// Eight int8 codes: rint(q) to nearest even, clamped to +-127 (NaN -> 0), element 0 low.
+__device__ __forceinline__ uint2 int8x8(const float (&q)[8]) {
+  uint32_t w[2] = {0, 0};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int r = max(-127, min(127, __float2int_rn(q[j])));
+    w[j >> 2] |= static_cast<uint32_t>(r & 0xFF) << (8 * (j & 3));
+  }
+  return make_uint2(w[0], w[1]);
+}
+// Eight e2m1 codes (nibble j = element j) of quotients: cvt.rn.satfinite.e2m1x2 rounds to
+// nearest even, which puts the ties where the reference's midpoint comparisons do (up at
+// 0.75, 1.75, 3.5; down at 0.25, 1.25, 2.5, 5) and saturates at +-6 like its clamp. The
+// reference has no negative zero and maps NaN to 0: NaN quotients are zeroed first and a
+// zero magnitude drops its sign bit.
+__device__ __forceinline__ uint32_t e2m1x8(const float (&qin)[8]) {
+  float q[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) q[j] = qin[j] == qin[j] ? qin[j] : 0.0f;
+  uint32_t out;
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n"
+      " cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n"
+      " cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n"
+      " cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n"
+      " cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n"
+      " mov.b32 %0, {b0, b1, b2, b3};\n}"
+      : "=r"(out)
+      : "f"(q[0]), "f"(q[1]), "f"(q[2]), "f"(q[3]), "f"(q[4]), "f"(q[5]), "f"(q[6]), "f"(q[7]));
+  const uint32_t mag = out & 0x77777777u;
+  const uint32_t nonzero = (mag + 0x77777777u) & 0x88888888u;  // bit 3 of each nibble with mag > 0
+  return mag | (out & nonzero);
+}
+
+// NaN-keeping max |v| as the bits of |v|: non-negative floats order like their bit patterns
+// and every NaN (0x7F800001 and up) is above +inf.
+__device__ __forceinline__ uint32_t abs_bits_max8(const float (&v)[8], uint32_t acc) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc = max(acc, __float_as_uint(v[j]) & 0x7FFFFFFFu);
+  return acc;
+}
+
 // ------------------------------------------------------------------ MX exponent rules
 
 // frexp of an fp32 value as (ex, mantissa == 0.5): q = m * 2^ex, m in [0.5, 1); 0, inf and
@@ -160,51 +247,38 @@ quant_rows_kernel(const void* __restrict__ x, int64_t ldx, const void* __restric
     }
   };
   float cache[MAXC > 0 ? MAXC : 1][8];
-  float amax = 0.0f;
+  uint32_t abits = 0;
   if constexpr (MAXC > 0) {
 #pragma unroll
     for (int c = 0; c < MAXC; ++c) {
       const int64_t ci = threadIdx.x + static_cast<int64_t>(c) * blockDim.x;
       if (ci < nchunks) {
         value8(ci, cache[c]);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) amax = amax_step(amax, cache[c][j]);
+        abits = abs_bits_max8(cache[c], abits);
       }
     }
   } else {
     for (int64_t ci = threadIdx.x; ci < nchunks; ci += blockDim.x) {
       float v[8];
       value8(ci, v);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) amax = amax_step(amax, v[j]);
+      abits = abs_bits_max8(v, abits);
     }
   }
-  amax = block_amax(amax, red);
+  const float amax = block_amax(__uint_as_float(abits), red);
   float sc;
   if constexpr (OUT == 0) sc = amax > 0.0f ? __fmul_rn(amax, kInt8Step) : 1.0f;   // quant.py:777-780
   else sc = amax > 0.0f ? __fdiv_rn(amax, kFp8Max) : 1.0f;                        // quant.py:374-375
   if (threadIdx.x == 0) scale[row] = sc;
+  const Divisor div(sc);
   auto emit = [&](int64_t ci, float (&v)[8]) {
     if (h != nullptr) store_h8<T>(h, row * k + ci * 8, v);
+    float qv[8];
     if constexpr (OUT == 0) {  // quant.py:770-774: round(v / scale) to nearest even, ±127
-      uint32_t w[2] = {0, 0};
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float r = clamp_keep_nan(rintf(__fdiv_rn(v[j], sc)), -127.0f, 127.0f);
-        const uint32_t b = static_cast<uint8_t>(static_cast<int8_t>(__float2int_rn(r)));
-        w[j >> 2] |= b << (8 * (j & 3));
-      }
-      *reinterpret_cast<uint2*>(reinterpret_cast<int8_t*>(q) + row * k + ci * 8) = make_uint2(w[0], w[1]);
+      quotients<kLowInt8>(v, div, qv);
+      *reinterpret_cast<uint2*>(reinterpret_cast<int8_t*>(q) + row * k + ci * 8) = int8x8(qv);
     } else {  // quant.py:376: (v / scale).clamp(±448) to e4m3
-      uint32_t w[2];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float a = clamp_keep_nan(__fdiv_rn(v[2 * j], sc), -kFp8Max, kFp8Max);
-        const float b = clamp_keep_nan(__fdiv_rn(v[2 * j + 1], sc), -kFp8Max, kFp8Max);
-        const uint32_t p = e4m3_pair(a, b);
-        if (j & 1) w[j >> 1] |= p << 16; else w[j >> 1] = p;
-      }
-      *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(q) + row * k + ci * 8) = make_uint2(w[0], w[1]);
+      quotients<kLowE4m3>(v, div, qv);
+      *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(q) + row * k + ci * 8) = e4m3x8(qv);
     }
   };
   if constexpr (MAXC > 0) {
@@ -228,36 +302,23 @@ quant_rows_kernel(const void* __restrict__ x, int64_t ldx, const void* __restric
 // LANES = G / 8 threads share a group (G = 32, 64 or 128).
 template <int T, int LANES>
 __global__ void __launch_bounds__(256)
-quant_groups_kernel(const void* __restrict__ x, int64_t ldx, int64_t rows, int64_t k,
-                    uint8_t* __restrict__ q, float* __restrict__ scales) {
-  const int64_t chunks_per_row = k >> 3;
-  const int64_t total = rows * chunks_per_row;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-       c - (threadIdx.x & 31) < total; c += stride) {
-    const bool live = c < total;
-    const int64_t row = live ? c / chunks_per_row : 0, j = live ? c % chunks_per_row : 0;
-    float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (live) load8<T>(x, row * ldx + j * 8, v);
-    float amax = 0.0f;
+quant_groups_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, uint8_t* __restrict__ q,
+                    float* __restrict__ scales) {
+  const int64_t row = blockIdx.x;
+  const int64_t j = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;  // chunk of 8
+  const bool live = j < (k >> 3);
+  float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (live) load8<T>(x, row * ldx + j * 8, v);
+  uint32_t abits = abs_bits_max8(v, 0u);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) amax = amax_step(amax, v[i]);
-#pragma unroll
-    for (int o = LANES / 2; o > 0; o >>= 1) amax = amax_merge(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    float s = __fdiv_rn(amax, kFp8Max);
-    s = s > 0.0f ? s : 1.0f;  // fp8lib.py:17-18 _safe
-    if (!live) continue;
-    uint32_t w[2];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float a = clamp_keep_nan(__fdiv_rn(v[2 * i], s), -kFp8Max, kFp8Max);
-      const float b = clamp_keep_nan(__fdiv_rn(v[2 * i + 1], s), -kFp8Max, kFp8Max);
-      const uint32_t p = e4m3_pair(a, b);
-      if (i & 1) w[i >> 1] |= p << 16; else w[i >> 1] = p;
-    }
-    *reinterpret_cast<uint2*>(q + row * k + j * 8) = make_uint2(w[0], w[1]);
-    if ((j % LANES) == 0) scales[row * (k / (LANES * 8)) + j / LANES] = s;
-  }
+  for (int o = LANES / 2; o > 0; o >>= 1) abits = max(abits, __shfl_xor_sync(0xffffffffu, abits, o));
+  if (!live) return;
+  float s = __fdiv_rn(__uint_as_float(abits), kFp8Max);
+  s = s > 0.0f ? s : 1.0f;  // fp8lib.py:17-18 _safe
+  float qv[8];
+  quotients<kLowE4m3>(v, Divisor(s), qv);
+  *reinterpret_cast<uint2*>(q + row * k + j * 8) = e4m3x8(qv);
+  if ((j % LANES) == 0) scales[row * (k / (LANES * 8)) + j / LANES] = s;
 }
 
 // ------------------------------------------------------------------ FP8 B x B blocks
@@ -271,32 +332,26 @@ quant_blocks128_kernel(const void* __restrict__ w, int64_t ldw, int64_t k,
   __shared__ float red[32];
   const int64_t nb = blockIdx.y, kb = blockIdx.x;
   float v[8][8];
-  float amax = 0.0f;
+  uint32_t abits = 0;
 #pragma unroll
   for (int c = 0; c < 8; ++c) {  // 2048 chunks of 8: row = idx / 16, column chunk = idx % 16
     const int idx = threadIdx.x + c * 256;
     const int64_t r = nb * 128 + (idx >> 4), col = kb * 128 + (idx & 15) * 8;
     load8<T>(w, r * ldw + col, v[c]);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) amax = amax_step(amax, v[c][j]);
+    abits = abs_bits_max8(v[c], abits);
   }
-  amax = block_amax(amax, red);
+  const float amax = block_amax(__uint_as_float(abits), red);
   float s = __fdiv_rn(amax, kFp8Max);
   s = s > 0.0f ? s : 1.0f;
   if (threadIdx.x == 0) scales[nb * (k / 128) + kb] = s;
+  const Divisor div(s);
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     const int idx = threadIdx.x + c * 256;
     const int64_t r = nb * 128 + (idx >> 4), col = kb * 128 + (idx & 15) * 8;
-    uint32_t wd[2];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float a = clamp_keep_nan(__fdiv_rn(v[c][2 * i], s), -kFp8Max, kFp8Max);
-      const float b = clamp_keep_nan(__fdiv_rn(v[c][2 * i + 1], s), -kFp8Max, kFp8Max);
-      const uint32_t p = e4m3_pair(a, b);
-      if (i & 1) wd[i >> 1] |= p << 16; else wd[i >> 1] = p;
-    }
-    *reinterpret_cast<uint2*>(q + r * k + col) = make_uint2(wd[0], wd[1]);
+    float qv[8];
+    quotients<kLowE4m3>(v[c], div, qv);
+    *reinterpret_cast<uint2*>(q + r * k + col) = e4m3x8(qv);
   }
 }
 
@@ -307,41 +362,28 @@ quant_blocks128_kernel(const void* __restrict__ w, int64_t ldw, int64_t k,
 template <int T, bool SILU>
 __global__ void __launch_bounds__(256)
 quant_mxfp8_kernel(const void* __restrict__ x, int64_t ldx, const void* __restrict__ up,
-                   int64_t ldu, int64_t rows, int64_t k, int rule, int swizzle,
-                   uint8_t* __restrict__ q, uint8_t* __restrict__ scales, void* __restrict__ h) {
-  const int64_t cpr = k >> 3;
-  const int64_t total = rows * cpr;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const int64_t cols = k >> 5;
-  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-       c - (threadIdx.x & 31) < total; c += stride) {
-    const bool live = c < total;
-    const int64_t row = live ? c / cpr : 0, j = live ? c % cpr : 0;
-    float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (live) load_producer8<T, SILU>(x, up, row * ldx + j * 8, row * ldu + j * 8, v);
-    float amax = 0.0f;
+                   int64_t ldu, int64_t k, int rule, int swizzle, uint8_t* __restrict__ q,
+                   uint8_t* __restrict__ scales, void* __restrict__ h) {
+  const int64_t row = blockIdx.x;
+  const int64_t j = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;  // chunk of 8
+  const bool live = j < (k >> 3);
+  float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (live) load_producer8<T, SILU>(x, up, row * ldx + j * 8, row * ldu + j * 8, v);
+  uint32_t abits = abs_bits_max8(v, 0u);
+  abits = max(abits, __shfl_xor_sync(0xffffffffu, abits, 1));
+  abits = max(abits, __shfl_xor_sync(0xffffffffu, abits, 2));
+  if (!live) return;
+  const int e = mx_exponent(__uint_as_float(abits), rule);
+  const float inv = pow2_neg(e);  // x / 2^e == x * 2^-e exactly (one rounding of the same value)
+  if (SILU && h != nullptr) store_h8<T>(h, row * k + j * 8, v);
+  float qv[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) amax = amax_step(amax, v[i]);
-    amax = amax_merge(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = amax_merge(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    if (!live) continue;
-    const int e = mx_exponent(amax, rule);
-    const float inv = pow2_neg(e);  // x / 2^e == x * 2^-e exactly
-    if (SILU && h != nullptr) store_h8<T>(h, row * k + j * 8, v);
-    uint32_t w[2];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float a = clamp_keep_nan(__fmul_rn(v[2 * i], inv), -kFp8Max, kFp8Max);
-      const float b = clamp_keep_nan(__fmul_rn(v[2 * i + 1], inv), -kFp8Max, kFp8Max);
-      const uint32_t p = e4m3_pair(a, b);
-      if (i & 1) w[i >> 1] |= p << 16; else w[i >> 1] = p;
-    }
-    *reinterpret_cast<uint2*>(q + row * k + j * 8) = make_uint2(w[0], w[1]);
-    if ((j & 3) == 0) {
-      const int64_t col = j >> 2;
-      const int64_t off = swizzle ? scale_offset_swizzled(row, col, cols) : row * cols + col;
-      scales[off] = static_cast<uint8_t>(e + 127);
-    }
+  for (int i = 0; i < 8; ++i) qv[i] = __fmul_rn(v[i], inv);
+  *reinterpret_cast<uint2*>(q + row * k + j * 8) = e4m3x8(qv);
+  if ((j & 3) == 0) {
+    const int64_t cols = k >> 5, col = j >> 2;
+    const int64_t off = swizzle ? scale_offset_swizzled(row, col, cols) : row * cols + col;
+    scales[off] = static_cast<uint8_t>(e + 127);
   }
 }
 
@@ -365,7 +407,8 @@ quant_fp4_kernel(const void* __restrict__ x, int64_t ldx, const void* __restrict
   constexpr int LANES = BLOCK / 8;
   const int64_t cols = k / BLOCK;
   float cache[MAXC][8];
-  float amax = 0.0f;
+  uint32_t cmax[MAXC];  // max |v| of each chunk, as bits (NaN-keeping)
+  uint32_t abits = 0;
 #pragma unroll
   for (int c = 0; c < MAXC; ++c) {
     const int64_t ci = threadIdx.x + static_cast<int64_t>(c) * blockDim.x;
@@ -374,14 +417,14 @@ quant_fp4_kernel(const void* __restrict__ x, int64_t ldx, const void* __restrict
     if (ci < nchunks) {
       load_producer8<T, SILU>(x, up, row * ldx + ci * 8, row * ldu + ci * 8, cache[c]);
       if (SILU && h != nullptr) store_h8<T>(h, row * k + ci * 8, cache[c]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) amax = amax_step(amax, cache[c][j]);
     }
+    cmax[c] = abs_bits_max8(cache[c], 0u);
+    abits = max(abits, cmax[c]);
   }
   float s_outer = 1.0f;  // outer (activations) or tensor scale (weights)
   if constexpr (FMT == 0) {
     if constexpr (MODE == 0) {
-      amax = block_amax(amax, red);
+      const float amax = block_amax(__uint_as_float(abits), red);
       s_outer = amax > 0.0f ? __fmul_rn(amax, kNvfp4OuterStep) : 1.0f;  // quant.py:1104
     } else if constexpr (MODE == 1) {
       const float a = *amax_in;
@@ -395,33 +438,30 @@ quant_fp4_kernel(const void* __restrict__ x, int64_t ldx, const void* __restrict
 #pragma unroll
   for (int c = 0; c < MAXC; ++c) {
     const int64_t ci = threadIdx.x + static_cast<int64_t>(c) * blockDim.x;
-    float bmax = 0.0f;
+    uint32_t bbits = cmax[c];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) bmax = amax_step(bmax, cache[c][j]);
-#pragma unroll
-    for (int o = LANES / 2; o > 0; o >>= 1) bmax = amax_merge(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+    for (int o = LANES / 2; o > 0; o >>= 1) bbits = max(bbits, __shfl_xor_sync(0xffffffffu, bbits, o));
     if (ci >= nchunks) continue;
+    const float bmax = __uint_as_float(bbits);
     uint32_t sbyte;
     float step;
-    bool clamp_min = false;
     if constexpr (FMT == 0) {
       const float ratio = __fdiv_rn(bmax, div6);
       sbyte = e4m3_byte(min_keep_nan(ratio, 448.0f));
       step = __fmul_rn(e4m3_value(static_cast<uint8_t>(sbyte)), s_outer);
-      clamp_min = MODE == 2;  // weights divide by step.clamp_min(1e-38) (quant.py:265)
     } else {
       const int e = MODE == 2 ? mxfp4_weight_exponent(bmax) : mxfp4_act_exponent(bmax);
       sbyte = static_cast<uint32_t>(e + 127);
       step = e8m0_value(static_cast<uint8_t>(sbyte));
-      clamp_min = MODE == 2;
     }
-    const float div = (clamp_min && step < 1e-38f) ? 1e-38f : step;
+    // weights divide by step.clamp_min(1e-38) (quant.py:265); activations give 0 codes for a
+    // zero (or NaN) step
+    const float div = (MODE == 2 && step < 1e-38f) ? 1e-38f : step;
     uint32_t packed = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      uint32_t code = 0;
-      if (step > 0.0f) code = e2m1_code(clamp_keep_nan(__fdiv_rn(cache[c][j], div), -6.0f, 6.0f));
-      packed |= code << (4 * j);
+    if (step > 0.0f) {
+      float qv[8];
+      quotients<kLowE2m1>(cache[c], Divisor(div), qv);
+      packed = e2m1x8(qv);
     }
     *reinterpret_cast<uint32_t*>(q + row * (k >> 1) + ci * 4) = packed;
     if ((ci % LANES) == 0) {

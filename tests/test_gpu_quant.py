@@ -295,3 +295,84 @@ def test_cpu_tensors_are_refused(kq):
         kq.quantize_fp4_activations(torch.zeros(2, 32, device=DEV), granularity="channel")
     e = kq.quantize_fp4_activations(torch.zeros(0, 32, device=DEV))
     assert [tuple(t.shape) for t in e] == [(0, 16), (0, 2), (0,)]
+
+
+def _near(values: np.ndarray, ulps: int = 6) -> np.ndarray:
+    """fp32 values within +-ulps units in the last place of each of ``values``."""
+    v = values.astype(np.float32)
+    out = [v]
+    up, down = v.copy(), v.copy()
+    for _ in range(ulps):
+        up = np.nextafter(up, np.float32(np.inf))
+        down = np.nextafter(down, np.float32(-np.inf))
+        out += [up, down]
+    return np.concatenate(out)
+
+
+def _rows_of(values: np.ndarray, lead: float, width: int) -> np.ndarray:
+    """Rows of ``width`` fp32 elements: ``lead`` first (the row's amax), then ``values``
+    (padded with zeros)."""
+    per = width - 1
+    n = -(-values.size // per)
+    body = np.zeros(n * per, np.float32)
+    body[: values.size] = values
+    rows = np.concatenate([np.full((n, 1), lead, np.float32), body.reshape(n, per)], axis=1)
+    return rows
+
+
+def test_rounding_boundaries_fp8_int8(kq):
+    """Quotients within a few ulps of every rounding boundary (e4m3 midpoints, k + 1/2):
+    the fast reciprocal path with its exact fallback gives the IEEE-division codes."""
+    from oracle.formats import e4m3_to_f32
+
+    e4 = np.sort(e4m3_to_f32(np.arange(0, 127, dtype=np.uint8)).astype(np.float64))
+    mids = (e4[:-1] + e4[1:]) / 2
+    for lead in (448.0 * 1.3, 448.0 * 0.77, 3.1e-3, 1.7e5):
+        sc = np.float32(np.float32(lead) / np.float32(448.0))
+        vals = _near(np.concatenate([mids, -mids]) * np.float64(sc))
+        x = torch.from_numpy(_rows_of(vals, lead, 1024))
+        q, s = kq.quantize_fp8_activations(x.to(DEV))
+        rq, rs = oq.quantize_fp8_activations(x.numpy())
+        assert np.array_equal(np_bytes(q), rq) and np.array_equal(s.cpu().numpy(), rs), lead
+    halves = np.arange(0, 127) + 0.5
+    for lead in (127.0 * 1.3, 0.91, 2.2e4):
+        sc = np.float32(np.float32(lead) * oq.INT8_STEP)
+        vals = _near(np.concatenate([halves, -halves]) * np.float64(sc))
+        x = torch.from_numpy(_rows_of(vals, lead, 1024))
+        q, s = kq.quantize_int8_activations(x.to(DEV))
+        rq, rs = oq.quantize_int8_activations(x.numpy())
+        assert np.array_equal(np_bytes(q).view(np.int8), rq) and np.array_equal(s.cpu().numpy(), rs), lead
+
+
+@pytest.mark.parametrize("fmt", ["nvfp4", "mxfp4"])
+def test_rounding_boundaries_fp4(kq, fmt):
+    """e2m1 midpoints (0.25 ... 5) times each block's step, +-6 ulps: codes equal the
+    oracle's (IEEE division), activations and weights."""
+    block = kq.FP4_FORMATS[fmt][0]
+    mids = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0])
+    g = np.random.default_rng(7)
+    k = 64 * block
+    lead = np.float32(13.37)
+    maxima = (lead * g.uniform(0.02, 1.0, size=k // block)).astype(np.float32)
+    maxima[0] = lead
+    skel = np.zeros((1, k), np.float32)
+    skel[0, ::block] = maxima
+    _, rs, ro = oq.quantize_fp4_activations(skel, fmt, "token")
+    from oracle.formats import e4m3_to_f32
+
+    if fmt == "nvfp4":
+        steps = (e4m3_to_f32(rs.reshape(-1)) * ro[0]).astype(np.float32)
+    else:
+        steps = np.ldexp(np.float32(1.0), rs.reshape(-1).astype(np.int32) - 127).astype(np.float32)
+    row = skel.copy()
+    for b in range(k // block):
+        pool = _near(np.concatenate([mids, -mids]) * np.float64(steps[b]), ulps=2)
+        cand = np.roll(pool, -b * (block - 1))[: block - 1]
+        row[0, b * block + 1 : (b + 1) * block] = cand
+    x = torch.from_numpy(np.repeat(row, 3, axis=0))
+    q, s, o = kq.quantize_fp4_activations(x.to(DEV), fmt, "token")
+    rq, rs2, ro2 = oq.quantize_fp4_activations(x.numpy(), fmt, "token")
+    assert np.array_equal(np_bytes(q), rq) and np.array_equal(np_bytes(s), rs2)
+    q, s, ts = kq.quantize_fp4(x.to(DEV), fmt)
+    rq, rs2, rts = oq.quantize_fp4(x.numpy(), fmt)
+    assert np.array_equal(np_bytes(q), rq) and np.array_equal(np_bytes(s), rs2)
