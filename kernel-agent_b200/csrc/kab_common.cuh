@@ -143,6 +143,11 @@ __device__ __forceinline__ float e4m3_value(uint8_t b) {
   else mag = __uint_as_float(((e + 120u) << 23) | (m << 20));
   return (b & 0x80) ? -mag : mag;
 }
+// The same value by the hardware conversion (e4m3 -> f16 is exact, f16 -> f32 too).
+__device__ __forceinline__ float e4m3_value_hw(uint8_t b) {
+  const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b), __NV_E4M3);
+  return __half2float(__half(h));
+}
 // 2^(b - 127) for an e8m0 byte b (b == 0: 2^-127, an fp32 subnormal; 255: NaN).
 __device__ __forceinline__ float e8m0_value(uint8_t b) {
   if (b == 255) return __uint_as_float(0x7FC00000u);

@@ -61,12 +61,13 @@ void launch_fp4(int maxc, unsigned rows, int threads, cudaStream_t s, const void
                 const void* up, int64_t ldu, int64_t nrows, int64_t k, const float* amax,
                 const float* ts, int swizzle, uint8_t* q, uint8_t* scales, float* outer, void* h) {
 #define KAB_FP4(MC) quant_fp4_kernel<T, MC, FMT, MODE, SILU><<<rows, threads, 0, s>>>(x, ldx, up, ldu, nrows, k, amax, ts, swizzle, q, scales, outer, h)
-  switch (maxc) {
-    case 1: KAB_FP4(1); break;
-    case 2: KAB_FP4(2); break;
-    case 4: KAB_FP4(4); break;
-    case 8: KAB_FP4(8); break;
-    default: KAB_FP4(16); break;
+  if constexpr (FMT == 0) {
+    if (maxc == 1) KAB_FP4(1);
+    else if (maxc == 2) KAB_FP4(2);
+    else KAB_FP4(4);
+  } else {
+    if (maxc == 1) KAB_FP4(1);
+    else KAB_FP4(2);
   }
 #undef KAB_FP4
 }
@@ -230,8 +231,15 @@ int kab_quant_fp4(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx
   KAB_REQUIRE(h == nullptr || aligned(h, 16), "h is not 16-byte aligned");
   KAB_REQUIRE(rows == 0 || (q != nullptr && scales != nullptr && aligned(q, 4)), "outputs are null or misaligned");
   if (rows == 0 || k == 0) return KAB_OK;
-  int threads, maxc;
-  row_shape(k / 8, threads, maxc);
+  // threads per row and scale blocks per thread: 256 threads where that suffices, up to 512
+  // with 4 (NVFP4) or 2 (MXFP4) register-resident blocks each
+  const int64_t nblk = k / block;
+  const int nb_max = fmt == KAB_NVFP4 ? 4 : 2;
+  int threads = static_cast<int>(nblk < 256 ? (nblk + 31) / 32 * 32 : 256);
+  if (nblk > static_cast<int64_t>(threads) * nb_max)
+    threads = static_cast<int>(((nblk + nb_max - 1) / nb_max + 31) / 32 * 32);
+  const int64_t per = (nblk + threads - 1) / threads;
+  const int maxc = per <= 1 ? 1 : per <= 2 ? 2 : 4;
   const cudaStream_t s = as_stream(stream);
   const unsigned grid = static_cast<unsigned>(rows);
   if (up != nullptr) {

@@ -32,9 +32,27 @@ __device__ __forceinline__ float round_to_input(float f) {
   else if constexpr (T == kF16) return __half2float(__float2half_rn(f));
   else return f;
 }
+__device__ __forceinline__ float rcp_approx(float s);
+template <int LOW>
+__device__ __forceinline__ bool near_short(float q);
+// RN(g / d) rounded to the input dtype: the rounding to bf16 / fp16 is a step function with
+// steps at floats of at most 9 / 12 significant bits, so g * rcp(d) decides it unless the
+// product lies next to such a float (then the IEEE division does).
+template <int T>
+__device__ __forceinline__ float div_to_input(float g, float d) {
+  if constexpr (T == kF32) {
+    return __fdiv_rn(g, d);
+  } else {
+    constexpr int LOW = T == kBF16 ? 15 : 12;
+    const float a = fabsf(d);
+    float q = __fmul_rn(g, rcp_approx(d));
+    if (!(a >= 2.350988701644575e-38f && a <= 4.253529586511731e+37f) || near_short<LOW>(q)) q = __fdiv_rn(g, d);
+    return round_to_input<T>(q);
+  }
+}
 template <int T>
 __device__ __forceinline__ float silu_mul(float g, float u) {
-  const float a = round_to_input<T>(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+  const float a = div_to_input<T>(g, __fadd_rn(1.0f, expf(-g)));
   return round_to_input<T>(__fmul_rn(a, u));
 }
 
@@ -76,37 +94,48 @@ __device__ __forceinline__ void load_producer8(const void* x, const void* up, in
 // The codes here (int8 rint, e4m3 and e2m1 round-to-nearest-even, each saturating) are step
 // functions of the IEEE quotient RN(v / s) whose steps sit at "short" floats: the rounding
 // boundaries (k + 1/2 for int8, the e4m3 and e2m1 midpoints) have at most 8, 4 and 3
-// significant bits, so their low LOW = 16, 19, 21 mantissa bits are zero. With y = RN(1 / s)
-// (__frcp_rn), RN(v * y) is within 3 units in the last place of RN(v / s) (three relative
-// roundings of 2^-24 each), so both give the same code unless the product lies within 8 units
-// of a short float. Only then (about 17 quotients in 2^LOW) does the thread recompute its
-// quotients with the IEEE division __fdiv_rn. The reciprocal path is taken only where y is a
-// normal float, |s| in [2^-125, 2^125]; other divisors always divide.
+// significant bits, so their low LOW = 16, 19, 21 mantissa bits are zero. With y the hardware
+// reciprocal of s (relative error at most 2^-22), RN(v * y) is within 6 units in the last
+// place of RN(v / s), so both give the same code unless the product lies within 16 units of a
+// short float. Only then (about 33 quotients in 2^LOW) does the thread recompute its
+// quotients with the IEEE division __fdiv_rn. The reciprocal path is taken only where 1 / s
+// is a normal float, |s| in [2^-125, 2^125]; other divisors always divide.
+// The hardware reciprocal (rcp.approx: within about one unit in the last place).
+__device__ __forceinline__ float rcp_approx(float s) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(s));
+  return y;
+}
 struct Divisor {
   float s, y;
   bool fast;
   __device__ __forceinline__ explicit Divisor(float s_) : s(s_) {
     const float a = fabsf(s_);
     fast = a >= 2.350988701644575e-38f && a <= 4.253529586511731e+37f;
-    y = fast ? __frcp_rn(s_) : 0.0f;
+    y = fast ? rcp_approx(s_) : 0.0f;
   }
 };
+// True when q is within 16 units in the last place of a float whose low LOW mantissa bits are
+// zero (with y within 2 units of 1 / s, RN(v * y) is within 6 units of RN(v / s)).
 template <int LOW>
 __device__ __forceinline__ bool near_short(float q) {
-  return ((__float_as_uint(q) + 8u) & ((1u << LOW) - 1u)) <= 16u;
+  return ((__float_as_uint(q) + 16u) & ((1u << LOW) - 1u)) <= 32u;
 }
 template <int LOW, int N>
 __device__ __forceinline__ void quotients(const float (&v)[N], const Divisor& d, float (&q)[N]) {
+  float t[N];  // q may alias v
   bool slow = !d.fast;
 #pragma unroll
   for (int i = 0; i < N; ++i) {
-    q[i] = __fmul_rn(v[i], d.y);
-    slow |= near_short<LOW>(q[i]);
+    t[i] = __fmul_rn(v[i], d.y);
+    slow |= near_short<LOW>(t[i]);
   }
   if (slow) {
 #pragma unroll
-    for (int i = 0; i < N; ++i) q[i] = __fdiv_rn(v[i], d.s);
+    for (int i = 0; i < N; ++i) t[i] = __fdiv_rn(v[i], d.s);
   }
+#pragma unroll
+  for (int i = 0; i < N; ++i) q[i] = t[i];
 }
 constexpr int kLowInt8 = 16, kLowE4m3 = 19, kLowE2m1 = 21;
 
@@ -130,12 +159,9 @@ __device__ __forceinline__ uint2 int8x8(const float (&q)[8]) {
 // Eight e2m1 codes (nibble j = element j) of quotients: cvt.rn.satfinite.e2m1x2 rounds to
 // nearest even, which puts the ties where the reference's midpoint comparisons do (up at
 // 0.75, 1.75, 3.5; down at 0.25, 1.25, 2.5, 5) and saturates at +-6 like its clamp. The
-// reference has no negative zero and maps NaN to 0: NaN quotients are zeroed first and a
-// zero magnitude drops its sign bit.
-__device__ __forceinline__ uint32_t e2m1x8(const float (&qin)[8]) {
-  float q[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) q[j] = qin[j] == qin[j] ? qin[j] : 0.0f;
+// reference has no negative zero: a zero magnitude drops its sign bit. It maps NaN to 0: the
+// caller zeroes NaN quotients first.
+__device__ __forceinline__ uint32_t e2m1x8(const float (&q)[8]) {
   uint32_t out;
   asm("{\n .reg .b8 b0, b1, b2, b3;\n"
       " cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n"
@@ -392,34 +418,45 @@ quant_mxfp8_kernel(const void* __restrict__ x, int64_t ldx, const void* __restri
 // FMT 0: NVFP4 (16 per e4m3 scale), 1: MXFP4 (32 per e8m0 scale).
 // MODE 0: activations per token (outer from the row's amax), 1: activations with one amax
 // per call (*amax_in), 2: weights (tensor scale *ts_in; quant.py:217-272).
-// One CTA per row; MAXC chunks of 8 per thread in registers.
-template <int T, int MAXC, int FMT, int MODE, bool SILU>
-__global__ void __launch_bounds__(256)
+// One CTA per row; each thread owns NB whole scale blocks of the row (block bi = thread +
+// j * blockDim), kept in registers between the row reduction and the conversion: the block
+// scale is computed once per block and the codes of a block leave in one 8- or 16-byte store.
+template <int T, int NB, int FMT, int MODE, bool SILU>
+__global__ void __launch_bounds__(512)
 quant_fp4_kernel(const void* __restrict__ x, int64_t ldx, const void* __restrict__ up,
                  int64_t ldu, int64_t rows, int64_t k, const float* __restrict__ amax_in,
                  const float* __restrict__ ts_in, int swizzle, uint8_t* __restrict__ q,
                  uint8_t* __restrict__ scales, float* __restrict__ outer_out,
                  void* __restrict__ h) {
   __shared__ float red[32];
-  const int64_t row = blockIdx.x;
-  const int64_t nchunks = k >> 3;
   constexpr int BLOCK = FMT == 0 ? 16 : 32;
-  constexpr int LANES = BLOCK / 8;
-  const int64_t cols = k / BLOCK;
-  float cache[MAXC][8];
-  uint32_t cmax[MAXC];  // max |v| of each chunk, as bits (NaN-keeping)
+  constexpr int CH = BLOCK / 8;  // chunks of 8 per block
+  const int64_t row = blockIdx.x;
+  const int nblk = static_cast<int>(k / BLOCK);
+  float v[NB][BLOCK];
+  uint32_t bbits[NB];  // max |v| of each block, as bits (NaN-keeping)
   uint32_t abits = 0;
 #pragma unroll
-  for (int c = 0; c < MAXC; ++c) {
-    const int64_t ci = threadIdx.x + static_cast<int64_t>(c) * blockDim.x;
+  for (int b = 0; b < NB; ++b) {
+    const int bi = threadIdx.x + b * blockDim.x;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) cache[c][j] = 0.0f;
-    if (ci < nchunks) {
-      load_producer8<T, SILU>(x, up, row * ldx + ci * 8, row * ldu + ci * 8, cache[c]);
-      if (SILU && h != nullptr) store_h8<T>(h, row * k + ci * 8, cache[c]);
+    for (int j = 0; j < BLOCK; ++j) v[b][j] = 0.0f;
+    if (bi < nblk) {
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        float chunk[8];
+        const int64_t col = static_cast<int64_t>(bi) * BLOCK + c * 8;
+        load_producer8<T, SILU>(x, up, row * ldx + col, row * ldu + col, chunk);
+        if (SILU && h != nullptr) store_h8<T>(h, row * k + col, chunk);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[b][c * 8 + j] = chunk[j];
+      }
     }
-    cmax[c] = abs_bits_max8(cache[c], 0u);
-    abits = max(abits, cmax[c]);
+    uint32_t m = 0;
+#pragma unroll
+    for (int j = 0; j < BLOCK; ++j) m = max(m, __float_as_uint(v[b][j]) & 0x7FFFFFFFu);
+    bbits[b] = m;
+    abits = max(abits, m);
   }
   float s_outer = 1.0f;  // outer (activations) or tensor scale (weights)
   if constexpr (FMT == 0) {
@@ -435,40 +472,51 @@ quant_fp4_kernel(const void* __restrict__ x, int64_t ldx, const void* __restrict
   }
   if (threadIdx.x == 0 && outer_out != nullptr) outer_out[row] = s_outer;
   const float div6 = __fmul_rn(s_outer, 6.0f);  // fp32(outer * 6), fp32(6 * tensor_scale)
+  const Divisor by6(div6);
+  const int64_t cols = nblk;
 #pragma unroll
-  for (int c = 0; c < MAXC; ++c) {
-    const int64_t ci = threadIdx.x + static_cast<int64_t>(c) * blockDim.x;
-    uint32_t bbits = cmax[c];
-#pragma unroll
-    for (int o = LANES / 2; o > 0; o >>= 1) bbits = max(bbits, __shfl_xor_sync(0xffffffffu, bbits, o));
-    if (ci >= nchunks) continue;
-    const float bmax = __uint_as_float(bbits);
+  for (int b = 0; b < NB; ++b) {
+    const int bi = threadIdx.x + b * blockDim.x;
+    if (bi >= nblk) continue;
+    const float bmax = __uint_as_float(bbits[b]);
     uint32_t sbyte;
     float step;
     if constexpr (FMT == 0) {
-      const float ratio = __fdiv_rn(bmax, div6);
-      sbyte = e4m3_byte(min_keep_nan(ratio, 448.0f));
-      step = __fmul_rn(e4m3_value(static_cast<uint8_t>(sbyte)), s_outer);
+      // e4m3(min(bmax / (outer * 6), 448)): satfinite saturates like the clamp, keeps NaN
+      const float bm[1] = {bmax};
+      float ratio[1];
+      quotients<kLowE4m3>(bm, by6, ratio);
+      sbyte = e4m3_byte(ratio[0]);
+      step = __fmul_rn(e4m3_value_hw(static_cast<uint8_t>(sbyte)), s_outer);
     } else {
       const int e = MODE == 2 ? mxfp4_weight_exponent(bmax) : mxfp4_act_exponent(bmax);
       sbyte = static_cast<uint32_t>(e + 127);
       step = e8m0_value(static_cast<uint8_t>(sbyte));
     }
-    // weights divide by step.clamp_min(1e-38) (quant.py:265); activations give 0 codes for a
-    // zero (or NaN) step
+    // weights divide by step.clamp_min(1e-38) (quant.py:265); a zero (or NaN) step gives 0 codes
     const float div = (MODE == 2 && step < 1e-38f) ? 1e-38f : step;
-    uint32_t packed = 0;
+    uint32_t packed[CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) packed[c] = 0;
     if (step > 0.0f) {
-      float qv[8];
-      quotients<kLowE2m1>(cache[c], Divisor(div), qv);
-      packed = e2m1x8(qv);
+      quotients<kLowE2m1>(v[b], Divisor(div), v[b]);  // in place: the values are not needed again
+      if (bbits[b] > 0x7F800000u) {  // a NaN in the block: its codes are 0
+#pragma unroll
+        for (int j = 0; j < BLOCK; ++j) v[b][j] = v[b][j] == v[b][j] ? v[b][j] : 0.0f;
+      }
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        float e8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) e8[j] = v[b][c * 8 + j];
+        packed[c] = e2m1x8(e8);
+      }
     }
-    *reinterpret_cast<uint32_t*>(q + row * (k >> 1) + ci * 4) = packed;
-    if ((ci % LANES) == 0) {
-      const int64_t col = ci / LANES;
-      const int64_t off = swizzle ? scale_offset_swizzled(row, col, cols) : row * cols + col;
-      scales[off] = static_cast<uint8_t>(sbyte);
-    }
+    uint8_t* dst = q + row * (k >> 1) + static_cast<int64_t>(bi) * (BLOCK / 2);
+    if constexpr (CH == 2) *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    const int64_t off = swizzle ? scale_offset_swizzled(row, bi, cols) : row * cols + bi;
+    scales[off] = static_cast<uint8_t>(sbyte);
   }
 }
 
