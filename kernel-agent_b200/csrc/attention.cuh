@@ -1,0 +1,374 @@
+// FP8 (e4m3) causal attention prefill with one scale per (batch, head), the "qkpv" emulation
+// of kernel-agent's docs/research-scripts/fp8-sm120/fp8lib.py:184-215 (emulated_sdpa):
+// Q, K, V quantised per head over [S, D] (_fq_last2, fp8lib.py:173-176: scale amax / 448,
+// a zero scale replaced by 1), S = Q K^T on e4m3 codes, P = exp(S - max) carried as
+// e4m3(P * 448) / 448 into P V, the row sum taken before P is rounded.
+//
+//  * quant_heads kernels: the per-head amax (one atomic max of the bits per block) and the
+//    codes, row-major [S, D] for Q and K, transposed [D, S] for V so that V^T is the
+//    K-major B operand of the P V product.
+//  * attention_fp8_kernel: one CTA per 128-query tile. Warp 0 loads Q once and K / V^T tiles
+//    of 128 keys through a 3-stage TMA ring; warp 1 issues the tcgen05 MMAs (kind::f8f6f4):
+//    S_j = Q K_j^T into one of two 128-column TMEM buffers, then O += P_j V_j into a third;
+//    warps 2-5 (one query row per thread) run the online softmax in the exp2 domain: the
+//    running max, the row sum of the unrounded P, P quantised to e4m3 and written into shared
+//    memory in the 128-byte swizzled layout the MMA reads, and the rescaling of O in TMEM
+//    when a row's max grows (after the previous P V has landed). The final O is divided by
+//    448 * rowsum, multiplied by the V scale and stored in bf16.
+//
+// The running max replaces the reference's global row max: P is rounded relative to the max
+// seen so far, so its codes differ from the reference's, and the result is judged against
+// fp32 attention by relative L2 and cosine, as the reference's own emulation is.
+// No load uses cluster multicast; every wait is bounded and records kDevTimeout.
+#pragma once
+
+#include "codes.cuh"
+#include "tcgen05.cuh"
+
+namespace kab {
+
+// g_attention_status: the device status word, defined by the including translation unit
+// (kab_attention.cu) before this header.
+
+// ------------------------------------------------------------------ per-head quantiser
+
+// Per-head NaN-keeping amax as float bits: grid (blocks per head, heads); a head is a
+// contiguous [S, D] slab of `per_head` elements. amax[] holds 0 before the launch.
+template <int T>
+__global__ void __launch_bounds__(256)
+head_amax_kernel(const void* __restrict__ x, int64_t per_head, unsigned* __restrict__ amax) {
+  __shared__ float red[32];
+  const int64_t head = blockIdx.y;
+  const int64_t chunks = per_head >> 3;
+  uint32_t bits = 0;
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < chunks;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float v[8];
+    load8<T>(x, head * per_head + c * 8, v);
+    bits = abs_bits_max8(v, bits);
+  }
+  const float m = block_amax(__uint_as_float(bits), red);
+  if (threadIdx.x == 0) atomicMax(amax + head, __float_as_uint(m) & 0x7FFFFFFFu);
+}
+
+// fp8lib.py:173-176: scale = amax / 448 (0 or NaN -> 1), codes e4m3(x / scale).
+__device__ __forceinline__ float head_scale(unsigned amax_bits) {
+  const float s = __fdiv_rn(__uint_as_float(amax_bits), kFp8Max);
+  return s > 0.0f ? s : 1.0f;
+}
+
+// Codes of a [64 rows, D] tile of one head: grid (S / 64, heads), 256 threads. TRANSPOSE
+// writes the tile into [D, S] (column block s0 .. s0 + 63 of each of the D rows).
+template <int T, bool TRANSPOSE>
+__global__ void __launch_bounds__(256)
+quant_heads_kernel(const void* __restrict__ x, int64_t seq, int d, const unsigned* __restrict__ amax,
+                   uint8_t* __restrict__ q, float* __restrict__ scales) {
+  extern __shared__ uint8_t tile[];  // [64][d] codes (TRANSPOSE only)
+  const int64_t head = blockIdx.y;
+  const int64_t s0 = static_cast<int64_t>(blockIdx.x) * 64;
+  const float sc = head_scale(amax[head]);
+  if (blockIdx.x == 0 && threadIdx.x == 0) scales[head] = sc;
+  const Divisor div(sc);
+  const int cpr = d >> 3;  // chunks of 8 per row
+  const int total = 64 * cpr;
+  for (int c = threadIdx.x; c < total; c += blockDim.x) {
+    const int r = c / cpr, col = (c % cpr) * 8;
+    if (s0 + r >= seq) continue;
+    float v[8], qv[8];
+    load8<T>(x, (head * seq + s0 + r) * d + col, v);
+    quotients<kLowE4m3>(v, div, qv);
+    const uint2 codes = e4m3x8(qv);
+    if constexpr (TRANSPOSE) *reinterpret_cast<uint2*>(tile + r * d + col) = codes;
+    else *reinterpret_cast<uint2*>(q + (head * seq + s0 + r) * d + col) = codes;
+  }
+  if constexpr (TRANSPOSE) {
+    __syncthreads();
+    // [D, S]: row dd gets the tile's 64 codes of column dd, 16 at a time
+    for (int c = threadIdx.x; c < d * 4; c += blockDim.x) {
+      const int dd = c >> 2, part = c & 3;
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) word |= static_cast<uint32_t>(tile[(part * 16 + i * 4 + b) * d + dd]) << (8 * b);
+        w[i] = word;
+      }
+      const int64_t col = s0 + part * 16;
+      if (col + 16 <= seq)
+        *reinterpret_cast<uint4*>(q + (head * d + dd) * seq + col) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ attention
+
+struct AttnArgs {
+  int seq;            // keys = queries, a multiple of 128
+  int heads_q, heads_kv;
+  int q_tiles;        // seq / 128
+  int causal;
+  const float* q_scale;  // [batch * heads_q]
+  const float* k_scale;  // [batch * heads_kv]
+  const float* v_scale;
+  float sm_scale_log2;   // softmax scale * log2(e)
+  void* out;             // [batch, heads_q, seq, 128] bf16
+};
+
+struct AttnLayout {
+  static constexpr int kTile = 128 * 128;  // bytes of a 128 x 128 e4m3 tile
+  static constexpr int kStages = 3;
+  static constexpr int kThreads = 192;
+  static constexpr int kQ = 0;
+  static constexpr int kK = kQ + kTile;
+  static constexpr int kV = kK + kStages * kTile;
+  static constexpr int kP = kV + kStages * kTile;
+  static constexpr int kBars = kP + 2 * kTile;
+  static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 2 + 1 + 1;
+  static constexpr int kSmem = 1024 + kBars + kNumBars * 8 + 16;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// A bounded wait whose outcome the whole warp shares (the softmax warps follow it with
+// .sync.aligned TMEM accesses, which need every lane).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity));
+}
+
+__global__ void __launch_bounds__(AttnLayout::kThreads, 1)
+attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constant__ CUtensorMap tma_k,
+                     const __grid_constant__ CUtensorMap tma_vt, AttnArgs g) {
+  using L = AttnLayout;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::kQ;
+  uint8_t* sK = smem + L::kK;
+  uint8_t* sV = smem + L::kV;
+  uint8_t* sP = smem + L::kP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBars);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + L::kStages;
+  uint64_t* s_full = kv_empty + L::kStages;  // [2]
+  uint64_t* s_empty = s_full + 2;            // [2], 4 softmax warps
+  uint64_t* p_full = s_empty + 2;            // [2], 4 softmax warps
+  uint64_t* p_empty = p_full + 2;            // [2]
+  uint64_t* o_ready = p_empty + 2;           // one P V product has landed in O
+  uint64_t* drain = o_ready + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  // heavy (long causal) tiles first
+  const int qt = g.q_tiles - 1 - static_cast<int>(blockIdx.x % g.q_tiles);
+  const int bh = static_cast<int>(blockIdx.x / g.q_tiles);  // b * heads_q + h
+  const int b = bh / g.heads_q, h = bh % g.heads_q;
+  const int hk = h / (g.heads_q / g.heads_kv);
+  const int bhk = b * g.heads_kv + hk;
+  const int n_kv = g.causal ? qt + 1 : g.q_tiles;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(q_full, 1);
+    for (int s = 0; s < L::kStages; ++s) {
+      tc::mbar_init(&kv_full[s], 1);
+      tc::mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&s_full[i], 1);
+      tc::mbar_init(&s_empty[i], 4);
+      tc::mbar_init(&p_full[i], 4);
+      tc::mbar_init(&p_empty[i], 1);
+    }
+    tc::mbar_init(o_ready, 1);
+    tc::mbar_init(drain, 1);
+    tc::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tensormap(&tma_q);
+    tc::prefetch_tensormap(&tma_k);
+    tc::prefetch_tensormap(&tma_vt);
+  }
+  if (warp == 1) { tc::tmem_alloc(tmem_slot, 512); tc::tmem_relinquish(); }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 256;  // S buffers at columns 0 and 128, O at 256
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---------------------------------------------------- TMA producer
+      bool ok = true;
+      tc::mbar_arrive_expect_tx(q_full, L::kTile);
+      tc::tma_load_2d(&tma_q, q_full, sQ, 0, bh * g.seq + qt * 128);
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % L::kStages;
+        const uint32_t ph = static_cast<uint32_t>((j / L::kStages) & 1);
+        if (!tc::mbar_wait(&kv_empty[s], ph ^ 1u)) { ok = false; break; }
+        tc::mbar_arrive_expect_tx(&kv_full[s], 2 * L::kTile);
+        tc::tma_load_2d(&tma_k, &kv_full[s], sK + s * L::kTile, 0, bhk * g.seq + j * 128);
+        tc::tma_load_2d(&tma_vt, &kv_full[s], sV + s * L::kTile, j * 128, bhk * 128);
+        issued = j + 1;
+      }
+      if (!ok) {
+        atomicOr(&g_attention_status, kDevTimeout);
+        tc::mbar_wait(q_full, 0);
+        for (int j = (issued > L::kStages ? issued - L::kStages : 0); j < issued; ++j)
+          tc::mbar_wait(&kv_full[j % L::kStages], static_cast<uint32_t>((j / L::kStages) & 1));
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---------------------------------------------------- MMA issuer
+      bool ok = tc::mbar_wait(q_full, 0);
+      const uint32_t idesc = tc::idesc_f8(128, 128);
+      const uint64_t qdesc = tc::desc_sw128(tc::smem_u32(sQ));
+      auto issue_pv = [&](int t) -> bool {
+        if (!tc::mbar_wait(&p_full[t & 1], static_cast<uint32_t>((t >> 1) & 1))) return false;
+        tc::fence_after_sync();
+        const int s = t % L::kStages;
+        const uint64_t pdesc = tc::desc_sw128(tc::smem_u32(sP + (t & 1) * L::kTile));
+        const uint64_t vdesc = tc::desc_sw128(tc::smem_u32(sV + s * L::kTile));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc::mma_f8(tO, pdesc + static_cast<uint64_t>(2 * kk), vdesc + static_cast<uint64_t>(2 * kk), idesc,
+                     (t > 0 || kk > 0) ? 1u : 0u);
+        tc::commit(&p_empty[t & 1]);
+        tc::commit(&kv_empty[s]);
+        tc::commit(o_ready);
+        return true;
+      };
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j % L::kStages;
+        if (!tc::mbar_wait(&kv_full[s], static_cast<uint32_t>((j / L::kStages) & 1))) { ok = false; break; }
+        if (!tc::mbar_wait(&s_empty[j & 1], static_cast<uint32_t>(((j >> 1) & 1) ^ 1))) { ok = false; break; }
+        tc::fence_after_sync();
+        const uint64_t kdesc = tc::desc_sw128(tc::smem_u32(sK + s * L::kTile));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc::mma_f8(tS + (j & 1) * 128, qdesc + static_cast<uint64_t>(2 * kk), kdesc + static_cast<uint64_t>(2 * kk),
+                     idesc, kk > 0 ? 1u : 0u);
+        tc::commit(&s_full[j & 1]);
+        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok && !issue_pv(n_kv - 1)) ok = false;
+      tc::commit(drain);  // every MMA issued has completed once this arrives
+      if (!tc::mbar_wait(drain, 0)) ok = false;
+      if (!ok) atomicOr(&g_attention_status, kDevTimeout);
+    }
+  } else {  // ------------------------------------------------------------ softmax warps
+    const int quarter = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * quarter) << 16;
+    const int r = 32 * quarter + lane;  // query row within the tile
+    const int qrow = qt * 128 + r;
+    const float scale_log2 = g.q_scale[bh] * g.k_scale[bhk] * g.sm_scale_log2;
+    float m_run = -INFINITY, l_run = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!warp_wait(&s_full[j & 1], static_cast<uint32_t>((j >> 1) & 1))) { ok = false; break; }
+      tc::fence_after_sync();
+      float sv[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t raw[32];
+        tc::tmem_ld32(tS + lane_base + (j & 1) * 128 + c * 32, raw);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(raw[i]);
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&s_empty[j & 1]);
+      const bool diag = g.causal && j == qt;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        float t = sv[i] * scale_log2;
+        if (diag && i > r) t = -INFINITY;  // key after the query
+        sv[i] = t;
+        mt = fmaxf(mt, t);
+      }
+      const float m_new = fmaxf(m_run, mt);
+      const float alpha = m_run == -INFINITY ? 0.0f : ex2(m_run - m_new);
+      float rowsum = 0.0f;
+      uint32_t pw[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float p0 = ex2(sv[4 * i] - m_new), p1 = ex2(sv[4 * i + 1] - m_new);
+        const float p2 = ex2(sv[4 * i + 2] - m_new), p3 = ex2(sv[4 * i + 3] - m_new);
+        rowsum += (p0 + p1) + (p2 + p3);
+        pw[i] = static_cast<uint32_t>(e4m3_pair(p0 * kFp8Max, p1 * kFp8Max)) |
+                (static_cast<uint32_t>(e4m3_pair(p2 * kFp8Max, p3 * kFp8Max)) << 16);
+      }
+      l_run = l_run * alpha + rowsum;
+      m_run = m_new;
+      // P_j into its buffer once P V_{j-2} has read it: row r, 16-byte chunk c at c ^ (r % 8)
+      if (!warp_wait(&p_empty[j & 1], static_cast<uint32_t>(((j >> 1) & 1) ^ 1))) { ok = false; break; }
+      uint8_t* prow = sP + (j & 1) * L::kTile + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
+            make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
+      tc::fence_proxy_async();
+      if (j >= 1) {  // O holds P V up to tile j - 1: rescale it to this tile's max
+        if (!warp_wait(o_ready, static_cast<uint32_t>((j - 1) & 1))) { ok = false; break; }
+        tc::fence_after_sync();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tc::tmem_ld32(tO + lane_base + c * 32, o);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint32_t v8[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v8[e] = __float_as_uint(__uint_as_float(o[8 * i + e]) * alpha);
+              tc::tmem_st8(tO + lane_base + c * 32 + 8 * i, v8);
+            }
+          }
+          tc::tmem_st_wait();
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&p_full[j & 1]);
+    }
+    // the last P V, then O / (448 * rowsum) * v_scale in bf16
+    if (ok && !warp_wait(o_ready, static_cast<uint32_t>((n_kv - 1) & 1))) ok = false;
+    if (ok) {
+      tc::fence_after_sync();
+      const float f = g.v_scale[bhk] / (kFp8Max * l_run);
+      __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(g.out) + (static_cast<int64_t>(bh) * g.seq + qrow) * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tc::tmem_ld32(tO + lane_base + c * 32, o);
+        tc::tmem_ld_wait();
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const __nv_bfloat162 hv = __floats2bfloat162_rn(__uint_as_float(o[2 * i]) * f, __uint_as_float(o[2 * i + 1]) * f);
+          w[i] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          reinterpret_cast<uint4*>(orow + c * 32)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+      }
+    } else if (lane == 0) {
+      atomicOr(&g_attention_status, kDevTimeout);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace kab

@@ -79,6 +79,10 @@ _SIGNATURES: dict[str, list] = {
                       c_int64, c_void_p, c_int, c_void_p, c_int, c_int64, c_void_p],
     "kab_gemm_f8_blockwise": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p,
                               c_int, c_void_p, c_int, c_int64, c_void_p],
+    "kab_quant_heads_fp8": [c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_void_p, c_void_p, c_void_p,
+                            c_void_p],
+    "kab_attention_fp8": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                          c_int64, c_int64, c_int, ctypes.c_float, c_void_p, c_void_p],
     "kab_compare_scratch_bytes": [c_int64],
     "kab_compare": [POINTER(KabCompareParams), c_void_p, c_size_t, c_void_p, c_void_p],
     "kab_compare_noalloc": [POINTER(KabCompareParams), c_void_p, c_void_p],

@@ -161,6 +161,16 @@ def main(src: str) -> None:
     va = torch.randn(1, 2, 64, 64, generator=gq).to(bf)
     ya = fp8lib.emulated_sdpa(qa, ka, va, is_causal=True, enable_gqa=True, mode="qkpv")
     out.update(att_q=bits(qa), att_k=bits(ka), att_v=bits(va), att_y=bits(ya))
+    # the GPU kernel's shape class (head_dim 128, whole 128-token tiles), causal and not, with
+    # the emulation's own fp32 attention for the error ratios
+    qb = torch.randn(1, 4, 256, 128, generator=gq).to(bf)
+    kb = torch.randn(1, 2, 256, 128, generator=gq).to(bf)
+    vb = torch.randn(1, 2, 256, 128, generator=gq).to(bf)
+    yb = fp8lib.emulated_sdpa(qb, kb, vb, is_causal=True, enable_gqa=True, mode="qkpv")
+    yb_nc = fp8lib.emulated_sdpa(qb, kb, vb, is_causal=False, enable_gqa=True, mode="qkpv")
+    yb_ref = fp8lib.emulated_sdpa(qb.float(), kb.float(), vb.float(), is_causal=True, enable_gqa=True, mode="none")
+    out.update(att2_q=bits(qb), att2_k=bits(kb), att2_v=bits(vb), att2_y=bits(yb), att2_y_nc=bits(yb_nc),
+               att2_y_fp32=yb_ref.numpy())
 
     # ---------------------------------------------------------------- comparator
     cases = []
