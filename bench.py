@@ -12,6 +12,7 @@ Workloads (synthetic, seeded; BASELINE.json's configurations):
   mxfp8_producer  config 3's fused SiLU(gate) * up -> MXFP8 producer (HBM-bound).
   compare  the comparator on a config-4-sized bf16 output pair (HBM-bound).
   fp8_blockwise  config 2: 1x128 FP8 producer + blockwise-scaled tcgen05 GEMM (M = 2048).
+  fp8_attention  config 5: per-head e4m3 quantisation + causal tcgen05 FP8 attention.
 
 ``value`` is the whole-job throughput with inputs resident in HBM, timed with CUDA events
 over exactly K steps between barriers, the max over ranks; ``e2e`` is the same metric through
@@ -676,7 +677,122 @@ class Fp8Blockwise(Workload):
         return rate, os.cpu_count() or 1, f"oracle blockwise FP8 linear on {rows} rows per step"
 
 
-WORKLOADS = {w.name: w for w in (W4A4Linear, Nvfp4Producer, Mxfp8Producer, Compare, Fp8Blockwise)}
+class Fp8Attention(Workload):
+    """Config 5: causal FP8 attention prefill, B 4, Hq 32, Hkv 8, S 4096, D 128: the per-head
+    e4m3 quantisation of Q, K, V plus the tcgen05 attention kernel; bf16 out."""
+
+    name = "fp8_attention"
+    unit = "TFLOP/s"
+    dtype = "e4m3 Q K^T and P V (fp32 softmax) -> bf16"
+    scaling = "weak"
+
+    def setup(self, dev, world, rank):
+        import torch
+
+        from kernel_agent_b200 import workloads
+        from kernel_agent_b200.kernels import attention
+
+        self.torch, self.attention = torch, attention
+        self.q, self.k, self.v = (t.to(dev) for t in workloads.config5(seed=0, device="cuda"))
+        b, hq, s, d = self.q.shape
+        self.b, self.hq, self.s, self.d = b, hq, s, d
+        # causal: sum over query tiles of the keys up to the diagonal, both products
+        self.flops = 4.0 * b * hq * d * (s * (s + 1) / 2)
+        self.units = self.flops / 1e12
+        self.kernel = "attention_fp8_kernel"
+        self.kernel_flops = self.flops
+        self.h2d = (self.q.numel() + self.k.numel() + self.v.numel()) * 2
+        self.d2h = self.q.numel() * 2
+        self.hosts = [t.cpu().pin_memory() for t in (self.q, self.k, self.v)]
+        self.y_host = torch.empty(self.q.shape, dtype=torch.bfloat16).pin_memory()
+        self.config = {
+            "workload": "config 5: causal FP8 attention prefill, Q [4, 32, 4096, 128], K/V [4, 8, 4096, 128] -> bf16",
+            "batch": b, "heads_q": hq, "heads_kv": self.k.shape[1], "seq": s, "head_dim": d,
+            "step": "per-head e4m3 quantisation of Q, K, V + tcgen05 attention (S = QK^T, online softmax, PV)",
+            "parallelism": "replicas", "l2": "inputs larger than L2 (Q, K, V, out 402 MB bf16)",
+        }
+
+    def step(self):
+        self.attention.attention_fp8(self.q, self.k, self.v, is_causal=True, enable_gqa=True)
+        return 7
+
+    def dominant(self):
+        if not hasattr(self, "_codes"):
+            a = self.attention
+            self._codes = (a.quantize_fp8_heads(self.q), a.quantize_fp8_heads(self.k),
+                           a.quantize_fp8_heads(self.v, transpose=True))
+            self._out = self.torch.empty(self.q.shape, dtype=self.torch.bfloat16, device=self.q.device)
+        from kernel_agent_b200 import _native as nat
+
+        (qc, qs), (kc, ks), (vt, vs) = self._codes
+        nat.call("kab_attention_fp8", qc.data_ptr(), qs.data_ptr(), kc.data_ptr(), ks.data_ptr(), vt.data_ptr(),
+                 vs.data_ptr(), self.b, self.hq, self.k.shape[1], self.s, self.d, 1, self.d ** -0.5,
+                 self._out.data_ptr(), nat.stream_of(self.q))
+        return 1
+
+    def e2e_step(self):
+        q, k, v = (h.to(self.q.device, non_blocking=True) for h in self.hosts)
+        y = self.attention.attention_fp8(q, k, v, is_causal=True, enable_gqa=True)
+        self.y_host.copy_(y, non_blocking=True)
+        return 7
+
+    def tensor_peak(self, pk, pk_kind):
+        return 2.0 * pk["bf16_tflops"], f"2 x {pk_kind} bf16 burst ({pk['bf16_tflops']:.0f} TFLOP/s): FP8 dense"
+
+    def library_bar(self):
+        """torch's bf16 flash attention (F.scaled_dot_product_attention, causal, GQA) on the
+        same inputs: TFLOP/s."""
+        torch = self.torch
+        import torch.nn.functional as F
+
+        try:
+            fn = lambda: F.scaled_dot_product_attention(self.q, self.k, self.v, is_causal=True, enable_gqa=True)  # noqa: E731
+            for _ in range(2):
+                fn()
+            ms, _ = timed(lambda: (fn(), 1)[1], 5, torch)
+            return {"sdpa_bf16_tflops": self.flops / (ms / 5 / 1e3) / 1e12,
+                    "what": "F.scaled_dot_product_attention bf16, causal, enable_gqa (not FP8)"}
+        except Exception as exc:
+            return {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+
+    def _head(self, b, h):
+        hk = h // (self.hq // self.k.shape[1])
+        return tuple(t.float().cpu().numpy() for t in (self.q[b, h], self.k[b, hk], self.v[b, hk]))
+
+    def cpu_baseline(self):
+        import time as _t
+
+        sys.path.insert(0, str(ROOT))
+        from oracle import fp8lib
+
+        q, k, v = self._head(0, 0)
+        flops_head = 4.0 * self.d * (self.s * (self.s + 1) / 2)
+        t0 = _t.perf_counter()
+        reps = 0
+        while _t.perf_counter() - t0 < 10.0:
+            fp8lib.attention_fp8_head(q, k, v, causal=True)
+            reps += 1
+        rate = flops_head * reps / (_t.perf_counter() - t0) / 1e12
+        return {"value": rate, "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port",
+                "sample": "oracle emulated_sdpa (qkpv) of one (batch, head) [4096 x 4096], float64 BLAS, "
+                          "repeated ~10 s"}
+
+    def reference(self, steps, warmup):
+        import time as _t
+
+        sys.path.insert(0, str(ROOT))
+        from oracle import fp8lib
+
+        q, k, v = self._head(0, 0)
+        flops_head = 4.0 * self.d * (self.s * (self.s + 1) / 2)
+        t0 = _t.perf_counter()
+        for _ in range(steps):
+            fp8lib.attention_fp8_head(q, k, v, causal=True)
+        rate = flops_head * steps / (_t.perf_counter() - t0) / 1e12
+        return rate, os.cpu_count() or 1, "oracle qkpv attention of one (batch, head) per step"
+
+
+WORKLOADS = {w.name: w for w in (W4A4Linear, Nvfp4Producer, Mxfp8Producer, Compare, Fp8Blockwise, Fp8Attention)}
 DEFAULT = "w4a4"
 
 
