@@ -265,6 +265,30 @@ int kab_channel_rms(const void* x, const void* alt, int dtype, int64_t rows,
                     int64_t channels, float* rms, void* scratch, size_t scratch_bytes,
                     void* stream);
 
+/* ------------------------------------------------------------------ scale-rule checks */
+
+/* What one scale-rule check found (device memory; zeroed by the call): block counts and the
+ * bits of the largest block-max / step ratio (a non-negative float; NaN kept). */
+typedef struct KabScaleCheck {
+  unsigned long long saturated, underflow, nonfinite, not_representable, coarser, not_pow2;
+  unsigned worst_ratio_bits;
+  unsigned pad;
+} KabScaleCheck;
+
+/* quant.py:623-660 mxfp8_saturation: x [rows, k] against fp32 MXFP8 scale values `step`
+ * [rows, k / 32] (unswizzled): saturated (ratio above 448 * (1 + 2^-10), or a zero step under a
+ * non-zero block), coarser (above the ceil rule's scale), not_pow2, worst ratio. */
+int kab_mxfp8_saturation(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                         const float* step, KabScaleCheck* result, void* stream);
+
+/* quant.py:1325-1416 fp4_scale_check: x [rows, k] against fp32 block-scale values `scale`
+ * [rows, k / block] (fmt KAB_NVFP4: e4m3 per 16; KAB_MXFP4: e8m0 per 32) and the outer scale
+ * (`outer`: [rows] with outer_per_row, else one value; null: 1): saturated, underflow,
+ * nonfinite, not_representable, coarser, worst ratio. */
+int kab_fp4_scale_check(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, int fmt,
+                        const float* scale, const float* outer, int outer_per_row,
+                        KabScaleCheck* result, void* stream);
+
 /* ------------------------------------------------------------------ FP8 attention prefill */
 
 /* Per-head e4m3 quantisation of x [heads, seq, d] (docs/research-scripts/fp8-sm120/

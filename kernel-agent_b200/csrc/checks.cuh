@@ -1,0 +1,150 @@
+// Scale-rule checks of block-scaled activations (the evaluator's scale guard): one reduction
+// pass over x and its block scales, counting the blocks each rule of kernel-agent's
+// src/kernel_agent/kernels/quant.py flags and the largest block-max / step ratio.
+//
+//  * mxfp8_saturation_kernel: quant.py:623-660 (saturated, coarser, not_pow2, worst_ratio);
+//  * fp4_scale_check_kernel:  quant.py:1325-1416 (saturated, underflow, nonfinite,
+//    not_representable, coarser, worst_ratio) for NVFP4 (FMT 0) and MXFP4 (FMT 1).
+//
+// One thread per scale block; counts are summed per warp and added to the result with one
+// 64-bit atomic per warp and count; the worst ratio (>= 0, NaN kept as the largest) with an
+// atomic max of its bits.
+#pragma once
+
+#include "quant.cuh"
+
+namespace kab {
+
+constexpr float kMxSaturationLimit = 448.4375f;      // 448 * (1 + 2^-10), exact
+constexpr float kNvfp4RoundingRatio = 6.375f;        // 6 * (1 + 2^-4), quant.py:1291
+constexpr float kFp4SlackFactor = 1.0009765625f;     // 1 + 2^-10, quant.py:1294
+constexpr float kLowTieFactor = 0.99999904632568359375f;  // fp32(1 - 2^-20)
+constexpr float kE4m3MinNormal = 0.015625f;          // 2^-6
+
+__device__ __forceinline__ void check_add(unsigned long long* dst, unsigned v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0 && v) atomicAdd(dst, static_cast<unsigned long long>(v));
+}
+__device__ __forceinline__ void check_max(unsigned* dst, float ratio) {
+  uint32_t b = ratio != ratio ? 0x7FC00000u : __float_as_uint(ratio);  // ratio >= 0 or NaN
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(dst, b);
+}
+
+// NaN-keeping max |x| of the BLOCK elements of block (row, col), as a float.
+template <int T, int BLOCK>
+__device__ __forceinline__ float block_max_of(const void* x, int64_t ldx, int64_t row, int64_t col) {
+  uint32_t m = 0;
+#pragma unroll
+  for (int c = 0; c < BLOCK / 8; ++c) {
+    float v[8];
+    load8<T>(x, row * ldx + col * BLOCK + c * 8, v);
+    m = abs_bits_max8(v, m);
+  }
+  return __uint_as_float(m);
+}
+
+// quant.py:623-660. `step`: fp32 scale values [rows, nb].
+template <int T>
+__global__ void __launch_bounds__(256)
+mxfp8_saturation_kernel(const void* __restrict__ x, int64_t ldx, int64_t rows, int64_t nb,
+                        const float* __restrict__ step, KabScaleCheck* out) {
+  const int64_t total = rows * nb;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  unsigned saturated = 0, coarser = 0, not_pow2 = 0;
+  float worst = 0.0f;
+  for (int64_t base = blockIdx.x * static_cast<int64_t>(blockDim.x); base < total; base += stride) {
+    const int64_t i = base + threadIdx.x;
+    if (i < total) {
+      const int64_t row = i / nb, col = i - row * nb;
+      const float amax = block_max_of<T, 32>(x, ldx, row, col);
+      const float s = step[i];
+      int ex;
+      bool half;
+      frexp_parts(s, ex, half);
+      not_pow2 += (!half && s > 0.0f) ? 1u : 0u;
+      const float ratio = amax > 0.0f ? __fdiv_rn(amax, s != s ? s : fmaxf(s, 1e-38f)) : 0.0f;
+      saturated += (ratio > kMxSaturationLimit || (s <= 0.0f && amax > 0.0f)) ? 1u : 0u;
+      if (amax > 0.0f) {
+        const int e = mx_exponent(amax, 0);
+        coarser += (static_cast<double>(s) > ldexp(1.0, e)) ? 1u : 0u;
+      }
+      worst = (ratio > worst || ratio != ratio) ? ratio : worst;
+    }
+  }
+  check_add(&out->saturated, saturated);
+  check_add(&out->coarser, coarser);
+  check_add(&out->not_pow2, not_pow2);
+  check_max(&out->worst_ratio_bits, worst);
+}
+
+// quant.py:1325-1416. `scale`: fp32 block-scale values [rows, nb]; `outer`: [rows] or one
+// value (outer_per_row 0), or null for 1.
+template <int T, int FMT>
+__global__ void __launch_bounds__(256)
+fp4_scale_check_kernel(const void* __restrict__ x, int64_t ldx, int64_t rows, int64_t nb,
+                       const float* __restrict__ scale, const float* __restrict__ outer, int outer_per_row,
+                       KabScaleCheck* out) {
+  constexpr int BLOCK = FMT == 0 ? 16 : 32;
+  const int64_t total = rows * nb;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  unsigned saturated = 0, underflow = 0, nonfinite = 0, not_repr = 0, coarser = 0;
+  float worst = 0.0f;
+  for (int64_t base = blockIdx.x * static_cast<int64_t>(blockDim.x); base < total; base += stride) {
+    const int64_t i = base + threadIdx.x;
+    if (i < total) {
+      const int64_t row = i / nb, col = i - row * nb;
+      const float bmax = block_max_of<T, BLOCK>(x, ldx, row, col);
+      const float s = scale[i];
+      const float o = outer == nullptr ? 1.0f : outer[outer_per_row ? row : 0];
+      const bool finite = isfinite(s) && isfinite(o) && o > 0.0f;
+      const float step = finite ? __fmul_rn(s, o) : 0.0f;
+      const bool live = finite && bmax > 0.0f;
+      const float ratio = (live && step > 0.0f) ? __fdiv_rn(bmax, fmaxf(step, 1e-38f)) : 0.0f;
+      const bool zero = live && step <= 0.0f;
+      float bound;
+      bool representable;
+      if constexpr (FMT == 0) {
+        const float safe = finite ? o : 1.0f;
+        const float r = __fdiv_rn(bmax, __fmul_rn(safe, 6.0f));
+        const float rn = e4m3_value_hw(e4m3_byte(min_keep_nan(r, 448.0f)));
+        const float rn_low = e4m3_value_hw(e4m3_byte(min_keep_nan(__fmul_rn(r, kLowTieFactor), 448.0f)));
+        bound = kNvfp4RoundingRatio;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {  // a subnormal scale's own rounding error
+          const float ref = t == 0 ? rn : rn_low;
+          const float ref_ratio = __fdiv_rn(bmax, fmaxf(__fmul_rn(ref, safe), 1e-38f));
+          if (ref > 0.0f && ref < kE4m3MinNormal) bound = fmaxf(bound, ref_ratio);
+        }
+        underflow += (zero && rn_low > 0.0f) ? 1u : 0u;
+        representable = e4m3_value_hw(e4m3_byte(s)) == s;
+        coarser += (live && s > rn) ? 1u : 0u;
+      } else {
+        bound = 6.0f;
+        underflow += zero ? 1u : 0u;
+        int ex;
+        bool half;
+        frexp_parts(s, ex, half);
+        representable = half && s > 0.0f;
+        frexp_parts(bmax, ex, half);
+        const float mant = bmax == 0.0f ? 0.0f : (isfinite(bmax) ? ldexpf(bmax, -ex) : bmax);  // frexp(inf) = inf
+        const int c = ex - 3 + (mant > 0.75f ? 1 : 0);
+        coarser += (live && s > __double2float_rn(ldexp(1.0, c))) ? 1u : 0u;
+      }
+      saturated += (live && ratio > __fmul_rn(bound, kFp4SlackFactor)) ? 1u : 0u;
+      nonfinite += finite ? 0u : 1u;
+      not_repr += (finite && !representable) ? 1u : 0u;
+      worst = (ratio > worst || ratio != ratio) ? ratio : worst;
+    }
+  }
+  check_add(&out->saturated, saturated);
+  check_add(&out->underflow, underflow);
+  check_add(&out->nonfinite, nonfinite);
+  check_add(&out->not_representable, not_repr);
+  check_add(&out->coarser, coarser);
+  check_max(&out->worst_ratio_bits, worst);
+}
+
+}  // namespace kab

@@ -1,5 +1,6 @@
 // extern "C" entry points of the quantise producers (quant.cuh): argument checks, launch
 // shapes and template dispatch.
+#include "checks.cuh"
 #include "kab_host.h"
 #include "quant.cuh"
 
@@ -303,6 +304,44 @@ int kab_fp4_values(const uint8_t* codes, const uint8_t* scales, int64_t rows, in
   const int grid = grid_for(rows * k, 256);
   fp4_values_kernel<<<grid, 256, 0, as_stream(stream)>>>(codes, scales, rows, k, fmt, out);
   return check_launch("kab_fp4_values");
+}
+
+int kab_mxfp8_saturation(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                         const float* step, KabScaleCheck* result, void* stream) {
+  if (int e = check_matrix(x, dtype, rows, k, ldx, "x")) return e;
+  KAB_REQUIRE(k % 32 == 0, "width %lld is not a multiple of the MXFP8 block (32)", (long long)k);
+  KAB_REQUIRE(result != nullptr && (rows == 0 || step != nullptr), "null pointer");
+  const cudaStream_t s = as_stream(stream);
+  if (cudaMemsetAsync(result, 0, sizeof(KabScaleCheck), s) != cudaSuccess) return check_launch("check reset");
+  const int64_t total = rows * (k / 32);
+  if (total == 0) return KAB_OK;
+  const int grid = grid_for(total, 256);
+  if (dtype == KAB_BF16) mxfp8_saturation_kernel<kBF16><<<grid, 256, 0, s>>>(x, ldx, rows, k / 32, step, result);
+  else if (dtype == KAB_F16) mxfp8_saturation_kernel<kF16><<<grid, 256, 0, s>>>(x, ldx, rows, k / 32, step, result);
+  else mxfp8_saturation_kernel<kF32><<<grid, 256, 0, s>>>(x, ldx, rows, k / 32, step, result);
+  return check_launch("kab_mxfp8_saturation");
+}
+
+int kab_fp4_scale_check(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, int fmt,
+                        const float* scale, const float* outer, int outer_per_row,
+                        KabScaleCheck* result, void* stream) {
+  if (int e = check_matrix(x, dtype, rows, k, ldx, "x")) return e;
+  KAB_REQUIRE(fmt == KAB_NVFP4 || fmt == KAB_MXFP4, "fmt %d is not NVFP4 (0) or MXFP4 (1)", fmt);
+  const int block = fmt == KAB_NVFP4 ? 16 : 32;
+  KAB_REQUIRE(k % block == 0, "width %lld is not a multiple of the block (%d)", (long long)k, block);
+  KAB_REQUIRE(result != nullptr && (rows == 0 || scale != nullptr), "null pointer");
+  const cudaStream_t s = as_stream(stream);
+  if (cudaMemsetAsync(result, 0, sizeof(KabScaleCheck), s) != cudaSuccess) return check_launch("check reset");
+  const int64_t nb = k / block, total = rows * nb;
+  if (total == 0) return KAB_OK;
+  const int grid = grid_for(total, 256);
+#define KAB_CHECK(TT, F) fp4_scale_check_kernel<TT, F><<<grid, 256, 0, s>>>(x, ldx, rows, nb, scale, outer, outer_per_row, result)
+#define KAB_CHECK_T(F) \
+  if (dtype == KAB_BF16) KAB_CHECK(kBF16, F); else if (dtype == KAB_F16) KAB_CHECK(kF16, F); else KAB_CHECK(kF32, F)
+  if (fmt == KAB_NVFP4) { KAB_CHECK_T(0); } else { KAB_CHECK_T(1); }
+#undef KAB_CHECK_T
+#undef KAB_CHECK
+  return check_launch("kab_fp4_scale_check");
 }
 
 }  // extern "C"

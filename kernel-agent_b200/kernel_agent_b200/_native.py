@@ -35,6 +35,19 @@ class KabCompareResult(ctypes.Structure):
     ]
 
 
+class KabScaleCheck(ctypes.Structure):
+    _fields_ = [
+        ("saturated", ctypes.c_ulonglong),
+        ("underflow", ctypes.c_ulonglong),
+        ("nonfinite", ctypes.c_ulonglong),
+        ("not_representable", ctypes.c_ulonglong),
+        ("coarser", ctypes.c_ulonglong),
+        ("not_pow2", ctypes.c_ulonglong),
+        ("worst_ratio_bits", ctypes.c_uint),
+        ("pad_", ctypes.c_uint),
+    ]
+
+
 class KabCompareParams(ctypes.Structure):
     _fields_ = [
         ("ref", c_void_p), ("new_", c_void_p), ("rerounded", c_void_p),
@@ -83,6 +96,9 @@ _SIGNATURES: dict[str, list] = {
                             c_void_p],
     "kab_attention_fp8": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                           c_int64, c_int64, c_int, ctypes.c_float, c_void_p, c_void_p],
+    "kab_mxfp8_saturation": [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
+    "kab_fp4_scale_check": [c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_void_p, c_void_p, c_int, c_void_p,
+                            c_void_p],
     "kab_compare_scratch_bytes": [c_int64],
     "kab_compare": [POINTER(KabCompareParams), c_void_p, c_size_t, c_void_p, c_void_p],
     "kab_compare_noalloc": [POINTER(KabCompareParams), c_void_p, c_void_p],

@@ -13,7 +13,9 @@ epilogue roundings.
 
 from __future__ import annotations
 
+import ctypes
 import math
+import struct
 from typing import Any
 
 import torch
@@ -519,3 +521,217 @@ def fp4_w4a4_linear(
     y = gemm.nvf4(xq, xs.view(torch.uint8), outer, codes, ws, ts, bias,
                   out_dtype=x.dtype if x.dtype in (torch.bfloat16, torch.float16, torch.float32) else torch.float32)
     return _linear_out(y, x, n)
+
+
+# ------------------------------------------------------------------ scale-rule checks (GPU reductions)
+
+
+def _check_result(out: torch.Tensor) -> "nat.KabScaleCheck":
+    host = out.cpu()  # one device-to-host read of the counts
+    return nat.KabScaleCheck.from_buffer_copy(bytes(host.numpy().tobytes()))
+
+
+def _worst(res) -> float:
+    return struct.unpack("<f", struct.pack("<I", res.worst_ratio_bits))[0]
+
+
+def mxfp8_saturation(x: torch.Tensor, scales: torch.Tensor) -> dict[str, Any]:
+    """quant.py:623-660: how MXFP8 ``scales`` ``[rows, K / 32]`` (e8m0, uint8 biased exponents
+    or values; unswizzled) fit the block maxima of ``x [..., K]``: ``blocks``, ``saturated``,
+    ``share``, ``worst_ratio``, ``coarser``, ``not_pow2`` (one GPU pass)."""
+    k = x.shape[-1]
+    x2 = _rows(_input(x)) if x.dim() else x
+    rows, nblocks = x2.shape[0], k // MX_BLOCK
+    if k % MX_BLOCK or tuple(scales.shape) != (rows, nblocks):
+        raise ValueError(
+            f"expected scales [{rows}, {nblocks}] (rows of x, K / 32, unswizzled) for x "
+            f"{tuple(x.shape)}, got {tuple(scales.shape)}"
+        )
+    nat.require_cuda(x2)
+    step = mx_scale_values(scales).to(x2.device).contiguous()
+    out = torch.empty(ctypes.sizeof(nat.KabScaleCheck), dtype=torch.uint8, device=x2.device)
+    nat.call("kab_mxfp8_saturation", x2.data_ptr(), nat.dtype_code(x2), rows, k, x2.stride(0) if rows else k,
+             step.data_ptr(), out.data_ptr(), _stream(x2))
+    res = _check_result(out)
+    blocks = rows * nblocks
+    return {
+        "blocks": blocks,
+        "saturated": int(res.saturated),
+        "share": _sig(res.saturated / blocks) if blocks else 0.0,
+        "worst_ratio": _sig(_worst(res)) if blocks else 0.0,
+        "coarser": int(res.coarser),
+        "not_pow2": int(res.not_pow2),
+    }
+
+
+def mxfp8_scale_problem(x: torch.Tensor, scales: torch.Tensor) -> str | None:
+    """quant.py:663-680: why ``scales`` are not a valid MXFP8 quantisation of ``x``; None when
+    they are."""
+    found = mxfp8_saturation(x, scales)
+    if found["saturated"]:
+        return (
+            f"{found['saturated']} of {found['blocks']} MXFP8 blocks ({found['share']:.1%}) "
+            f"saturate: block maximum up to {found['worst_ratio']:.4g} x scale, above e4m3's "
+            "448 (their largest elements are clamped). Use the scale 2^ceil(log2(amax / 448)); "
+            "the OCP rule 2^(floor(log2 amax) - 8) saturates maxima in (448, 512) x scale"
+        )
+    if found["not_pow2"]:
+        return (
+            f"{found['not_pow2']} of {found['blocks']} MXFP8 scales are not powers of two "
+            "(ue8m0 holds an exponent only)"
+        )
+    return None
+
+
+def _stress_blocks(rows: int, nb: int, block: int, seed: int) -> torch.Tensor:
+    """Gaussian blocks ``[rows, nb, block]`` scaled so that each block's largest magnitude is
+    1, at its largest Gaussian value (the stress inputs' shape, from a CPU generator)."""
+    gen = torch.Generator().manual_seed(seed)
+    v = torch.randn(rows, nb, block, generator=gen)
+    peak = v.abs().argmax(dim=-1, keepdim=True)
+    return v / v.abs().gather(-1, peak)
+
+
+def mxfp8_stress_input(shape, *, dtype: torch.dtype = torch.bfloat16, device="cpu", seed: int = 0) -> torch.Tensor:
+    """quant.py:683-704: blocks of 32 with maxima at ±1.9 x 2^e, e from -8 to 8 across blocks
+    (the OCP floor rule saturates every block, the ceil rule none)."""
+    k = int(shape[-1])
+    if k % MX_BLOCK:
+        raise ValueError(f"the last dimension {k} is not a multiple of the MXFP8 block (32)")
+    rows = math.prod(int(n) for n in shape[:-1])
+    v = _stress_blocks(rows, k // MX_BLOCK, MX_BLOCK, seed)
+    e = torch.arange(rows * (k // MX_BLOCK)).reshape(rows, k // MX_BLOCK, 1) % 17 - 8
+    v = v * 1.9 * torch.pow(2.0, e.float())
+    return v.reshape(*shape).to(dtype=dtype, device=device)
+
+
+def fp4_format_of(k: int, scales: torch.Tensor) -> str:
+    """quant.py:1300-1316: the FP4 format of activation scales for ``K`` = ``k``."""
+    if scales.dtype == torch.float8_e4m3fn:
+        return "nvfp4"
+    if scales.dtype == torch.float8_e8m0fnu:
+        return "mxfp4"
+    width = scales.shape[-1] if scales.dim() == 2 else -1
+    for fmt, (block, _) in FP4_FORMATS.items():
+        if k % block == 0 and width == k // block:
+            return fmt
+    raise ValueError(
+        f"expected FP4 activation scales [rows, K / 16] (NVFP4, e4m3) or [rows, K / 32] (MXFP4, "
+        f"e8m0), unswizzled, for K = {k}; got {scales.dtype} {tuple(scales.shape)}"
+    )
+
+
+def fp4_scale_values(scales: torch.Tensor, fmt: str) -> torch.Tensor:
+    """quant.py:1319-1324: fp32 values of FP4 block scales."""
+    if scales.dtype == torch.uint8:
+        scales = scales.view(FP4_FORMATS[fmt][1])
+    return scales.float()
+
+
+def fp4_scale_check(x: torch.Tensor, scales: torch.Tensor, outer: torch.Tensor | float | None = None,
+                    fmt: str | None = None) -> dict[str, Any]:
+    """quant.py:1325-1416: how W4A4 activation block scales (unswizzled) fit the block maxima
+    of ``x`` with the given outer scale: ``format``, ``blocks``, ``saturated``, ``share``,
+    ``worst_ratio``, ``underflow``, ``nonfinite``, ``not_representable``, ``coarser`` (one
+    GPU pass)."""
+    k = x.shape[-1]
+    x2 = _rows(_input(x))
+    rows = x2.shape[0]
+    fmt = fmt or fp4_format_of(k, scales)
+    block = FP4_FORMATS[fmt][0]
+    nb = k // block if k % block == 0 else -1
+    if nb < 0 or tuple(scales.shape) != (rows, nb):
+        raise ValueError(
+            f"expected {fmt} scales [{rows}, {max(nb, 0)}] (rows of x, K / {block}, unswizzled) "
+            f"for x {tuple(x.shape)}, got {tuple(scales.shape)}"
+        )
+    nat.require_cuda(x2)
+    s = fp4_scale_values(scales, fmt).to(x2.device).contiguous()
+    if outer is None:
+        o, per_row = None, 0
+    else:
+        o = torch.as_tensor(outer).detach().float().to(x2.device).reshape(-1).contiguous()
+        if o.numel() == 1:
+            per_row = 0
+        elif o.numel() == rows:
+            per_row = 1
+        else:
+            raise ValueError(f"expected an outer scale per row ([{rows}]) or one, got {o.numel()}")
+    out = torch.empty(ctypes.sizeof(nat.KabScaleCheck), dtype=torch.uint8, device=x2.device)
+    nat.call("kab_fp4_scale_check", x2.data_ptr(), nat.dtype_code(x2), rows, k, x2.stride(0) if rows else k,
+             nat.KAB_NVFP4 if fmt == "nvfp4" else nat.KAB_MXFP4, s.data_ptr(), nat.ptr(o), per_row,
+             out.data_ptr(), _stream(x2))
+    res = _check_result(out)
+    blocks = rows * nb
+    return {
+        "format": fmt,
+        "blocks": blocks,
+        "saturated": int(res.saturated),
+        "share": _sig(res.saturated / blocks) if blocks else 0.0,
+        "worst_ratio": _sig(_worst(res)) if blocks else 0.0,
+        "underflow": int(res.underflow),
+        "nonfinite": int(res.nonfinite),
+        "not_representable": int(res.not_representable),
+        "coarser": int(res.coarser),
+    }
+
+
+def fp4_scale_problem(x: torch.Tensor, scales: torch.Tensor, outer: torch.Tensor | float | None = None,
+                      fmt: str | None = None) -> str | None:
+    """quant.py:1419-1457: why ``(scales, outer)`` are not a valid W4A4 activation
+    quantisation of ``x``; None when they are."""
+    found = fp4_scale_check(x, scales, outer, fmt)
+    blocks, fmt = found["blocks"], found["format"]
+    if found["nonfinite"]:
+        return (
+            f"{found['nonfinite']} of {blocks} {fmt} blocks have a scale or an outer scale that "
+            "is not finite, or an outer scale <= 0"
+        )
+    if found["saturated"] and fmt == "nvfp4":
+        return (
+            f"{found['saturated']} of {blocks} NVFP4 blocks ({found['share']:.1%}) saturate "
+            f"beyond the rounding of their e4m3 scale: block maximum up to "
+            f"{found['worst_ratio']:.4g} x step (scale x outer), above {NVFP4_ROUNDING_RATIO:g} "
+            "(6 x (1 + e4m3's half step)); round the block scale bmax / (outer x 6) to "
+            "nearest (or up), never down, and keep the outer scale at amax / (6 x 448) per "
+            "row or per call so that no block scale clamps at 448"
+        )
+    if found["saturated"]:
+        return (
+            f"{found['saturated']} of {blocks} MXFP4 blocks ({found['share']:.1%}) saturate: "
+            f"block maximum up to {found['worst_ratio']:.4g} x scale, above e2m1's 6 (their "
+            "largest elements are clamped). Use the scale 2^ceil(log2(amax / 6)); the OCP rule "
+            "2^(floor(log2 amax) - 2) saturates maxima in (6, 8) x scale"
+        )
+    if found["underflow"]:
+        return (
+            f"{found['underflow']} of {blocks} NVFP4 blocks with a non-zero maximum got block "
+            "scale 0 where e4m3 rounding to nearest gives a non-zero (subnormal, 2^-9 steps) "
+            "scale: all their codes are 0 (subnormal scales flushed to zero?)"
+        )
+    if found["not_representable"]:
+        what = "e4m3 values" if fmt == "nvfp4" else "powers of two (e8m0 holds an exponent only)"
+        return f"{found['not_representable']} of {blocks} {fmt} block scales are not {what}"
+    return None
+
+
+def fp4_stress_input(shape, fmt: str = "nvfp4", *, dtype: torch.dtype = torch.bfloat16, device="cpu",
+                     seed: int = 0) -> torch.Tensor:
+    """quant.py:1467-1508: activations on which saturating W4A4 scale rules show (NVFP4: the
+    row maximum 64 in each row's first block, the other blocks' maxima 64 x m / 448 for m of
+    ``NVFP4_STRESS_RATIOS``; MXFP4: :func:`mxfp8_stress_input`)."""
+    if fmt == "mxfp4":
+        return mxfp8_stress_input(shape, dtype=dtype, device=device, seed=seed)
+    if fmt != "nvfp4":
+        raise ValueError(f"unknown FP4 format {fmt!r} (one of {', '.join(FP4_FORMATS)})")
+    block = FP4_FORMATS[fmt][0]
+    k = int(shape[-1])
+    if k % block:
+        raise ValueError(f"the last dimension {k} is not a multiple of the NVFP4 block (16)")
+    rows, nb = math.prod(int(n) for n in shape[:-1]), k // block
+    v = _stress_blocks(rows, nb, block, seed)
+    targets = torch.tensor(NVFP4_STRESS_RATIOS)
+    index = torch.arange(rows * nb).reshape(rows, nb) % len(NVFP4_STRESS_RATIOS)
+    bmax = 64.0 * targets[index] / 448.0
+    bmax[:, 0] = 64.0
+    return (v * bmax[..., None]).reshape(*shape).to(dtype=dtype, device=device)
