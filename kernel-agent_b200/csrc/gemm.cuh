@@ -32,6 +32,7 @@ struct GemmArgs {
   const uint8_t* sfa;           // swizzled block scales of A (KIND 2, 3)
   const uint8_t* sfb;           // ... of B
   int64_t sfa_ncb, sfb_ncb;     // 4-column blocks per 128-row block of each
+  int64_t sfb_chunks;           // 128-row blocks of B's scales (ceil(n / 128))
   const float* a_scale;         // per row of A: token scale (KIND 0, 1), outer (KIND 3)
   const float* b_scale;         // per row of B (KIND 0, 1), tensor scale(s) (KIND 3)
   int b_scale_per_col;          // KIND 3: b_scale[n] instead of b_scale[0]
@@ -62,33 +63,50 @@ struct GemmLayout {
   static constexpr bool kScaled = KIND >= 2;
   static constexpr int kABytes = kBM * BKB;
   static constexpr int kBBytes = BN * BKB;
-  // block scales per 128 rows per stage: NVFP4 one 512-byte chunk per MMA (K = 64), MXFP8 one
-  // chunk per 4 MMAs (K = 128: the stage)
-  static constexpr int kSfaBytes = KIND == 3 ? 512 * kKSteps : (KIND == 2 ? 512 : 0);
-  static constexpr int kSfbBytes = kSfaBytes * (BN / 128);
+  static constexpr int kGroups = BN / 32;  // 32-row groups of B per tile
+  // Block scales per 128 rows per stage (one 512-byte chunk of the swizzled layout per 64
+  // elements of K for NVFP4, per 128 for MXFP8) and the 128-row chunks a B tile can span
+  // (BN need not be a multiple of 128).
+  static constexpr int kSfChunkBytes = KIND == 3 ? 512 * kKSteps : 512;
+  static constexpr int kSfaBytes = kScaled ? kSfChunkBytes : 0;
+  // groups start at word 0 or 2 of a chunk (BN a multiple of 64), so a tile spans
+  // ceil((2 + kGroups) / 4) chunks at most (kGroups / 4 when BN is a multiple of 128)
+  static constexpr int kSfbChunks = !kScaled ? 0 : (kGroups % 4 == 0 ? kGroups / 4 : (kGroups + 2 + 3) / 4);
+  static constexpr int kSfbBytes = kSfbChunks * kSfChunkBytes;
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
-  // TMEM columns of block scales per stage: each 512-byte chunk (32 rows of 16 bytes: row
-  // r % 32 holds rows {r, r + 32, r + 64, r + 96}) lands in 4 columns of every lane quarter,
-  // lane l holding chunk row l (the layout tcgen05.cp.32x128b.warpx4 makes); the
-  // scale-factor warps write it with tcgen05.st, each into its own quarter.
-  static constexpr int kSfaCols = KIND == 3 ? 4 * kKSteps : (KIND == 2 ? 4 : 0);
-  static constexpr int kSfbCols = kSfaCols * (BN / 128);
+  // TMEM columns of block scales per stage. Each 512-byte chunk (32 rows of 16 bytes: row
+  // r % 32 holds the scale words of rows {r, r + 32, r + 64, r + 96}) lands in 4 columns of
+  // every lane quarter, lane l holding chunk row l (the layout tcgen05.cp.32x128b.warpx4
+  // makes); the scale-factor warps 10-13 write it with tcgen05.st, each into its own quarter.
+  // A: 4 columns per scale set; B: one per 32 rows. NVFP4 has one set per MMA (K = 64),
+  // MXFP8 one per stage (the MMA picks its byte by sf_id).
+  static constexpr int kSfSets = KIND == 3 ? kKSteps : 1;
+  static constexpr int kSfaCols = kScaled ? 4 * kSfSets : 0;
+  static constexpr int kSfbCols = kScaled ? kGroups * kSfSets : 0;
   static constexpr int kSfColsPerStage = kSfaCols + kSfbCols;
   static constexpr int kEpiWarps = 8;  // two per TMEM lane quarter
+  // warps: 0 TMA, 1 MMA, 2-9 epilogue; block-scaled kinds add warps 10-13 for the scale factors
   static constexpr int kThreads = 32 * (2 + kEpiWarps + (kScaled ? 4 : 0));
-  static constexpr int kAccBufs = kScaled ? 1 : 2;
+  // stages whose scale factors the warp writes before one wait for the stores to land
+  static constexpr int kSfBatch = 1;
+  static constexpr int kAccBufs = 2;  // the epilogue drains one accumulator while the MMAs fill the other
   static constexpr int kSfCol = kAccBufs * BN;
+  // the scale-factor ring in the columns the accumulators leave
+  static constexpr int kSfSlotsFit = kScaled ? (512 - kSfCol) / kSfColsPerStage : 0;
+  static constexpr int kSfSlots = kSfSlotsFit > 8 ? 8 : kSfSlotsFit;
   // epilogue staging: 8 warps x 2 buffers x [32 rows, 32 columns]
   static constexpr int kStageOutBytes = 32 * 32 * out_bytes(OUT);
   static constexpr int kStagingBytes = kEpiWarps * 2 * kStageOutBytes;
   static constexpr int kSmemLimit = 232448;
-  static constexpr int kFixed = 1024 + kStagingBytes + 320;
+  static constexpr int kFixed = 1024 + kStagingBytes + 384;
   static constexpr int kStagesFit = (kSmemLimit - kFixed) / kStageBytes;
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
-  static constexpr int kBarriers = 3 * kStages + 2 * kAccBufs + 1;
+  static constexpr int kBarriers = 2 * kStages + 2 * kSfSlots + 2 * kAccBufs + 1;
   static constexpr int kSmem = 1024 + kStages * kStageBytes + kStagingBytes + kBarriers * 8 + 16;
+  static_assert(BN % 64 == 0 && BN <= 256, "BN must be a multiple of 64, at most 256");
   static_assert(kStages >= 2, "shared memory does not fit two stages");
-  static_assert(kSfCol + kStages * kSfColsPerStage <= 512, "TMEM overflow");
+  static_assert(!kScaled || kSfSlots >= 2 * kSfBatch, "TMEM does not fit two batches of scale-factor slots");
+  static_assert(kSfCol + kSfSlots * kSfColsPerStage <= 512, "TMEM overflow");
   static_assert(kSmem <= kSmemLimit, "shared memory overflow");
 };
 
@@ -208,10 +226,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
   uint8_t* sSFB = sSFA + STAGES * L::kSfaBytes;
   uint8_t* sOut = sSFB + STAGES * L::kSfbBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + L::kStagingBytes);
+  constexpr int SLOTS = L::kSfSlots;
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
-  uint64_t* sf_full = bars + 2 * STAGES;  // scale factors of stage s are in TMEM (4 arrivals)
-  uint64_t* acc_full = bars + 3 * STAGES;
+  uint64_t* sf_full = bars + 2 * STAGES;   // a stage's scale factors are in TMEM slot (4 arrivals)
+  uint64_t* sf_empty = sf_full + SLOTS;    // the MMAs that read the slot have completed
+  uint64_t* acc_full = sf_empty + SLOTS;
   uint64_t* acc_empty = acc_full + L::kAccBufs;
   uint64_t* drain = acc_empty + L::kAccBufs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -221,7 +241,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
     for (int s = 0; s < STAGES; ++s) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < SLOTS; ++s) {
       tc::mbar_init(&sf_full[s], 4);
+      tc::mbar_init(&sf_empty[s], 1);
     }
     for (int b = 0; b < L::kAccBufs; ++b) { tc::mbar_init(&acc_full[b], 1); tc::mbar_init(&acc_empty[b], L::kEpiWarps); }
     tc::mbar_init(drain, 1);
@@ -251,23 +274,22 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
         int mt, nt;
         tile_coords(t, g.m_tiles, g.n_tiles, mt, nt);
+        // the 128-row scale chunks B's rows [nt * BN, nt * BN + BN) span (those that exist)
+        const int64_t c0 = static_cast<int64_t>(nt) * L::kGroups / 4;
+        int64_t c1 = (static_cast<int64_t>(nt) * L::kGroups + L::kGroups - 1) / 4;
+        if (c1 > g.sfb_chunks - 1) c1 = g.sfb_chunks - 1;
+        const uint32_t tx = kTx - static_cast<uint32_t>(L::kSfbChunks - (c1 - c0 + 1)) * L::kSfChunkBytes;
         for (int kb = 0; kb < g.k_stages; ++kb) {
           if (!tc::mbar_wait(&empty[s], ph ^ 1u)) { ok = false; break; }
-          tc::mbar_arrive_expect_tx(&full[s], kTx);
+          tc::mbar_arrive_expect_tx(&full[s], L::kScaled ? tx : kTx);
           tc::tma_load_2d(&tma_a, &full[s], sA + s * L::kABytes, kb * BKB, mt * 128);
           tc::tma_load_2d(&tma_b, &full[s], sB + s * L::kBBytes, kb * BKB, nt * BN);
-          if constexpr (KIND == 3) {  // KS chunks of 512 bytes per 128 rows: contiguous
-            tc::bulk_load(sSFA + s * L::kSfaBytes, g.sfa + (mt * g.sfa_ncb + KS * kb) * 512, L::kSfaBytes, &full[s]);
-#pragma unroll
-            for (int h = 0; h < BN / 128; ++h)
-              tc::bulk_load(sSFB + s * L::kSfbBytes + h * L::kSfaBytes,
-                            g.sfb + ((nt * (BN / 128) + h) * g.sfb_ncb + KS * kb) * 512, L::kSfaBytes, &full[s]);
-          } else if constexpr (KIND == 2) {
-            tc::bulk_load(sSFA + s * L::kSfaBytes, g.sfa + (mt * g.sfa_ncb + kb) * 512, 512, &full[s]);
-#pragma unroll
-            for (int h = 0; h < BN / 128; ++h)
-              tc::bulk_load(sSFB + s * L::kSfbBytes + h * 512,
-                            g.sfb + ((nt * (BN / 128) + h) * g.sfb_ncb + kb) * 512, 512, &full[s]);
+          if constexpr (L::kScaled) {  // one chunk per 128 rows per stage (KS chunks for NVFP4: contiguous)
+            const int64_t kc = KIND == 3 ? static_cast<int64_t>(KS) * kb : kb;
+            tc::bulk_load(sSFA + s * L::kSfaBytes, g.sfa + (mt * g.sfa_ncb + kc) * 512, L::kSfChunkBytes, &full[s]);
+            for (int64_t c = c0; c <= c1; ++c)
+              tc::bulk_load(sSFB + s * L::kSfbBytes + (c - c0) * L::kSfChunkBytes, g.sfb + (c * g.sfb_ncb + kc) * 512,
+                            L::kSfChunkBytes, &full[s]);
           }
           issued[s] = true;
           issued_ph[s] = ph;
@@ -282,8 +304,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---------------------------------------------------- MMA issuer
-      int s = 0, ab = 0;
-      uint32_t ph = 0, aph = 0;
+      int s = 0, ab = 0, slot = 0;
+      uint32_t ph = 0, aph = 0, sph = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
         if (!tc::mbar_wait(&acc_empty[ab], aph ^ 1u)) { ok = false; break; }
@@ -292,14 +314,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         for (int kb = 0; kb < g.k_stages; ++kb) {
           if (!tc::mbar_wait(&full[s], ph)) { ok = false; break; }
           if constexpr (L::kScaled) {
-            if (!tc::mbar_wait(&sf_full[s], ph)) { ok = false; break; }
+            if (!tc::mbar_wait(&sf_full[slot], sph)) { ok = false; break; }
           }
           tc::fence_after_sync();
           const uint32_t abase = tc::smem_u32(sA + s * L::kABytes);
           const uint32_t bbase = tc::smem_u32(sB + s * L::kBBytes);
           const uint64_t adesc = BKB == 128 ? tc::desc_sw128(abase) : tc::desc_sw64(abase);
           const uint64_t bdesc = BKB == 128 ? tc::desc_sw128(bbase) : tc::desc_sw64(bbase);
-          const uint32_t sf = tmem + L::kSfCol + s * L::kSfColsPerStage;
+          const uint32_t sf = tmem + L::kSfCol + slot * L::kSfColsPerStage;
 #pragma unroll
           for (int j = 0; j < KS; ++j) {
             const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
@@ -311,12 +333,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
               tc::mma_f8(d, a, b, tc::idesc_f8(128, BN), acc);
             } else if constexpr (KIND == 2) {  // one scale byte per row per MMA (sf_id = j)
               tc::mma_mxf8(d, a, b, tc::idesc_mxf8(128, BN, j), sf, sf + L::kSfaCols, acc);
-            } else {  // this MMA's chunk: 4 columns for A, 4 per 128 rows of B
-              tc::mma_nvf4(d, a, b, tc::idesc_nvf4(128, BN), sf + 4 * j, sf + L::kSfaCols + 4 * (BN / 128) * j, acc);
+            } else {  // this MMA's scale set: 4 columns for A, one per 32 rows of B
+              tc::mma_nvf4(d, a, b, tc::idesc_nvf4(128, BN), sf + 4 * j, sf + L::kSfaCols + L::kGroups * j, acc);
             }
           }
           tc::commit(&empty[s]);
           if (++s == STAGES) { s = 0; ph ^= 1u; }
+          if constexpr (L::kScaled) {
+            tc::commit(&sf_empty[slot]);
+            if (++slot == SLOTS) { slot = 0; sph ^= 1u; }
+          }
         }
         if (!ok) break;
         tc::commit(&acc_full[ab]);
@@ -326,42 +352,85 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       if (!tc::mbar_wait(drain, 0)) ok = false;
       if (!ok) atomicOr(&g_gemm_status, kDevTimeout);
     }
-  } else if (warp >= 2 + L::kEpiWarps) {  // ---------------------------------- scale-factor warps
+  } else if (warp >= 2 + L::kEpiWarps) {  // ----------------------------------- scale-factor warps
     if constexpr (L::kScaled) {
-      const int q = warp & 3;
-      const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
-      int s = 0;
-      uint32_t ph = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
-        for (int kb = 0; kb < g.k_stages; ++kb) {
-          if (!tc::mbar_wait(&full[s], ph)) { ok = false; break; }
-          const uint32_t col = tmem + lane_base + L::kSfCol + s * L::kSfColsPerStage;
-          const uint8_t* ca = sSFA + s * L::kSfaBytes + lane * 16;
-          const uint8_t* cb = sSFB + s * L::kSfbBytes + lane * 16;
-          if constexpr (KIND == 3) {  // MMA j: A chunk j at +4 j, B chunks (j, h) at +4 (BN/128) j + 4 h
+      {
+        constexpr int NB = L::kSfBatch;
+        const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+        int s = 0, slot = 0, pending = 0;
+        uint32_t ph = 0, sph = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+          int mt, nt;
+          tile_coords(t, g.m_tiles, g.n_tiles, mt, nt);
+          const int64_t g0 = static_cast<int64_t>(nt) * L::kGroups;
+          const bool last_tile = t + static_cast<int>(gridDim.x) >= total;
+          // B's 32-row groups g0 .. g0 + kGroups - 1 start at word p = g0 % 4 (0, or 2 when
+          // kGroups % 4 == 2) of chunk g0 / 4 and run over the following chunks; a chunk past the
+          // end of B reads as zeros
+          const int p = static_cast<int>(g0 & 3);
+          bool live[L::kSfbChunks];
 #pragma unroll
-            for (int j = 0; j < KS; ++j) {
-              tc::tmem_st4(col + 4 * j, *reinterpret_cast<const uint4*>(ca + j * 512));
+          for (int c = 0; c < L::kSfbChunks; ++c) live[c] = g0 / 4 + c < g.sfb_chunks;
+          for (int kb = 0; kb < g.k_stages; ++kb) {
+            if (!tc::mbar_wait(&full[s], ph)) { ok = false; break; }
+            if (!tc::mbar_wait(&sf_empty[slot], sph ^ 1u)) { ok = false; break; }
+            tc::fence_after_sync();
+            const uint32_t col = tmem + lane_base + L::kSfCol + slot * L::kSfColsPerStage;
+            const uint8_t* ca = sSFA + s * L::kSfaBytes + lane * 16;
+            const uint8_t* cb = sSFB + s * L::kSfbBytes + lane * 16;
+            // every load first (chunk row `lane` of A's chunk and of B's chunks, per scale set)
+            uint4 av[L::kSfSets], bv[L::kSfSets][L::kSfbChunks];
 #pragma unroll
-              for (int h = 0; h < BN / 128; ++h)
-                tc::tmem_st4(col + L::kSfaCols + 4 * (BN / 128) * j + 4 * h,
-                             *reinterpret_cast<const uint4*>(cb + h * L::kSfaBytes + j * 512));
+            for (int j = 0; j < L::kSfSets; ++j) {
+              av[j] = *reinterpret_cast<const uint4*>(ca + j * 512);
+#pragma unroll
+              for (int c = 0; c < L::kSfbChunks; ++c)
+                bv[j][c] = live[c] ? *reinterpret_cast<const uint4*>(cb + c * L::kSfChunkBytes + j * 512)
+                                   : make_uint4(0u, 0u, 0u, 0u);
             }
-          } else {  // one chunk per 128 rows covers the stage's 4 MMAs
-            tc::tmem_st4(col, *reinterpret_cast<const uint4*>(ca));
+            // the stage's columns in order (A's sets, then B's sets) in a few wide stores
+            uint32_t sw[L::kSfColsPerStage];
 #pragma unroll
-            for (int h = 0; h < BN / 128; ++h)
-              tc::tmem_st4(col + L::kSfaCols + 4 * h, *reinterpret_cast<const uint4*>(cb + h * 512));
+            for (int j = 0; j < L::kSfSets; ++j) {
+              sw[4 * j] = av[j].x;  // A: the words of rows lane, lane + 32, + 64, + 96
+              sw[4 * j + 1] = av[j].y;
+              sw[4 * j + 2] = av[j].z;
+              sw[4 * j + 3] = av[j].w;
+            }
+#pragma unroll
+            for (int j = 0; j < L::kSfSets; ++j) {
+              uint32_t w[4 * L::kSfbChunks];
+#pragma unroll
+              for (int c = 0; c < L::kSfbChunks; ++c) {
+                w[4 * c] = bv[j][c].x;
+                w[4 * c + 1] = bv[j][c].y;
+                w[4 * c + 2] = bv[j][c].z;
+                w[4 * c + 3] = bv[j][c].w;
+              }
+#pragma unroll
+              for (int gi = 0; gi < L::kGroups; ++gi) {
+                uint32_t v = w[gi];
+                if constexpr (L::kGroups % 4 == 2) v = p == 0 ? w[gi] : w[gi + 2];
+                sw[L::kSfaCols + L::kGroups * j + gi] = v;
+              }
+            }
+            tc::tmem_st_n<L::kSfColsPerStage>(col, sw);
+            if (++s == STAGES) { s = 0; ph ^= 1u; }
+            if (++slot == SLOTS) { slot = 0; sph ^= 1u; }
+            // one wait for the stores of NB stages (or of the last ones), then their signals
+            if (++pending == NB || (last_tile && kb == g.k_stages - 1)) {
+              tc::tmem_st_wait();
+              tc::fence_before_sync();
+              __syncwarp();
+              if (lane == 0)
+                for (int b = pending; b >= 1; --b) tc::mbar_arrive(&sf_full[(slot - b + SLOTS) % SLOTS]);
+              pending = 0;
+            }
           }
-          tc::tmem_st_wait();
-          tc::fence_before_sync();
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(&sf_full[s]);
-          if (++s == STAGES) { s = 0; ph ^= 1u; }
         }
+        if (!ok && lane == 0) atomicOr(&g_gemm_status, kDevTimeout);
       }
-      if (!ok && lane == 0) atomicOr(&g_gemm_status, kDevTimeout);
     }
   } else {  // ------------------------------------------------------------- epilogue warps
     // warps 2..9: lane quarter = warp % 4 (the quarter a warp may read), column half = (warp - 2) / 4

@@ -97,7 +97,7 @@ int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
 template <int KIND, int BN>
 int launch_out(int out, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const GemmArgs& g,
                cudaStream_t s) {
-  constexpr int BKB = KIND == 3 ? 64 : 128;
+  constexpr int BKB = 128;
   if constexpr (KIND == 0) {
     if (out == kOutI32) return launch_one<KIND, BN, BKB, kOutI32>(ma, mb, mo, g, s);
   }
@@ -114,7 +114,7 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
   if (m == 0 || n == 0) return KAB_OK;
   KAB_REQUIRE(a != nullptr && b != nullptr, "operand is null");
   KAB_REQUIRE(aligned(a, 16) && aligned(b, 16), "operands must be 16-byte aligned");
-  const int bkb = KIND == 3 ? 64 : 128;
+  const int bkb = 128;
   KAB_REQUIRE(k_bytes > 0 && k_bytes % bkb == 0,
               "K must be a positive multiple of %d bytes per row (128 int8 / e4m3, 256 e2m1); got %lld bytes",
               bkb, (long long)k_bytes);
@@ -125,7 +125,16 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
   KAB_REQUIRE(g.ldo >= n && g.ldo % 8 == 0, "ldo %lld must be >= n and a multiple of 8", (long long)g.ldo);
   KAB_REQUIRE(aligned(out, 16), "output must be 16-byte aligned");
   KAB_REQUIRE(m <= (int64_t(1) << 30) && n <= (int64_t(1) << 30), "shape too large");
-  const int bn = (n % 256 == 0 || !GemmTraits<KIND>::kScaled) && n >= 256 ? 256 : 128;
+  // tile width: 256 (two 256-column accumulators) for int8 / fp8; the block-scaled kinds keep
+  // room for their scale-factor ring next to two accumulators: 192 unless that pads N by more
+  // than 1/16, else 128
+  int bn;
+  if (!GemmTraits<KIND>::kScaled) {
+    bn = n >= 256 ? 256 : 128;
+  } else {
+    const int64_t pad192 = (n + 191) / 192 * 192 - n;
+    bn = (n >= 192 && pad192 * 16 <= n) ? 192 : 128;
+  }
   g.m = m;
   g.n = n;
   g.k_stages = static_cast<int>(k_bytes / bkb);
@@ -135,7 +144,12 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
   if (int e = make_map(&ma, a, m, k_bytes, k_bytes, 128, bkb, "A")) return e;
   if (int e = make_map(&mb, b, n, k_bytes, k_bytes, bn, bkb, "B")) return e;
   if (int e = make_out_map(&mo, out, out_dtype, m, n, g.ldo)) return e;
-  if (bn == 256) return launch_out<KIND, 256>(out_dtype, ma, mb, mo, g, s);
+  if constexpr (GemmTraits<KIND>::kScaled) {
+    g.sfb_chunks = (n + 127) / 128;
+    if (bn == 192) return launch_out<KIND, 192>(out_dtype, ma, mb, mo, g, s);
+  } else {
+    if (bn == 256) return launch_out<KIND, 256>(out_dtype, ma, mb, mo, g, s);
+  }
   return launch_out<KIND, 128>(out_dtype, ma, mb, mo, g, s);
 }
 

@@ -149,6 +149,34 @@ __device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint4& v) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};"
                ::"r"(taddr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
 }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+// N consecutive columns from v[0 .. N) in as few stores as the 16 / 8 / 4 / 2 / 1 shapes allow.
+template <int N>
+__device__ __forceinline__ void tmem_st_n(uint32_t taddr, const uint32_t* v) {
+  if constexpr (N >= 16) {
+    tmem_st16(taddr, v);
+    tmem_st_n<N - 16>(taddr + 16, v + 16);
+  } else if constexpr (N >= 8) {
+    const uint32_t w[8] = {v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7]};
+    tmem_st8(taddr, w);
+    tmem_st_n<N - 8>(taddr + 8, v + 8);
+  } else if constexpr (N >= 4) {
+    tmem_st4(taddr, make_uint4(v[0], v[1], v[2], v[3]));
+    tmem_st_n<N - 4>(taddr + 4, v + 4);
+  } else if constexpr (N >= 2) {
+    tmem_st2(taddr, v[0], v[1]);
+    tmem_st_n<N - 2>(taddr + 2, v + 2);
+  } else if constexpr (N == 1) {
+    tmem_st1(taddr, v[0]);
+  }
+}
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ------------------------------------------------------------------ descriptors

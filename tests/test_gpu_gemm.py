@@ -138,7 +138,7 @@ def test_fp8_w8a8_linear(kq, m, k, n):
     close_bf16(y, golden_like, "fp8 vs dequant-matmul")
 
 
-@pytest.mark.parametrize("m,k,n", [(44, 256, 128), (300, 1024, 512), (4096, 14336, 256)])
+@pytest.mark.parametrize("m,k,n", [(44, 256, 128), (300, 1024, 512), (4096, 14336, 256), (130, 512, 3200)])
 def test_mxfp8_linear(kq, m, k, n, golden):
     g = torch.Generator().manual_seed(m)
     x = torch.randn(m, k, generator=g).to(torch.bfloat16)
@@ -162,7 +162,8 @@ def test_mxfp8_linear(kq, m, k, n, golden):
     close_bf16_tol(yl, bf16_to_f32(gg["mxl_y"]), "mxfp8 golden")
 
 
-@pytest.mark.parametrize("m,k,n", [(48, 256, 128), (200, 1024, 384), (1024, 8192, 512)])
+@pytest.mark.parametrize("m,k,n", [(48, 256, 128), (200, 1024, 384), (1024, 8192, 512), (130, 512, 3200),
+                                   (256, 1024, 3264)])
 def test_fp4_w4a4_linear(kq, m, k, n, golden):
     g = torch.Generator().manual_seed(n)
     x = torch.randn(m, k, generator=g).to(torch.bfloat16)
