@@ -29,6 +29,7 @@ struct GemmArgs {
   int64_t m, n;
   int k_stages;                 // K bytes per row / 128
   int m_tiles, n_tiles;
+  int group_n;                  // tile order: see tile_coords
   const uint8_t* sfa;           // swizzled block scales of A (KIND 2, 3)
   const uint8_t* sfb;           // ... of B
   int64_t sfa_ncb, sfb_ncb;     // 4-column blocks per 128-row block of each
@@ -199,12 +200,23 @@ __device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const uint32_t
   }
 }
 
-// Tile t of the persistent schedule -> (m tile, n tile): groups of 8 m-tiles sweep n.
-__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mt, int& nt) {
+// Tile t of the persistent schedule -> (m tile, n tile). group_n == 0: groups of 8 m-tiles
+// sweep n (an A panel stays in L2 while B streams); group_n > 0: groups of group_n n-tiles
+// sweep m (for a B larger than L2: each B panel is read from HBM once while A, the smaller
+// operand, stays in L2).
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int group_n, int& mt, int& nt) {
+  if (group_n > 0) {
+    const int group_size = group_n * m_tiles;
+    const int first = (t / group_size) * group_n;
+    const int gn = min(n_tiles - first, group_n);
+    const int r = t % group_size;
+    nt = first + r % gn;
+    mt = r / gn;
+    return;
+  }
   constexpr int kGroup = 8;
   const int group_size = kGroup * n_tiles;
-  const int g = t / group_size;
-  const int first = g * kGroup;
+  const int first = (t / group_size) * kGroup;
   const int gm = min(m_tiles - first, kGroup);
   const int r = t % group_size;
   mt = first + r % gm;
@@ -273,7 +285,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       for (int i = 0; i < STAGES; ++i) issued[i] = false;
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
         int mt, nt;
-        tile_coords(t, g.m_tiles, g.n_tiles, mt, nt);
+        tile_coords(t, g.m_tiles, g.n_tiles, g.group_n, mt, nt);
         // the 128-row scale chunks B's rows [nt * BN, nt * BN + BN) span (those that exist)
         const int64_t c0 = static_cast<int64_t>(nt) * L::kGroups / 4;
         int64_t c1 = (static_cast<int64_t>(nt) * L::kGroups + L::kGroups - 1) / 4;
@@ -362,7 +374,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         bool ok = true;
         for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
           int mt, nt;
-          tile_coords(t, g.m_tiles, g.n_tiles, mt, nt);
+          tile_coords(t, g.m_tiles, g.n_tiles, g.group_n, mt, nt);
           const int64_t g0 = static_cast<int64_t>(nt) * L::kGroups;
           const bool last_tile = t + static_cast<int>(gridDim.x) >= total;
           // B's 32-row groups g0 .. g0 + kGroups - 1 start at word p = g0 % 4 (0, or 2 when
@@ -444,7 +456,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
     int chunk = 0;  // chunks this warp has staged (selects the staging buffer)
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int mt, nt;
-      tile_coords(t, g.m_tiles, g.n_tiles, mt, nt);
+      tile_coords(t, g.m_tiles, g.n_tiles, g.group_n, mt, nt);
       if (!tc::mbar_wait(&acc_full[ab], aph)) {
         if (lane == 0) atomicOr(&g_gemm_status, kDevTimeout);
         break;

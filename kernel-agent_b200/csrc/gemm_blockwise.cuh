@@ -105,7 +105,7 @@ gemm_blockwise_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
       for (int i = 0; i < STAGES; ++i) issued[i] = false;
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
         int mt, nt;
-        tile_coords(t, g.m_tiles, g.n_tiles, mt, nt);
+        tile_coords(t, g.m_tiles, g.n_tiles, 0, mt, nt);
         for (int kb = 0; kb < KB; ++kb) {
           if (!tc::mbar_wait(&empty[s], ph ^ 1u)) { ok = false; break; }
           tc::mbar_arrive_expect_tx(&full[s], L::kStageBytes);
@@ -161,7 +161,7 @@ gemm_blockwise_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
     bool ok = true;
     for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
       int mt, nt;
-      tile_coords(t, g.m_tiles, g.n_tiles, mt, nt);
+      tile_coords(t, g.m_tiles, g.n_tiles, 0, mt, nt);
       const int row0 = mt * 128 + 32 * quarter;
       const int64_t row = static_cast<int64_t>(row0) + lane;
       const bool live = row < g.m;

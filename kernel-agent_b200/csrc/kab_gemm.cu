@@ -140,6 +140,8 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
   g.k_stages = static_cast<int>(k_bytes / bkb);
   g.m_tiles = static_cast<int>((m + 127) / 128);
   g.n_tiles = static_cast<int>((n + bn - 1) / bn);
+  // B larger than A (a weight panel sweep): keep A in L2 and stream each B panel once
+  g.group_n = n > m && g.m_tiles > 8 ? 16 : 0;
   CUtensorMap ma, mb, mo;
   if (int e = make_map(&ma, a, m, k_bytes, k_bytes, 128, bkb, "A")) return e;
   if (int e = make_map(&mb, b, n, k_bytes, k_bytes, bn, bkb, "B")) return e;
