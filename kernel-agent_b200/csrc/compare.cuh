@@ -51,9 +51,43 @@ __device__ __forceinline__ void block_sum_partial(CmpPartial& p, CmpPartial* sm)
   __syncthreads();
 }
 
-template <int T>
-__device__ __forceinline__ void cmp_element(const KabCompareParams& P, float a, float b,
-                                            float alt, int64_t i, CmpPartial& p) {
+// One thread's running results: 32-bit counts (a thread sees far fewer than 2^31 elements),
+// float64 sums, NaN-keeping maxima, and for the fast path the operands (bd, bal) of its
+// largest diff / allowed, so that the one IEEE division happens at the end (rounding is
+// monotonic, so the largest rounded ratio is the rounding of the largest exact one).
+struct CmpThread {
+  int cnt[KAB_CMP_NCOUNT];
+  double sum[KAB_CMP_NSUM];
+  float mx[KAB_CMP_NMAX];
+  float bd, bal;
+};
+
+__device__ __forceinline__ void cmp_init(CmpThread& t) {
+#pragma unroll
+  for (int i = 0; i < KAB_CMP_NCOUNT; ++i) t.cnt[i] = 0;
+#pragma unroll
+  for (int i = 0; i < KAB_CMP_NSUM; ++i) t.sum[i] = 0.0;
+#pragma unroll
+  for (int i = 0; i < KAB_CMP_NMAX; ++i) t.mx[i] = 0.0f;
+  t.bd = 0.0f;
+  t.bal = 1.0f;
+}
+
+// (bd, bal) <- (d, al) when d / al > bd / bal exactly (finite d >= 0, al > 0): a float filter
+// that never drops a larger ratio (its products are within 2^-23 of exact), then the exact
+// comparison of the float64 products (exact for float operands).
+__device__ __forceinline__ void ratio_max(float d, float al, float& bd, float& bal) {
+  if (d * bal >= (bd * al) * 0.99999905f) {
+    if (static_cast<double>(d) * bal > static_cast<double>(bd) * al) {
+      bd = d;
+      bal = al;
+    }
+  }
+}
+
+// The general element step (any mode, any value), compare.py:684-739.
+__device__ __forceinline__ void cmp_element(const KabCompareParams& P, float a, float b, float alt, int64_t i,
+                                            CmpThread& p) {
   const bool an = a != a, bn = b != b;
   const bool ap = a == INFINITY, bp = b == INFINITY, am = a == -INFINITY, bm = b == -INFINITY;
   p.cnt[KAB_CMP_NAN_REF] += an; p.cnt[KAB_CMP_NAN_NEW] += bn; p.cnt[KAB_CMP_NAN_DIFF] += an != bn;
@@ -90,38 +124,109 @@ __device__ __forceinline__ void cmp_element(const KabCompareParams& P, float a, 
   }
 }
 
-template <int T>
+// The common case of 8 elements (no rerounded / alternative bound / widening / element
+// ratio; every a and b finite): the same counts and maxima with float partial sums over the
+// 8 products added to the float64 totals, and the ratio kept as its operands.
+__device__ __forceinline__ void cmp_chunk_fast(const KabCompareParams& P, const float (&a)[8], const float (&b)[8],
+                                               CmpThread& t) {
+  float s_aa = 0.0f, s_bb = 0.0f, s_ab = 0.0f, s_dd = 0.0f, s_d = 0.0f;
+  float mxd = t.mx[KAB_CMP_MAX_D];
+  int mism = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float d = fabsf(__fsub_rn(a[j], b[j]));
+    const float allowed = __fadd_rn(P.atol, __fmul_rn(P.rtol, fabsf(a[j])));
+    mism += d > allowed;
+    ratio_max(d, fmaxf(allowed, 1e-30f), t.bd, t.bal);
+    mxd = fmaxf(mxd, d);
+    s_aa = fmaf(a[j], a[j], s_aa);
+    s_bb = fmaf(b[j], b[j], s_bb);
+    s_ab = fmaf(a[j], b[j], s_ab);
+    s_dd = fmaf(d, d, s_dd);
+    s_d += d;
+  }
+  t.mx[KAB_CMP_MAX_D] = mxd;
+  t.cnt[KAB_CMP_FINITE] += 8;
+  t.cnt[KAB_CMP_MISMATCH] += mism;
+  t.sum[KAB_CMP_SUM_AA] += s_aa;
+  t.sum[KAB_CMP_SUM_BB] += s_bb;
+  t.sum[KAB_CMP_SUM_AB] += s_ab;
+  t.sum[KAB_CMP_SUM_DD] += s_dd;
+  t.sum[KAB_CMP_SUM_D] += s_d;
+}
+
+__device__ __forceinline__ bool all_finite8(const float (&a)[8], const float (&b)[8]) {
+  bool ok = true;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ok = ok && fabsf(a[j]) < INFINITY && fabsf(b[j]) < INFINITY;
+  return ok;
+}
+
+// SIMPLE: no rerounded tensor, alternative bound, widening or element ratio (the first pass
+// of every tier): chunks whose values are all finite take the fast step.
+template <int T, bool SIMPLE>
 __global__ void __launch_bounds__(256)
 compare_kernel(KabCompareParams P, CmpPartial* __restrict__ partials) {
   __shared__ CmpPartial sm[8];
-  CmpPartial p;
-#pragma unroll
-  for (int i = 0; i < KAB_CMP_NCOUNT; ++i) p.cnt[i] = 0;
-#pragma unroll
-  for (int i = 0; i < KAB_CMP_NSUM; ++i) p.sum[i] = 0.0;
-#pragma unroll
-  for (int i = 0; i < KAB_CMP_NMAX; ++i) p.mx[i] = 0.0f;
+  CmpThread t;
+  cmp_init(t);
   const int64_t n = P.n;
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   if (P.vector) {  // 8 elements per thread per step (16-byte loads of 2-byte types)
     const int64_t nv = n >> 3;
-    for (int64_t c = tid; c < nv; c += stride) {
+    int64_t c = tid;
+    if constexpr (SIMPLE && T != kF32) {  // four chunks of raw 16-byte loads in flight per thread
+      constexpr int U = 4;
+      for (; c + (U - 1) * stride < nv; c += U * stride) {
+        uint4 ra[U], rb[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          ra[u] = __ldg(reinterpret_cast<const uint4*>(P.ref) + (c + u * stride));
+          rb[u] = __ldg(reinterpret_cast<const uint4*>(P.new_) + (c + u * stride));
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          float a[8], b[8];
+          unpack8<T>(ra[u], a);
+          unpack8<T>(rb[u], b);
+          if (all_finite8(a, b)) {
+            cmp_chunk_fast(P, a, b, t);
+          } else {
+            for (int j = 0; j < 8; ++j) cmp_element(P, a[j], b[j], 0.0f, (c + u * stride) * 8 + j, t);
+          }
+        }
+      }
+    }
+    for (; c < nv; c += stride) {
       float a[8], b[8], r[8];
       load8<T>(P.ref, c * 8, a);
       load8<T>(P.new_, c * 8, b);
-      if (P.has_rerounded) load8<T>(P.rerounded, c * 8, r);
+      if (!SIMPLE && P.has_rerounded) load8<T>(P.rerounded, c * 8, r);
+      if (SIMPLE && all_finite8(a, b)) {
+        cmp_chunk_fast(P, a, b, t);
+      } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) cmp_element<T>(P, a[j], b[j], P.has_rerounded ? r[j] : 0.0f, c * 8 + j, p);
+        for (int j = 0; j < 8; ++j)
+          cmp_element(P, a[j], b[j], (!SIMPLE && P.has_rerounded) ? r[j] : 0.0f, c * 8 + j, t);
+      }
     }
     for (int64_t i = nv * 8 + tid; i < n; i += stride)
-      cmp_element<T>(P, load_elem<T>(P.ref, i), load_elem<T>(P.new_, i),
-                     P.has_rerounded ? load_elem<T>(P.rerounded, i) : 0.0f, i, p);
+      cmp_element(P, load_elem<T>(P.ref, i), load_elem<T>(P.new_, i),
+                  P.has_rerounded ? load_elem<T>(P.rerounded, i) : 0.0f, i, t);
   } else {
     for (int64_t i = tid; i < n; i += stride)
-      cmp_element<T>(P, load_elem<T>(P.ref, i), load_elem<T>(P.new_, i),
-                     P.has_rerounded ? load_elem<T>(P.rerounded, i) : 0.0f, i, p);
+      cmp_element(P, load_elem<T>(P.ref, i), load_elem<T>(P.new_, i),
+                  P.has_rerounded ? load_elem<T>(P.rerounded, i) : 0.0f, i, t);
   }
+  CmpPartial p;
+#pragma unroll
+  for (int i = 0; i < KAB_CMP_NCOUNT; ++i) p.cnt[i] = t.cnt[i];
+#pragma unroll
+  for (int i = 0; i < KAB_CMP_NSUM; ++i) p.sum[i] = t.sum[i];
+#pragma unroll
+  for (int i = 0; i < KAB_CMP_NMAX; ++i) p.mx[i] = t.mx[i];
+  p.mx[KAB_CMP_MAX_RATIO] = amax_merge(p.mx[KAB_CMP_MAX_RATIO], __fdiv_rn(t.bd, t.bal));
   block_sum_partial(p, sm);
   if (threadIdx.x == 0) partials[blockIdx.x] = sm[0];
 }

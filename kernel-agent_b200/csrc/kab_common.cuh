@@ -72,6 +72,23 @@ __device__ __forceinline__ void load8(const void* base, int64_t i, float (&v)[8]
   }
 }
 
+// The 8 floats of 16 bytes of 2-byte elements (bf16 or fp16), element 0 in the low half.
+template <int T>
+__device__ __forceinline__ void unpack8(const uint4& raw, float (&v)[8]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if constexpr (T == kBF16) {
+      v[2 * j] = __uint_as_float(w[j] << 16);
+      v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    } else {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  }
+}
+
 // fp32 -> bf16 bits, round to nearest even; NaN -> 0x7FC0 (torch's conversion).
 __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
   uint32_t u = __float_as_uint(f);

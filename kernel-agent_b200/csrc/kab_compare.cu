@@ -76,9 +76,14 @@ int kab_compare(const KabCompareParams* params, void* scratch, size_t scratch_by
               static_cast<size_t>(grid) * sizeof(CmpPartial));
   const cudaStream_t s = as_stream(stream);
   CmpPartial* partials = static_cast<CmpPartial*>(scratch);
-  if (P.dtype == KAB_BF16) compare_kernel<kBF16><<<grid, 256, 0, s>>>(P, partials);
-  else if (P.dtype == KAB_F16) compare_kernel<kF16><<<grid, 256, 0, s>>>(P, partials);
-  else compare_kernel<kF32><<<grid, 256, 0, s>>>(P, partials);
+  const bool simple = !P.has_rerounded && !P.alt_bound && P.widen_mode == 0 && P.element_mode == 0;
+#define KAB_CMP(TT)                                                        \
+  if (simple) compare_kernel<TT, true><<<grid, 256, 0, s>>>(P, partials);  \
+  else compare_kernel<TT, false><<<grid, 256, 0, s>>>(P, partials)
+  if (P.dtype == KAB_BF16) { KAB_CMP(kBF16); }
+  else if (P.dtype == KAB_F16) { KAB_CMP(kF16); }
+  else { KAB_CMP(kF32); }
+#undef KAB_CMP
   if (int e = check_launch("kab_compare")) return e;
   compare_finalize_kernel<<<1, 256, 0, s>>>(partials, grid, result);
   return check_launch("kab_compare finalize");
