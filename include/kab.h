@@ -148,6 +148,15 @@ int kab_gemm_f8(const uint8_t* a, const uint8_t* b, int64_t m, int64_t n, int64_
                 const float* a_scale, const float* b_scale, const void* bias, int bias_dtype,
                 void* out, int out_dtype, int64_t ldo, void* stream);
 
+/* MXFP4: packed e2m1 A [m, k / 2], B [n, k / 2] with e8m0 scales per 32 along K (swizzled),
+ * applied by the tensor core (kind::mxf4nvf4.block_scale.scale_vec::2X); out = acc * ts
+ * (+ bias), ts = b_scale[0], b_scale[n] (b_scale_per_col) or 1 (null) (quant.py:1201-1257
+ * fp4_w4a4_linear, fmt "mxfp4": the activations' outer scale is 1). k % 256 == 0. */
+int kab_gemm_mxf4(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf,
+                  const float* b_scale, int b_scale_per_col, int64_t m, int64_t n, int64_t k,
+                  const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo,
+                  void* stream);
+
 /* Blockwise FP8: e4m3 A [m, k] with fp32 scales a_scale [m, k / 128] (1 x 128 groups), e4m3
  * B [n, k] with fp32 scales b_scale [n / 128, k / 128] (128 x 128 blocks); out = sum over
  * 128-wide K steps of (partial * a_scale[m, kb]) * b_scale[n / 128, kb] in fp32 (+ bias), one

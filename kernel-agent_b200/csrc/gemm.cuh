@@ -7,6 +7,8 @@
 //   KIND 2  kind::mxf8f6f4  e4m3 x e4m3 with e8m0 scales per 32 applied by the tensor core
 //   KIND 3  kind::mxf4nvf4  e2m1 x e2m1 with e4m3 scales per 16 applied by the tensor core;
 //                            epilogue acc * (outer[m] * ts[n or one]) (+ bias)
+//   KIND 4  kind::mxf4nvf4  e2m1 x e2m1 with e8m0 scales per 32 (MXFP4, scale_vec::2X);
+//                            epilogue acc * (1 * ts) (+ bias): MXFP4 activations have outer 1
 //
 // One persistent CTA per SM: warp 0 issues the TMA loads (one thread), warp 1 the MMAs (one
 // thread) and owns the TMEM allocation, warps 2-9 drain the accumulator (tcgen05.ld, one TMEM
@@ -68,7 +70,7 @@ struct GemmLayout {
   // Block scales per 128 rows per stage (one 512-byte chunk of the swizzled layout per 64
   // elements of K for NVFP4, per 128 for MXFP8) and the 128-row chunks a B tile can span
   // (BN need not be a multiple of 128).
-  static constexpr int kSfChunkBytes = KIND == 3 ? 512 * kKSteps : 512;
+  static constexpr int kSfChunkBytes = KIND == 3 ? 512 * kKSteps : (KIND == 4 ? 256 * kKSteps : 512);
   static constexpr int kSfaBytes = kScaled ? kSfChunkBytes : 0;
   // groups start at word 0 or 2 of a chunk (BN a multiple of 64), so a tile spans
   // ceil((2 + kGroups) / 4) chunks at most (kGroups / 4 when BN is a multiple of 128)
@@ -81,7 +83,7 @@ struct GemmLayout {
   // makes); the scale-factor warps 10-13 write it with tcgen05.st, each into its own quarter.
   // A: 4 columns per scale set; B: one per 32 rows. NVFP4 has one set per MMA (K = 64),
   // MXFP8 one per stage (the MMA picks its byte by sf_id).
-  static constexpr int kSfSets = KIND == 3 ? kKSteps : 1;
+  static constexpr int kSfSets = KIND == 3 ? kKSteps : (KIND == 4 ? kKSteps / 2 : 1);
   static constexpr int kSfaCols = kScaled ? 4 * kSfSets : 0;
   static constexpr int kSfbCols = kScaled ? kGroups * kSfSets : 0;
   static constexpr int kSfColsPerStage = kSfaCols + kSfbCols;
@@ -156,7 +158,7 @@ __device__ __forceinline__ void epilogue_math(const GemmArgs& g, const uint32_t 
       y[i] = __float_as_uint(v);
     }
   } else {
-    // quant.py:1254-1256: acc * (outer[m] * ts) (+ bias.float())
+    // quant.py:1254-1256: acc * (outer[m] * ts) (+ bias.float()); MXFP4's outer is 1
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const float ts = __shfl_sync(0xffffffffu, cs, i);
@@ -297,7 +299,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
           tc::tma_load_2d(&tma_a, &full[s], sA + s * L::kABytes, kb * BKB, mt * 128);
           tc::tma_load_2d(&tma_b, &full[s], sB + s * L::kBBytes, kb * BKB, nt * BN);
           if constexpr (L::kScaled) {  // one chunk per 128 rows per stage (KS chunks for NVFP4: contiguous)
-            const int64_t kc = KIND == 3 ? static_cast<int64_t>(KS) * kb : kb;
+            const int64_t kc = KIND == 3 ? static_cast<int64_t>(KS) * kb : (KIND == 4 ? static_cast<int64_t>(KS / 2) * kb : kb);
             tc::bulk_load(sSFA + s * L::kSfaBytes, g.sfa + (mt * g.sfa_ncb + kc) * 512, L::kSfChunkBytes, &full[s]);
             for (int64_t c = c0; c <= c1; ++c)
               tc::bulk_load(sSFB + s * L::kSfbBytes + (c - c0) * L::kSfChunkBytes, g.sfb + (c * g.sfb_ncb + kc) * 512,
@@ -345,8 +347,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
               tc::mma_f8(d, a, b, tc::idesc_f8(128, BN), acc);
             } else if constexpr (KIND == 2) {  // one scale byte per row per MMA (sf_id = j)
               tc::mma_mxf8(d, a, b, tc::idesc_mxf8(128, BN, j), sf, sf + L::kSfaCols, acc);
-            } else {  // this MMA's scale set: 4 columns for A, one per 32 rows of B
+            } else if constexpr (KIND == 3) {  // this MMA's scale set: 4 columns for A, one per 32 rows of B
               tc::mma_nvf4(d, a, b, tc::idesc_nvf4(128, BN), sf + 4 * j, sf + L::kSfaCols + L::kGroups * j, acc);
+            } else {  // MXFP4: set j / 2 covers two MMAs, sf_id 0 / 2 picks the pair of scale bytes
+              tc::mma_mxf4(d, a, b, tc::idesc_mxf4(128, BN, 2 * (j & 1)), sf + 4 * (j >> 1),
+                           sf + L::kSfaCols + L::kGroups * (j >> 1), acc);
             }
           }
           tc::commit(&empty[s]);
@@ -468,7 +473,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       const uint32_t tbase = tmem + lane_base + ab * BN + half * (BN / 2);
       // this tile's row scale and (lane i of chunk c) column scale / bias, loaded once
       float sa = 0.0f;
-      if constexpr (KIND != 2 && OUT != kOutI32) sa = row < g.m ? __ldg(g.a_scale + row) : 0.0f;
+      if constexpr (KIND == 4) sa = 1.0f;  // MXFP4 activations: outer 1
+      else if constexpr (KIND != 2 && OUT != kOutI32) sa = row < g.m ? __ldg(g.a_scale + row) : 0.0f;
       float cs[HC], cbv[HC];
 #pragma unroll
       for (int c = 0; c < HC; ++c) {
@@ -477,7 +483,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         cbv[c] = 0.0f;
         if constexpr (OUT != kOutI32) {
           if constexpr (KIND == 0 || KIND == 1) cs[c] = col < g.n ? __ldg(g.b_scale + col) : 0.0f;
-          if constexpr (KIND == 3) cs[c] = g.b_scale_per_col ? (col < g.n ? __ldg(g.b_scale + col) : 0.0f) : __ldg(g.b_scale);
+          if constexpr (KIND == 3 || KIND == 4) {
+            if (KIND == 4 && g.b_scale == nullptr) cs[c] = 1.0f;
+            else cs[c] = g.b_scale_per_col ? (col < g.n ? __ldg(g.b_scale + col) : 0.0f) : __ldg(g.b_scale);
+          }
           if (g.bias != nullptr && col < g.n) cbv[c] = load_bias(g.bias, g.bias_dtype, col);
         }
       }

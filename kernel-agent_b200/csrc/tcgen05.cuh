@@ -229,6 +229,12 @@ __host__ __device__ constexpr uint32_t idesc_mxf8(int m, int n, int sf_id) {
 __host__ __device__ constexpr uint32_t idesc_nvf4(int m, int n) {
   return (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
+// kind::mxf4nvf4.block_scale.scale_vec::2X: e2m1 x e2m1 with ue8m0 scales per 32 (MXFP4);
+// sf_id 0 or 2 picks the two scale bytes of the 32-bit word this MMA's 64 elements of K use.
+__host__ __device__ constexpr uint32_t idesc_mxf4(int m, int n, int sf_id) {
+  return (static_cast<uint32_t>(sf_id) << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (1u << 23) | (static_cast<uint32_t>(m >> 4) << 24) | (static_cast<uint32_t>(sf_id) << 29);
+}
 
 // ------------------------------------------------------------------ MMA issue (one thread)
 
@@ -259,6 +265,14 @@ __device__ __forceinline__ void mma_nvf4(uint32_t d, uint64_t a, uint64_t b, uin
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %6, 0;\n"
       " tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%4], [%5], p;\n}\n"
+      ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(sfa), "r"(sfb), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_mxf4(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa,
+                                         uint32_t sfb, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %6, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%4], [%5], p;\n}\n"
       ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(sfa), "r"(sfb), "r"(acc)
       : "memory");
 }

@@ -130,6 +130,31 @@ def nvf4(a: torch.Tensor, a_sf_swizzled: torch.Tensor, a_outer: torch.Tensor, b:
     return out
 
 
+def mxf4(a: torch.Tensor, a_sf_swizzled: torch.Tensor, b: torch.Tensor, b_sf_swizzled: torch.Tensor,
+         b_scale: torch.Tensor | None = None, bias=None, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """MXFP4 ``a [M, K/2] @ b [N, K/2]ᵀ`` (packed e2m1) with e8m0 scales per 32 (swizzled)
+    applied by the tensor core, then ``acc * ts (+ bias)``; ``b_scale``: None (1), one value or
+    one per row of b. K % 256 == 0."""
+    _bind()
+    m, n, k = a.shape[0], b.shape[0], 2 * a.shape[1]
+    if k % 256:
+        raise ValueError(f"the MXFP4 GEMM needs K a multiple of 256 (got {k})")
+    odt, code = _out_code(out_dtype)
+    ldo = n + (-n % 8)
+    out = torch.empty(m, ldo, dtype=odt, device=a.device)
+    bb, bcode = _bias(bias, n, a.device)
+    ts, per_col = None, 0
+    if b_scale is not None:
+        ts = b_scale.float().to(a.device).reshape(-1).contiguous()
+        per_col = int(ts.numel() > 1)
+        if per_col and ts.numel() != n:
+            raise ValueError(f"b_scale has {ts.numel()} values, expected 1 or {n}")
+    nat.call("kab_gemm_mxf4", a.contiguous().data_ptr(), a_sf_swizzled.data_ptr(), b.contiguous().data_ptr(),
+             b_sf_swizzled.data_ptr(), nat.ptr(ts), per_col, m, n, k, nat.ptr(bb), bcode, out.data_ptr(), code, ldo,
+             nat.stream_of(a))
+    return out[:, :n] if ldo != n else out
+
+
 def fp8_blockwise(a: torch.Tensor, a_scale: torch.Tensor, b: torch.Tensor, b_scale: torch.Tensor, bias=None,
                   out_dtype=torch.bfloat16) -> torch.Tensor:
     """Blockwise FP8 ``a [M, K] @ b [N, K]ᵀ``: ``a_scale [M, K/128]`` per 1 x 128 group,

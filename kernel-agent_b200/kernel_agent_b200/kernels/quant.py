@@ -494,32 +494,43 @@ def fp4_w4a4_linear(
     rotate: int | None = None,
     unbiased: bool = False,
 ) -> torch.Tensor:
-    """quant.py:1201-1257: ``x`` quantised to NVFP4 per call (block scales written swizzled,
-    outer scale per token or per call), the block-scaled GEMM (tcgen05 kind::mxf4nvf4, e4m3
-    scales per 16 applied by the tensor core, fp32 accumulation), then ``acc * (outer[m] *
-    tensor_scale) (+ bias)`` in fp32 and one rounding to ``x``'s dtype. ``scales``: the
-    weight's ``[N, K / 16]`` (or already swizzled, flat)."""
+    """quant.py:1201-1257: ``x`` quantised per call (block scales written swizzled; NVFP4's
+    outer scale per token or per call, MXFP4's 1), the block-scaled GEMM (tcgen05
+    kind::mxf4nvf4: e4m3 scales per 16 or e8m0 per 32 applied by the tensor core, fp32
+    accumulation), then ``acc * (outer[m] * tensor_scale) (+ bias)`` in fp32 and one rounding
+    to ``x``'s dtype. ``scales``: the weight's ``[N, K / block]`` (or already swizzled, flat,
+    when K is a multiple of 256)."""
     if fmt not in FP4_FORMATS:
         raise ValueError(f"unknown FP4 format {fmt!r} (one of {', '.join(FP4_FORMATS)})")
     if granularity not in FP4_GRANULARITIES:
         raise ValueError(f"unknown granularity {granularity!r} ({', '.join(FP4_GRANULARITIES)})")
-    if fmt != "nvfp4":
-        raise NotImplementedError("fp4_w4a4_linear: MXFP4 (kind::mxf4) is not built yet; use nvfp4")
     if rotate or unbiased:
         raise NotImplementedError("fp4_w4a4_linear: rotate / unbiased are not built yet")
     nat.require_cuda(x, codes)
+    block = FP4_FORMATS[fmt][0]
     k = x.shape[-1]
-    if k % 16:
-        raise ValueError(f"the last dimension {k} is not a multiple of the nvfp4 block (16)")
-    x2 = _rows(_input(x))
-    mode = nat.KAB_FP4_TENSOR if granularity == "tensor" else nat.KAB_FP4_TOKEN
-    amax = _amax(x2) if granularity == "tensor" else None
-    xq, xs, outer = _fp4(x2, "nvfp4", mode, amax=amax, swizzle=True)
+    if k % block:
+        raise ValueError(f"the last dimension {k} is not a multiple of the {fmt} block ({block})")
     n = codes.shape[0]
-    ws = _swizzled(scales, n, k // 16)
+    x2 = _rows(_input(x))
+    kp = k + (-k % 256)  # the GEMM's k-step: zero codes and scales pad K (they add nothing)
+    ws = scales
+    if kp != k:
+        if scales.dim() != 2:
+            raise ValueError(f"K = {k} needs padding to {kp}: pass the unswizzled [N, K / {block}] scales")
+        x2 = torch.nn.functional.pad(x2, (0, kp - k))
+        codes = torch.nn.functional.pad(codes.view(torch.uint8), (0, (kp - k) // 2))
+        ws = torch.nn.functional.pad(scales.view(torch.uint8), (0, (kp - k) // block))
+    odt = x.dtype if x.dtype in (torch.bfloat16, torch.float16, torch.float32) else torch.float32
     ts = torch.as_tensor(tensor_scale, dtype=torch.float32, device=x2.device)
-    y = gemm.nvf4(xq, xs.view(torch.uint8), outer, codes, ws, ts, bias,
-                  out_dtype=x.dtype if x.dtype in (torch.bfloat16, torch.float16, torch.float32) else torch.float32)
+    if fmt == "nvfp4":
+        mode = nat.KAB_FP4_TENSOR if granularity == "tensor" else nat.KAB_FP4_TOKEN
+        amax = _amax(x2) if granularity == "tensor" else None
+        xq, xs, outer = _fp4(x2, "nvfp4", mode, amax=amax, swizzle=True)
+        y = gemm.nvf4(xq, xs.view(torch.uint8), outer, codes, _swizzled(ws, n, kp // 16), ts, bias, out_dtype=odt)
+    else:  # MXFP4: e8m0 scales per 32, outer 1 (quant.py:1079-1087)
+        xq, xs, _ = _fp4(x2, "mxfp4", nat.KAB_FP4_TOKEN, swizzle=True)
+        y = gemm.mxf4(xq, xs.view(torch.uint8), codes, _swizzled(ws, n, kp // 32), ts, bias, out_dtype=odt)
     return _linear_out(y, x, n)
 
 

@@ -185,6 +185,24 @@ def test_fp4_w4a4_linear(kq, m, k, n, golden):
     assert float(np.mean(ul <= 1)) >= 0.99 and ul.max() <= 4, (np.mean(ul == 0), ul.max())
 
 
+@pytest.mark.parametrize("fmt,m,k,n", [("mxfp4", 64, 256, 128), ("mxfp4", 200, 1024, 384), ("mxfp4", 130, 96, 3200),
+                                       ("mxfp4", 256, 2048, 3264), ("nvfp4", 70, 48, 256), ("nvfp4", 33, 4128, 192)])
+def test_fp4_w4a4_linear_formats_and_ragged_k(kq, fmt, m, k, n):
+    """MXFP4 (kind::mxf4nvf4 scale_vec::2X, e8m0 per 32) and K that is not a multiple of the
+    GEMM's 256-element k-step (zero-padded codes and scales)."""
+    g = torch.Generator().manual_seed(m * 7 + k)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.01).to(torch.bfloat16)
+    b = (torch.randn(n, generator=g) * 0.05).to(torch.bfloat16)
+    q, s, ts = kq.quantize_fp4(w.to(DEV), fmt)
+    y = kq.fp4_w4a4_linear(x.to(DEV), q, s, ts, b.to(DEV), fmt=fmt)
+    assert y.shape == (m, n) and y.dtype == torch.bfloat16
+    rows = slice(0, min(m, 96))
+    want = oq.fp4_w4a4_linear(np_values(x[rows]), np_bytes(q), np_bytes(s), float(ts), np_values(b), fmt=fmt,
+                              out_dtype="f32")
+    close_bf16(y[rows], want, f"{fmt} {m}x{k}x{n}")
+
+
 def test_fp4_config4_row_sample(kq):
     """Config 4's shapes (K = 8192, N = 28672 sliced to 1024 output channels for the oracle)."""
     from kernel_agent_b200 import workloads
