@@ -149,12 +149,13 @@ int kab_gemm_f8(const uint8_t* a, const uint8_t* b, int64_t m, int64_t n, int64_
                 void* out, int out_dtype, int64_t ldo, void* stream);
 
 /* MXFP4: packed e2m1 A [m, k / 2], B [n, k / 2] with e8m0 scales per 32 along K (swizzled),
- * applied by the tensor core (kind::mxf4nvf4.block_scale.scale_vec::2X); out = acc * ts
- * (+ bias), ts = b_scale[0], b_scale[n] (b_scale_per_col) or 1 (null) (quant.py:1201-1257
- * fp4_w4a4_linear, fmt "mxfp4": the activations' outer scale is 1). k % 256 == 0. */
-int kab_gemm_mxf4(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf,
-                  const float* b_scale, int b_scale_per_col, int64_t m, int64_t n, int64_t k,
-                  const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo,
+ * applied by the tensor core (kind::mxf4nvf4.block_scale.scale_vec::2X); out = acc * (outer[m]
+ * * ts) (+ bias), outer = a_outer[m] or 1 (null: MXFP4 activations), ts = b_scale[0],
+ * b_scale[n] (b_scale_per_col) or 1 (null) (quant.py:1201-1257 fp4_w4a4_linear, fmt
+ * "mxfp4"). k % 256 == 0. */
+int kab_gemm_mxf4(const uint8_t* a, const uint8_t* a_sf, const float* a_outer, const uint8_t* b,
+                  const uint8_t* b_sf, const float* b_scale, int b_scale_per_col, int64_t m, int64_t n,
+                  int64_t k, const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo,
                   void* stream);
 
 /* Blockwise FP8: e4m3 A [m, k] with fp32 scales a_scale [m, k / 128] (1 x 128 groups), e4m3
@@ -273,6 +274,19 @@ size_t kab_channel_rms_scratch_bytes(int64_t rows, int64_t channels);
 int kab_channel_rms(const void* x, const void* alt, int dtype, int64_t rows,
                     int64_t channels, float* rms, void* scratch, size_t scratch_bytes,
                     void* stream);
+
+/* quant.py:1150-1173 hadamard_rotate: each `block` (a power of two) consecutive elements of
+ * the rows of x [rows, k] times the orthonormal Sylvester-Hadamard matrix, fp32 out
+ * [rows, k] (k <= 32768). */
+int kab_hadamard_rotate(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, int block,
+                        float* out, void* stream);
+
+/* quant.py:1117-1148 fp4_bias_correction: per row of x [rows, k] quantised to (codes,
+ * scales [rows, k / block] bytes, row-major or `swizzled`, outer [rows] / one value / null),
+ * c = sum x^2 / sum x x^ in float64 (1 when sum x x^ <= 0 or c is not finite); fp32 out [rows]. */
+int kab_fp4_bias_correction(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                            const uint8_t* codes, const uint8_t* scales, int fmt, int swizzled,
+                            const float* outer, int outer_per_row, float* out, void* stream);
 
 /* ------------------------------------------------------------------ scale-rule checks */
 

@@ -473,7 +473,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       const uint32_t tbase = tmem + lane_base + ab * BN + half * (BN / 2);
       // this tile's row scale and (lane i of chunk c) column scale / bias, loaded once
       float sa = 0.0f;
-      if constexpr (KIND == 4) sa = 1.0f;  // MXFP4 activations: outer 1
+      if constexpr (KIND == 4) sa = g.a_scale == nullptr ? 1.0f : (row < g.m ? __ldg(g.a_scale + row) : 0.0f);
       else if constexpr (KIND != 2 && OUT != kOutI32) sa = row < g.m ? __ldg(g.a_scale + row) : 0.0f;
       float cs[HC], cbv[HC];
 #pragma unroll

@@ -248,10 +248,11 @@ int kab_gemm_nvf4(const uint8_t* a, const uint8_t* a_sf, const float* a_outer, c
   return run<3>(a, b, m, n, k / 2, g, out_dtype, as_stream(stream));
 }
 
-int kab_gemm_mxf4(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf,
-                  const float* b_scale, int b_scale_per_col, int64_t m, int64_t n, int64_t k, const void* bias,
-                  int bias_dtype, void* out, int out_dtype, int64_t ldo, void* stream) {
+int kab_gemm_mxf4(const uint8_t* a, const uint8_t* a_sf, const float* a_outer, const uint8_t* b,
+                  const uint8_t* b_sf, const float* b_scale, int b_scale_per_col, int64_t m, int64_t n, int64_t k,
+                  const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo, void* stream) {
   GemmArgs g = args_of(bias, bias_dtype, out, out_dtype, ldo);
+  g.a_scale = a_outer;
   g.b_scale = b_scale;
   g.b_scale_per_col = b_scale != nullptr && b_scale_per_col;
   KAB_REQUIRE(a_sf != nullptr && b_sf != nullptr && aligned(a_sf, 16) && aligned(b_sf, 16),

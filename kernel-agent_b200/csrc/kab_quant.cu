@@ -344,4 +344,46 @@ int kab_fp4_scale_check(const void* x, int dtype, int64_t rows, int64_t k, int64
   return check_launch("kab_fp4_scale_check");
 }
 
+int kab_hadamard_rotate(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, int block, float* out,
+                        void* stream) {
+  KAB_REQUIRE(valid_dtype(dtype), "unknown dtype %d", dtype);
+  KAB_REQUIRE(rows >= 0 && k >= 0 && ldx >= k, "bad shape [%lld, %lld] (ld %lld)", (long long)rows, (long long)k,
+              (long long)ldx);
+  KAB_REQUIRE(block >= 1 && (block & (block - 1)) == 0, "the Hadamard order must be a power of two, got %d", block);
+  KAB_REQUIRE(k % block == 0, "the last dimension %lld is not a multiple of the rotation (%d)", (long long)k, block);
+  KAB_REQUIRE(k <= 32768, "rows of %lld elements exceed the shared-memory row (32768)", (long long)k);
+  KAB_REQUIRE(rows == 0 || (x != nullptr && out != nullptr), "null pointer");
+  if (rows == 0 || k == 0) return KAB_OK;
+  const size_t smem = static_cast<size_t>(k) * sizeof(float);
+  const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(block)));
+  const cudaStream_t s = as_stream(stream);
+#define KAB_HAD(TT)                                                                                   \
+  do {                                                                                                \
+    cudaFuncSetAttribute(hadamard_rotate_kernel<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 32768 * 4); \
+    hadamard_rotate_kernel<TT><<<static_cast<unsigned>(rows), 512, smem, s>>>(x, ldx, k, block, inv, out); \
+  } while (0)
+  if (dtype == KAB_BF16) KAB_HAD(kBF16);
+  else if (dtype == KAB_F16) KAB_HAD(kF16);
+  else KAB_HAD(kF32);
+#undef KAB_HAD
+  return check_launch("kab_hadamard_rotate");
+}
+
+int kab_fp4_bias_correction(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, const uint8_t* codes,
+                            const uint8_t* scales, int fmt, int swizzled, const float* outer, int outer_per_row,
+                            float* out, void* stream) {
+  if (int e = check_matrix(x, dtype, rows, k, ldx, "x")) return e;
+  KAB_REQUIRE(fmt == KAB_NVFP4 || fmt == KAB_MXFP4, "fmt %d is not NVFP4 (0) or MXFP4 (1)", fmt);
+  const int block = fmt == KAB_NVFP4 ? 16 : 32;
+  KAB_REQUIRE(k % block == 0, "width %lld is not a multiple of the block (%d)", (long long)k, block);
+  KAB_REQUIRE(rows == 0 || (codes != nullptr && scales != nullptr && out != nullptr), "null pointer");
+  if (rows == 0) return KAB_OK;
+  const cudaStream_t s = as_stream(stream);
+  const unsigned grid = static_cast<unsigned>(rows);
+  if (dtype == KAB_BF16) fp4_bias_correction_kernel<kBF16><<<grid, 256, 0, s>>>(x, ldx, k, codes, scales, fmt, swizzled, outer, outer_per_row, out);
+  else if (dtype == KAB_F16) fp4_bias_correction_kernel<kF16><<<grid, 256, 0, s>>>(x, ldx, k, codes, scales, fmt, swizzled, outer, outer_per_row, out);
+  else fp4_bias_correction_kernel<kF32><<<grid, 256, 0, s>>>(x, ldx, k, codes, scales, fmt, swizzled, outer, outer_per_row, out);
+  return check_launch("kab_fp4_bias_correction");
+}
+
 }  // extern "C"

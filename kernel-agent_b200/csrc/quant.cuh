@@ -490,4 +490,76 @@ __global__ void fp4_values_kernel(const uint8_t* __restrict__ codes, const uint8
   }
 }
 
+// e2m1 code (sign in bit 3) -> its value.
+__device__ __forceinline__ float e2m1_value(uint32_t code) {
+  const uint32_t idx = code & 7;
+  const float mag = idx <= 4 ? 0.5f * static_cast<float>(idx) : static_cast<float>(idx - 2) + (idx == 7 ? 1.0f : 0.0f);
+  return (code & 8) ? -mag : mag;
+}
+
+// Block-diagonal Walsh-Hadamard rotation (quant.py:1150-1173 hadamard_rotate): every `block`
+// consecutive elements of a row times the orthonormal Sylvester-Hadamard matrix, in fp32 (the
+// butterflies of H x, then one multiplication by fp32(1 / sqrt(block))). One CTA per row, the
+// row in shared memory; out fp32 [rows, k].
+template <int T>
+__global__ void __launch_bounds__(512)
+hadamard_rotate_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, int block, float inv_sqrt,
+                       float* __restrict__ out) {
+  extern __shared__ float hrow[];
+  const int64_t r = blockIdx.x;
+  for (int64_t i = threadIdx.x; i < k; i += blockDim.x) hrow[i] = load_elem<T>(x, r * ldx + i);
+  __syncthreads();
+  for (int h = 1; h < block; h <<= 1) {
+    for (int64_t p = threadIdx.x; p < k / 2; p += blockDim.x) {
+      const int64_t i = (p / h) * (2 * h) + (p % h);  // the pair (i, i + h) of one block
+      const float a = hrow[i], b = hrow[i + h];
+      hrow[i] = __fadd_rn(a, b);
+      hrow[i + h] = __fsub_rn(a, b);
+    }
+    __syncthreads();
+  }
+  for (int64_t i = threadIdx.x; i < k; i += blockDim.x) out[r * k + i] = __fmul_rn(hrow[i], inv_sqrt);
+}
+
+// quant.py:1117-1148 fp4_bias_correction: per row c = sum x^2 / sum x x^ (float64 sums) with
+// x^ = e2m1 * scale * outer; 1 when sum x x^ is not positive or c is not finite. One CTA per
+// row; scales [rows, k / block] bytes, row-major or swizzled; outer per row, one value or null.
+template <int T>
+__global__ void __launch_bounds__(256)
+fp4_bias_correction_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const uint8_t* __restrict__ codes,
+                           const uint8_t* __restrict__ scales, int fmt, int swizzled, const float* __restrict__ outer,
+                           int outer_per_row, float* __restrict__ out) {
+  __shared__ double red[2][32];
+  const int64_t r = blockIdx.x;
+  const int block = fmt == 0 ? 16 : 32;
+  const int64_t cols = k / block;
+  const double o = outer == nullptr ? 1.0 : static_cast<double>(outer[outer_per_row ? r : 0]);
+  double num = 0.0, den = 0.0;
+  for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+    const double a = load_elem<T>(x, r * ldx + i);
+    const uint8_t byte = codes[r * (k >> 1) + (i >> 1)];
+    const uint32_t code = (i & 1) ? (byte >> 4) : (byte & 0xF);
+    const int64_t c = i / block;
+    const uint8_t sb = scales[swizzled ? scale_offset_swizzled(r, c, cols) : r * cols + c];
+    const float s = fmt == 0 ? e4m3_value(sb) : e8m0_value(sb);
+    const double xh = static_cast<double>(__fmul_rn(e2m1_value(code), s)) * o;
+    num += a * a;
+    den += a * xh;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    num += __shfl_xor_sync(0xffffffffu, num, off);
+    den += __shfl_xor_sync(0xffffffffu, den, off);
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) { red[0][warp] = num; red[1][warp] = den; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double n = 0.0, d = 0.0;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) { n += red[0][w]; d += red[1][w]; }
+    const double cval = n / fmax(d, 1e-300);
+    out[r] = (d > 0.0 && isfinite(cval)) ? static_cast<float>(cval) : 1.0f;
+  }
+}
+
 }  // namespace kab

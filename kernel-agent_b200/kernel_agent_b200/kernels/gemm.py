@@ -131,10 +131,11 @@ def nvf4(a: torch.Tensor, a_sf_swizzled: torch.Tensor, a_outer: torch.Tensor, b:
 
 
 def mxf4(a: torch.Tensor, a_sf_swizzled: torch.Tensor, b: torch.Tensor, b_sf_swizzled: torch.Tensor,
-         b_scale: torch.Tensor | None = None, bias=None, out_dtype=torch.bfloat16) -> torch.Tensor:
+         b_scale: torch.Tensor | None = None, bias=None, out_dtype=torch.bfloat16,
+         a_outer: torch.Tensor | None = None) -> torch.Tensor:
     """MXFP4 ``a [M, K/2] @ b [N, K/2]ᵀ`` (packed e2m1) with e8m0 scales per 32 (swizzled)
-    applied by the tensor core, then ``acc * ts (+ bias)``; ``b_scale``: None (1), one value or
-    one per row of b. K % 256 == 0."""
+    applied by the tensor core, then ``acc * (outer[m] * ts) (+ bias)``; ``a_outer``: None (1)
+    or one per row of a; ``b_scale``: None (1), one value or one per row of b. K % 256 == 0."""
     _bind()
     m, n, k = a.shape[0], b.shape[0], 2 * a.shape[1]
     if k % 256:
@@ -149,9 +150,10 @@ def mxf4(a: torch.Tensor, a_sf_swizzled: torch.Tensor, b: torch.Tensor, b_sf_swi
         per_col = int(ts.numel() > 1)
         if per_col and ts.numel() != n:
             raise ValueError(f"b_scale has {ts.numel()} values, expected 1 or {n}")
-    nat.call("kab_gemm_mxf4", a.contiguous().data_ptr(), a_sf_swizzled.data_ptr(), b.contiguous().data_ptr(),
-             b_sf_swizzled.data_ptr(), nat.ptr(ts), per_col, m, n, k, nat.ptr(bb), bcode, out.data_ptr(), code, ldo,
-             nat.stream_of(a))
+    outer = None if a_outer is None else a_outer.float().reshape(-1).contiguous()
+    nat.call("kab_gemm_mxf4", a.contiguous().data_ptr(), a_sf_swizzled.data_ptr(), nat.ptr(outer),
+             b.contiguous().data_ptr(), b_sf_swizzled.data_ptr(), nat.ptr(ts), per_col, m, n, k, nat.ptr(bb), bcode,
+             out.data_ptr(), code, ldo, nat.stream_of(a))
     return out[:, :n] if ldo != n else out
 
 

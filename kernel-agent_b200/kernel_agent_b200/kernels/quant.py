@@ -351,8 +351,6 @@ def quantize_fp4(
     rows, cols = weight.shape
     if cols % block:
         raise ValueError(f"in_features {cols} is not a multiple of the {fmt} block ({block})")
-    if unbiased:
-        raise NotImplementedError("quantize_fp4(unbiased=True): the bias correction is not built yet")
     nat.require_cuda(weight)
     w = _rows(_input(weight))
     amax = _amax(w)
@@ -364,6 +362,8 @@ def quantize_fp4(
     else:
         ts = torch.ones((), dtype=torch.float32, device=w.device)
     q, s, _ = _fp4(w, fmt, nat.KAB_FP4_WEIGHT, ts=ts)
+    if unbiased:  # quant.py:270-271: one factor per output channel, in the tensor scale's place
+        ts = ts * fp4_bias_correction(w, q, s, ts)
     return q, s, ts
 
 
@@ -482,6 +482,65 @@ def mxfp8_linear(
     return _linear_out(y, x, q.shape[0])
 
 
+def hadamard(n: int, device: torch.device | str | None = None) -> torch.Tensor:
+    """quant.py:1150-1159: the orthonormal Sylvester-Hadamard matrix of order ``n`` (a power of
+    two), fp32."""
+    if n < 1 or n & (n - 1):
+        raise ValueError(f"the Hadamard order must be a power of two, got {n}")
+    h = torch.ones(1, 1, device=device)
+    while h.shape[0] < n:
+        h = torch.cat([torch.cat([h, h], 1), torch.cat([h, -h], 1)], 0)
+    return h / math.sqrt(n)
+
+
+def hadamard_rotate(x: torch.Tensor, block: int) -> torch.Tensor:
+    """quant.py:1162-1173: ``x [..., K]`` with every ``block`` consecutive elements along K
+    multiplied by ``hadamard(block)``, fp32 (one GPU pass: butterflies in shared memory)."""
+    k = x.shape[-1]
+    if k % block:
+        raise ValueError(f"the last dimension {k} is not a multiple of the rotation ({block})")
+    if block < 1 or block & (block - 1):
+        raise ValueError(f"the Hadamard order must be a power of two, got {block}")
+    nat.require_cuda(x)
+    x2 = _rows(_input(x))
+    out = torch.empty(x2.shape[0], k, dtype=torch.float32, device=x2.device)
+    if x2.shape[0] and k:
+        nat.call("kab_hadamard_rotate", x2.data_ptr(), nat.dtype_code(x2), x2.shape[0], k, x2.stride(0), block,
+                 out.data_ptr(), _stream(x2))
+    return out.reshape(*x.shape[:-1], k)
+
+
+def _bias_correction(x2, codes, scales, fmt: str, outer, swizzled: bool) -> torch.Tensor:
+    rows, k = x2.shape
+    out = torch.empty(rows, dtype=torch.float32, device=x2.device)
+    o, per_row = None, 0
+    if outer is not None:
+        o = torch.as_tensor(outer).detach().float().to(x2.device).reshape(-1).contiguous()
+        per_row = int(o.numel() == rows and rows != 1)
+        if o.numel() not in (1, rows):
+            raise ValueError(f"expected an outer scale per row ([{rows}]) or one, got {o.numel()}")
+    if rows:
+        nat.call("kab_fp4_bias_correction", x2.data_ptr(), nat.dtype_code(x2), rows, k, x2.stride(0),
+                 codes.contiguous().data_ptr(), scales.view(torch.uint8).contiguous().data_ptr(),
+                 nat.KAB_NVFP4 if fmt == "nvfp4" else nat.KAB_MXFP4, int(swizzled), nat.ptr(o), per_row,
+                 out.data_ptr(), _stream(x2))
+    return out
+
+
+def fp4_bias_correction(x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor,
+                        outer: torch.Tensor | float | None = None) -> torch.Tensor:
+    """quant.py:1117-1148: per row of ``x [rows, K]`` quantised to ``(codes, scales [rows, K /
+    block] unswizzled, outer)``, ``c = sum x^2 / sum x x^`` (float64 sums; 1 where ``sum x x^``
+    is not positive), fp32 ``[rows]`` (one GPU pass)."""
+    nat.require_cuda(x, codes)
+    x2 = _rows(_input(x))
+    k = x2.shape[1]
+    fmt = "nvfp4" if scales.shape[-1] * 16 == k else "mxfp4"
+    if scales.dim() != 2 or scales.shape[-1] * FP4_FORMATS[fmt][0] != k:
+        raise ValueError(f"expected unswizzled scales [rows, K / block] for K = {k}, got {tuple(scales.shape)}")
+    return _bias_correction(x2, codes, scales, fmt, outer, swizzled=False)
+
+
 def fp4_w4a4_linear(
     x: torch.Tensor,
     codes: torch.Tensor,
@@ -504,15 +563,13 @@ def fp4_w4a4_linear(
         raise ValueError(f"unknown FP4 format {fmt!r} (one of {', '.join(FP4_FORMATS)})")
     if granularity not in FP4_GRANULARITIES:
         raise ValueError(f"unknown granularity {granularity!r} ({', '.join(FP4_GRANULARITIES)})")
-    if rotate or unbiased:
-        raise NotImplementedError("fp4_w4a4_linear: rotate / unbiased are not built yet")
     nat.require_cuda(x, codes)
     block = FP4_FORMATS[fmt][0]
     k = x.shape[-1]
     if k % block:
         raise ValueError(f"the last dimension {k} is not a multiple of the {fmt} block ({block})")
     n = codes.shape[0]
-    x2 = _rows(_input(x))
+    x2 = hadamard_rotate(_rows(_input(x)), rotate) if rotate else _rows(_input(x))
     kp = k + (-k % 256)  # the GEMM's k-step: zero codes and scales pad K (they add nothing)
     ws = scales
     if kp != k:
@@ -527,10 +584,14 @@ def fp4_w4a4_linear(
         mode = nat.KAB_FP4_TENSOR if granularity == "tensor" else nat.KAB_FP4_TOKEN
         amax = _amax(x2) if granularity == "tensor" else None
         xq, xs, outer = _fp4(x2, "nvfp4", mode, amax=amax, swizzle=True)
+        if unbiased:  # quant.py:1231-1232: the activations' factor in the epilogue's outer scale
+            outer = outer * _bias_correction(x2, xq, xs, "nvfp4", outer, swizzled=True)
         y = gemm.nvf4(xq, xs.view(torch.uint8), outer, codes, _swizzled(ws, n, kp // 16), ts, bias, out_dtype=odt)
     else:  # MXFP4: e8m0 scales per 32, outer 1 (quant.py:1079-1087)
-        xq, xs, _ = _fp4(x2, "mxfp4", nat.KAB_FP4_TOKEN, swizzle=True)
-        y = gemm.mxf4(xq, xs.view(torch.uint8), codes, _swizzled(ws, n, kp // 32), ts, bias, out_dtype=odt)
+        xq, xs, outer = _fp4(x2, "mxfp4", nat.KAB_FP4_TOKEN, swizzle=True)
+        outer = outer * _bias_correction(x2, xq, xs, "mxfp4", outer, swizzled=True) if unbiased else None
+        y = gemm.mxf4(xq, xs.view(torch.uint8), codes, _swizzled(ws, n, kp // 32), ts, bias, out_dtype=odt,
+                      a_outer=outer)
     return _linear_out(y, x, n)
 
 

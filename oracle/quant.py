@@ -8,6 +8,8 @@ CPU fp32 matmul, are computed here in float64 and rounded once to fp32.
 
 from __future__ import annotations
 
+import math
+
 import numpy as np
 
 from .formats import (
@@ -346,9 +348,10 @@ def quantize_fp4_activations(x, fmt="nvfp4", granularity="token"):
     return _fp4_codes(blocks, step), scales, outer
 
 
-def quantize_fp4(weight, fmt="nvfp4"):
-    """quant.py:217-272 (``unbiased`` off): packed codes, block scale bytes and the fp32
-    tensor scale (``float(amax) / (6 * 448)`` in double, rounded to fp32; 1 for MXFP4)."""
+def quantize_fp4(weight, fmt="nvfp4", unbiased=False):
+    """quant.py:217-272: packed codes, block scale bytes and the fp32 tensor scale
+    (``float(amax) / (6 * 448)`` in double, rounded to fp32; 1 for MXFP4); ``unbiased``: the
+    tensor scale times each output channel's :func:`fp4_bias_correction` (fp32 ``[out]``)."""
     w = f32(weight)
     if w.ndim != 2:
         raise ValueError(f"expected a 2-D weight [out, in], got shape {tuple(w.shape)}")
@@ -382,7 +385,51 @@ def quantize_fp4(weight, fmt="nvfp4"):
             F32(0),
         )
         codes = e2m1_codes(np.clip(v, -FP4_MAX, FP4_MAX).astype(F32)).reshape(rows, cols)
-    return pack_e2m1(codes), scales, ts
+    packed = pack_e2m1(codes)
+    if unbiased:
+        ts = (F32(ts) * fp4_bias_correction(w, packed, scales, ts, fmt)).astype(F32)
+    return packed, scales, ts
+
+
+def fp4_bias_correction(x, codes, scales, outer=None, fmt=None) -> np.ndarray:
+    """quant.py:1117-1148: per row ``c = sum x^2 / sum x x^`` in float64 with ``x^ = e2m1 *
+    scale * outer``; 1 where ``sum x x^`` is not positive or ``c`` is not finite; fp32."""
+    a = _rows(x).astype(np.float64)
+    rows, k = a.shape
+    s = np.asarray(scales, np.uint8)
+    fmt = fmt or ("nvfp4" if s.shape[-1] * 16 == k else "mxfp4")
+    xh = fp4_values(codes, s, fmt).astype(np.float64)
+    if outer is not None:
+        o = np.asarray(outer, np.float64).reshape(-1)
+        xh = xh * (o if o.size == rows else np.full(rows, o[0]))[:, None]
+    num, den = (a * a).sum(axis=1), (a * xh).sum(axis=1)
+    with np.errstate(**_ERRSTATE):
+        c = num / np.maximum(den, 1e-300)
+    ok = (den > 0) & np.isfinite(c)
+    return np.where(ok, c, 1.0).astype(F32)
+
+
+def hadamard(n: int) -> np.ndarray:
+    """quant.py:1150-1159: the orthonormal Sylvester-Hadamard matrix of order ``n``, fp32."""
+    if n < 1 or n & (n - 1):
+        raise ValueError(f"the Hadamard order must be a power of two, got {n}")
+    h = np.ones((1, 1), F32)
+    while h.shape[0] < n:
+        h = np.block([[h, h], [h, -h]]).astype(F32)
+    return (h / F32(math.sqrt(n))).astype(F32)
+
+
+def hadamard_rotate(x, block: int) -> np.ndarray:
+    """quant.py:1162-1173: every ``block`` elements along K times ``hadamard(block)``; each
+    output a float64 sum of the fp32 products, rounded to fp32 (torch's fp32 matmul orders its
+    sum its own way: parity is within a few fp32 units)."""
+    a = f32(x)
+    k = a.shape[-1]
+    if k % block:
+        raise ValueError(f"the last dimension {k} is not a multiple of the rotation ({block})")
+    h = hadamard(block).astype(np.float64)
+    v = a.reshape(-1, k // block, block).astype(np.float64) @ h
+    return v.astype(F32).reshape(a.shape)
 
 
 def fp4_values(codes, scales, fmt="nvfp4") -> np.ndarray:
@@ -405,11 +452,15 @@ def fp4_epilogue(acc, outer, ts, bias=None) -> np.ndarray:
 
 
 def fp4_w4a4_linear(x, codes, scales, ts, bias=None, fmt="nvfp4", granularity="token",
-                    out_dtype="bf16") -> np.ndarray:
-    """quant.py:1201-1257 (no rotation, not unbiased; the fp32 path): activations quantised
-    per call, block-scaled products accumulated in float64 and rounded to fp32, then the
-    fp32 epilogue and one rounding to the output dtype."""
-    xq, xs, outer = quantize_fp4_activations(x, fmt, granularity)
+                    out_dtype="bf16", rotate=None, unbiased=False) -> np.ndarray:
+    """quant.py:1201-1257 (the fp32 path): activations rotated (``rotate``) and quantised per
+    call, block-scaled products accumulated in float64 and rounded to fp32, the outer scale
+    times the activations' bias correction (``unbiased``), then the fp32 epilogue and one
+    rounding to the output dtype."""
+    xr = hadamard_rotate(x, rotate) if rotate else x
+    xq, xs, outer = quantize_fp4_activations(xr, fmt, granularity)
+    if unbiased:
+        outer = (f32(outer) * fp4_bias_correction(xr, xq, xs, outer, fmt)).astype(F32)
     acc = (fp4_values(xq, xs, fmt).astype(np.float64)
            @ fp4_values(codes, scales, fmt).astype(np.float64).T).astype(F32)
     return to_dtype(fp4_epilogue(acc, outer, ts, bias), out_dtype)

@@ -141,6 +141,25 @@ def main(src: str) -> None:
     y4 = quant.fp4_w4a4_linear(x4, c4, s4, t4, b4)
     out.update(w4a4_x=bits(x4), w4a4_w=bits(w4), w4a4_bias=bits(b4), w4a4_q=c4.numpy(),
                w4a4_s=bits(s4), w4a4_ts=t4.numpy(), w4a4_y=bits(y4))
+    # rotation and the opt-in bias correction (W4A4 options of fp4_w4a4_linear / quantize_fp4)
+    gr = torch.Generator().manual_seed(11)
+    xr = torch.randn(24, 256, generator=gr).to(bf)
+    xr[3, 17] = 40.0
+    wr = (torch.randn(160, 256, generator=gr) * 0.02).to(bf)
+    br = (torch.randn(160, generator=gr) * 0.05).to(bf)
+    out.update(rot_x=bits(xr), rot_w=bits(wr), rot_b=bits(br),
+               rot_x16=quant.hadamard_rotate(xr, 16).numpy(), rot_x128=quant.hadamard_rotate(xr, 128).numpy())
+    for fmt in ("nvfp4", "mxfp4"):
+        cx, sx, ox = quant.quantize_fp4_activations(xr, fmt)
+        out[f"bc_{fmt}_x"] = quant.fp4_bias_correction(xr, cx, sx, ox).numpy()
+        cu, su, tu = quant.quantize_fp4(wr, fmt, unbiased=True)
+        out.update({f"ub_{fmt}_q": cu.numpy(), f"ub_{fmt}_s": bits(su), f"ub_{fmt}_ts": tu.numpy()})
+        out[f"ub_{fmt}_y"] = bits(quant.fp4_w4a4_linear(xr, cu, su, tu, br, fmt=fmt, unbiased=True))
+        wrot = quant.hadamard_rotate(wr, 16).to(bf)
+        cr, sr, tr = quant.quantize_fp4(wrot, fmt)
+        out.update({f"rot_{fmt}_wq": cr.numpy(), f"rot_{fmt}_ws": bits(sr), f"rot_{fmt}_ts": tr.numpy()})
+        out[f"rot_{fmt}_y"] = bits(quant.fp4_w4a4_linear(xr, cr, sr, tr, br, fmt=fmt, rotate=16))
+
     # e2m1 ties: the hardware's directions
     ties = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, -0.25, -5.0])
     out.update(e2m1_ties=ties.numpy(), e2m1_ties_codes=quant._round_e2m1(ties).numpy())

@@ -223,3 +223,30 @@ def test_scale_checks(golden, golden_meta):
                 s = golden["stress_fp4_trunc_scales"]
             got = oq.fp4_scale_check(x, s, o, fmt)
         assert got == chk["result"], (chk, got)
+
+
+def test_rotation_and_bias_correction(golden):
+    """hadamard_rotate (fp32 within a few units: torch's matmul orders its sums its own way),
+    fp4_bias_correction, quantize_fp4(unbiased=True) and fp4_w4a4_linear with rotate / unbiased
+    against the reference's CPU results."""
+    g = golden
+    x, w, b = bf(g, "rot_x"), bf(g, "rot_w"), bf(g, "rot_b")
+    for block in (16, 128):
+        got = oq.hadamard_rotate(x, block)
+        want = g[f"rot_x{block}"]
+        assert np.max(np.abs(got - want)) <= 1e-6 * np.max(np.abs(want)) * block
+    for fmt in ("nvfp4", "mxfp4"):
+        cx, sx, ox = oq.quantize_fp4_activations(x, fmt)
+        c = oq.fp4_bias_correction(x, cx, sx, ox, fmt)
+        assert np.array_equal(c, g[f"bc_{fmt}_x"]), fmt
+        q, s, ts = oq.quantize_fp4(w, fmt, unbiased=True)
+        assert np.array_equal(q, g[f"ub_{fmt}_q"]) and np.array_equal(s, g[f"ub_{fmt}_s"])
+        assert np.array_equal(np.asarray(ts, np.float32).reshape(-1), g[f"ub_{fmt}_ts"].reshape(-1)), fmt
+        y = oq.fp4_w4a4_linear(x, q, s, ts, b, fmt=fmt, unbiased=True)
+        assert bf16_close(y, g[f"ub_{fmt}_y"], max_ulps=1, frac=0.99), fmt
+        wrot = bf16_to_f32(f32_to_bf16(oq.hadamard_rotate(w, 16)))
+        q, s, ts = oq.quantize_fp4(wrot, fmt)
+        frac_q = float(np.mean(q == g[f"rot_{fmt}_wq"]))
+        assert frac_q > 0.999, (fmt, frac_q)  # the rotation's last-unit differences can flip a code
+        y = oq.fp4_w4a4_linear(x, g[f"rot_{fmt}_wq"], g[f"rot_{fmt}_ws"], g[f"rot_{fmt}_ts"], b, fmt=fmt, rotate=16)
+        assert bf16_close(y, g[f"rot_{fmt}_y"], max_ulps=2, frac=0.98), fmt
