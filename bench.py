@@ -46,6 +46,7 @@ METRIC = "scaled-GEMM TFLOPS & % block-scaled tensor peak; quantize GB/s & % HBM
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 TRAFFIC_FILE = ROOT / "profiles" / "traffic.json"
 SHAPE: tuple[int, int, int] | None = None  # (M, K, N) override of the w4a4 workload
+ASSEMBLE = "peer"  # w4a4 at N > 1: "peer" (GEMM epilogue stores into every rank's output) or "nccl"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -390,7 +391,9 @@ class Compare(Workload):
 class W4A4Linear(Workload):
     """Config 4: y = fp4_w4a4_linear(x, W) with bias, W [28672, 8192] NVFP4 (tensor scale from
     the whole weight), X [8192, 8192] quantised per token on every step. At N ranks each rank
-    holds N / world output channels of W and the bf16 outputs are all-gathered (NCCL)."""
+    holds N / world output channels of W; the GEMM epilogue writes each tile into every rank's
+    [M, N] output over NVLink (CUDA IPC peer stores, ``--assemble peer``, the default), or the
+    shards are all-gathered by NCCL and reordered (``--assemble nccl``)."""
 
     name = "w4a4"
     unit = "TFLOP/s"
@@ -419,9 +422,18 @@ class W4A4Linear(Workload):
         self.ts = ts
         self.bias = self.bias_full[cols].contiguous()
         self.w_unswizzled = (codes, scales)
-        self.out_local = torch.empty(m, ns, dtype=torch.bfloat16, device=dev)
-        self.out = torch.empty(m, n, dtype=torch.bfloat16, device=dev) if world > 1 else self.out_local
-        self.gathered = torch.empty(world, m, ns, dtype=torch.bfloat16, device=dev) if world > 1 else None
+        self.peers = None
+        if world > 1 and ASSEMBLE == "peer":
+            self.peers = sharded.PeerOutput(m, n, torch.bfloat16, device=dev)
+            self.col0 = cols.start
+            self.out_local = self.peers.buffer[:, cols]
+            self.peer_ptrs = self.peers.peer_ptrs(cols.start)
+            self.out, self.gathered = self.peers.buffer, None
+        else:
+            self.peer_ptrs = None
+            self.out_local = torch.empty(m, ns, dtype=torch.bfloat16, device=dev)
+            self.out = torch.empty(m, n, dtype=torch.bfloat16, device=dev) if world > 1 else self.out_local
+            self.gathered = torch.empty(world, m, ns, dtype=torch.bfloat16, device=dev) if world > 1 else None
         self.flops = 2.0 * m * n * k
         self.units = self.flops / 1e12
         self.kernel = "gemm_kernel<KIND=3 nvf4>"
@@ -433,20 +445,27 @@ class W4A4Linear(Workload):
         self.config = {
             "workload": "config 4: W4A4 NVFP4 linear with bias, X [8192, 8192] x W [28672, 8192]^T -> bf16",
             "m": m, "k": k, "n": n, "step": "NVFP4 activation producer + tcgen05 mxf4nvf4 GEMM with fused epilogue"
-            + (" + NCCL all-gather of the column shards" if world > 1 else ""),
+            + ("" if world == 1 else " storing every tile into all ranks' outputs over NVLink (CUDA IPC),"
+               " ordered by two 1-element NCCL all-reduces" if self.peers is not None
+               else " + NCCL all-gather of the column shards and a reordering copy"),
             "parallelism": f"column-sharded over {world} GPU(s)" if world > 1 else "1 GPU",
             "l2": "inputs larger than L2 (W codes 117 MB, X 134 MB, output 470 MB per step)",
         }
 
     def _gemm(self, xq, xs, outer):
         return self.gemm.nvf4(xq, xs.view(self.torch.uint8), outer, self.wq, self.ws, self.ts, self.bias,
-                              out=self.out_local)
+                              out=self.out_local, peer_out=self.peer_ptrs)
 
     def step(self):
         xq, xs, outer = self.producers.quantize_rows_fp4(self.x, swizzle=True)
-        self._gemm(xq, xs, outer)
-        if self.world > 1:
-            self.sharded.gather_columns(self.out_local, out=self.out, staging=self.gathered)
+        if self.peers is not None:
+            self.peers.barrier()  # every rank has finished reading the previous step's output
+            self._gemm(xq, xs, outer)
+            self.peers.barrier()  # every rank's tiles have landed in every output
+        else:
+            self._gemm(xq, xs, outer)
+            if self.world > 1:
+                self.sharded.gather_columns(self.out_local, out=self.out, staging=self.gathered)
         return 2
 
     def dominant(self):
@@ -461,9 +480,16 @@ class W4A4Linear(Workload):
             y = self.quant.fp4_w4a4_linear(x, self.wq, self.ws, self.ts, self.bias)
         else:
             y = self.sharded.fp4_w4a4_linear_sharded(x, self.wq, self.ws, self.ts, self.bias,
-                                                     out_local=self.out_local, out=self.out, staging=self.gathered)
+                                                     out_local=self.out_local, out=self.out, staging=self.gathered,
+                                                     peers=self.peers)
         self.y_host.copy_(y, non_blocking=True)
         return 2
+
+    def close(self):
+        if self.peers is not None:
+            self.peers.barrier()  # no rank unmaps while another may still store into it
+            self.torch.cuda.synchronize()
+            self.peers.close()
 
     def tensor_peak(self, pk, pk_kind):
         """The dense NVFP4 tensor peak as 4 x the measured bf16 GEMM burst (B200: 9 vs 2.25
@@ -854,10 +880,13 @@ def main() -> int:
     ap.add_argument("--impl", choices=("kab", "reference"), default="kab")
     ap.add_argument("--workload", default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--assemble", choices=("peer", "nccl"), default="peer",
+                    help="w4a4 at N > 1: GEMM epilogue peer stores (CUDA IPC) or an NCCL all-gather")
     ap.add_argument("--shape", default=None,
                     help="M,N,K of the w4a4 / fp8_blockwise workload (default: the config's shape)")
     args = ap.parse_args()
-    global SHAPE
+    global SHAPE, ASSEMBLE
+    ASSEMBLE = args.assemble
     if args.shape:
         m_, n_, k_ = (int(v) for v in args.shape.split(","))
         SHAPE = (m_, k_, n_)

@@ -148,6 +148,15 @@ int kab_gemm_f8(const uint8_t* a, const uint8_t* b, int64_t m, int64_t n, int64_
                 const float* a_scale, const float* b_scale, const void* bias, int bias_dtype,
                 void* out, int out_dtype, int64_t ldo, void* stream);
 
+/* kab_gemm_nvf4 whose epilogue also writes every output tile into `npeers` (<= 7) other
+ * buffers of the same layout (peer_out[p]: the [m, ldo] origin in another rank's output,
+ * mapped by kab_ipc_open) with 16-byte stores over NVLink; columns past n are not written.
+ * The caller orders the peers' uses of those buffers (a barrier before and after). */
+int kab_gemm_nvf4_scatter(const uint8_t* a, const uint8_t* a_sf, const float* a_outer, const uint8_t* b,
+                          const uint8_t* b_sf, const float* b_scale, int b_scale_per_col, int64_t m,
+                          int64_t n, int64_t k, const void* bias, int bias_dtype, void* out, int out_dtype,
+                          int64_t ldo, void* const* peer_out, int npeers, void* stream);
+
 /* MXFP4: packed e2m1 A [m, k / 2], B [n, k / 2] with e8m0 scales per 32 along K (swizzled),
  * applied by the tensor core (kind::mxf4nvf4.block_scale.scale_vec::2X); out = acc * (outer[m]
  * * ts) (+ bias), outer = a_outer[m] or 1 (null: MXFP4 activations), ts = b_scale[0],
@@ -287,6 +296,17 @@ int kab_hadamard_rotate(const void* x, int dtype, int64_t rows, int64_t k, int64
 int kab_fp4_bias_correction(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
                             const uint8_t* codes, const uint8_t* scales, int fmt, int swizzled,
                             const float* outer, int outer_per_row, float* out, void* stream);
+
+/* ------------------------------------------------------------------ peer output buffers */
+
+/* CUDA IPC of a device buffer for the column-sharded GEMM (each rank writes its tiles into
+ * every rank's output over NVLink). kab_ipc_handle: the 64-byte handle of the allocation that
+ * holds `ptr` and ptr's byte offset in it; kab_ipc_open: that allocation mapped into this
+ * process (*base; add the offset); kab_ipc_close: unmaps it. */
+#define KAB_IPC_HANDLE_BYTES 64
+int kab_ipc_handle(const void* ptr, void* handle, int64_t* offset);
+int kab_ipc_open(const void* handle, void** base);
+int kab_ipc_close(void* base);
 
 /* ------------------------------------------------------------------ scale-rule checks */
 

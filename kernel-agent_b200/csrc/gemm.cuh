@@ -27,6 +27,8 @@ namespace kab {
 
 __device__ unsigned g_gemm_status = 0;
 
+constexpr int kMaxPeers = 7;  // peer outputs one GEMM epilogue writes (8 GPUs of a box)
+
 struct GemmArgs {
   int64_t m, n;
   int k_stages;                 // K bytes per row / 128
@@ -45,6 +47,8 @@ struct GemmArgs {
   int out_dtype;
   int64_t ldo;
   int32_t* acc_out;             // KIND 0: raw int32 products [m, ldo] instead of `out`
+  void* peer_out[kMaxPeers];     // other ranks' output origins ([m, ldo] like `out`), or none
+  int npeers;
 };
 
 template <int KIND>
@@ -100,6 +104,7 @@ struct GemmLayout {
   // epilogue staging: 8 warps x 2 buffers x [32 rows, 32 columns]
   static constexpr int kStageOutBytes = 32 * 32 * out_bytes(OUT);
   static constexpr int kStagingBytes = kEpiWarps * 2 * kStageOutBytes;
+  static_assert(kStagingBytes % 1024 == 0, "the operand tiles after the staging tiles need 1024-byte alignment");
   static constexpr int kSmemLimit = 232448;
   static constexpr int kFixed = 1024 + kStagingBytes + 384;
   static constexpr int kStagesFit = (kSmemLimit - kFixed) / kStageBytes;
@@ -170,18 +175,14 @@ __device__ __forceinline__ void epilogue_math(const GemmArgs& g, const uint32_t 
   }
 }
 
-// Writes one row of 32 outputs (this lane's row) into a [32 rows, 32 columns] staging tile.
+// One row of 32 outputs packed in the output type: 32 words (4-byte types) or 16 (2-byte
+// types, rounded to nearest even, two per conversion instruction).
 template <int OUT>
-__device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const uint32_t (&y)[32]) {
+__device__ __forceinline__ void pack_row(const uint32_t (&y)[32], uint32_t (&w)[32]) {
   if constexpr (out_bytes(OUT) == 4) {
-    uint4* p = reinterpret_cast<uint4*>(buf + lane * 128);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int j = (i + lane) & 7;  // rotate the 16-byte chunks: fewer bank conflicts
-      p[j] = make_uint4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
-    }
+    for (int i = 0; i < 32; ++i) w[i] = y[i];
   } else {
-    uint32_t w[16];  // round to nearest even, two per conversion instruction
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const float a = __uint_as_float(y[2 * i]), b = __uint_as_float(y[2 * i + 1]);
@@ -193,11 +194,55 @@ __device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const uint32_t
         w[i] = *reinterpret_cast<const uint32_t*>(&h);
       }
     }
-    uint4* p = reinterpret_cast<uint4*>(buf + lane * 64);
+  }
+}
+
+// Writes one packed row (this lane's row) into a [32 rows, 32 columns] staging tile in the
+// layout of the output tensor map's swizzle (64-byte rows: SWIZZLE_64B, 16-byte chunk i of row
+// r at i ^ ((r >> 1) & 3); 128-byte rows: SWIZZLE_128B, at i ^ (r & 7)), so each quarter-warp
+// phase of the stores covers all 32 banks. The tile must be 1024-byte aligned.
+template <int OUT>
+__device__ __forceinline__ void stage_packed(uint8_t* buf, int lane, const uint32_t (&w)[32]) {
+  constexpr int kChunks = 32 * out_bytes(OUT) / 16;
+  const int sw = kChunks == 8 ? (lane & 7) : ((lane >> 1) & 3);
+  uint4* p = reinterpret_cast<uint4*>(buf + lane * (32 * out_bytes(OUT)));
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int j = (i + lane) & 3;
-      p[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+  for (int i = 0; i < kChunks; ++i) p[i ^ sw] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+}
+
+template <int OUT>
+__device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const uint32_t (&y)[32]) {
+  uint32_t w[32];
+  pack_row<OUT>(y, w);
+  stage_packed<OUT>(buf, lane, w);
+}
+
+// The warp's staged [32 rows, 32 columns] tile (rows row0.., columns col0..; swizzled as
+// stage_packed writes it) stored into every peer output (other GPUs' buffers, mapped by CUDA
+// IPC) over NVLink. Each store instruction covers whole rows' 64 or 128 contiguous bytes
+// (full 32-byte sectors, 8 or 4 rows per instruction): the lanes of a row take its 16-byte
+// chunks. Rows at or past m and columns at or past n are skipped.
+template <int OUT>
+__device__ __forceinline__ void peer_store_tile(const GemmArgs& g, const uint8_t* buf, int lane, int64_t row0,
+                                                int64_t col0) {
+  constexpr int kChunks = 32 * out_bytes(OUT) / 16;  // 16-byte chunks per row: 4 or 8
+  constexpr int kRowsPer = 32 / kChunks;             // rows per instruction: 8 or 4
+  constexpr int kIters = 32 / kRowsPer;
+  constexpr int kPer = 16 / out_bytes(OUT);          // elements per chunk
+  const int c = lane % kChunks;
+  const bool col_ok = col0 + (c + 1) * kPer <= g.n;
+#pragma unroll
+  for (int i = 0; i < kIters; ++i) {
+    const int r = i * kRowsPer + lane / kChunks;
+    const int sw = kChunks == 8 ? (r & 7) : ((r >> 1) & 3);
+    const uint4 v = *reinterpret_cast<const uint4*>(buf + r * (32 * out_bytes(OUT)) + 16 * (c ^ sw));
+    const int64_t row = row0 + r;
+    if (!col_ok || row >= g.m) continue;
+    const int64_t off = (row * g.ldo + col0 + c * kPer) * out_bytes(OUT);
+#pragma unroll
+    for (int p = 0; p < kMaxPeers; ++p) {  // static indices: the parameter array stays in constant memory
+      if (p >= g.npeers) break;
+      *reinterpret_cast<uint4*>(static_cast<uint8_t*>(g.peer_out[p]) + off) = v;
     }
   }
 }
@@ -234,12 +279,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
   constexpr int KS = L::kKSteps;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
+  uint8_t* sOut = smem;  // first: the swizzled staging tiles need 1024-byte alignment
+  uint8_t* sA = sOut + L::kStagingBytes;
   uint8_t* sB = sA + STAGES * L::kABytes;
   uint8_t* sSFA = sB + STAGES * L::kBBytes;
   uint8_t* sSFB = sSFA + STAGES * L::kSfaBytes;
-  uint8_t* sOut = sSFB + STAGES * L::kSfbBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + L::kStagingBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSFB + STAGES * L::kSfbBytes);
   constexpr int SLOTS = L::kSfSlots;
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
@@ -509,13 +554,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
           if (lane == 0) tc::bulk_wait_read<1>();
           __syncwarp();
         }
-        stage_row<OUT>(buf, lane, y);
+        uint32_t w[32];
+        pack_row<OUT>(y, w);
+        stage_packed<OUT>(buf, lane, w);
         tc::fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
           tc::tma_store_2d(&tma_out, buf, colh + c * 32, row0);
           tc::bulk_commit();
         }
+        if (g.npeers > 0) peer_store_tile<OUT>(g, buf, lane, row0, colh + c * 32);
         ++chunk;
         if (c + 1 < HC) tc::tmem_ld_wait();
       }

@@ -1,6 +1,10 @@
-// Library-wide entry points: errors, version, device checks and device status.
+// Library-wide entry points: errors, version, device checks and device status, and the CUDA
+// IPC mapping of an output buffer into the other ranks' address spaces.
+#include <cudaTypedefs.h>
+
 #include "kab_host.h"
 
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -72,6 +76,47 @@ int kab_device_status(unsigned* bits, int clear, void* stream) {
   const cudaError_t e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return kab::fail(KAB_ECUDA, "device status: %s", cudaGetErrorString(e));
   *bits = v;
+  return KAB_OK;
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) == KAB_IPC_HANDLE_BYTES, "IPC handle size");
+
+int kab_ipc_handle(const void* ptr, void* handle, int64_t* offset) {
+  KAB_REQUIRE(ptr != nullptr && handle != nullptr && offset != nullptr, "null pointer");
+  static PFN_cuMemGetAddressRange_v3020 range = nullptr;
+  if (range == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &p, 3020, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return kab::fail(KAB_EUNSUPPORTED, "cuMemGetAddressRange is unavailable");
+    range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return kab::fail(KAB_EINVAL, "not a device allocation");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return kab::fail(KAB_ECUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  memcpy(handle, &h, sizeof h);
+  *offset = static_cast<int64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+  return KAB_OK;
+}
+
+int kab_ipc_open(const void* handle, void** base) {
+  KAB_REQUIRE(handle != nullptr && base != nullptr, "null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof h);
+  const cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return kab::fail(KAB_ECUDA, "cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+  return KAB_OK;
+}
+
+int kab_ipc_close(void* base) {
+  KAB_REQUIRE(base != nullptr, "null pointer");
+  const cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return kab::fail(KAB_ECUDA, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
   return KAB_OK;
 }
 

@@ -56,7 +56,8 @@ int make_map(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols_byt
   return KAB_OK;
 }
 
-// The output [m, n] (row stride ldo elements) written in [32, 32] boxes by TMA stores.
+// The output [m, n] (row stride ldo elements) written in [32, 32] boxes by TMA stores, from
+// staging tiles swizzled at the width of their rows (64 or 128 bytes).
 int make_out_map(CUtensorMap* map, void* ptr, int out, uint64_t m, uint64_t n, uint64_t ldo) {
   auto fn = encode_fn();
   if (fn == nullptr) return fail(KAB_EUNSUPPORTED, "cuTensorMapEncodeTiled is unavailable (driver too old?)");
@@ -69,7 +70,8 @@ int make_out_map(CUtensorMap* map, void* ptr, int out, uint64_t m, uint64_t n, u
   cuuint32_t box[2] = {32, 32};
   cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, dt, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        out_bytes(out) == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(KAB_EINVAL, "tensor map of the output failed (CUresult %d)", static_cast<int>(r));
   return KAB_OK;
@@ -234,6 +236,32 @@ int kab_gemm_nvf4(const uint8_t* a, const uint8_t* a_sf, const float* a_outer, c
                   const uint8_t* b_sf, const float* b_scale, int b_scale_per_col, int64_t m, int64_t n, int64_t k,
                   const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo, void* stream) {
   GemmArgs g = args_of(bias, bias_dtype, out, out_dtype, ldo);
+  KAB_REQUIRE(a_sf != nullptr && b_sf != nullptr && aligned(a_sf, 16) && aligned(b_sf, 16),
+              "block scales are null or not 16-byte aligned");
+  KAB_REQUIRE(a_outer != nullptr && b_scale != nullptr, "outer / tensor scales are null");
+  KAB_REQUIRE(k % 2 == 0, "K must be even");
+  KAB_REQUIRE(bias == nullptr || valid_dtype(bias_dtype), "unknown bias dtype %d", bias_dtype);
+  g.sfa = a_sf;
+  g.sfb = b_sf;
+  g.sfa_ncb = g.sfb_ncb = (k / 16 + 3) / 4;
+  g.a_scale = a_outer;
+  g.b_scale = b_scale;
+  g.b_scale_per_col = b_scale_per_col;
+  return run<3>(a, b, m, n, k / 2, g, out_dtype, as_stream(stream));
+}
+
+int kab_gemm_nvf4_scatter(const uint8_t* a, const uint8_t* a_sf, const float* a_outer, const uint8_t* b,
+                          const uint8_t* b_sf, const float* b_scale, int b_scale_per_col, int64_t m, int64_t n,
+                          int64_t k, const void* bias, int bias_dtype, void* out, int out_dtype, int64_t ldo,
+                          void* const* peer_out, int npeers, void* stream) {
+  KAB_REQUIRE(npeers >= 0 && npeers <= kMaxPeers, "npeers %d not in 0..%d", npeers, kMaxPeers);
+  KAB_REQUIRE(npeers == 0 || peer_out != nullptr, "peer_out is null");
+  GemmArgs g = args_of(bias, bias_dtype, out, out_dtype, ldo);
+  for (int p = 0; p < npeers; ++p) {
+    KAB_REQUIRE(peer_out[p] != nullptr && aligned(peer_out[p], 16), "peer output %d is null or not 16-byte aligned", p);
+    g.peer_out[p] = peer_out[p];
+  }
+  g.npeers = npeers;
   KAB_REQUIRE(a_sf != nullptr && b_sf != nullptr && aligned(a_sf, 16) && aligned(b_sf, 16),
               "block scales are null or not 16-byte aligned");
   KAB_REQUIRE(a_outer != nullptr && b_scale != nullptr, "outer / tensor scales are null");

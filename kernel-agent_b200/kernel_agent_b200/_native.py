@@ -90,6 +90,11 @@ _SIGNATURES: dict[str, list] = {
                       c_void_p, c_int, c_int64, c_void_p],
     "kab_gemm_nvf4": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64,
                       c_int64, c_void_p, c_int, c_void_p, c_int, c_int64, c_void_p],
+    "kab_gemm_nvf4_scatter": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64,
+                              c_int64, c_void_p, c_int, c_void_p, c_int, c_int64, c_void_p, c_int, c_void_p],
+    "kab_ipc_handle": [c_void_p, c_void_p, POINTER(c_int64)],
+    "kab_ipc_open": [c_void_p, POINTER(c_void_p)],
+    "kab_ipc_close": [c_void_p],
     "kab_gemm_mxf4": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64,
                       c_int64, c_void_p, c_int, c_void_p, c_int, c_int64, c_void_p],
     "kab_hadamard_rotate": [c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_void_p, c_void_p],

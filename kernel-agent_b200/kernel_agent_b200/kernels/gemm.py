@@ -9,6 +9,8 @@ k-steps (K a multiple of 128 for 8-bit codes, 256 for FP4) and, block-scaled, N 
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from .. import _native as nat
@@ -102,11 +104,13 @@ def mxf8(a: torch.Tensor, a_sf_swizzled: torch.Tensor, b: torch.Tensor, b_sf_swi
 
 def nvf4(a: torch.Tensor, a_sf_swizzled: torch.Tensor, a_outer: torch.Tensor, b: torch.Tensor,
          b_sf_swizzled: torch.Tensor, b_scale: torch.Tensor, bias=None, out_dtype=torch.bfloat16,
-         out: torch.Tensor | None = None) -> torch.Tensor:
+         out: torch.Tensor | None = None, peer_out: list[int] | None = None) -> torch.Tensor:
     """NVFP4 ``a [M, K/2] @ b [N, K/2]ᵀ`` (packed e2m1) with e4m3 scales per 16 (swizzled)
     applied by the tensor core, then ``acc * (a_outer[m] * b_scale) (+ bias)``; ``b_scale``:
-    one value or one per row of b. K % 256 == 0, N % 128 == 0. ``out``: an optional
-    ``[M, N]`` destination (a column block of a wider buffer: its row stride is used)."""
+    one value or one per row of b. K % 256 == 0. ``out``: an optional ``[M, N]`` destination
+    (a column block of a wider buffer: its row stride is used). ``peer_out``: device addresses
+    (other ranks' buffers mapped by CUDA IPC) of the same block in buffers of the same layout,
+    which the epilogue also writes over NVLink."""
     _bind()
     m, n, k = a.shape[0], b.shape[0], 2 * a.shape[1]
     if k % 256:
@@ -123,10 +127,14 @@ def nvf4(a: torch.Tensor, a_sf_swizzled: torch.Tensor, a_outer: torch.Tensor, b:
     per_col = int(ts.numel() > 1)
     if per_col and ts.numel() != n:
         raise ValueError(f"b_scale has {ts.numel()} values, expected 1 or {n}")
-    nat.call("kab_gemm_nvf4", a.contiguous().data_ptr(), a_sf_swizzled.data_ptr(),
-             a_outer.float().contiguous().data_ptr(), b.contiguous().data_ptr(), b_sf_swizzled.data_ptr(),
-             ts.data_ptr(), per_col, m, n, k, nat.ptr(bb), bcode, out.data_ptr(), code, out.stride(0),
-             nat.stream_of(a))
+    args = (a.contiguous().data_ptr(), a_sf_swizzled.data_ptr(), a_outer.float().contiguous().data_ptr(),
+            b.contiguous().data_ptr(), b_sf_swizzled.data_ptr(), ts.data_ptr(), per_col, m, n, k, nat.ptr(bb), bcode,
+            out.data_ptr(), code, out.stride(0))
+    if peer_out:
+        arr = (ctypes.c_void_p * len(peer_out))(*peer_out)
+        nat.call("kab_gemm_nvf4_scatter", *args, arr, len(peer_out), nat.stream_of(a))
+    else:
+        nat.call("kab_gemm_nvf4", *args, nat.stream_of(a))
     return out
 
 

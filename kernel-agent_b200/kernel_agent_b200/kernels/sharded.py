@@ -10,11 +10,17 @@ The reference has no collectives: its toolkit runs one linear on one device
 * X is replicated and quantised per rank (identical codes on every rank); each rank runs its
   GEMM into ``[M, N / g]`` and the bf16 shards are all-gathered and laid out as ``[M, N]``.
 
-Collectives go through ``torch.distributed`` (NCCL on GPUs; gloo works for the host logic).
+Two ways to assemble the output: :func:`gather_columns` (an NCCL all-gather of the shards and
+one reordering copy), or :class:`PeerOutput` (fused: every rank's GEMM epilogue writes its
+tiles straight into every rank's ``[M, N]`` buffer over NVLink, through CUDA IPC mappings, so
+the transfer overlaps the math and no reorder is needed; two tiny all-reduces order the
+buffer's uses). Collectives go through ``torch.distributed`` (NCCL on GPUs; gloo works for
+the host logic).
 """
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -95,13 +101,60 @@ def gather_columns(local: torch.Tensor, group=None, out: torch.Tensor | None = N
     return out
 
 
+class PeerOutput:
+    """A ``[M, N]`` output buffer on every rank of ``group``, each mapped into every other
+    rank's address space (CUDA IPC), for GEMM epilogues that write their column shard into all
+    of them. ``peer_ptrs(col0)``: the device addresses of column ``col0`` in the other ranks'
+    buffers (rank order, this rank skipped). :meth:`close` unmaps them."""
+
+    def __init__(self, m: int, n: int, dtype: torch.dtype = torch.bfloat16, device=None, group=None):
+        world, rank = _world(group)
+        self.group, self.world, self.rank = group, world, rank
+        self.buffer = torch.empty(m, n, dtype=dtype, device=device)
+        self._bases: list[int] = []
+        self._offsets: list[int] = []
+        if world == 1:
+            return
+        handle = (ctypes.c_uint8 * 64)()
+        offset = ctypes.c_int64(0)
+        nat.call("kab_ipc_handle", self.buffer.data_ptr(), handle, ctypes.byref(offset))
+        mine = (bytes(handle), int(offset.value))
+        everyone: list = [None] * world
+        dist.all_gather_object(everyone, mine, group=group)
+        for r, (h, off) in enumerate(everyone):
+            if r == rank:
+                continue
+            base = ctypes.c_void_p(0)
+            nat.call("kab_ipc_open", (ctypes.c_uint8 * 64).from_buffer_copy(h), ctypes.byref(base))
+            self._bases.append(int(base.value))
+            self._offsets.append(off)
+        self._sync = torch.zeros(1, dtype=torch.float32, device=self.buffer.device)
+
+    def peer_ptrs(self, col0: int = 0) -> list[int]:
+        step = self.buffer.element_size() * col0
+        return [b + off + step for b, off in zip(self._bases, self._offsets)]
+
+    def barrier(self) -> None:
+        """Every rank's work on its stream up to here is done before anyone goes on (one
+        1-element all-reduce on the current stream)."""
+        if self.world > 1:
+            dist.all_reduce(self._sync, group=self.group)
+
+    def close(self) -> None:
+        for b in self._bases:
+            nat.call("kab_ipc_close", ctypes.c_void_p(b))
+        self._bases, self._offsets = [], []
+
+
 def fp4_w4a4_linear_sharded(x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor, tensor_scale,
                             bias: torch.Tensor | None = None, group=None, *, out_local: torch.Tensor | None = None,
-                            out: torch.Tensor | None = None, staging: torch.Tensor | None = None) -> torch.Tensor:
+                            out: torch.Tensor | None = None, staging: torch.Tensor | None = None,
+                            peers: PeerOutput | None = None) -> torch.Tensor:
     """``fp4_w4a4_linear`` with this rank's shard of the weight (``codes [N / g, K / 2]``,
     ``scales`` its ``[N / g, K / 16]`` block scales or their swizzled flat form, the whole
     weight's ``tensor_scale``, ``bias`` this shard's ``[N / g]``): the full ``[..., N]``
-    output on every rank."""
+    output on every rank. ``peers``: the fused path (the epilogue writes the shard into every
+    rank's ``peers.buffer``, which is returned); else an all-gather of the shards."""
     nat.require_cuda(x, codes)
     k = x.shape[-1]
     if k % 16:
@@ -112,6 +165,14 @@ def fp4_w4a4_linear_sharded(x: torch.Tensor, codes: torch.Tensor, scales: torch.
     ws = q._swizzled(scales, ns, k // 16)
     ts = torch.as_tensor(tensor_scale, dtype=torch.float32, device=x2.device)
     odt = x.dtype if x.dtype in (torch.bfloat16, torch.float16, torch.float32) else torch.float32
-    y = gemm.nvf4(xq, xs.view(torch.uint8), outer, codes, ws, ts, bias, out_dtype=odt, out=out_local)
-    full = gather_columns(y, group, out=out, staging=staging)
+    if peers is not None:
+        col0 = peers.rank * ns
+        peers.barrier()  # the other ranks are done with the buffers' previous contents
+        gemm.nvf4(xq, xs.view(torch.uint8), outer, codes, ws, ts, bias, out_dtype=odt,
+                  out=peers.buffer[:, col0:col0 + ns], peer_out=peers.peer_ptrs(col0))
+        peers.barrier()  # every rank's shard has landed in every buffer
+        full = peers.buffer
+    else:
+        y = gemm.nvf4(xq, xs.view(torch.uint8), outer, codes, ws, ts, bias, out_dtype=odt, out=out_local)
+        full = gather_columns(y, group, out=out, staging=staging)
     return full.reshape(*x.shape[:-1], full.shape[-1])

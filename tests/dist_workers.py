@@ -85,3 +85,36 @@ def w4a4_body(rank: int, world: int):
     y = sharded.fp4_w4a4_linear_sharded(x.to(dev), codes, scales, ts, b[cols].to(dev))
     y_full = quant.fp4_w4a4_linear(x.to(dev), fc, fs, fts, b.to(dev))
     return [same_codes, same_ts, bool(torch.equal(y, y_full)), float((y.float() - y_full.float()).abs().max())]
+
+
+def w4a4_fused_body(rank: int, world: int):
+    """The fused path: each rank's GEMM epilogue writes its column shard into every rank's
+    output (CUDA IPC). Two calls on one buffer (the second after the output changed), with M
+    not a multiple of the 128-row tile; each must equal the one-GPU linear bit for bit."""
+    import torch
+
+    from kernel_agent_b200 import workloads
+    from kernel_agent_b200.kernels import quant, sharded
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    m, k, n = 200, 1024, 1536
+    x, w, b = workloads.config4(seed=5, device="cpu", m=m, k=k, n=n)
+    cols = sharded.shard_columns(n, world, rank)
+    codes, scales, ts = sharded.quantize_fp4_weight_shard(w[cols].to(dev))
+    fc, fs, fts = quant.quantize_fp4(w.to(dev))
+    peers = sharded.PeerOutput(m, n, torch.bfloat16, device=dev)
+    results = []
+    try:
+        for scale in (1.0, -0.5):
+            xs = (x * scale).to(dev)
+            y = sharded.fp4_w4a4_linear_sharded(xs, codes, scales, ts, b[cols].to(dev), peers=peers)
+            y_full = quant.fp4_w4a4_linear(xs, fc, fs, fts, b.to(dev))
+            torch.cuda.synchronize()
+            results.append(bool(torch.equal(y, y_full)))
+            results.append(float((y.float() - y_full.float()).abs().max()))
+        peers.barrier()  # nobody unmaps while another rank may still write
+        torch.cuda.synchronize()
+    finally:
+        peers.close()
+    return results

@@ -17,3 +17,12 @@ def test_w4a4_sharded_matches_one_gpu():
     for same_codes, same_ts, same_y, max_diff in run_ranks("w4a4_body", world=2, backend="nccl", timeout=300):
         assert same_codes and same_ts
         assert same_y, max_diff
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_w4a4_fused_peer_stores_match_one_gpu():
+    """The GEMM epilogue writes every rank's shard straight into every rank's output (CUDA IPC
+    over NVLink): the full output equals the one-GPU linear, on two successive calls."""
+    for eq1, d1, eq2, d2 in run_ranks("w4a4_fused_body", world=2, backend="nccl", timeout=300):
+        assert eq1, d1
+        assert eq2, d2
