@@ -270,6 +270,68 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
   nt = r / gm;
 }
 
+// One epilogue warp's share of a finished accumulator tile: rows row0 + lane (its TMEM lane
+// quarter), HC chunks of 32 columns from colh, read from TMEM at tbase. Each chunk is scaled
+// (epilogue_math), staged in shared memory, stored by TMA (and to the peer outputs); `release`
+// runs (lane 0, after a warp sync) once the last chunk has been read from TMEM.
+template <int KIND, int OUT, int HC, class Release>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& g, const CUtensorMap* tma_out, uint32_t tbase, int row0,
+                                              int colh, uint8_t* stage0, int& chunk, int lane, Release release) {
+  constexpr int kStageOutBytes = 32 * 32 * out_bytes(OUT);
+  const int64_t row = static_cast<int64_t>(row0) + lane;
+  // this tile's row scale and (lane i of chunk c) column scale / bias, loaded once
+  float sa = 0.0f;
+  if constexpr (KIND == 4) sa = g.a_scale == nullptr ? 1.0f : (row < g.m ? __ldg(g.a_scale + row) : 0.0f);
+  else if constexpr (KIND != 2 && OUT != kOutI32) sa = row < g.m ? __ldg(g.a_scale + row) : 0.0f;
+  float cs[HC], cbv[HC];
+#pragma unroll
+  for (int c = 0; c < HC; ++c) {
+    const int64_t col = static_cast<int64_t>(colh) + c * 32 + lane;
+    cs[c] = 0.0f;
+    cbv[c] = 0.0f;
+    if constexpr (OUT != kOutI32) {
+      if constexpr (KIND == 0 || KIND == 1) cs[c] = col < g.n ? __ldg(g.b_scale + col) : 0.0f;
+      if constexpr (KIND == 3 || KIND == 4) {
+        if (KIND == 4 && g.b_scale == nullptr) cs[c] = 1.0f;
+        else cs[c] = g.b_scale_per_col ? (col < g.n ? __ldg(g.b_scale + col) : 0.0f) : __ldg(g.b_scale);
+      }
+      if (g.bias != nullptr && col < g.n) cbv[c] = load_bias(g.bias, g.bias_dtype, col);
+    }
+  }
+  uint32_t r[32];
+  tc::tmem_ld32(tbase, r);
+  tc::tmem_ld_wait();
+#pragma unroll
+  for (int c = 0; c < HC; ++c) {
+    uint32_t y[32];
+    epilogue_math<KIND, OUT>(g, r, sa, cs[c], cbv[c], y);
+    if (c + 1 < HC) {
+      tc::tmem_ld32(tbase + (c + 1) * 32, r);
+    } else {  // this warp's columns are read: hand the accumulator back to the MMA warp
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) release();
+    }
+    uint8_t* buf = stage0 + (chunk & 1) * kStageOutBytes;
+    if (chunk >= 2) {  // the store two chunks ago has finished reading this buffer
+      if (lane == 0) tc::bulk_wait_read<1>();
+      __syncwarp();
+    }
+    uint32_t w[32];
+    pack_row<OUT>(y, w);
+    stage_packed<OUT>(buf, lane, w);
+    tc::fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+      tc::tma_store_2d(tma_out, buf, colh + c * 32, row0);
+      tc::bulk_commit();
+    }
+    if (g.npeers > 0) peer_store_tile<OUT>(g, buf, lane, row0, colh + c * 32);
+    ++chunk;
+    if (c + 1 < HC) tc::tmem_ld_wait();
+  }
+}
+
 template <int KIND, int BN, int BKB, int OUT>
 __global__ void __launch_bounds__(GemmLayout<KIND, BN, BKB, OUT>::kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
@@ -513,60 +575,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       }
       tc::fence_after_sync();
       const int row0 = mt * 128 + 32 * quarter;
-      const int64_t row = static_cast<int64_t>(row0) + lane;
       const int colh = nt * BN + half * (BN / 2);
       const uint32_t tbase = tmem + lane_base + ab * BN + half * (BN / 2);
-      // this tile's row scale and (lane i of chunk c) column scale / bias, loaded once
-      float sa = 0.0f;
-      if constexpr (KIND == 4) sa = g.a_scale == nullptr ? 1.0f : (row < g.m ? __ldg(g.a_scale + row) : 0.0f);
-      else if constexpr (KIND != 2 && OUT != kOutI32) sa = row < g.m ? __ldg(g.a_scale + row) : 0.0f;
-      float cs[HC], cbv[HC];
-#pragma unroll
-      for (int c = 0; c < HC; ++c) {
-        const int64_t col = static_cast<int64_t>(colh) + c * 32 + lane;
-        cs[c] = 0.0f;
-        cbv[c] = 0.0f;
-        if constexpr (OUT != kOutI32) {
-          if constexpr (KIND == 0 || KIND == 1) cs[c] = col < g.n ? __ldg(g.b_scale + col) : 0.0f;
-          if constexpr (KIND == 3 || KIND == 4) {
-            if (KIND == 4 && g.b_scale == nullptr) cs[c] = 1.0f;
-            else cs[c] = g.b_scale_per_col ? (col < g.n ? __ldg(g.b_scale + col) : 0.0f) : __ldg(g.b_scale);
-          }
-          if (g.bias != nullptr && col < g.n) cbv[c] = load_bias(g.bias, g.bias_dtype, col);
-        }
-      }
-      uint32_t r[32];
-      tc::tmem_ld32(tbase, r);
-      tc::tmem_ld_wait();
-#pragma unroll
-      for (int c = 0; c < HC; ++c) {
-        uint32_t y[32];
-        epilogue_math<KIND, OUT>(g, r, sa, cs[c], cbv[c], y);
-        if (c + 1 < HC) {
-          tc::tmem_ld32(tbase + (c + 1) * 32, r);
-        } else {  // this warp's columns are read: hand the accumulator back to the MMA warp
-          tc::fence_before_sync();
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(&acc_empty[ab]);
-        }
-        uint8_t* buf = stage0 + (chunk & 1) * L::kStageOutBytes;
-        if (chunk >= 2) {  // the store two chunks ago has finished reading this buffer
-          if (lane == 0) tc::bulk_wait_read<1>();
-          __syncwarp();
-        }
-        uint32_t w[32];
-        pack_row<OUT>(y, w);
-        stage_packed<OUT>(buf, lane, w);
-        tc::fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) {
-          tc::tma_store_2d(&tma_out, buf, colh + c * 32, row0);
-          tc::bulk_commit();
-        }
-        if (g.npeers > 0) peer_store_tile<OUT>(g, buf, lane, row0, colh + c * 32);
-        ++chunk;
-        if (c + 1 < HC) tc::tmem_ld_wait();
-      }
+      uint64_t* release_bar = &acc_empty[ab];
+      epilogue_tile<KIND, OUT, HC>(g, &tma_out, tbase, row0, colh, stage0, chunk, lane,
+                                   [release_bar] { tc::mbar_arrive(release_bar); });
       if (++ab == L::kAccBufs) { ab = 0; aph ^= 1u; }
     }
     if (lane == 0) tc::bulk_wait_all();

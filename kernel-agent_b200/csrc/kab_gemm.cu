@@ -2,10 +2,12 @@
 // the persistent launch, and this translation unit's device status word.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm.cuh"
 #include "gemm_blockwise.cuh"
+#include "gemm_pair.cuh"
 #include "kab_host.h"
 
 namespace kab {
@@ -108,6 +110,77 @@ int launch_out(int out, const CUtensorMap& ma, const CUtensorMap& mb, const CUte
   return launch_one<KIND, BN, BKB, KAB_F32>(ma, mb, mo, g, s);
 }
 
+// A swizzled block-scale tensor of `bytes` bytes as [bytes / 256, 256] read in boxes of
+// `box_rows` rows (one stage's chunk of one 128-row block), no swizzle.
+int make_sf_map(CUtensorMap* map, const void* ptr, uint64_t bytes, uint32_t box_rows, const char* name) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(KAB_EUNSUPPORTED, "cuTensorMapEncodeTiled is unavailable (driver too old?)");
+  cuuint64_t dims[2] = {256, bytes / 256};
+  cuuint64_t strides[1] = {256};
+  cuuint32_t box[2] = {256, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KAB_EINVAL, "tensor map of %s failed (CUresult %d)", name, static_cast<int>(r));
+  return KAB_OK;
+}
+
+// The CTA-pair kernel (gemm_pair.cuh): one cluster of 2 per SM pair, as many pairs as can be
+// resident at once (persistent), at most one per tile.
+template <int KIND, int OUT>
+int launch_pair_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& msa, const CUtensorMap& msb,
+                    const CUtensorMap& mo, const GemmArgs& g, cudaStream_t s) {
+  using L = PairLayout<KIND, OUT>;
+  auto kernel = gemm_pair_kernel<KIND, OUT>;
+  static int pairs_of[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int pairs = dev < 64 ? pairs_of[dev] : 0;
+  if (pairs == 0) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem) != cudaSuccess)
+      return fail(KAB_ECUDA, "cannot set %d bytes of shared memory", L::kSmem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (sm_count() / 2));
+    cfg.blockDim = dim3(L::kThreads);
+    cfg.dynamicSmemBytes = L::kSmem;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1) {
+      cudaGetLastError();
+      clusters = sm_count() / 2;
+    }
+    pairs = clusters;
+    if (dev < 64) pairs_of[dev] = pairs;
+  }
+  const int tiles = g.m_tiles * g.n_tiles;
+  const int grid = 2 * (tiles < pairs ? tiles : pairs);
+  kernel<<<grid, L::kThreads, L::kSmem, s>>>(ma, mb, msa, msb, mo, g);
+  return check_launch("gemm pair kernel");
+}
+
+template <int KIND>
+int launch_pair(int out, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& msa, const CUtensorMap& msb,
+                const CUtensorMap& mo, const GemmArgs& g, cudaStream_t s) {
+  if constexpr (KIND == 0) {
+    if (out == kOutI32) return launch_pair_one<KIND, kOutI32>(ma, mb, msa, msb, mo, g, s);
+  }
+  if (out == KAB_BF16) return launch_pair_one<KIND, KAB_BF16>(ma, mb, msa, msb, mo, g, s);
+  if (out == KAB_F16) return launch_pair_one<KIND, KAB_F16>(ma, mb, msa, msb, mo, g, s);
+  return launch_pair_one<KIND, KAB_F32>(ma, mb, msa, msb, mo, g, s);
+}
+
+// KAB_GEMM_PAIR=1 routes shapes with M > 128 and N >= 256 to the CTA-pair kernel. Off by
+// default: on B200 it measured 2.96 PFLOP/s on NVFP4 8192^3 against 3.66 for the one-CTA
+// kernel (its tcgen05.cp scale copies share the tensor pipe with the MMAs, ~44 cycles each,
+// 12 per stage, and without them the pair is still feed-limited at ~3.35).
+bool pair_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("KAB_GEMM_PAIR");
+    return v != nullptr && v[0] == '1';
+  }();
+  return on;
+}
+
 // Common checks and launch: a [m, k_bytes] and b [n, k_bytes] K-major byte matrices.
 template <int KIND>
 int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, GemmArgs g, int out_dtype,
@@ -127,9 +200,36 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
   KAB_REQUIRE(g.ldo >= n && g.ldo % 8 == 0, "ldo %lld must be >= n and a multiple of 8", (long long)g.ldo);
   KAB_REQUIRE(aligned(out, 16), "output must be 16-byte aligned");
   KAB_REQUIRE(m <= (int64_t(1) << 30) && n <= (int64_t(1) << 30), "shape too large");
-  // tile width: 256 (two 256-column accumulators) for int8 / fp8; the block-scaled kinds keep
-  // room for their scale-factor ring next to two accumulators: 192 unless that pads N by more
-  // than 1/16, else 128
+  // 256 x 256 tiles on SM pairs when there are at least two 128-row blocks of A and padding N
+  // to 256 costs at most 1/16 more columns
+  const int64_t pad256 = (n + 255) / 256 * 256 - n;
+  if (pair_enabled() && m > 128 && n >= 256 && pad256 * 16 <= n) {
+    g.m = m;
+    g.n = n;
+    g.k_stages = static_cast<int>(k_bytes / bkb);
+    g.m_tiles = static_cast<int>((m + 255) / 256);
+    g.n_tiles = static_cast<int>((n + 255) / 256);
+    g.group_n = n > m && g.m_tiles > 4 ? 16 : 0;
+    g.sfb_chunks = (n + 127) / 128;
+    CUtensorMap ma, mb, msa, msb, mo;
+    if (int e = make_map(&ma, a, m, k_bytes, k_bytes, 128, bkb, "A")) return e;
+    if (int e = make_map(&mb, b, n, k_bytes, k_bytes, 128, bkb, "B")) return e;
+    if (int e = make_out_map(&mo, out, out_dtype, m, n, g.ldo)) return e;
+    msa = ma;
+    msb = mb;
+    if constexpr (GemmTraits<KIND>::kScaled) {
+      constexpr uint32_t rows = PairLayout<KIND, KAB_BF16>::kSfRows;
+      const uint64_t a_blocks = static_cast<uint64_t>((m + 127) / 128);
+      if (int e = make_sf_map(&msa, g.sfa, a_blocks * g.sfa_ncb * 512, rows, "A's block scales")) return e;
+      if (int e = make_sf_map(&msb, g.sfb, static_cast<uint64_t>(g.sfb_chunks) * g.sfb_ncb * 512, rows,
+                              "B's block scales"))
+        return e;
+    }
+    return launch_pair<KIND>(out_dtype, ma, mb, msa, msb, mo, g, s);
+  }
+  // one-CTA tiles, width 256 (two 256-column accumulators) for int8 / fp8; the block-scaled
+  // kinds keep room for their scale-factor ring next to two accumulators: 192 unless that pads
+  // N by more than 1/16, else 128
   int bn;
   if (!GemmTraits<KIND>::kScaled) {
     bn = n >= 256 ? 256 : 128;
