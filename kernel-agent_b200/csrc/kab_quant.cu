@@ -72,6 +72,29 @@ void launch_fp4(int maxc, unsigned rows, int threads, cudaStream_t s, const void
   }
 #undef KAB_FP4
 }
+template <int T, int F, int M>
+void launch_fp4_fast_nb(int maxc, unsigned rows, int threads, cudaStream_t s, const void* x, int64_t ldx, int64_t k,
+                        const float* amax, const float* ts, int swizzle, uint8_t* q, uint8_t* scales, float* outer) {
+  constexpr int kNbMax = F == 0 ? 4 : 2;
+  if (maxc == 1) quant_fp4_fast_kernel<T, 1, F, M><<<rows, threads, 0, s>>>(x, ldx, k, amax, ts, swizzle, q, scales, outer);
+  else if (maxc == 2) quant_fp4_fast_kernel<T, 2, F, M><<<rows, threads, 0, s>>>(x, ldx, k, amax, ts, swizzle, q, scales, outer);
+  else quant_fp4_fast_kernel<T, kNbMax, F, M><<<rows, threads, 0, s>>>(x, ldx, k, amax, ts, swizzle, q, scales, outer);
+}
+template <int T>
+void launch_fp4_fast(int fmt, int mode, int maxc, unsigned rows, int threads, cudaStream_t s, const void* x,
+                     int64_t ldx, int64_t k, const float* amax, const float* ts, int swizzle, uint8_t* q,
+                     uint8_t* scales, float* outer) {
+#define KAB_FP4F(F, M) launch_fp4_fast_nb<T, F, M>(maxc, rows, threads, s, x, ldx, k, amax, ts, swizzle, q, scales, outer)
+  if (fmt == KAB_NVFP4) {
+    if (mode == KAB_FP4_TOKEN) KAB_FP4F(0, 0);
+    else if (mode == KAB_FP4_TENSOR) KAB_FP4F(0, 1);
+    else KAB_FP4F(0, 2);
+  } else {
+    if (mode == KAB_FP4_WEIGHT) KAB_FP4F(1, 2);
+    else KAB_FP4F(1, 0);
+  }
+#undef KAB_FP4F
+}
 template <int T, bool SILU>
 void launch_fp4_fmt(int fmt, int mode, int maxc, unsigned rows, int threads, cudaStream_t s,
                     const void* x, int64_t ldx, const void* up, int64_t ldu, int64_t nrows,
@@ -247,8 +270,8 @@ int kab_quant_fp4(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx
     if (dtype == KAB_BF16) launch_fp4_fmt<kBF16, true>(fmt, mode, maxc, grid, threads, s, x, ldx, up, ldu, rows, k, amax, tensor_scale, swizzle, q, scales, outer, h);
     else launch_fp4_fmt<kF16, true>(fmt, mode, maxc, grid, threads, s, x, ldx, up, ldu, rows, k, amax, tensor_scale, swizzle, q, scales, outer, h);
   } else {
-    if (dtype == KAB_BF16) launch_fp4_fmt<kBF16, false>(fmt, mode, maxc, grid, threads, s, x, ldx, nullptr, 0, rows, k, amax, tensor_scale, swizzle, q, scales, outer, nullptr);
-    else if (dtype == KAB_F16) launch_fp4_fmt<kF16, false>(fmt, mode, maxc, grid, threads, s, x, ldx, nullptr, 0, rows, k, amax, tensor_scale, swizzle, q, scales, outer, nullptr);
+    if (dtype == KAB_BF16) launch_fp4_fast<kBF16>(fmt, mode, maxc, grid, threads, s, x, ldx, k, amax, tensor_scale, swizzle, q, scales, outer);
+    else if (dtype == KAB_F16) launch_fp4_fast<kF16>(fmt, mode, maxc, grid, threads, s, x, ldx, k, amax, tensor_scale, swizzle, q, scales, outer);
     else launch_fp4_fmt<kF32, false>(fmt, mode, maxc, grid, threads, s, x, ldx, nullptr, 0, rows, k, amax, tensor_scale, swizzle, q, scales, outer, nullptr);
   }
   return check_launch("kab_quant_fp4");

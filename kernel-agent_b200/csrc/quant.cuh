@@ -421,6 +421,146 @@ quant_fp4_kernel(const void* __restrict__ x, int64_t ldx, const void* __restrict
   }
 }
 
+// Lean NVFP4 / MXFP4 producer for bf16 / fp16 inputs without the SiLU gate: the codes and
+// scales of quant_fp4_kernel (the same block scale, the same quotient RN(v * y) with the same
+// exactness window and IEEE-division fallback, the same e2m1 conversion), in fewer
+// instructions per element:
+//  * the row is kept as packed 16-bit pairs; block maxima come from __vmaxu2 on |pairs|
+//    (non-negative bf16 / fp16 values order like their bit patterns, NaN above inf);
+//  * two quotients per mul.rn.f32x2;
+//  * the window test "(bits + 16) mod 2^21 <= 32" is bits * 2^11 + 2^15 (mod 2^32) < 33 * 2^11,
+//    one IMAD, folded over the block with a running unsigned min.
+template <int T>
+__device__ __forceinline__ float half_bits_to_float(uint32_t h) {
+  if constexpr (T == kBF16) return __uint_as_float(h << 16);
+  else return __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float b) {
+  unsigned long long r;
+  const unsigned long long av = (static_cast<unsigned long long>(__float_as_uint(a.y)) << 32) | __float_as_uint(a.x);
+  const unsigned long long bv = (static_cast<unsigned long long>(__float_as_uint(b)) << 32) | __float_as_uint(b);
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(av), "l"(bv));
+  return make_float2(__uint_as_float(static_cast<uint32_t>(r)), __uint_as_float(static_cast<uint32_t>(r >> 32)));
+}
+template <int T>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  if constexpr (T == kBF16) return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+  else return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+template <int T, int NB, int FMT, int MODE>
+__global__ void __launch_bounds__(512)
+quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const float* __restrict__ amax_in,
+                      const float* __restrict__ ts_in, int swizzle, uint8_t* __restrict__ q,
+                      uint8_t* __restrict__ scales, float* __restrict__ outer_out) {
+  __shared__ float red[32];
+  constexpr int BLOCK = FMT == 0 ? 16 : 32;
+  constexpr int W = BLOCK / 2;  // packed words per block
+  constexpr uint32_t kHalfInf = T == kBF16 ? 0x7F80u : 0x7C00u;
+  const int64_t row = blockIdx.x;
+  const int nblk = static_cast<int>(k / BLOCK);
+  const uint4* xr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + row * ldx);
+  uint32_t w[NB][W];
+  uint32_t bm[NB];  // |max| of each block as a 16-bit pattern
+  uint32_t am = 0;
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    const int bi = threadIdx.x + b * blockDim.x;
+    uint32_t m = 0;
+    if (bi < nblk) {
+#pragma unroll
+      for (int c = 0; c < W / 4; ++c) {
+        const uint4 r = __ldg(xr + static_cast<int64_t>(bi) * (W / 4) + c);
+        w[b][4 * c] = r.x;
+        w[b][4 * c + 1] = r.y;
+        w[b][4 * c + 2] = r.z;
+        w[b][4 * c + 3] = r.w;
+      }
+#pragma unroll
+      for (int j = 0; j < W; ++j) m = __vmaxu2(m, w[b][j] & 0x7FFF7FFFu);
+    } else {
+#pragma unroll
+      for (int j = 0; j < W; ++j) w[b][j] = 0;
+    }
+    bm[b] = max(m & 0xFFFFu, m >> 16);
+    am = max(am, bm[b]);
+  }
+  float s_outer = 1.0f;
+  if constexpr (FMT == 0) {
+    if constexpr (MODE == 0) {
+      const float amax = block_amax(half_bits_to_float<T>(am), red);
+      s_outer = amax > 0.0f ? __fmul_rn(amax, kNvfp4OuterStep) : 1.0f;  // quant.py:1104
+    } else if constexpr (MODE == 1) {
+      const float a = *amax_in;
+      s_outer = a > 0.0f ? __fmul_rn(a, kNvfp4OuterStep) : 1.0f;
+    } else {
+      s_outer = *ts_in;
+    }
+  }
+  if (threadIdx.x == 0 && outer_out != nullptr) outer_out[row] = s_outer;
+  const Divisor by6(__fmul_rn(s_outer, 6.0f));
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    const int bi = threadIdx.x + b * blockDim.x;
+    if (bi >= nblk) continue;
+    const float bmax = half_bits_to_float<T>(bm[b]);
+    uint32_t sbyte;
+    float step;
+    if constexpr (FMT == 0) {
+      const float bmv[1] = {bmax};
+      float ratio[1];
+      quotients<kLowE4m3>(bmv, by6, ratio);
+      sbyte = e4m3_byte(ratio[0]);
+      step = __fmul_rn(e4m3_value_hw(static_cast<uint8_t>(sbyte)), s_outer);
+    } else {
+      const int e = MODE == 2 ? mxfp4_weight_exponent(bmax) : mxfp4_act_exponent(bmax);
+      sbyte = static_cast<uint32_t>(e + 127);
+      step = e8m0_value(static_cast<uint8_t>(sbyte));
+    }
+    const float div = (MODE == 2 && step < 1e-38f) ? 1e-38f : step;
+    uint32_t packed[BLOCK / 8];
+#pragma unroll
+    for (int c = 0; c < BLOCK / 8; ++c) packed[c] = 0;
+    if (step > 0.0f) {
+      const Divisor d(div);
+      float t[BLOCK];
+      uint32_t mn = d.fast ? 0xFFFFFFFFu : 0u;
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        const float2 p = mul2_rn(unpack2<T>(w[b][j]), d.y);
+        t[2 * j] = p.x;
+        t[2 * j + 1] = p.y;
+        mn = min(mn, __float_as_uint(p.x) * 2048u + 32768u);
+        mn = min(mn, __float_as_uint(p.y) * 2048u + 32768u);
+      }
+      if (mn < 33u * 2048u) {  // near an e2m1 decision point (or no fast reciprocal): divide
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          const float2 v = unpack2<T>(w[b][j]);
+          t[2 * j] = __fdiv_rn(v.x, d.s);
+          t[2 * j + 1] = __fdiv_rn(v.y, d.s);
+        }
+      }
+      if (bm[b] > kHalfInf) {  // a NaN in the block: its codes are 0
+#pragma unroll
+        for (int j = 0; j < BLOCK; ++j) t[j] = t[j] == t[j] ? t[j] : 0.0f;
+      }
+#pragma unroll
+      for (int c = 0; c < BLOCK / 8; ++c) {
+        float e8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) e8[j] = t[c * 8 + j];
+        packed[c] = e2m1x8(e8);
+      }
+    }
+    uint8_t* dst = q + row * (k >> 1) + static_cast<int64_t>(bi) * (BLOCK / 2);
+    if constexpr (BLOCK == 16) *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    const int64_t off = swizzle ? scale_offset_swizzled(row, bi, nblk) : row * nblk + bi;
+    scales[off] = static_cast<uint8_t>(sbyte);
+  }
+}
+
 // ------------------------------------------------------------------ global amax
 
 // NaN-keeping max |x| of a [rows, k] matrix into *out (which holds 0 before the launch):
