@@ -10,15 +10,17 @@
 //  * attention_fp8_kernel: one CTA per 128-query tile. Warp 0 loads Q once and K / V^T tiles
 //    of 128 keys through a 3-stage TMA ring; warp 1 issues the tcgen05 MMAs (kind::f8f6f4):
 //    S_j = Q K_j^T into one of two 128-column TMEM buffers, then O += P_j V_j into a third;
-//    warps 2-5 (one query row per thread) run the online softmax in the exp2 domain: the
-//    running max, the row sum of the unrounded P, P quantised to e4m3 and written into shared
-//    memory in the 128-byte swizzled layout the MMA reads, and the rescaling of O in TMEM
-//    when a row's max grows (after the previous P V has landed). The final O is divided by
-//    448 * rowsum, multiplied by the V scale and stored in bf16.
+//    warps 2-5 (one query row per thread) run the online softmax in the exp2 domain: a
+//    running row max m raised only when a tile's max exceeds it by more than 3 (so
+//    p = 2^(t - m) <= 8), the row sum of the unrounded codes' values, P as e4m3(p * 448 / 8)
+//    written into shared memory in the 128-byte swizzled layout the MMA reads, and the
+//    rescaling of O in TMEM when m moves (after the previous P V has landed). The final O is
+//    divided by the row sum, multiplied by the V scale and stored in bf16.
 //
 // The running max replaces the reference's global row max: P is rounded relative to the max
-// seen so far, so its codes differ from the reference's, and the result is judged against
-// fp32 attention by relative L2 and cosine, as the reference's own emulation is.
+// seen so far (with 8x headroom), so its codes differ from the reference's, and the result is
+// judged against fp32 attention by relative L2 and cosine, as the reference's own emulation
+// is.
 // No load uses cluster multicast; every wait is bounded and records kDevTimeout.
 #pragma once
 
@@ -124,7 +126,7 @@ struct AttnLayout {
   static constexpr int kV = kK + kStages * kTile;
   static constexpr int kP = kV + kStages * kTile;
   static constexpr int kBars = kP + 2 * kTile;
-  static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 2 + 1 + 1;
+  static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 2 + 1;
   static constexpr int kSmem = 1024 + kBars + kNumBars * 8 + 16;
 };
 
@@ -158,8 +160,7 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
   uint64_t* s_empty = s_full + 2;            // [2], 4 softmax warps
   uint64_t* p_full = s_empty + 2;            // [2], 4 softmax warps
   uint64_t* p_empty = p_full + 2;            // [2]
-  uint64_t* o_ready = p_empty + 2;           // one P V product has landed in O
-  uint64_t* drain = o_ready + 1;
+  uint64_t* drain = p_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   // heavy (long causal) tiles first
@@ -183,7 +184,6 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
       tc::mbar_init(&p_full[i], 4);
       tc::mbar_init(&p_empty[i], 1);
     }
-    tc::mbar_init(o_ready, 1);
     tc::mbar_init(drain, 1);
     tc::fence_barrier_init();
   }
@@ -238,7 +238,6 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
                      (t > 0 || kk > 0) ? 1u : 0u);
         tc::commit(&p_empty[t & 1]);
         tc::commit(&kv_empty[s]);
-        tc::commit(o_ready);
         return true;
       };
       for (int j = 0; ok && j < n_kv; ++j) {
@@ -265,6 +264,12 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
     const int r = 32 * quarter + lane;  // query row within the tile
     const int qrow = qt * 128 + r;
     const float scale_log2 = g.q_scale[bh] * g.k_scale[bhk] * g.sm_scale_log2;
+    // P is taken relative to a row max m that is only raised when a tile's max exceeds it by
+    // more than kHeadroom (log2 units): p = 2^(t - m) <= 2^kHeadroom, and the codes hold
+    // e4m3(p * 448 * 2^-kHeadroom) <= 448. O and the row sum are rescaled only when m moves,
+    // so the softmax rarely waits for the previous P V.
+    constexpr float kHeadroom = 3.0f;
+    constexpr float kCodeLog2 = 8.807354922057604f - kHeadroom;  // log2(448) - headroom
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
@@ -282,26 +287,26 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&s_empty[j & 1]);
-      const bool diag = g.causal && j == qt;
-      float mt = -INFINITY;
+      if (g.causal && j == qt) {  // keys after the query: -inf
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        float t = sv[i] * scale_log2;
-        if (diag && i > r) t = -INFINITY;  // key after the query
-        sv[i] = t;
-        mt = fmaxf(mt, t);
+        for (int i = 0; i < 128; ++i) sv[i] = i > r ? -INFINITY : sv[i];
       }
-      const float m_new = fmaxf(m_run, mt);
-      const float alpha = m_run == -INFINITY ? 0.0f : ex2(m_run - m_new);
+      float mx = sv[0];
+#pragma unroll
+      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, sv[i]);
+      const float tmax = mx * scale_log2;  // the scale is positive: the max of the scaled scores
+      const bool raise = !(tmax <= m_run + kHeadroom);
+      const float m_new = raise ? tmax : m_run;
+      const float alpha = m_run == -INFINITY ? 0.0f : (raise ? ex2(m_run - m_new) : 1.0f);
+      const float bias = kCodeLog2 - m_new;
       float rowsum = 0.0f;
       uint32_t pw[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float p0 = ex2(sv[4 * i] - m_new), p1 = ex2(sv[4 * i + 1] - m_new);
-        const float p2 = ex2(sv[4 * i + 2] - m_new), p3 = ex2(sv[4 * i + 3] - m_new);
+        const float p0 = ex2(fmaf(sv[4 * i], scale_log2, bias)), p1 = ex2(fmaf(sv[4 * i + 1], scale_log2, bias));
+        const float p2 = ex2(fmaf(sv[4 * i + 2], scale_log2, bias)), p3 = ex2(fmaf(sv[4 * i + 3], scale_log2, bias));
         rowsum += (p0 + p1) + (p2 + p3);
-        pw[i] = static_cast<uint32_t>(e4m3_pair(p0 * kFp8Max, p1 * kFp8Max)) |
-                (static_cast<uint32_t>(e4m3_pair(p2 * kFp8Max, p3 * kFp8Max)) << 16);
+        pw[i] = static_cast<uint32_t>(e4m3_pair(p0, p1)) | (static_cast<uint32_t>(e4m3_pair(p2, p3)) << 16);
       }
       l_run = l_run * alpha + rowsum;
       m_run = m_new;
@@ -313,10 +318,13 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
         *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
             make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
       tc::fence_proxy_async();
-      if (j >= 1) {  // O holds P V up to tile j - 1: rescale it to this tile's max
-        if (!warp_wait(o_ready, static_cast<uint32_t>((j - 1) & 1))) { ok = false; break; }
+      // O holds P V up to tile j - 1: rescale it when a row's max moved. P V_{j-1} has landed
+      // once p_empty[(j - 1) & 1] completes its phase (j - 1) >> 1; this warp waited for the
+      // phase before it at tile j - 1, so the parity wait is exact.
+      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        if (!warp_wait(&p_empty[(j - 1) & 1], static_cast<uint32_t>(((j - 1) >> 1) & 1))) { ok = false; break; }
         tc::fence_after_sync();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+        {
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
@@ -337,11 +345,12 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&p_full[j & 1]);
     }
-    // the last P V, then O / (448 * rowsum) * v_scale in bf16
-    if (ok && !warp_wait(o_ready, static_cast<uint32_t>((n_kv - 1) & 1))) ok = false;
+    // the last P V (the same exact wait as the rescale's), then O / rowsum * v_scale in bf16
+    // (the code scale cancels)
+    if (ok && !warp_wait(&p_empty[(n_kv - 1) & 1], static_cast<uint32_t>(((n_kv - 1) >> 1) & 1))) ok = false;
     if (ok) {
       tc::fence_after_sync();
-      const float f = g.v_scale[bhk] / (kFp8Max * l_run);
+      const float f = g.v_scale[bhk] / l_run;
       __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(g.out) + (static_cast<int64_t>(bh) * g.seq + qrow) * 128;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
