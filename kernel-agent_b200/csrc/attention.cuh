@@ -276,13 +276,15 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
       if (!warp_wait(&s_full[j & 1], static_cast<uint32_t>((j >> 1) & 1))) { ok = false; break; }
       tc::fence_after_sync();
       float sv[128];
+      {  // the four loads in flight together, one wait
+        uint32_t raw[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t raw[32];
-        tc::tmem_ld32(tS + lane_base + (j & 1) * 128 + c * 32, raw);
+        for (int c = 0; c < 4; ++c) tc::tmem_ld32(tS + lane_base + (j & 1) * 128 + c * 32, raw[c]);
         tc::tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(raw[i]);
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(raw[c][i]);
       }
       tc::fence_before_sync();
       __syncwarp();
@@ -291,23 +293,28 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
 #pragma unroll
         for (int i = 0; i < 128; ++i) sv[i] = i > r ? -INFINITY : sv[i];
       }
-      float mx = sv[0];
+      float mxs[8];  // eight independent chains, then a tree
 #pragma unroll
-      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, sv[i]);
+      for (int a = 0; a < 8; ++a) mxs[a] = sv[a];
+#pragma unroll
+      for (int i = 8; i < 128; ++i) mxs[i & 7] = fmaxf(mxs[i & 7], sv[i]);
+      const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                             fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
       const float tmax = mx * scale_log2;  // the scale is positive: the max of the scaled scores
       const bool raise = !(tmax <= m_run + kHeadroom);
       const float m_new = raise ? tmax : m_run;
       const float alpha = m_run == -INFINITY ? 0.0f : (raise ? ex2(m_run - m_new) : 1.0f);
       const float bias = kCodeLog2 - m_new;
-      float rowsum = 0.0f;
+      float sums[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // four independent chains
       uint32_t pw[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const float p0 = ex2(fmaf(sv[4 * i], scale_log2, bias)), p1 = ex2(fmaf(sv[4 * i + 1], scale_log2, bias));
         const float p2 = ex2(fmaf(sv[4 * i + 2], scale_log2, bias)), p3 = ex2(fmaf(sv[4 * i + 3], scale_log2, bias));
-        rowsum += (p0 + p1) + (p2 + p3);
+        sums[i & 3] += (p0 + p1) + (p2 + p3);
         pw[i] = static_cast<uint32_t>(e4m3_pair(p0, p1)) | (static_cast<uint32_t>(e4m3_pair(p2, p3)) << 16);
       }
+      const float rowsum = (sums[0] + sums[1]) + (sums[2] + sums[3]);
       l_run = l_run * alpha + rowsum;
       m_run = m_new;
       // P_j into its buffer once P V_{j-2} has read it: row r, 16-byte chunk c at c ^ (r % 8)
