@@ -26,6 +26,22 @@ struct BlockwiseArgs {
   int bias_dtype;
 };
 
+// Two fp32 lanes in one 64-bit register (element 0 low): the promotion runs on packed
+// f32x2 multiplies and adds, each lane rounded to nearest like its scalar form.
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+  return (static_cast<unsigned long long>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 template <int OUT>
 struct BlockwiseLayout {
   static constexpr int kBM = 128, kBN = 128, kBK = 128;  // bytes of K per stage = one scale group
@@ -168,9 +184,9 @@ gemm_blockwise_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
       const int col0 = nt * BN + half * 64;
       const float* sa_row = g.sa + (live ? row : 0) * static_cast<int64_t>(KB);
       const float* sb_col = g.sb + static_cast<int64_t>(nt) * KB;
-      float acc[64];
+      unsigned long long acc[32];  // columns 2i, 2i + 1
 #pragma unroll
-      for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
+      for (int i = 0; i < 32; ++i) acc[i] = 0ull;
       for (int kb = 0; kb < KB; ++kb) {
         const float sa = live ? __ldg(sa_row + kb) : 0.0f;
         const float sb = __ldg(sb_col + kb);
@@ -186,10 +202,13 @@ gemm_blockwise_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
         if (lane == 0) tc::mbar_arrive(&part_empty[p]);
         if (++p == NP) { p = 0; pph ^= 1u; }
         // gemm_bench.py:39-68: acc += (partial * sa[m, kb]) * sb[n / 128, kb], each rounded
+        const unsigned long long sa2 = f2_pack(sa, sa), sb2 = f2_pack(sb, sb);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          acc[i] = __fadd_rn(acc[i], __fmul_rn(__fmul_rn(__uint_as_float(r0[i]), sa), sb));
-          acc[32 + i] = __fadd_rn(acc[32 + i], __fmul_rn(__fmul_rn(__uint_as_float(r1[i]), sa), sb));
+        for (int i = 0; i < 16; ++i) {
+          const unsigned long long p0 = f2_pack(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+          const unsigned long long p1 = f2_pack(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+          acc[i] = f2_add(acc[i], f2_mul(f2_mul(p0, sa2), sb2));
+          acc[16 + i] = f2_add(acc[16 + i], f2_mul(f2_mul(p1, sa2), sb2));
         }
       }
       if (!ok) break;
@@ -201,7 +220,8 @@ gemm_blockwise_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_co
         if (g.bias != nullptr && col0 + c * 32 + lane < g.n) bv = load_bias(g.bias, g.bias_dtype, col0 + c * 32 + lane);
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          float v = acc[c * 32 + i];
+          const unsigned long long a2 = acc[c * 16 + i / 2];
+          float v = __uint_as_float(static_cast<uint32_t>(i & 1 ? a2 >> 32 : a2));
           const float b = __shfl_sync(0xffffffffu, bv, i);
           if (g.bias != nullptr) v = __fadd_rn(v, b);
           y[i] = __float_as_uint(v);
