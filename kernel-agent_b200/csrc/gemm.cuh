@@ -51,6 +51,12 @@ struct GemmArgs {
   int npeers;
 };
 
+// Tensor maps of the other ranks' outputs (CUDA IPC mappings of buffers laid out like `out`):
+// the epilogue stores each staged tile to them with TMA, like the local output.
+struct PeerMaps {
+  CUtensorMap m[kMaxPeers];
+};
+
 template <int KIND>
 struct GemmTraits {
   static constexpr bool kScaled = KIND >= 2;
@@ -217,36 +223,6 @@ __device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const uint32_t
   stage_packed<OUT>(buf, lane, w);
 }
 
-// The warp's staged [32 rows, 32 columns] tile (rows row0.., columns col0..; swizzled as
-// stage_packed writes it) stored into every peer output (other GPUs' buffers, mapped by CUDA
-// IPC) over NVLink. Each store instruction covers whole rows' 64 or 128 contiguous bytes
-// (full 32-byte sectors, 8 or 4 rows per instruction): the lanes of a row take its 16-byte
-// chunks. Rows at or past m and columns at or past n are skipped.
-template <int OUT>
-__device__ __forceinline__ void peer_store_tile(const GemmArgs& g, const uint8_t* buf, int lane, int64_t row0,
-                                                int64_t col0) {
-  constexpr int kChunks = 32 * out_bytes(OUT) / 16;  // 16-byte chunks per row: 4 or 8
-  constexpr int kRowsPer = 32 / kChunks;             // rows per instruction: 8 or 4
-  constexpr int kIters = 32 / kRowsPer;
-  constexpr int kPer = 16 / out_bytes(OUT);          // elements per chunk
-  const int c = lane % kChunks;
-  const bool col_ok = col0 + (c + 1) * kPer <= g.n;
-#pragma unroll
-  for (int i = 0; i < kIters; ++i) {
-    const int r = i * kRowsPer + lane / kChunks;
-    const int sw = kChunks == 8 ? (r & 7) : ((r >> 1) & 3);
-    const uint4 v = *reinterpret_cast<const uint4*>(buf + r * (32 * out_bytes(OUT)) + 16 * (c ^ sw));
-    const int64_t row = row0 + r;
-    if (!col_ok || row >= g.m) continue;
-    const int64_t off = (row * g.ldo + col0 + c * kPer) * out_bytes(OUT);
-#pragma unroll
-    for (int p = 0; p < kMaxPeers; ++p) {  // static indices: the parameter array stays in constant memory
-      if (p >= g.npeers) break;
-      *reinterpret_cast<uint4*>(static_cast<uint8_t*>(g.peer_out[p]) + off) = v;
-    }
-  }
-}
-
 // Tile t of the persistent schedule -> (m tile, n tile). group_n == 0: groups of 8 m-tiles
 // sweep n (an A panel stays in L2 while B streams); group_n > 0: groups of group_n n-tiles
 // sweep m (for a B larger than L2: each B panel is read from HBM once while A, the smaller
@@ -272,11 +248,14 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
 
 // One epilogue warp's share of a finished accumulator tile: rows row0 + lane (its TMEM lane
 // quarter), HC chunks of 32 columns from colh, read from TMEM at tbase. Each chunk is scaled
-// (epilogue_math), staged in shared memory, stored by TMA (and to the peer outputs); `release`
-// runs (lane 0, after a warp sync) once the last chunk has been read from TMEM.
+// (epilogue_math), staged in shared memory and stored by TMA to the output and to each of the
+// g.npeers peer outputs in `peers` (over NVLink: the copies run on the TMA unit while the warp
+// goes on); `release` runs (lane 0, after a warp sync) once the last chunk has been read from
+// TMEM.
 template <int KIND, int OUT, int HC, class Release>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& g, const CUtensorMap* tma_out, uint32_t tbase, int row0,
-                                              int colh, uint8_t* stage0, int& chunk, int lane, Release release) {
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& g, const CUtensorMap* tma_out, const PeerMaps* peers,
+                                              uint32_t tbase, int row0, int colh, uint8_t* stage0, int& chunk, int lane,
+                                              Release release) {
   constexpr int kStageOutBytes = 32 * 32 * out_bytes(OUT);
   const int64_t row = static_cast<int64_t>(row0) + lane;
   // this tile's row scale and (lane i of chunk c) column scale / bias, loaded once
@@ -324,9 +303,15 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, const CUtensorM
     __syncwarp();
     if (lane == 0) {
       tc::tma_store_2d(tma_out, buf, colh + c * 32, row0);
-      tc::bulk_commit();
+      if (peers != nullptr) {
+#pragma unroll
+        for (int p = 0; p < kMaxPeers; ++p) {
+          if (p >= g.npeers) break;
+          tc::tma_store_2d(&peers->m[p], buf, colh + c * 32, row0);
+        }
+      }
+      tc::bulk_commit();  // one group per chunk: the buffer is free once its reads are done
     }
-    if (g.npeers > 0) peer_store_tile<OUT>(g, buf, lane, row0, colh + c * 32);
     ++chunk;
     if (c + 1 < HC) tc::tmem_ld_wait();
   }
@@ -335,7 +320,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, const CUtensorM
 template <int KIND, int BN, int BKB, int OUT>
 __global__ void __launch_bounds__(GemmLayout<KIND, BN, BKB, OUT>::kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-            const __grid_constant__ CUtensorMap tma_out, GemmArgs g) {
+            const __grid_constant__ CUtensorMap tma_out, GemmArgs g, const __grid_constant__ PeerMaps peers) {
   using L = GemmLayout<KIND, BN, BKB, OUT>;
   constexpr int STAGES = L::kStages;
   constexpr int KS = L::kKSteps;
@@ -578,8 +563,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       const int colh = nt * BN + half * (BN / 2);
       const uint32_t tbase = tmem + lane_base + ab * BN + half * (BN / 2);
       uint64_t* release_bar = &acc_empty[ab];
-      epilogue_tile<KIND, OUT, HC>(g, &tma_out, tbase, row0, colh, stage0, chunk, lane,
-                                   [release_bar] { tc::mbar_arrive(release_bar); });
+      epilogue_tile<KIND, OUT, HC>(g, &tma_out, g.npeers > 0 ? &peers : nullptr, tbase, row0, colh, stage0, chunk,
+                                   lane, [release_bar] { tc::mbar_arrive(release_bar); });
       if (++ab == L::kAccBufs) { ab = 0; aph ^= 1u; }
     }
     if (lane == 0) tc::bulk_wait_all();

@@ -257,7 +257,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
       const int colh = nt * BN + half * (BN / 2);
       const uint32_t tbase = tmem + lane_base + ab * BN + half * (BN / 2);
       const uint32_t release_bar = acc_empty_leader + 8 * ab;
-      epilogue_tile<KIND, OUT, HC>(g, &tma_out, tbase, row0, colh, stage0, chunk, lane,
+      epilogue_tile<KIND, OUT, HC>(g, &tma_out, nullptr, tbase, row0, colh, stage0, chunk, lane,
                                    [release_bar] { tc::mbar_arrive_cluster(release_bar); });
       if (++ab == AB) { ab = 0; aph ^= 1u; }
     }

@@ -81,7 +81,7 @@ int make_out_map(CUtensorMap* map, void* ptr, int out, uint64_t m, uint64_t n, u
 
 template <int KIND, int BN, int BKB, int OUT>
 int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const GemmArgs& g,
-               cudaStream_t s) {
+               const PeerMaps& pm, cudaStream_t s) {
   using L = GemmLayout<KIND, BN, BKB, OUT>;
   auto kernel = gemm_kernel<KIND, BN, BKB, OUT>;
   static bool configured[64] = {};
@@ -94,20 +94,20 @@ int launch_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
   }
   const int tiles = g.m_tiles * g.n_tiles;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kernel<<<grid, L::kThreads, L::kSmem, s>>>(ma, mb, mo, g);
+  kernel<<<grid, L::kThreads, L::kSmem, s>>>(ma, mb, mo, g, pm);
   return check_launch("gemm kernel");
 }
 
 template <int KIND, int BN>
 int launch_out(int out, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const GemmArgs& g,
-               cudaStream_t s) {
+               const PeerMaps& pm, cudaStream_t s) {
   constexpr int BKB = 128;
   if constexpr (KIND == 0) {
-    if (out == kOutI32) return launch_one<KIND, BN, BKB, kOutI32>(ma, mb, mo, g, s);
+    if (out == kOutI32) return launch_one<KIND, BN, BKB, kOutI32>(ma, mb, mo, g, pm, s);
   }
-  if (out == KAB_BF16) return launch_one<KIND, BN, BKB, KAB_BF16>(ma, mb, mo, g, s);
-  if (out == KAB_F16) return launch_one<KIND, BN, BKB, KAB_F16>(ma, mb, mo, g, s);
-  return launch_one<KIND, BN, BKB, KAB_F32>(ma, mb, mo, g, s);
+  if (out == KAB_BF16) return launch_one<KIND, BN, BKB, KAB_BF16>(ma, mb, mo, g, pm, s);
+  if (out == KAB_F16) return launch_one<KIND, BN, BKB, KAB_F16>(ma, mb, mo, g, pm, s);
+  return launch_one<KIND, BN, BKB, KAB_F32>(ma, mb, mo, g, pm, s);
 }
 
 // A swizzled block-scale tensor of `bytes` bytes as [bytes / 256, 256] read in boxes of
@@ -203,7 +203,7 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
   // 256 x 256 tiles on SM pairs when there are at least two 128-row blocks of A and padding N
   // to 256 costs at most 1/16 more columns
   const int64_t pad256 = (n + 255) / 256 * 256 - n;
-  if (pair_enabled() && m > 128 && n >= 256 && pad256 * 16 <= n) {
+  if (pair_enabled() && g.npeers == 0 && m > 128 && n >= 256 && pad256 * 16 <= n) {
     g.m = m;
     g.n = n;
     g.k_stages = static_cast<int>(k_bytes / bkb);
@@ -248,13 +248,16 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
   if (int e = make_map(&ma, a, m, k_bytes, k_bytes, 128, bkb, "A")) return e;
   if (int e = make_map(&mb, b, n, k_bytes, k_bytes, bn, bkb, "B")) return e;
   if (int e = make_out_map(&mo, out, out_dtype, m, n, g.ldo)) return e;
+  PeerMaps pm{};
+  for (int p = 0; p < g.npeers; ++p)
+    if (int e = make_out_map(&pm.m[p], g.peer_out[p], out_dtype, m, n, g.ldo)) return e;
   if constexpr (GemmTraits<KIND>::kScaled) {
     g.sfb_chunks = (n + 127) / 128;
-    if (bn == 192) return launch_out<KIND, 192>(out_dtype, ma, mb, mo, g, s);
+    if (bn == 192) return launch_out<KIND, 192>(out_dtype, ma, mb, mo, g, pm, s);
   } else {
-    if (bn == 256) return launch_out<KIND, 256>(out_dtype, ma, mb, mo, g, s);
+    if (bn == 256) return launch_out<KIND, 256>(out_dtype, ma, mb, mo, g, pm, s);
   }
-  return launch_out<KIND, 128>(out_dtype, ma, mb, mo, g, s);
+  return launch_out<KIND, 128>(out_dtype, ma, mb, mo, g, pm, s);
 }
 
 template <int OUT>
