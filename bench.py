@@ -232,7 +232,7 @@ class Nvfp4Producer(Workload):
         self.x = x.to(dev)
         self.bytes = self.m * self.k * 2 + self.m * self.k // 2 + self.m * self.k // 16 + 4 * self.m
         self.units = self.bytes / 1e9  # GB per step
-        self.kernel = "quant_fp4_kernel"
+        self.kernel = "quant_fp4_fast_kernel"
         self.kernel_bytes = self.bytes
         self.x_host = self.x.cpu().pin_memory()
         self.h2d = self.x.numel() * 2
