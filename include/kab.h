@@ -290,6 +290,15 @@ int kab_channel_rms(const void* x, const void* alt, int dtype, int64_t rows,
 int kab_hadamard_rotate(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, int block,
                         float* out, void* stream);
 
+/* The RMSNorm of the fused producers rmsnorm_fp8 / rmsnorm_fp4
+ * (src/kernel_agent/agent/examples/triton_fp8_producers.py:120-133, 191-202;
+ * triton_fp4_producers.py:261-294, 384-405): per row r = rsqrt(sum(x^2) / k + eps) in fp32,
+ * out = dtype(dtype(x * r) * weight) [rows, k] (k % 8 == 0, weight [k] in x's dtype). The
+ * producers then quantise out with the quantisers above, so codes and scales are exactly
+ * those of out. */
+int kab_rmsnorm(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, const void* weight, float eps,
+                void* out, void* stream);
+
 /* quant.py:1117-1148 fp4_bias_correction: per row of x [rows, k] quantised to (codes,
  * scales [rows, k / block] bytes, row-major or `swizzled`, outer [rows] / one value / null),
  * c = sum x^2 / sum x x^ in float64 (1 when sum x x^ <= 0 or c is not finite); fp32 out [rows]. */

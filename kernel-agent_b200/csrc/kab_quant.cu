@@ -367,6 +367,22 @@ int kab_fp4_scale_check(const void* x, int dtype, int64_t rows, int64_t k, int64
   return check_launch("kab_fp4_scale_check");
 }
 
+int kab_rmsnorm(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, const void* weight, float eps,
+                void* out, void* stream) {
+  if (int e = check_matrix(x, dtype, rows, k, ldx, "x")) return e;
+  KAB_REQUIRE(k % 8 == 0, "the last dimension %lld is not a multiple of 8", (long long)k);
+  KAB_REQUIRE(rows == 0 || (weight != nullptr && out != nullptr && aligned(weight, 16) && aligned(out, 16)),
+              "weight or out is null or not 16-byte aligned");
+  KAB_REQUIRE(eps >= 0.0f, "eps must be non-negative");
+  if (rows == 0 || k == 0) return KAB_OK;
+  const cudaStream_t s = as_stream(stream);
+  const unsigned grid = static_cast<unsigned>(rows);
+  if (dtype == KAB_BF16) rmsnorm_rows_kernel<kBF16><<<grid, 256, 0, s>>>(x, ldx, k, weight, eps, out);
+  else if (dtype == KAB_F16) rmsnorm_rows_kernel<kF16><<<grid, 256, 0, s>>>(x, ldx, k, weight, eps, out);
+  else rmsnorm_rows_kernel<kF32><<<grid, 256, 0, s>>>(x, ldx, k, weight, eps, out);
+  return check_launch("kab_rmsnorm");
+}
+
 int kab_hadamard_rotate(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, int block, float* out,
                         void* stream) {
   KAB_REQUIRE(valid_dtype(dtype), "unknown dtype %d", dtype);

@@ -561,6 +561,47 @@ quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const 
   }
 }
 
+// ------------------------------------------------------------------ RMSNorm
+
+// The RMSNorm of the fused producers (triton_fp8_producers.py:120-133,
+// triton_fp4_producers.py:261-294; the arithmetic of Llama / Qwen / Mistral RMSNorm): per row
+// r = rsqrt(sum(x^2) / k + eps) in fp32 (squares and sum each rounded, the sum as a tree),
+// h = T(T(x * r) * w) in x's dtype T, written to h [rows, k]. One CTA per row: the sum of
+// squares over 16-byte chunks and a block reduction, then a second read of the row (from L2)
+// for h. The quantisers then read h, so the codes are exactly those of h.
+template <int T>
+__global__ void __launch_bounds__(256)
+rmsnorm_rows_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const void* __restrict__ w, float eps,
+                    void* __restrict__ h) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int64_t chunks = k >> 3;
+  float ss = 0.0f;
+  for (int64_t c = threadIdx.x; c < chunks; c += blockDim.x) {
+    float v[8];
+    load8<T>(x, row * ldx + c * 8, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = lane < nwarps ? red[lane] : 0.0f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot = __fadd_rn(tot, __shfl_xor_sync(0xffffffffu, tot, o));
+  const float r = rsqrtf(__fadd_rn(__fdiv_rn(tot, static_cast<float>(k)), eps));
+  for (int64_t c = threadIdx.x; c < chunks; c += blockDim.x) {
+    float v[8], wv[8], o8[8];
+    load8<T>(x, row * ldx + c * 8, v);
+    load8<T>(w, c * 8, wv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o8[j] = round_to_input<T>(__fmul_rn(round_to_input<T>(__fmul_rn(v[j], r)), wv[j]));
+    store_h8<T>(h, row * k + c * 8, o8);
+  }
+}
+
 // ------------------------------------------------------------------ global amax
 
 // NaN-keeping max |x| of a [rows, k] matrix into *out (which holds 0 before the launch):

@@ -269,6 +269,22 @@ def silu_mul(gate, up) -> np.ndarray:
         return round_bf16((a * u).astype(F32))
 
 
+def rmsnorm(x, weight, eps: float, dtype: str = "bf16") -> np.ndarray:
+    """RMSNorm times weight as eager computes it (triton_fp8_producers.py:120-133,
+    triton_fp4_producers.py:261-294): ``x * rsqrt(mean(x^2) + eps)`` in fp32 rounded to x's
+    dtype, times the weight, rounded again. The mean is taken in float64 and rounded to fp32,
+    rsqrt in float64 then fp32 (the device's order of the sum and its rsqrt may differ in
+    the last bit, which moves a bf16 / fp16 result on a small share of elements)."""
+    a = _rows(x)
+    rnd = round_bf16 if dtype == "bf16" else (lambda v: v.astype(np.float16).astype(F32))
+    with np.errstate(**_ERRSTATE):
+        sq = (a * a).astype(F32).astype(np.float64)
+        var = (sq.mean(axis=1) if a.shape[1] else np.zeros(a.shape[0])).astype(F32)
+        r = (1.0 / np.sqrt((var + F32(eps)).astype(F32).astype(np.float64))).astype(F32)
+        hn = rnd((a * r[:, None]).astype(F32))
+        return rnd((hn * f32(weight).reshape(1, -1)).astype(F32))
+
+
 def mxfp8_saturation(x, scales) -> dict:
     """quant.py:623-660: how MXFP8 scales fit the block maxima of ``x``."""
     a = _rows(x)

@@ -1,0 +1,105 @@
+"""RMSNorm producers (kernel-agent's rmsnorm_fp8 / rmsnorm_fp4 example producers,
+src/kernel_agent/agent/examples/triton_fp8_producers.py:191-202 and
+triton_fp4_producers.py:384-405) on the GPU, checked as the reference's own tests check them
+(tests/test_fp8_toolkit.py, tests/test_fp4_producers.py): the codes and scales equal the
+quantisation of the producer's own norm output bit for bit (the oracle's quantisers), and that
+output equals eager RMSNorm (the oracle's) on at least 99 % of the elements. The FP4
+producers' unbiased factor is outer times the oracle's fp4_bias_correction."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import np_bytes, np_values
+from oracle import quant as oq
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def prod():
+    from kernel_agent_b200.kernels import producers
+
+    return producers
+
+
+def inputs(m, k, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.randn(m, k, generator=g) * 3).to(dtype)
+    x[0, : k // 4] = 0.0
+    w = (1.0 + 0.1 * torch.randn(k, generator=g)).to(dtype)
+    return x.to(DEV), w.to(DEV)
+
+
+def eager_share(out, x, w, dtype):
+    ref = oq.rmsnorm(np_values(x), np_values(w), 1e-6, "bf16" if dtype == torch.bfloat16 else "f16")
+    got = np_values(out)
+    return float((got == ref).mean())
+
+
+@pytest.mark.parametrize("m,k", [(353, 1024), (64, 4096), (5, 256), (130, 8192)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_rmsnorm_fp4_codes_of_its_output(prod, m, k, dtype):
+    x, w = inputs(m, k, dtype, m + k)
+    out = torch.empty(m, k, dtype=dtype, device=DEV)
+    q, s, o, e = prod.rmsnorm_fp4(x, w, 1e-6, out=out, unbiased=True)
+    h = np_values(out)
+    rq, rs, ro = oq.quantize_fp4_activations(h)
+    assert np.array_equal(np_bytes(q), rq) and np.array_equal(np_bytes(s), rs)
+    assert np.array_equal(np_values(o), ro)
+    want_e = (ro * oq.fp4_bias_correction(h, rq, rs, ro)).astype(np.float32)
+    assert np.allclose(np_values(e), want_e, rtol=1e-6, atol=0)
+    assert eager_share(out, x, w, dtype) >= 0.99
+    # MXFP4 and swizzled scales from the same norm
+    q2, s2, o2 = prod.rmsnorm_fp4(x, w, 1e-6, mx=True)
+    rq2, rs2, ro2 = oq.quantize_fp4_activations(h, "mxfp4")
+    assert np.array_equal(np_bytes(q2), rq2) and np.array_equal(np_bytes(s2), rs2)
+    _, sw, _ = prod.rmsnorm_fp4(x, w, 1e-6, swizzle=True)
+    assert np.array_equal(np_bytes(sw), oq.swizzle_scales(rs))
+
+
+@pytest.mark.parametrize("m,k", [(353, 1024), (16, 4096), (3, 64)])
+def test_rmsnorm_fp8_codes_of_its_output(prod, m, k):
+    x, w = inputs(m, k, torch.bfloat16, 7 * m + k)
+    out = torch.empty(m, k, dtype=torch.bfloat16, device=DEV)
+    q, s = prod.rmsnorm_fp8(x, w, 1e-6, out=out)
+    h = np_values(out)
+    rq, rs = oq.quantize_fp8_activations(h)
+    assert np.array_equal(np_bytes(q), rq) and np.array_equal(np_values(s), rs)
+    assert eager_share(out, x, w, torch.bfloat16) >= 0.99
+    if k % 32 == 0:
+        qm, sm = prod.rmsnorm_fp8(x, w, 1e-6, mx=True)
+        rqm, rsm = oq.quantize_mxfp8(h)
+        assert np.array_equal(np_bytes(qm), rqm) and np.array_equal(np_bytes(sm), rsm)
+        _, blocked = prod.rmsnorm_fp8(x, w, 1e-6, mx=True, blocked=True)
+        assert np.array_equal(np_bytes(blocked), oq.swizzle_scales(rsm))
+
+
+def test_unbiased_factor_of_the_other_fp4_producers(prod):
+    x, _ = inputs(200, 2048, torch.bfloat16, 11)
+    q, s, o, e = prod.quantize_rows_fp4(x, unbiased=True)
+    h = np_values(x)
+    rq, rs, ro = oq.quantize_fp4_activations(h)
+    assert np.array_equal(np_bytes(q), rq) and np.array_equal(np_bytes(s), rs)
+    assert np.allclose(np_values(e), ro * oq.fp4_bias_correction(h, rq, rs, ro), rtol=1e-6, atol=0)
+    gu = (torch.randn(64, 2 * 1024, generator=torch.Generator().manual_seed(3)) * 2).to(torch.bfloat16).to(DEV)
+    out = torch.empty(64, 1024, dtype=torch.bfloat16, device=DEV)
+    q, s, o, e = prod.silu_mul_fp4(gu, out=out, unbiased=True)
+    hv = np_values(out)
+    rq, rs, ro = oq.quantize_fp4_activations(hv)
+    assert np.array_equal(np_bytes(q), rq)
+    assert np.allclose(np_values(e), ro * oq.fp4_bias_correction(hv, rq, rs, ro), rtol=1e-6, atol=0)
+    q2, s2, o2, e2 = prod.silu_mul_fp4(gu, unbiased=True)  # the product into a temporary
+    assert torch.equal(q2, q) and torch.equal(e2, e)
+
+
+def test_rmsnorm_rejects_bad_shapes(prod):
+    x = torch.randn(4, 100, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        prod.rmsnorm_fp8(x, torch.ones(100, device=DEV, dtype=torch.bfloat16), 1e-6)
+    x = torch.randn(4, 128, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        prod.rmsnorm_fp4(x, torch.ones(64, device=DEV, dtype=torch.bfloat16), 1e-6)
