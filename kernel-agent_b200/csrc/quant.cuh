@@ -421,6 +421,8 @@ quant_fp4_kernel(const void* __restrict__ x, int64_t ldx, const void* __restrict
   }
 }
 
+constexpr int kFp4MaxRowBlocks = 32768 / 16;  // scale blocks of the longest row (k <= 32768)
+
 // Lean NVFP4 / MXFP4 producer for bf16 / fp16 inputs without the SiLU gate: the codes and
 // scales of quant_fp4_kernel (the same block scale, the same quotient RN(v * y) with the same
 // exactness window and IEEE-division fallback, the same e2m1 conversion), in fewer
@@ -429,7 +431,11 @@ quant_fp4_kernel(const void* __restrict__ x, int64_t ldx, const void* __restrict
 //    (non-negative bf16 / fp16 values order like their bit patterns, NaN above inf);
 //  * two quotients per mul.rn.f32x2;
 //  * the window test "(bits + 16) mod 2^21 <= 32" is bits * 2^11 + 2^15 (mod 2^32) < 33 * 2^11,
-//    one IMAD, folded over the block with a running unsigned min.
+//    one IMAD, folded over the block with a running unsigned min;
+//  * a block that trips it (6.7 % of them on config 4's activations: ratios of bf16 values
+//    often land exactly on short floats) goes on a shared-memory list and is recomputed with
+//    the IEEE division after the row by the whole CTA, instead of one lane dividing while its
+//    warp waits.
 template <int T>
 __device__ __forceinline__ float half_bits_to_float(uint32_t h) {
   if constexpr (T == kBF16) return __uint_as_float(h << 16);
@@ -448,16 +454,57 @@ __device__ __forceinline__ float2 unpack2(uint32_t w) {
   else return __half22float2(*reinterpret_cast<const __half2*>(&w));
 }
 
+// The scale byte and step of one block from its |max| (16-bit pattern): quant.py:1067-1107
+// (NVFP4: e4m3(min(bmax / (outer * 6), 448)), step = value * outer; MXFP4: the e8m0 exponent
+// rule of activations or weights).
+template <int T, int FMT, int MODE>
+__device__ __forceinline__ void fp4_block_scale(uint32_t bm, float s_outer, const Divisor& by6, uint32_t& sbyte,
+                                                float& step) {
+  const float bmax = half_bits_to_float<T>(bm);
+  if constexpr (FMT == 0) {
+    const float bmv[1] = {bmax};
+    float ratio[1];
+    quotients<kLowE4m3>(bmv, by6, ratio);
+    sbyte = e4m3_byte(ratio[0]);
+    step = __fmul_rn(e4m3_value_hw(static_cast<uint8_t>(sbyte)), s_outer);
+  } else {
+    const int e = MODE == 2 ? mxfp4_weight_exponent(bmax) : mxfp4_act_exponent(bmax);
+    sbyte = static_cast<uint32_t>(e + 127);
+    step = e8m0_value(static_cast<uint8_t>(sbyte));
+  }
+}
+
+// e2m1 codes of one block's quotients t (NaN quotients of a block holding a NaN become 0).
+template <int T, int BLOCK>
+__device__ __forceinline__ void fp4_block_pack(float (&t)[BLOCK], uint32_t bm, uint32_t (&packed)[BLOCK / 8]) {
+  constexpr uint32_t kHalfInf = T == kBF16 ? 0x7F80u : 0x7C00u;
+  if (bm > kHalfInf) {
+#pragma unroll
+    for (int j = 0; j < BLOCK; ++j) t[j] = t[j] == t[j] ? t[j] : 0.0f;
+  }
+#pragma unroll
+  for (int c = 0; c < BLOCK / 8; ++c) {
+    float e8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) e8[j] = t[c * 8 + j];
+    packed[c] = e2m1x8(e8);
+  }
+}
+
 template <int T, int NB, int FMT, int MODE>
 __global__ void __launch_bounds__(512)
 quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const float* __restrict__ amax_in,
                       const float* __restrict__ ts_in, int swizzle, uint8_t* __restrict__ q,
                       uint8_t* __restrict__ scales, float* __restrict__ outer_out) {
   __shared__ float red[32];
+  // blocks whose quotients need the IEEE division, redone by the whole CTA after the row
+  __shared__ int fix[kFp4MaxRowBlocks];
+  __shared__ int nfix;
   constexpr int BLOCK = FMT == 0 ? 16 : 32;
+  if (threadIdx.x == 0) nfix = 0;
+  __syncthreads();
   constexpr int W = BLOCK / 2;  // packed words per block
-  constexpr uint32_t kHalfInf = T == kBF16 ? 0x7F80u : 0x7C00u;
-  const int64_t row = blockIdx.x;
+    const int64_t row = blockIdx.x;
   const int nblk = static_cast<int>(k / BLOCK);
   const uint4* xr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + row * ldx);
   uint32_t w[NB][W];
@@ -503,20 +550,9 @@ quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const 
   for (int b = 0; b < NB; ++b) {
     const int bi = threadIdx.x + b * blockDim.x;
     if (bi >= nblk) continue;
-    const float bmax = half_bits_to_float<T>(bm[b]);
     uint32_t sbyte;
     float step;
-    if constexpr (FMT == 0) {
-      const float bmv[1] = {bmax};
-      float ratio[1];
-      quotients<kLowE4m3>(bmv, by6, ratio);
-      sbyte = e4m3_byte(ratio[0]);
-      step = __fmul_rn(e4m3_value_hw(static_cast<uint8_t>(sbyte)), s_outer);
-    } else {
-      const int e = MODE == 2 ? mxfp4_weight_exponent(bmax) : mxfp4_act_exponent(bmax);
-      sbyte = static_cast<uint32_t>(e + 127);
-      step = e8m0_value(static_cast<uint8_t>(sbyte));
-    }
+    fp4_block_scale<T, FMT, MODE>(bm[b], s_outer, by6, sbyte, step);
     const float div = (MODE == 2 && step < 1e-38f) ? 1e-38f : step;
     uint32_t packed[BLOCK / 8];
 #pragma unroll
@@ -533,31 +569,50 @@ quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const 
         mn = min(mn, __float_as_uint(p.x) * 2048u + 32768u);
         mn = min(mn, __float_as_uint(p.y) * 2048u + 32768u);
       }
-      if (mn < 33u * 2048u) {  // near an e2m1 decision point (or no fast reciprocal): divide
-#pragma unroll
-        for (int j = 0; j < W; ++j) {
-          const float2 v = unpack2<T>(w[b][j]);
-          t[2 * j] = __fdiv_rn(v.x, d.s);
-          t[2 * j + 1] = __fdiv_rn(v.y, d.s);
-        }
-      }
-      if (bm[b] > kHalfInf) {  // a NaN in the block: its codes are 0
-#pragma unroll
-        for (int j = 0; j < BLOCK; ++j) t[j] = t[j] == t[j] ? t[j] : 0.0f;
-      }
-#pragma unroll
-      for (int c = 0; c < BLOCK / 8; ++c) {
-        float e8[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) e8[j] = t[c * 8 + j];
-        packed[c] = e2m1x8(e8);
-      }
+      // near an e2m1 decision point (or no fast reciprocal): these codes are provisional; the
+      // block is redone with the IEEE division after the row, with all lanes busy
+      if (mn < 33u * 2048u) fix[atomicAdd(&nfix, 1)] = bi;
+      fp4_block_pack<T, BLOCK>(t, bm[b], packed);
     }
     uint8_t* dst = q + row * (k >> 1) + static_cast<int64_t>(bi) * (BLOCK / 2);
     if constexpr (BLOCK == 16) *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
     else *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
     const int64_t off = swizzle ? scale_offset_swizzled(row, bi, nblk) : row * nblk + bi;
     scales[off] = static_cast<uint8_t>(sbyte);
+  }
+  __syncthreads();  // every provisional code is written and the list is complete
+  const int nf = nfix;
+  for (int i = threadIdx.x; i < nf; i += blockDim.x) {
+    const int bi = fix[i];
+    uint32_t wv[W];
+    uint32_t m = 0;
+#pragma unroll
+    for (int c = 0; c < W / 4; ++c) {
+      const uint4 r = __ldg(xr + static_cast<int64_t>(bi) * (W / 4) + c);
+      wv[4 * c] = r.x;
+      wv[4 * c + 1] = r.y;
+      wv[4 * c + 2] = r.z;
+      wv[4 * c + 3] = r.w;
+    }
+#pragma unroll
+    for (int j = 0; j < W; ++j) m = __vmaxu2(m, wv[j] & 0x7FFF7FFFu);
+    const uint32_t bmi = max(m & 0xFFFFu, m >> 16);
+    uint32_t sbyte;
+    float step;
+    fp4_block_scale<T, FMT, MODE>(bmi, s_outer, by6, sbyte, step);
+    const float div = (MODE == 2 && step < 1e-38f) ? 1e-38f : step;
+    float t[BLOCK];
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      const float2 v = unpack2<T>(wv[j]);
+      t[2 * j] = __fdiv_rn(v.x, div);
+      t[2 * j + 1] = __fdiv_rn(v.y, div);
+    }
+    uint32_t packed[BLOCK / 8];
+    fp4_block_pack<T, BLOCK>(t, bmi, packed);
+    uint8_t* dst = q + row * (k >> 1) + static_cast<int64_t>(bi) * (BLOCK / 2);
+    if constexpr (BLOCK == 16) *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
   }
 }
 
