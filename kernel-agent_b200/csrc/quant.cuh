@@ -504,7 +504,7 @@ quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const 
   if (threadIdx.x == 0) nfix = 0;
   __syncthreads();
   constexpr int W = BLOCK / 2;  // packed words per block
-    const int64_t row = blockIdx.x;
+  const int64_t row = blockIdx.x;
   const int nblk = static_cast<int>(k / BLOCK);
   const uint4* xr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + row * ldx);
   uint32_t w[NB][W];
