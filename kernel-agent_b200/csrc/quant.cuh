@@ -491,8 +491,9 @@ __device__ __forceinline__ void fp4_block_pack(float (&t)[BLOCK], uint32_t bm, u
   }
 }
 
+// (NVFP4 with up to two blocks per thread: at most 42 registers, six 256-thread CTAs per SM)
 template <int T, int NB, int FMT, int MODE>
-__global__ void __launch_bounds__(512)
+__global__ void __launch_bounds__(512, FMT == 0 && NB <= 2 ? 3 : 1)
 quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const float* __restrict__ amax_in,
                       const float* __restrict__ ts_in, int swizzle, uint8_t* __restrict__ q,
                       uint8_t* __restrict__ scales, float* __restrict__ outer_out) {
