@@ -8,6 +8,7 @@
 #include "gemm.cuh"
 #include "gemm_blockwise.cuh"
 #include "gemm_pair.cuh"
+#include "gemm_skinny.cuh"
 #include "kab_host.h"
 
 namespace kab {
@@ -169,6 +170,34 @@ int launch_pair(int out, const CUtensorMap& ma, const CUtensorMap& mb, const CUt
   return launch_pair_one<KIND, KAB_F32>(ma, mb, msa, msb, mo, g, s);
 }
 
+// The skinny kernel (gemm_skinny.cuh) for M <= 32: one CTA per 128-channel panel of W.
+template <int KIND, int NT, int OUT>
+int launch_skinny_one(const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& g, cudaStream_t s) {
+  using L = SkinnyLayout<NT, OUT>;
+  auto kernel = gemm_skinny_kernel<KIND, NT, OUT>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem) != cudaSuccess)
+      return fail(KAB_ECUDA, "cannot set %d bytes of shared memory", L::kSmem);
+    configured[dev] = true;
+  }
+  const unsigned grid = static_cast<unsigned>((g.n + 127) / 128);
+  kernel<<<grid, L::kThreads, L::kSmem, s>>>(mw, mx, g);
+  return check_launch("skinny gemm kernel");
+}
+
+template <int KIND, int NT>
+int launch_skinny_nt(int out, const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& g, cudaStream_t s) {
+  if constexpr (KIND == 0) {
+    if (out == kOutI32) return launch_skinny_one<KIND, NT, kOutI32>(mw, mx, g, s);
+  }
+  if (out == KAB_BF16) return launch_skinny_one<KIND, NT, KAB_BF16>(mw, mx, g, s);
+  if (out == KAB_F16) return launch_skinny_one<KIND, NT, KAB_F16>(mw, mx, g, s);
+  return launch_skinny_one<KIND, NT, KAB_F32>(mw, mx, g, s);
+}
+
 // KAB_GEMM_PAIR=1 routes shapes with M > 128 and N >= 256 to the CTA-pair kernel. Off by
 // default: on B200 it measured 2.96 PFLOP/s on NVFP4 8192^3 against 3.66 for the one-CTA
 // kernel (its tcgen05.cp scale copies share the tensor pipe with the MMAs, ~44 cycles each,
@@ -200,6 +229,21 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
   KAB_REQUIRE(g.ldo >= n && g.ldo % 8 == 0, "ldo %lld must be >= n and a multiple of 8", (long long)g.ldo);
   KAB_REQUIRE(aligned(out, 16), "output must be 16-byte aligned");
   KAB_REQUIRE(m <= (int64_t(1) << 30) && n <= (int64_t(1) << 30), "shape too large");
+  // decode sizes of the W8A8 kinds: the weight streams as the MMA's A operand, the tokens are
+  // its N (16 or 32)
+  if constexpr (KIND == 0 || KIND == 1) {
+    if (m <= 32 && g.npeers == 0) {
+      const int nt = m <= 16 ? 16 : 32;
+      g.m = m;
+      g.n = n;
+      g.k_stages = static_cast<int>(k_bytes / bkb);
+      CUtensorMap mw, mx;
+      if (int e = make_map(&mw, b, n, k_bytes, k_bytes, 128, bkb, "W")) return e;
+      if (int e = make_map(&mx, a, m, k_bytes, k_bytes, nt, bkb, "X")) return e;
+      if (nt == 16) return launch_skinny_nt<KIND, 16>(out_dtype, mw, mx, g, s);
+      return launch_skinny_nt<KIND, 32>(out_dtype, mw, mx, g, s);
+    }
+  }
   // 256 x 256 tiles on SM pairs when there are at least two 128-row blocks of A and padding N
   // to 256 costs at most 1/16 more columns
   const int64_t pad256 = (n + 255) / 256 * 256 - n;

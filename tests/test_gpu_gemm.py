@@ -279,3 +279,37 @@ def test_gemm_status_clean():
     from kernel_agent_b200 import _native
 
     assert _native.device_status() == 0
+
+
+# ------------------------------------------------------------------ decode sizes (M <= 32)
+# kernel-agent's skinny W8A8 examples (agent/examples/cuda_int8_skinny_gemm.py,
+# cuda_fp8_skinny_gemm.py): the weight streams through the tensor core, the tokens are the
+# MMA's N. Same numerics as the tiled path: INT8 bit for bit, FP8 within the bf16 tolerance.
+
+@pytest.mark.parametrize("m", [1, 3, 8, 16, 17, 31, 32])
+@pytest.mark.parametrize("k,n", [(1024, 1024), (4096, 4160), (896, 200)])
+def test_int8_w8a8_linear_decode_sizes(kq, m, k, n):
+    g = torch.Generator().manual_seed(m * 131 + n)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16)
+    q, s = kq.quantize_int8(w.to(DEV))
+    y = kq.int8_w8a8_linear(x.to(DEV), q, s, b.to(DEV))
+    want = oq.int8_w8a8_linear(np_values(x), np_bytes(q).view(np.int8), s.cpu().numpy(), np_values(b))
+    assert y.shape == (m, n) and np.array_equal(np_bf16_bits(y), want)
+    a = rand_i8(g, m, k)
+    got = kq.int8_matmul(a.to(DEV), q).cpu().numpy()
+    assert np.array_equal(got, oq.int8_matmul(a.numpy(), np_bytes(q).view(np.int8)))
+
+
+@pytest.mark.parametrize("m", [1, 16, 24, 32])
+@pytest.mark.parametrize("k,n", [(1024, 3072), (4096, 4096)])
+def test_fp8_w8a8_linear_decode_sizes(kq, m, k, n):
+    g = torch.Generator().manual_seed(m + 3 * n)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16)
+    q, s = kq.quantize_fp8(w.to(DEV))
+    y = kq.fp8_w8a8_linear(x.to(DEV), q, s, b.to(DEV))
+    close_bf16(y, oq.fp8_w8a8_linear(np_values(x), np_bytes(q), s.cpu().numpy(), np_values(b), out_dtype="f32"),
+               f"fp8 decode {m}x{k}x{n}")
