@@ -13,6 +13,7 @@ Workloads (synthetic, seeded; BASELINE.json's configurations):
   compare  the comparator on a config-4-sized bf16 output pair (HBM-bound).
   fp8_blockwise  config 2: 1x128 FP8 producer + blockwise-scaled tcgen05 GEMM (M = 2048).
   fp8_attention  config 5: per-head e4m3 quantisation + causal tcgen05 FP8 attention.
+  w8a8_decode    decode-size INT8 W8A8 linear (M = 16): per-token producer + skinny GEMM.
 
 ``value`` is the whole-job throughput with inputs resident in HBM, timed with CUDA events
 over exactly K steps between barriers, the max over ranks; ``e2e`` is the same metric through
@@ -165,6 +166,9 @@ def _cpu_worker(args):
     elif kind == "w4a4":
         x, codes, scales, ts, bias = payload
         oq.fp4_w4a4_linear(x, codes, scales, ts, bias)
+    elif kind == "w8a8":
+        x, q, sc, bias = payload
+        oq.int8_w8a8_linear(x, q, sc, bias)
     elif kind == "compare":
         from oracle import compare as ocmp
 
@@ -332,6 +336,122 @@ class Mxfp8Producer(Workload):
         gb = rows * self.f * (4 + 1 + 1 / 32) / 1e9
         rate, cores = cpu_rate("mxfp8_silu", chunks, gb, 2.0 * max(steps, 1), procs)
         return rate, cores, f"oracle SiLU*up + MXFP8 on {rows} x {self.f} per step, {procs} processes"
+
+
+class W8a8Decode(Workload):
+    """SURVEY 8(f) decode-size W8A8: y = int8_w8a8_linear(x, W) at M = 16 tokens, X [16, 4096],
+    W [14336, 4096] int8 (58.7 MB, per-channel scales), bf16 out: the per-token producer and
+    the skinny GEMM (the weight streams through the tensor core). Four weight copies rotate so
+    every step reads its weight from HBM (4 x 58.7 MB > L2)."""
+
+    name = "w8a8_decode"
+    unit = "GB/s"
+    dtype = "int8 x int8 -> int32 -> bf16"
+    graph = True  # a step is microseconds: the K timed steps run as one CUDA graph
+
+    def setup(self, dev, world, rank):
+        import torch
+
+        from kernel_agent_b200.kernels import gemm, quant
+
+        self.torch, self.quant, self.gemm = torch, quant, gemm
+        self.m, self.k, self.n = 16, 4096, 14336
+        g = torch.Generator(device="cuda").manual_seed(0)
+        self.x = torch.randn(self.m, self.k, device=dev, generator=g).to(torch.bfloat16)
+        w = (torch.randn(self.n, self.k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        q, s = quant.quantize_int8(w)
+        del w
+        self.copies = [(q.clone(), s.clone()) for _ in range(4)]
+        self.bias = (torch.randn(self.n, device=dev, generator=g) * 0.1).to(torch.bfloat16)
+        self.i = 0
+        wbytes = self.n * self.k + 4 * self.n
+        self.bytes = wbytes + self.m * self.k * 2 + self.m * self.n * 2
+        self.units = self.bytes / 1e9
+        self.kernel = "gemm_skinny_kernel<KIND=0 int8>"
+        self.kernel_bytes = wbytes + self.m * self.k + self.m * self.n * 2
+        self.x_host = self.x.cpu().pin_memory()
+        self.y_host = torch.empty(self.m, self.n, dtype=torch.bfloat16).pin_memory()
+        self.h2d = self.m * self.k * 2
+        self.d2h = self.m * self.n * 2
+        self.config = {"workload": "decode-size W8A8 INT8 linear, X [16, 4096] x W [14336, 4096]^T -> bf16",
+                       "m": self.m, "k": self.k, "n": self.n,
+                       "l2": "4 rotating weight copies (235 MB) larger than L2",
+                       "launch": "the K timed steps are one CUDA graph (2 kernels per step)"}
+
+    def _next(self):
+        q, s = self.copies[self.i % len(self.copies)]
+        self.i += 1
+        return q, s
+
+    def step_at(self, i):
+        q, s = self.copies[i % len(self.copies)]
+        self.quant.int8_w8a8_linear(self.x, q, s, self.bias)
+        return 2
+
+    def dominant_at(self, i):
+        if not hasattr(self, "_xq"):
+            self._xq = self.quant.quantize_int8_activations(self.x)
+        q, s = self.copies[i % len(self.copies)]
+        xq, xs = self._xq
+        self.gemm.int8(xq, q, xs, s, self.bias, out_dtype=self.torch.bfloat16)
+        return 1
+
+    def step(self):
+        return self.step_at(0)
+
+    def e2e_step(self):
+        x = self.x_host.to(self.x.device, non_blocking=True)
+        q, s = self._next()
+        y = self.quant.int8_w8a8_linear(x, q, s, self.bias)
+        self.y_host.copy_(y, non_blocking=True)
+        return 2
+
+    def library_bar(self):
+        """cuBLASLt's int8 GEMM (torch._int_mm, M padded to 32) on the same codes: GB/s of
+        weight streamed."""
+        torch = self.torch
+        try:
+            xq, _ = self.quant.quantize_int8_activations(self.x)
+            xp = torch.zeros(32, self.k, dtype=torch.int8, device=self.x.device)
+            xp[: self.m] = xq
+            qs = [c[0] for c in self.copies]
+            for i in range(3):
+                torch._int_mm(xp, qs[i % 4].t())
+            torch.cuda.synchronize()
+            run = as_graph(lambda: [torch._int_mm(xp, qs[i % 4].t()) for i in range(20)], torch)
+            run()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+            a.record()
+            run()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / 20
+            return {"cublaslt_int8_gbs": (self.n * self.k) / (ms / 1e3) / 1e9,
+                    "what": "torch._int_mm int8 (M padded to 32), weight bytes per second, no epilogue, "
+                            "20 calls in one CUDA graph"}
+        except Exception as e:  # noqa: BLE001 - the bar is informational
+            return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+
+    def cpu_baseline(self):
+        return self._cpu(10.0, 1)
+
+    def _cpu(self, budget, procs):
+        import numpy as np
+
+        q, s = self.copies[0]
+        cols = 1024
+        chunks = [(self.x.float().cpu().numpy(), q[:cols].cpu().numpy().view(np.int8), s[:cols].cpu().numpy(),
+                   self.bias[:cols].float().cpu().numpy())]
+        gb = (cols * self.k + self.m * self.k * 2 + self.m * cols * 2) / 1e9
+        rate, cores = cpu_rate("w8a8", chunks * procs, gb * procs, budget, procs)
+        return {"value": rate, "unit": "GB/s", "cores": cores, "kind": "port",
+                "sample": f"oracle int8_w8a8_linear on X [16, 4096] x {cols} weight rows, repeated ~{budget:.0f} s"}
+
+    def reference(self, steps, warmup):
+        procs = os.cpu_count() or 1
+        r = self._cpu(2.0 * max(steps, 1), procs)
+        return r["value"], r["cores"], r["sample"] + f", {procs} processes"
 
 
 class Compare(Workload):
@@ -818,7 +938,8 @@ class Fp8Attention(Workload):
         return rate, os.cpu_count() or 1, "oracle qkpv attention of one (batch, head) per step"
 
 
-WORKLOADS = {w.name: w for w in (W4A4Linear, Nvfp4Producer, Mxfp8Producer, Compare, Fp8Blockwise, Fp8Attention)}
+WORKLOADS = {w.name: w for w in (W4A4Linear, Nvfp4Producer, Mxfp8Producer, Compare, Fp8Blockwise, Fp8Attention,
+                                  W8a8Decode)}
 DEFAULT = "w4a4"
 
 

@@ -4,7 +4,7 @@
 // cuda_fp8_skinny_gemm.py) on tcgen05: D[channel, token] = W[channel, :] . X[token, :].
 //
 // One CTA per 128-channel panel of W: warp 0 loads W [128 x 128 bytes] and X [NT x 128 bytes]
-// stages by TMA (rows of X past M read as zeros) into a 5-stage ring, warp 1 issues
+// stages by TMA (rows of X past M read as zeros) into a 10- or 5-stage ring, warp 1 issues
 // tcgen05.mma (kind::i8 exact int32, or kind::f8f6f4 fp32) into a [128 lanes x NT] TMEM
 // accumulator, warps 2-5 read it back (lane = channel) and apply the epilogue of the tiled
 // kernel, quant.py:920-922's acc.float() * xs[m] * sw[n] (+ bias), left to right in fp32, one
@@ -17,21 +17,23 @@
 
 namespace kab {
 
-template <int NT, int OUT>
+// STAGES 10 when the grid fits on the SMs (one CTA each, the deepest ring), 5 otherwise (two
+// CTAs per SM).
+template <int NT, int OUT, int STAGES>
 struct SkinnyLayout {
   static constexpr int kWBytes = 128 * 128;
   static constexpr int kXBytes = NT * 128;
   static constexpr int kStageBytes = kWBytes + kXBytes;
-  static constexpr int kStages = 5;  // two CTAs per SM
+  static constexpr int kStages = STAGES;
   static constexpr int kThreads = 192;
   static constexpr int kSmem = 1024 + kStages * kStageBytes + (2 * kStages + 1) * 8 + 16;
-  static_assert(kSmem <= 232448 / 2, "two CTAs per SM");
+  static_assert(kSmem <= (STAGES > 5 ? 232448 : 232448 / 2), "shared memory per CTA");
 };
 
-template <int KIND, int NT, int OUT>
+template <int KIND, int NT, int OUT, int STAGES_>
 __global__ void __launch_bounds__(192, 2)
 gemm_skinny_kernel(const __grid_constant__ CUtensorMap tma_w, const __grid_constant__ CUtensorMap tma_x, GemmArgs g) {
-  using L = SkinnyLayout<NT, OUT>;
+  using L = SkinnyLayout<NT, OUT, STAGES_>;
   constexpr int STAGES = L::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));

@@ -171,10 +171,10 @@ int launch_pair(int out, const CUtensorMap& ma, const CUtensorMap& mb, const CUt
 }
 
 // The skinny kernel (gemm_skinny.cuh) for M <= 32: one CTA per 128-channel panel of W.
-template <int KIND, int NT, int OUT>
+template <int KIND, int NT, int OUT, int STAGES>
 int launch_skinny_one(const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& g, cudaStream_t s) {
-  using L = SkinnyLayout<NT, OUT>;
-  auto kernel = gemm_skinny_kernel<KIND, NT, OUT>;
+  using L = SkinnyLayout<NT, OUT, STAGES>;
+  auto kernel = gemm_skinny_kernel<KIND, NT, OUT, STAGES>;
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -188,14 +188,20 @@ int launch_skinny_one(const CUtensorMap& mw, const CUtensorMap& mx, const GemmAr
   return check_launch("skinny gemm kernel");
 }
 
+template <int KIND, int NT, int OUT>
+int launch_skinny_stages(const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& g, cudaStream_t s) {
+  if ((g.n + 127) / 128 <= sm_count()) return launch_skinny_one<KIND, NT, OUT, 10>(mw, mx, g, s);
+  return launch_skinny_one<KIND, NT, OUT, 5>(mw, mx, g, s);
+}
+
 template <int KIND, int NT>
 int launch_skinny_nt(int out, const CUtensorMap& mw, const CUtensorMap& mx, const GemmArgs& g, cudaStream_t s) {
   if constexpr (KIND == 0) {
-    if (out == kOutI32) return launch_skinny_one<KIND, NT, kOutI32>(mw, mx, g, s);
+    if (out == kOutI32) return launch_skinny_stages<KIND, NT, kOutI32>(mw, mx, g, s);
   }
-  if (out == KAB_BF16) return launch_skinny_one<KIND, NT, KAB_BF16>(mw, mx, g, s);
-  if (out == KAB_F16) return launch_skinny_one<KIND, NT, KAB_F16>(mw, mx, g, s);
-  return launch_skinny_one<KIND, NT, KAB_F32>(mw, mx, g, s);
+  if (out == KAB_BF16) return launch_skinny_stages<KIND, NT, KAB_BF16>(mw, mx, g, s);
+  if (out == KAB_F16) return launch_skinny_stages<KIND, NT, KAB_F16>(mw, mx, g, s);
+  return launch_skinny_stages<KIND, NT, KAB_F32>(mw, mx, g, s);
 }
 
 // KAB_GEMM_PAIR=1 routes shapes with M > 128 and N >= 256 to the CTA-pair kernel. Off by
