@@ -14,6 +14,8 @@ Workloads (synthetic, seeded; BASELINE.json's configurations):
   fp8_blockwise  config 2: 1x128 FP8 producer + blockwise-scaled tcgen05 GEMM (M = 2048).
   fp8_attention  config 5: per-head e4m3 quantisation + causal tcgen05 FP8 attention.
   w8a8_decode    decode-size INT8 W8A8 linear (M = 16): per-token producer + skinny GEMM.
+  kv_decode      FP8 KV-cache decode attention (16 / 2 heads, head_dim 128, batch 4, 4096
+                 cached tokens): split-KV tcgen05 attention over e4m3 K / V.
 
 ``value`` is the whole-job throughput with inputs resident in HBM, timed with CUDA events
 over exactly K steps between barriers, the max over ranks; ``e2e`` is the same metric through
@@ -169,6 +171,10 @@ def _cpu_worker(args):
     elif kind == "w8a8":
         x, q, sc, bias = payload
         oq.int8_w8a8_linear(x, q, sc, bias)
+    elif kind == "kv":
+        from oracle import kv_quant as okv
+
+        okv.fp8_kv_attention(*payload)
     elif kind == "compare":
         from oracle import compare as ocmp
 
@@ -339,7 +345,7 @@ class Mxfp8Producer(Workload):
 
 
 class W8a8Decode(Workload):
-    """SURVEY 8(f) decode-size W8A8: y = int8_w8a8_linear(x, W) at M = 16 tokens, X [16, 4096],
+    """Decode-size W8A8: y = int8_w8a8_linear(x, W) at M = 16 tokens, X [16, 4096],
     W [14336, 4096] int8 (58.7 MB, per-channel scales), bf16 out: the per-token producer and
     the skinny GEMM (the weight streams through the tensor core). Four weight copies rotate so
     every step reads its weight from HBM (4 x 58.7 MB > L2)."""
@@ -447,6 +453,116 @@ class W8a8Decode(Workload):
         rate, cores = cpu_rate("w8a8", chunks * procs, gb * procs, budget, procs)
         return {"value": rate, "unit": "GB/s", "cores": cores, "kind": "port",
                 "sample": f"oracle int8_w8a8_linear on X [16, 4096] x {cols} weight rows, repeated ~{budget:.0f} s"}
+
+    def reference(self, steps, warmup):
+        procs = os.cpu_count() or 1
+        r = self._cpu(2.0 * max(steps, 1), procs)
+        return r["value"], r["cores"], r["sample"] + f", {procs} processes"
+
+
+class KvDecode(Workload):
+    """FP8 KV-cache decode (kv_quant.py, triton_fp8_kv_decode.py): one query token per sequence,
+    16 query / 2 KV heads, head_dim 128, batch 4, 4096 cached tokens (the reference selftest's
+    long-cache call, selftest.py:749), e4m3 K / V with one fp32 scale per (token, head). A step
+    is one fp8_kv_decode call: one kernel (split-KV, the splits merged in the same launch).
+    24 cache copies rotate so that every step reads its cache from HBM (24 x 8.65 MB > L2)."""
+
+    name = "kv_decode"
+    unit = "GB/s"
+    dtype = "e4m3 K / V, bf16 q -> fp32 -> bf16"
+    graph = True
+
+    def setup(self, dev, world, rank):
+        import torch
+
+        from kernel_agent_b200.kernels import kv_quant
+
+        self.torch, self.kv = torch, kv_quant
+        self.b, self.hq, self.hkv, self.l, self.d = 4, 16, 2, 4096, 128
+        g = torch.Generator(device="cuda").manual_seed(0)
+        self.q = torch.randn(self.b, self.hq, self.d, device=dev, generator=g).to(torch.bfloat16)
+        self.copies = []
+        for _ in range(24):
+            k = torch.randn(self.b, self.hkv, self.l, self.d, device=dev, generator=g).to(torch.bfloat16)
+            v = torch.randn(self.b, self.hkv, self.l, self.d, device=dev, generator=g).to(torch.bfloat16)
+            self.copies.append((*kv_quant.quantize_kv(k), *kv_quant.quantize_kv(v)))
+        self.bf16_kv = (k, v)
+        rows = self.b * self.hkv * self.l
+        qo = 2 * self.b * self.hq * self.d * 2
+        self.bytes = 2 * rows * self.d + 2 * rows * 4 + qo
+        self.units = self.bytes / 1e9
+        self.kernel = "kv_decode_kernel<128, 16, bf16>"
+        self.kernel_bytes = self.bytes
+        self.q_host = self.q.cpu().pin_memory()
+        self.y_host = torch.empty(self.b, self.hq, self.d, dtype=torch.bfloat16).pin_memory()
+        self.h2d = self.b * self.hq * self.d * 2
+        self.d2h = self.h2d
+        self.config = {"workload": "FP8 KV-cache decode, q [4, 16, 128] over e4m3 K / V [4, 2, 4096, 128]",
+                       "batch": self.b, "heads_q": self.hq, "heads_kv": self.hkv, "tokens": self.l,
+                       "head_dim": self.d,
+                       "l2": "24 rotating cache copies (208 MB) larger than L2",
+                       "launch": "the K timed steps are one CUDA graph (1 kernel per step)"}
+
+    def step_at(self, i):
+        kc, ks, vc, vs = self.copies[i % len(self.copies)]
+        self.kv.fp8_kv_decode(self.q, kc, ks, vc, vs)
+        return 1
+
+    def dominant_at(self, i):
+        return self.step_at(i)
+
+    def step(self):
+        return self.step_at(0)
+
+    def e2e_step(self):
+        q = self.q_host.to(self.q.device, non_blocking=True)
+        self.i = getattr(self, "i", 0) + 1
+        kc, ks, vc, vs = self.copies[self.i % len(self.copies)]
+        y = self.kv.fp8_kv_decode(q, kc, ks, vc, vs)
+        self.y_host.copy_(y, non_blocking=True)
+        return 1
+
+    def library_bar(self):
+        """torch SDPA (bf16, GQA) on the unquantised bf16 cache: the decode the e4m3 cache
+        replaces (half the cache bytes)."""
+        torch = self.torch
+        try:
+            k, v = self.bf16_kv
+            q4 = self.q[:, :, None]
+            f = lambda: torch.nn.functional.scaled_dot_product_attention(q4, k, v, enable_gqa=True)  # noqa: E731
+            for _ in range(3):
+                f()
+            torch.cuda.synchronize()
+            run = as_graph(lambda: [f() for _ in range(20)], torch)
+            run()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+            a.record()
+            run()
+            b.record()
+            torch.cuda.synchronize()
+            us = a.elapsed_time(b) / 20 * 1e3
+            return {"sdpa_bf16_us": us, "sdpa_bf16_gbs": (2 * k.numel() * 2) / (us / 1e6) / 1e9,
+                    "what": "torch SDPA bf16 GQA decode on the bf16 cache (L2-warm: one cache), 20 calls "
+                            "in one CUDA graph"}
+        except Exception as e:  # noqa: BLE001 - the bar is informational
+            return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+
+    def cpu_baseline(self):
+        return self._cpu(10.0, 1)
+
+    def _cpu(self, budget, procs):
+        import numpy as np
+
+        kc, ks, vc, vs = self.copies[0]
+        q = self.q[:1, :, None].float().cpu().numpy()  # one sequence of the batch
+        u8 = lambda t: t[:1].cpu().view(self.torch.uint8).numpy()  # noqa: E731
+        chunk = (q, u8(kc), ks[:1].cpu().numpy(), u8(vc), vs[:1].cpu().numpy())
+        gb = self.bytes / self.b / 1e9
+        rate, cores = cpu_rate("kv", [chunk] * procs, gb * procs, budget, procs)
+        return {"value": rate, "unit": "GB/s", "cores": cores, "kind": "port",
+                "sample": "oracle fp8_kv_attention (float64) on one sequence of the batch, repeated "
+                          f"~{budget:.0f} s"}
 
     def reference(self, steps, warmup):
         procs = os.cpu_count() or 1
@@ -939,7 +1055,7 @@ class Fp8Attention(Workload):
 
 
 WORKLOADS = {w.name: w for w in (W4A4Linear, Nvfp4Producer, Mxfp8Producer, Compare, Fp8Blockwise, Fp8Attention,
-                                  W8a8Decode)}
+                                  W8a8Decode, KvDecode)}
 DEFAULT = "w4a4"
 
 

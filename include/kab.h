@@ -360,6 +360,56 @@ int kab_attention_fp8(const uint8_t* q, const float* q_scale, const uint8_t* k, 
                       int64_t heads_kv, int64_t seq, int64_t head_dim, int causal, float sm_scale,
                       void* out, void* stream);
 
+/* ------------------------------------------------------------------ FP8 KV cache */
+
+/* kv_quant.py:38-46 quantize_fp8_kv (and triton_fp8_kv_decode.py:51-64 _quant_kv_kernel):
+ * one fp32 scale per row of d elements (a token of one KV head), amax / 448 where amax > 0
+ * else 1, codes e4m3(v / scale) clamped to +-448, nearest even. Rows are outer x inner; row
+ * (o, i) reads x + o * xs_o + i * xs_i, writes codes + o * cs_o + i * cs_i and
+ * scales + o * ss_o + i * ss_i (element strides): an append writes straight into the slots
+ * of a preallocated cache (kv_quant.py:133-151 Fp8KVCache.append). d a power of two in
+ * 16..256; x 16-byte aligned; row starts multiples of 8 elements. */
+int kab_quant_kv_fp8(const void* x, int dtype, int64_t outer, int64_t inner, int64_t d, int64_t xs_o,
+                     int64_t xs_i, uint8_t* codes, int64_t cs_o, int64_t cs_i, float* scales,
+                     int64_t ss_o, int64_t ss_i, void* stream);
+
+/* Decode attention over an e4m3 KV cache (kv_quant.py:56-83 fp8_kv_attention;
+ * triton_fp8_kv_decode.py:195-260 fp8_kv_decode): softmax(Q K^T * sm_scale) V with
+ * K = k_codes * k_scales[..., None], V likewise, grouped-query heads (heads_q a multiple of
+ * heads_kv), optional per-sequence lengths (the first lengths[b] tokens, >= 1), every query
+ * token seeing every valid cached token. q [batch, heads_q, q_len, head_dim] (element
+ * strides: q_stride_b between sequences, q_stride_row between the rows of one KV head's group,
+ * which are the query heads x query tokens, contiguous in that order), codes [batch, heads_kv,
+ * length, head_dim] (byte strides, multiples of 16), scales [batch, heads_kv, length] fp32
+ * (unit last stride); out [batch, heads_q, q_len, head_dim] bf16, contiguous. head_dim 64 or
+ * 128; heads_q / heads_kv * q_len <= 32. `splits`: chunks of the cache per (sequence,
+ * KV head), at most 256; 0 for one wave of the CTAs that fit on the GPU. */
+typedef struct KabKvDecodeParams {
+  const void* q;
+  int q_dtype;
+  int64_t q_stride_b, q_stride_row;
+  const uint8_t* k_codes;
+  const float* k_scales;
+  const uint8_t* v_codes;
+  const float* v_scales;
+  int64_t kc_stride_b, kc_stride_h, kc_stride_l;
+  int64_t vc_stride_b, vc_stride_h, vc_stride_l;
+  int64_t ks_stride_b, ks_stride_h;
+  int64_t vs_stride_b, vs_stride_h;
+  const int32_t* lengths; /* [batch] or NULL */
+  int64_t batch, heads_q, heads_kv, q_len, length, head_dim;
+  float sm_scale;
+  int splits;
+  void* out;
+} KabKvDecodeParams;
+
+/* The splits the launch will use and the workspace bytes it needs (0 with one split). The
+ * workspace holds the per-split partials and one counter per (sequence, KV head): zero it
+ * once when it is allocated; every launch leaves the counters at zero. */
+int kab_kv_decode_workspace(const KabKvDecodeParams* params, int* splits, size_t* bytes);
+int kab_kv_decode_fp8(const KabKvDecodeParams* params, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -3,6 +3,7 @@
 // device status word.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "kab_host.h"
@@ -12,6 +13,7 @@ __device__ unsigned g_attention_status = 0;
 }  // namespace kab
 
 #include "attention.cuh"
+#include "attention_decode.cuh"
 
 namespace kab {
 
@@ -55,6 +57,108 @@ int byte_map(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, co
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(KAB_EINVAL, "tensor map of %s failed (CUresult %d)", name, static_cast<int>(r));
   return KAB_OK;
+}
+
+// A [B, H, L, D] e4m3 cache (element strides sb, sh, sl; unit last stride) read in boxes of
+// 128 tokens x D bytes of one (sequence, head), swizzled like the MMA operands (D = 128: the
+// 128-byte swizzle, D = 64: the 64-byte one); tokens at or past L read as zeros.
+int cache_map(CUtensorMap* map, const void* ptr, int64_t b, int64_t hh, int64_t l, int64_t d, int64_t sb, int64_t sh,
+              int64_t sl, const char* name) {
+  auto fn = attn_encode_fn();
+  if (fn == nullptr) return fail(KAB_EUNSUPPORTED, "cuTensorMapEncodeTiled is unavailable (driver too old?)");
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(l), static_cast<cuuint64_t>(hh),
+                        static_cast<cuuint64_t>(b)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(sl), static_cast<cuuint64_t>(sh), static_cast<cuuint64_t>(sb)};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(d), 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, d == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KAB_EINVAL, "tensor map of %s failed (CUresult %d)", name, static_cast<int>(r));
+  return KAB_OK;
+}
+
+template <int D, int GP>
+auto decode_kernel_for(int qt) {
+  return qt == KAB_BF16 ? kv_decode_kernel<D, GP, kBF16>
+         : qt == KAB_F16 ? kv_decode_kernel<D, GP, kF16>
+                         : kv_decode_kernel<D, GP, kF32>;
+}
+
+// Opts the kernel instance into its shared memory (once per device) and returns the CTAs of
+// it that fit on one SM.
+template <int D, int GP>
+int decode_prepare(int qt) {
+  using L = DecodeLayout<D, GP>;
+  static int resident[3][64] = {};
+  const int ti = qt == KAB_BF16 ? 0 : qt == KAB_F16 ? 1 : 2;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64) return 1;
+  if (resident[ti][dev] == 0) {
+    auto kern = decode_kernel_for<D, GP>(qt);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem) != cudaSuccess) return -1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, L::kThreads, L::kSmem) != cudaSuccess) return -1;
+    resident[ti][dev] = n > 0 ? n : 1;
+  }
+  return resident[ti][dev];
+}
+
+int decode_resident(int64_t d, int gp, int qt) {
+  if (d == 128)
+    return gp == 8 ? decode_prepare<128, 8>(qt) : gp == 16 ? decode_prepare<128, 16>(qt) : decode_prepare<128, 32>(qt);
+  return gp == 8 ? decode_prepare<64, 8>(qt) : gp == 16 ? decode_prepare<64, 16>(qt) : decode_prepare<64, 32>(qt);
+}
+
+// Splits per (sequence, KV head) and tokens per split (a multiple of 128): the asked splits,
+// or with 0 one wave of the CTAs that fit on the GPU (triton_fp8_kv_decode.py:232-235 asks
+// for ~4 programs per SM).
+void decode_split(const KabKvDecodeParams* p, int resident, int* splits, int* chunk) {
+  const int64_t tiles = (p->length + 127) / 128;
+  int64_t s = p->splits;
+  if (s <= 0) {
+    const int64_t pairs = p->batch * p->heads_kv;
+    s = (static_cast<int64_t>(resident) * sm_count() + pairs - 1) / pairs;
+  }
+  s = std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(s, tiles), 256));  // the merge's weights fit in the ring
+  const int64_t per = (p->length + s - 1) / s;
+  const int64_t c = (per + 127) / 128 * 128;
+  *chunk = static_cast<int>(c);
+  *splits = static_cast<int>((p->length + c - 1) / c);
+}
+
+size_t decode_workspace_bytes(const KabKvDecodeParams* p, int splits, int gp) {
+  if (splits <= 1) return 0;
+  const size_t pairs = static_cast<size_t>(p->batch * p->heads_kv);
+  const size_t counters = (pairs * 4 + 255) / 256 * 256;
+  const size_t ml = (pairs * splits * 2 * gp * 4 + 255) / 256 * 256;
+  return counters + ml + pairs * splits * gp * static_cast<size_t>(p->head_dim) * 4;
+}
+
+int decode_check(const KabKvDecodeParams* p, int* gp) {
+  KAB_REQUIRE(p != nullptr, "null parameters");
+  KAB_REQUIRE(p->batch >= 0 && p->heads_q >= 0 && p->heads_kv > 0 && p->length >= 0 && p->q_len >= 1,
+              "bad shape");
+  KAB_REQUIRE(p->head_dim == 64 || p->head_dim == 128, "head_dim %lld: the kernel takes 64 or 128",
+              (long long)p->head_dim);
+  KAB_REQUIRE(p->heads_q % p->heads_kv == 0, "heads_q %lld is not a multiple of heads_kv %lld",
+              (long long)p->heads_q, (long long)p->heads_kv);
+  const int64_t rows = p->heads_q / p->heads_kv * p->q_len;
+  KAB_REQUIRE(rows <= 32, "%lld query rows per KV head (query heads per KV head x query tokens): at most 32",
+              (long long)rows);
+  *gp = rows <= 8 ? 8 : rows <= 16 ? 16 : 32;
+  return KAB_OK;
+}
+
+template <int D, int GP>
+int launch_decode_t(const CUtensorMap& mk, const CUtensorMap& mv, const DecodeArgs& g, int qt, int64_t pairs,
+                    cudaStream_t s) {
+  using L = DecodeLayout<D, GP>;
+  auto kern = decode_kernel_for<D, GP>(qt);
+  const dim3 grid(static_cast<unsigned>(g.splits), static_cast<unsigned>(pairs));
+  kern<<<grid, L::kThreads, L::kSmem, s>>>(mk, mv, g);
+  return check_launch("kab_kv_decode_fp8");
 }
 
 }  // namespace
@@ -137,6 +241,121 @@ int kab_attention_fp8(const uint8_t* q, const float* q_scale, const uint8_t* k, 
   attention_fp8_kernel<<<static_cast<unsigned>(ctas), AttnLayout::kThreads, AttnLayout::kSmem, as_stream(stream)>>>(
       mq, mk, mv, g);
   return check_launch("kab_attention_fp8");
+}
+
+int kab_quant_kv_fp8(const void* x, int dtype, int64_t outer, int64_t inner, int64_t d, int64_t xs_o, int64_t xs_i,
+                     uint8_t* codes, int64_t cs_o, int64_t cs_i, float* scales, int64_t ss_o, int64_t ss_i,
+                     void* stream) {
+  KAB_REQUIRE(valid_dtype(dtype), "unknown dtype %d", dtype);
+  KAB_REQUIRE(outer >= 0 && inner >= 0 && d >= 0, "negative shape");
+  if (outer == 0 || inner == 0) return KAB_OK;
+  KAB_REQUIRE(x != nullptr && codes != nullptr && scales != nullptr, "null pointer");
+  KAB_REQUIRE(d == 16 || d == 32 || d == 64 || d == 128 || d == 256, "head_dim %lld: a power of two in 16..256",
+              (long long)d);
+  KAB_REQUIRE(aligned(x, 16) && aligned(codes, 8) && xs_o % 8 == 0 && xs_i % 8 == 0 && cs_o % 8 == 0 &&
+                  cs_i % 8 == 0,
+              "x must be 16-byte aligned, codes 8-byte aligned, and every row start a multiple of 8 elements");
+  const int64_t rows = outer * inner;
+  const int64_t lanes = d / 8;
+  const int64_t blocks = (rows * lanes + 255) / 256;
+  KAB_REQUIRE(blocks < (int64_t(1) << 31), "too many rows");
+  const cudaStream_t s = as_stream(stream);
+#define KAB_KV(TT, LN)                                                                                      \
+  quant_kv_kernel<TT, LN><<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, rows, inner, xs_o, xs_i, codes, \
+                                                                         cs_o, cs_i, scales, ss_o, ss_i)
+#define KAB_KV_D(TT)                  \
+  switch (lanes) {                    \
+    case 2: KAB_KV(TT, 2); break;     \
+    case 4: KAB_KV(TT, 4); break;     \
+    case 8: KAB_KV(TT, 8); break;     \
+    case 16: KAB_KV(TT, 16); break;   \
+    default: KAB_KV(TT, 32); break;   \
+  }
+  if (dtype == KAB_BF16) { KAB_KV_D(kBF16) }
+  else if (dtype == KAB_F16) { KAB_KV_D(kF16) }
+  else { KAB_KV_D(kF32) }
+#undef KAB_KV_D
+#undef KAB_KV
+  return check_launch("kab_quant_kv_fp8");
+}
+
+int kab_kv_decode_workspace(const KabKvDecodeParams* p, int* splits, size_t* bytes) {
+  int gp = 16;
+  if (int e = decode_check(p, &gp)) return e;
+  KAB_REQUIRE(bytes != nullptr, "null pointer");
+  int sp = 1, chunk = 128;
+  if (p->length > 0) {
+    const int resident = decode_resident(p->head_dim, gp, valid_dtype(p->q_dtype) ? p->q_dtype : KAB_BF16);
+    if (resident < 0) return fail(KAB_ECUDA, "cannot configure the decode kernel");
+    decode_split(p, resident, &sp, &chunk);
+  }
+  if (splits != nullptr) *splits = sp;
+  *bytes = decode_workspace_bytes(p, sp, gp);
+  return KAB_OK;
+}
+
+int kab_kv_decode_fp8(const KabKvDecodeParams* p, void* workspace, size_t workspace_bytes, void* stream) {
+  int gp = 16;
+  if (int e = decode_check(p, &gp)) return e;
+  if (p->batch == 0 || p->heads_q == 0) return KAB_OK;
+  KAB_REQUIRE(p->length >= 1, "an empty cache: at least one token is needed");
+  KAB_REQUIRE(valid_dtype(p->q_dtype), "unknown q dtype %d", p->q_dtype);
+  KAB_REQUIRE(p->q && p->k_codes && p->k_scales && p->v_codes && p->v_scales && p->out, "null pointer");
+  KAB_REQUIRE(aligned(p->k_codes, 16) && aligned(p->v_codes, 16), "the codes must be 16-byte aligned");
+  const int64_t d = p->head_dim;
+  KAB_REQUIRE(p->kc_stride_l % 16 == 0 && p->kc_stride_h % 16 == 0 && p->kc_stride_b % 16 == 0 &&
+                  p->vc_stride_l % 16 == 0 && p->vc_stride_h % 16 == 0 && p->vc_stride_b % 16 == 0,
+              "code strides must be multiples of 16 bytes");
+  KAB_REQUIRE(p->length < (int64_t(1) << 30) && p->batch * p->heads_kv < 65536, "problem too large");
+  const int resident = decode_resident(d, gp, p->q_dtype);
+  if (resident < 0) return fail(KAB_ECUDA, "cannot configure the decode kernel");
+  int splits = 1, chunk = 128;
+  decode_split(p, resident, &splits, &chunk);
+  const size_t need = decode_workspace_bytes(p, splits, gp);
+  KAB_REQUIRE(need == 0 || (workspace != nullptr && workspace_bytes >= need && aligned(workspace, 256)),
+              "the workspace needs %zu bytes, 256-byte aligned (kab_kv_decode_workspace)", need);
+  CUtensorMap mk, mv;
+  if (int e = cache_map(&mk, p->k_codes, p->batch, p->heads_kv, p->length, d, p->kc_stride_b, p->kc_stride_h,
+                        p->kc_stride_l, "K codes"))
+    return e;
+  if (int e = cache_map(&mv, p->v_codes, p->batch, p->heads_kv, p->length, d, p->vc_stride_b, p->vc_stride_h,
+                        p->vc_stride_l, "V codes"))
+    return e;
+  DecodeArgs g{};
+  g.heads_kv = static_cast<int>(p->heads_kv);
+  g.group = static_cast<int>(p->heads_q / p->heads_kv * p->q_len);
+  g.length = static_cast<int>(p->length);
+  g.chunk = chunk;
+  g.splits = splits;
+  g.q = p->q;
+  g.sqb = p->q_stride_b;
+  g.sqh = p->q_stride_row;
+  g.k_scale = p->k_scales;
+  g.ksb = p->ks_stride_b;
+  g.ksh = p->ks_stride_h;
+  g.v_scale = p->v_scales;
+  g.vsb = p->vs_stride_b;
+  g.vsh = p->vs_stride_h;
+  g.lengths = p->lengths;
+  g.scale_log2 = p->sm_scale * 1.4426950408889634f;
+  g.out = p->out;
+  const int64_t pairs = p->batch * p->heads_kv;
+  if (need > 0) {
+    uint8_t* w = static_cast<uint8_t*>(workspace);
+    const size_t counters = (static_cast<size_t>(pairs) * 4 + 255) / 256 * 256;
+    const size_t ml = (static_cast<size_t>(pairs) * splits * 2 * gp * 4 + 255) / 256 * 256;
+    g.counters = reinterpret_cast<unsigned*>(w);
+    g.part_ml = reinterpret_cast<float*>(w + counters);
+    g.part_o = reinterpret_cast<float*>(w + counters + ml);
+  }
+  const cudaStream_t s = as_stream(stream);
+  if (d == 128)
+    return gp == 8    ? launch_decode_t<128, 8>(mk, mv, g, p->q_dtype, pairs, s)
+           : gp == 16 ? launch_decode_t<128, 16>(mk, mv, g, p->q_dtype, pairs, s)
+                      : launch_decode_t<128, 32>(mk, mv, g, p->q_dtype, pairs, s);
+  return gp == 8    ? launch_decode_t<64, 8>(mk, mv, g, p->q_dtype, pairs, s)
+         : gp == 16 ? launch_decode_t<64, 16>(mk, mv, g, p->q_dtype, pairs, s)
+                    : launch_decode_t<64, 32>(mk, mv, g, p->q_dtype, pairs, s);
 }
 
 }  // extern "C"

@@ -60,6 +60,21 @@ class KabCompareParams(ctypes.Structure):
     ]
 
 
+class KabKvDecodeParams(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("q_dtype", c_int), ("q_stride_b", c_int64), ("q_stride_row", c_int64),
+        ("k_codes", c_void_p), ("k_scales", c_void_p), ("v_codes", c_void_p), ("v_scales", c_void_p),
+        ("kc_stride_b", c_int64), ("kc_stride_h", c_int64), ("kc_stride_l", c_int64),
+        ("vc_stride_b", c_int64), ("vc_stride_h", c_int64), ("vc_stride_l", c_int64),
+        ("ks_stride_b", c_int64), ("ks_stride_h", c_int64),
+        ("vs_stride_b", c_int64), ("vs_stride_h", c_int64),
+        ("lengths", c_void_p),
+        ("batch", c_int64), ("heads_q", c_int64), ("heads_kv", c_int64), ("q_len", c_int64),
+        ("length", c_int64), ("head_dim", c_int64),
+        ("sm_scale", c_float), ("splits", c_int), ("out", c_void_p),
+    ]
+
+
 # name -> argument types (the return type is int unless listed in _RESTYPES)
 _SIGNATURES: dict[str, list] = {
     "kab_last_error": [],
@@ -107,6 +122,10 @@ _SIGNATURES: dict[str, list] = {
                             c_void_p],
     "kab_attention_fp8": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                           c_int64, c_int64, c_int, ctypes.c_float, c_void_p, c_void_p],
+    "kab_quant_kv_fp8": [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64,
+                         c_void_p, c_int64, c_int64, c_void_p],
+    "kab_kv_decode_workspace": [POINTER(KabKvDecodeParams), POINTER(c_int), POINTER(c_size_t)],
+    "kab_kv_decode_fp8": [POINTER(KabKvDecodeParams), c_void_p, c_size_t, c_void_p],
     "kab_mxfp8_saturation": [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
     "kab_fp4_scale_check": [c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_void_p, c_void_p, c_int, c_void_p,
                             c_void_p],
