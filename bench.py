@@ -481,12 +481,13 @@ class KvDecode(Workload):
         self.b, self.hq, self.hkv, self.l, self.d = 4, 16, 2, 4096, 128
         g = torch.Generator(device="cuda").manual_seed(0)
         self.q = torch.randn(self.b, self.hq, self.d, device=dev, generator=g).to(torch.bfloat16)
-        self.copies = []
-        for _ in range(24):
+        self.copies, self.bf16_kv = [], []
+        for i in range(24):
             k = torch.randn(self.b, self.hkv, self.l, self.d, device=dev, generator=g).to(torch.bfloat16)
             v = torch.randn(self.b, self.hkv, self.l, self.d, device=dev, generator=g).to(torch.bfloat16)
             self.copies.append((*kv_quant.quantize_kv(k), *kv_quant.quantize_kv(v)))
-        self.bf16_kv = (k, v)
+            if i < 12:  # the bf16 cache of the library bar, rotated the same way (201 MB > L2)
+                self.bf16_kv.append((k, v))
         rows = self.b * self.hkv * self.l
         qo = 2 * self.b * self.hq * self.d * 2
         self.bytes = 2 * rows * self.d + 2 * rows * 4 + qo
@@ -527,13 +528,14 @@ class KvDecode(Workload):
         replaces (half the cache bytes)."""
         torch = self.torch
         try:
-            k, v = self.bf16_kv
             q4 = self.q[:, :, None]
-            f = lambda: torch.nn.functional.scaled_dot_product_attention(q4, k, v, enable_gqa=True)  # noqa: E731
-            for _ in range(3):
-                f()
+            kvs = self.bf16_kv
+            f = lambda i: torch.nn.functional.scaled_dot_product_attention(  # noqa: E731
+                q4, kvs[i % len(kvs)][0], kvs[i % len(kvs)][1], enable_gqa=True)
+            for i in range(3):
+                f(i)
             torch.cuda.synchronize()
-            run = as_graph(lambda: [f() for _ in range(20)], torch)
+            run = as_graph(lambda: [f(i) for i in range(24)], torch)
             run()
             torch.cuda.synchronize()
             a, b = torch.cuda.Event(True), torch.cuda.Event(True)
@@ -541,10 +543,10 @@ class KvDecode(Workload):
             run()
             b.record()
             torch.cuda.synchronize()
-            us = a.elapsed_time(b) / 20 * 1e3
-            return {"sdpa_bf16_us": us, "sdpa_bf16_gbs": (2 * k.numel() * 2) / (us / 1e6) / 1e9,
-                    "what": "torch SDPA bf16 GQA decode on the bf16 cache (L2-warm: one cache), 20 calls "
-                            "in one CUDA graph"}
+            us = a.elapsed_time(b) / 24 * 1e3
+            return {"sdpa_bf16_us": us, "sdpa_bf16_gbs": (2 * kvs[0][0].numel() * 2) / (us / 1e6) / 1e9,
+                    "what": "torch SDPA bf16 GQA decode on the unquantised bf16 cache, 12 rotating copies "
+                            "(201 MB, larger than L2), 24 calls in one CUDA graph"}
         except Exception as e:  # noqa: BLE001 - the bar is informational
             return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
 

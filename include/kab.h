@@ -325,6 +325,9 @@ typedef struct KabScaleCheck {
   unsigned long long saturated, underflow, nonfinite, not_representable, coarser, not_pow2;
   unsigned worst_ratio_bits;
   unsigned pad;
+  /* kab_fp4_scale_check: blocks whose ratio exceeds 6 * (1 + 2^-20), quant.py:1260-1297
+   * fp4_saturation's count */
+  unsigned long long saturated_plain;
 } KabScaleCheck;
 
 /* quant.py:623-660 mxfp8_saturation: x [rows, k] against fp32 MXFP8 scale values `step`
@@ -340,6 +343,14 @@ int kab_mxfp8_saturation(const void* x, int dtype, int64_t rows, int64_t k, int6
 int kab_fp4_scale_check(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, int fmt,
                         const float* scale, const float* outer, int outer_per_row,
                         KabScaleCheck* result, void* stream);
+
+/* Per-row sums of a pair of [rows, k] matrices x, y (x and y each fp32 / bf16 / fp16, rows
+ * ldx / ldy elements apart), the reductions of the error reports (quant.py:133-181, 302-326,
+ * 420-476, 707-768, 926-1000, 1511-1573; kv_quant.py:86-101): out[row * 8 + i] for
+ * i = 0..7: sum x^2, sum y^2, sum (x - y)^2, sum x * y, max |x|, count(x != 0),
+ * count(x != 0 and y == 0), max |y|; float64, NaN propagating. */
+int kab_row_pair_stats(const void* x, int x_dtype, int64_t ldx, const void* y, int y_dtype, int64_t ldy,
+                       int64_t rows, int64_t k, double* out, void* stream);
 
 /* ------------------------------------------------------------------ FP8 attention prefill */
 

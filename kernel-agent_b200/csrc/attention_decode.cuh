@@ -94,24 +94,25 @@ struct DecodeLayout {
   static constexpr int kTile = 128 * kRow;        // one K or V tile
   static constexpr int kZero = D < 128 ? kTile : 0;  // zero rows M = D..127 of V^T (D = 64)
   static constexpr int kStage = 2 * kTile + kZero;
-  static constexpr int kStages = D < 128 ? 4 : 3;
+  static constexpr int kStages = D < 128 ? 7 : 5;
   static constexpr int kN = 2 * GP;               // MMA N: two terms per query head
   static constexpr int kQ = 0;                    // [kN rows, D bytes], K-major swizzled
   static constexpr int kP = kQ + ((kN * kRow + 1023) & ~1023);  // 2 x [kN / 16 blocks][128 tok][16 B]
   static constexpr int kPBytes = (kN / 16) * 2048;
   static constexpr int kRing = kP + 2 * kPBytes;  // stage s: K | V | zeros
-  static constexpr int kRed = kRing + kStages * kStage;  // [2][4 warps][GP + 1] floats
-  // stats slot [2]: a[GP], c[GP] (the running merge's factors), m[GP] (the running max),
-  // f (the tile's P scale exponent) + 3 pad, l[4][GP] (the tile's row sums per softmax warp)
-  static constexpr int kStats = kRed + 2 * 4 * (GP + 4) * 4;
-  static constexpr int kSA = 0, kSC = GP, kSM = 2 * GP, kSF = 3 * GP, kSL = 3 * GP + 4;
-  static constexpr int kStatsFloats = 3 * GP + 4 + 4 * GP;
+  // [2 groups][2 slots][4 warps][GP + 4] floats: the warps' maxima of a tile
+  static constexpr int kRed = kRing + kStages * kStage;
+  // stats slot [2]: m[GP] (the tile's max per row, log2 domain), f (the tile's P scale
+  // exponent) + 3 pad, l[4][GP] (the tile's row sums per softmax warp)
+  static constexpr int kStats = kRed + 2 * 2 * 4 * (GP + 4) * 4;
+  static constexpr int kSM = 0, kSF = GP, kSL = GP + 4;
+  static constexpr int kStatsFloats = GP + 4 + 4 * GP;
   static constexpr int kQinv = kStats + 2 * kStatsFloats * 4;   // [2][GP] term factors of the scores
   static constexpr int kLfin = kQinv + 2 * GP * 4;              // [GP] final row sums
   static constexpr int kBars = (kLfin + GP * 4 + 7) & ~7;
   static constexpr int kNumBars = 2 * kStages + 2 * 6 + 1;
   static constexpr int kSmem = 1024 + kBars + kNumBars * 8 + 32;
-  static constexpr int kThreads = 320;
+  static constexpr int kThreads = 448;  // TMA, MMA, 2 x 4 softmax warps, 4 merge warps
   static constexpr int kTmemCols = 4 * kN <= 128 ? 128 : 256;  // S x 2 and O x 2, kN columns each
 };
 
@@ -228,7 +229,7 @@ __device__ __forceinline__ float warp_reduce_scatter(float (&v)[N], int lane) {
 }
 
 template <int D, int GP, int QT>
-__global__ void __launch_bounds__(320, GP <= 16 ? 2 : 1)
+__global__ void __launch_bounds__(448, 1)
 kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constant__ CUtensorMap tma_v, DecodeArgs g) {
   using L = DecodeLayout<D, GP>;
   constexpr int N = L::kN;
@@ -298,7 +299,7 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
   // ---- Q as two e4m3 terms per row (warps 2-9, one query head per warp at a time)
   if (warp >= 2) {
     constexpr int PER = D / 32;  // elements per lane
-    for (int gi = warp - 2; gi < GP; gi += 8) {
+    for (int gi = warp - 2; gi < GP; gi += 12) {
       float v[PER];
       if (gi < g.group) {
         const int64_t base = static_cast<int64_t>(b) * g.sqb + static_cast<int64_t>(h * g.group + gi) * g.sqh;
@@ -352,7 +353,7 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
       const int t = threadIdx.x - 64;
       for (int s = 0; s < S; ++s) {
         uint4* z = reinterpret_cast<uint4*>(sRing + s * L::kStage + 2 * L::kTile);
-        for (int i = t; i < L::kZero / 16; i += 256) z[i] = make_uint4(0, 0, 0, 0);
+        for (int i = t; i < L::kZero / 16; i += L::kThreads - 64) z[i] = make_uint4(0, 0, 0, 0);
       }
     }
     tc::fence_proxy_async();
@@ -427,22 +428,39 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
       if (!tc::mbar_wait(drain, 0)) ok = false;
       if (!ok) atomicOr(&g_attention_status, kDevTimeout);
     }
-  } else if (warp < 6) {  // ------------------------------------------------- softmax warps
+  } else if (warp < 10) {  // ------------------------------------------------ softmax warps
+    // two groups of four warps take the even and the odd tiles; a warp's TMEM lane quarter
+    // (warp % 4) holds 32 of a tile's tokens
+    const int grp = (warp - 2) >> 2;
     const int quarter = warp & 3;
-    const int wi = warp - 2;  // 0..3
+    const int wi = (warp - 2) & 3;  // 0..3 within the group
     const uint32_t lane_base = static_cast<uint32_t>(32 * quarter) << 16;
     const int tok = 32 * quarter + lane;  // TMEM lane = token within the tile
-    float m_run = -INFINITY;  // warp 2, lane j < GP: the running max of query row j (log2 domain)
     const float* ksp = g.k_scale + static_cast<int64_t>(b) * g.ksb + static_cast<int64_t>(h) * g.ksh;
     const float* vsp = g.v_scale + static_cast<int64_t>(b) * g.vsb + static_cast<int64_t>(h) * g.vsh;
-    // A failed wait leaves `ok` false; the four warps agree on it at the next named barrier
-    // (a reduction) and leave the loop together, so that none waits there for a warp that left.
+    // A failed wait leaves `ok` false; the group's four warps agree on it at the next named
+    // barrier (a reduction) and leave the loop together, so that none waits there for a warp
+    // that left.
     bool ok = true;
-    for (int i = 0; i < n_tiles; ++i) {
+    // the token scales two of the group's tiles ahead (a DRAM round trip per tile would sit on
+    // the critical path); the raw values are kept until their tile so that no use waits early
+    auto ld_scales = [&](int i, float& ks, float& vs) {
+      const int t = t_begin + i * 128 + tok;
+      const bool valid = i < n_tiles && t < t_end;
+      ks = valid ? __ldg(ksp + t) : 0.0f;
+      vs = valid ? __ldg(vsp + t) : 0.0f;
+    };
+    float ks_a, vs_a, ks_b, vs_b;
+    ld_scales(grp, ks_a, vs_a);
+    ld_scales(grp + 2, ks_b, vs_b);
+    for (int i = grp; i < n_tiles; i += 2) {
       const int t = t_begin + i * 128 + tok;
       const bool valid = t < t_end;
-      const float kq = valid ? __ldg(ksp + t) * g.scale_log2 : 0.0f;
-      const float vs = valid ? __ldg(vsp + t) : 0.0f;
+      const float kq = ks_a * g.scale_log2;
+      const float vs = vs_a;
+      ks_a = ks_b;
+      vs_a = vs_b;
+      ld_scales(i + 4, ks_b, vs_b);
       if (ok) ok = warp_wait_d(&s_full[i & 1], static_cast<uint32_t>((i >> 1) & 1));
       float sl[GP];
 #pragma unroll
@@ -469,18 +487,19 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
       float vmax = vs;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, off));
-      float* rd = red + ((i & 1) * 4 + wi) * (GP + 4);
+      const int slot = grp * 2 + ((i >> 1) & 1);  // two slots per group: tiles i and i + 2
+      float* rd = red + (slot * 4 + wi) * (GP + 4);
       constexpr int kShift = GP == 8 ? 2 : GP == 16 ? 1 : 0;  // lane >> kShift: the row a lane reduced
       if ((lane & ((1 << kShift) - 1)) == 0) rd[lane >> kShift] = wmax;
       if (lane == 0) rd[GP] = vmax;
-      if (named_sync_any(1, 128, !ok)) { ok = false; break; }
+      if (named_sync_any(1 + grp, 128, !ok)) { ok = false; break; }
       float mt[GP];
       float vt = 0.0f;
 #pragma unroll
       for (int j = 0; j < GP; ++j) mt[j] = -INFINITY;
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
-        const float* rw = red + ((i & 1) * 4 + w) * (GP + 4);
+        const float* rw = red + (slot * 4 + w) * (GP + 4);
 #pragma unroll
         for (int j = 0; j < GP; j += 4) {
           const float4 m4 = *reinterpret_cast<const float4*>(rw + j);
@@ -538,15 +557,11 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
       float* st = stats + (i & 1) * L::kStatsFloats;
       if ((lane & ((1 << kShift) - 1)) == 0) st[L::kSL + wi * GP + (lane >> kShift)] = wsum;
       if (wi == 0) {
-        if (lane < GP) {  // the running max of row `lane` and the merge's factors for tile i
+        if (lane < GP) {  // the tile's max of row `lane`
           float mi = -INFINITY;
 #pragma unroll
-          for (int w = 0; w < 4; ++w) mi = fmaxf(mi, red[((i & 1) * 4 + w) * (GP + 4) + lane]);
-          const float mn = fmaxf(m_run, mi);
-          st[L::kSA + lane] = m_run == -INFINITY ? 0.0f : ex2(m_run - mn);
-          st[L::kSC + lane] = ex2(mi - mn);
-          st[L::kSM + lane] = mn;
-          m_run = mn;
+          for (int w = 0; w < 4; ++w) mi = fmaxf(mi, red[(slot * 4 + w) * (GP + 4) + lane]);
+          st[L::kSM + lane] = mi;
         }
         if (lane == 0) st[L::kSF] = __int_as_float(f);
       }
@@ -560,9 +575,9 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
     const int quarter = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(32 * quarter) << 16;
     const int d = 32 * quarter + lane;  // TMEM lane = head-dim element
-    float o_run[GP];
+    float o_run[GP], m_run[GP];  // the running output and max (log2 domain) per query row
 #pragma unroll
-    for (int j = 0; j < GP; ++j) o_run[j] = 0.0f;
+    for (int j = 0; j < GP; ++j) { o_run[j] = 0.0f; m_run[j] = -INFINITY; }
     float l_run = 0.0f;  // thread d < GP: the running row sum of query row d
     bool ok = true;
     for (int i = 0; i < n_tiles; ++i) {
@@ -575,16 +590,22 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
       // phase of tile i cannot have been overtaken (the next needs this warp's o_free below)
       if (!warp_wait_d(&p_full[i & 1], static_cast<uint32_t>((i >> 1) & 1))) { ok = false; break; }
       const float* st = stats + (i & 1) * L::kStatsFloats;
-      if (d < GP)
-        l_run = l_run * st[L::kSA + d] +
-                ((st[L::kSL + d] + st[L::kSL + GP + d]) + (st[L::kSL + 2 * GP + d] + st[L::kSL + 3 * GP + d])) *
-                    st[L::kSC + d];
       const float down = pow2f(-__float_as_int(st[L::kSF]));
+      float la = 0.0f, lc = 0.0f;
 #pragma unroll
-      for (int j = 0; j < GP; ++j) {
+      for (int j = 0; j < GP; ++j) {  // merge tile i with its own max into the running state
+        const float mi = st[L::kSM + j];
+        const float mn = fmaxf(m_run[j], mi);
+        const float a = m_run[j] == -INFINITY ? 0.0f : ex2(m_run[j] - mn);
+        const float c = ex2(mi - mn);
         const float oi = (__uint_as_float(raw[j]) + __uint_as_float(raw[GP + j]) * 0.0625f) * down;
-        o_run[j] = o_run[j] * st[L::kSA + j] + oi * st[L::kSC + j];
+        o_run[j] = o_run[j] * a + oi * c;
+        m_run[j] = mn;
+        if (j == d) { la = a; lc = c; }
       }
+      if (d < GP)
+        l_run = l_run * la +
+                ((st[L::kSL + d] + st[L::kSL + GP + d]) + (st[L::kSL + 2 * GP + d] + st[L::kSL + 3 * GP + d])) * lc;
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&o_free[i & 1]);
@@ -592,12 +613,14 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
     if (!ok && lane == 0) atomicOr(&g_attention_status, kDevTimeout);
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out);
     const int64_t orow = static_cast<int64_t>(b) * g.heads_kv * g.group + static_cast<int64_t>(h) * g.group;
-    // the running max after the last tile (its stats slot is not written again); empty: -inf
-    const float m_fin = (d < GP && n_tiles > 0) ? stats[((n_tiles - 1) & 1) * L::kStatsFloats + L::kSM + d] : -INFINITY;
+    float m_fin = -INFINITY;  // thread d < GP: the running max of row d (empty split: -inf)
+#pragma unroll
+    for (int j = 0; j < GP; ++j)
+      if (j == d) m_fin = m_run[j];
     if (g.splits == 1) {
       float* lfin = reinterpret_cast<float*>(smem + L::kLfin);
       if (d < GP) lfin[d] = l_run;
-      named_sync(2, 128);
+      named_sync(3, 128);
       if (d < D) {
         for (int j = 0; j < GP; ++j)
           if (j < g.group) out[(orow + j) * D + d] = __float2bfloat16_rn(o_run[j] / lfin[j]);
@@ -617,8 +640,8 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
         pml[GP + d] = l_run;
       }
       __threadfence();
-      named_sync(2, 128);
-      if (threadIdx.x == 192) {
+      named_sync(3, 128);
+      if (threadIdx.x == 320) {
         const unsigned old = atomicAdd(g.counters + bh, 1u);
         const bool last = old == static_cast<unsigned>(g.splits - 1);
         if (last) atomicExch(g.counters + bh, 0u);
@@ -658,23 +681,30 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
     __syncthreads();
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out);
     const int64_t orow = static_cast<int64_t>(b) * g.heads_kv * g.group + static_cast<int64_t>(h) * g.group;
-    for (int o = tid; o < g.group * D; o += L::kThreads) {
-      const int j = o / D, dd = o % D;
-      const float* po = g.part_o + (first * GP + j) * D + dd;
-      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      int s2 = 0;
-      for (; s2 + 8 <= g.splits; s2 += 8) {  // eight loads in flight
-        float v[8];
+    // one thread per 4 consecutive outputs of a row; the partials' float4 loads of 16 splits
+    // are in flight together
+    for (int o = tid; o < g.group * (D / 4); o += L::kThreads) {
+      const int j = o / (D / 4), d4 = (o % (D / 4)) * 4;
+      const float4* po = reinterpret_cast<const float4*>(g.part_o + (first * GP + j) * D + d4);
+      const int64_t step = static_cast<int64_t>(GP) * D / 4;  // float4s between splits
+      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      for (int s0 = 0; s0 < g.splits; s0 += 16) {
+        float4 v[16];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) v[u] = __ldcg(po + static_cast<int64_t>(s2 + u) * GP * D);
+        for (int u = 0; u < 16; ++u)
+          v[u] = s0 + u < g.splits ? __ldcg(po + static_cast<int64_t>(s0 + u) * step) : make_float4(0, 0, 0, 0);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) acc[u & 3] += wts[(s2 + u) * 2 * GP + j] * v[u];
+        for (int u = 0; u < 16; ++u) {
+          const float w = s0 + u < g.splits ? wts[(s0 + u) * 2 * GP + j] : 0.0f;
+          acc.x += w * v[u].x;
+          acc.y += w * v[u].y;
+          acc.z += w * v[u].z;
+          acc.w += w * v[u].w;
+        }
       }
-      for (; s2 < g.splits; ++s2) {
-        const float w = wts[s2 * 2 * GP + j];
-        if (w != 0.0f) acc[0] += w * __ldcg(po + static_cast<int64_t>(s2) * GP * D);
-      }
-      out[(orow + j) * D + dd] = __float2bfloat16_rn((acc[0] + acc[1]) + (acc[2] + acc[3]));
+      __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(out + (orow + j) * D + d4);
+      dst[0] = __floats2bfloat162_rn(acc.x, acc.y);
+      dst[1] = __floats2bfloat162_rn(acc.z, acc.w);
     }
   }
 }

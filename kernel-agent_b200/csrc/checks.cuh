@@ -20,6 +20,7 @@ constexpr float kNvfp4RoundingRatio = 6.375f;        // 6 * (1 + 2^-4), quant.py
 constexpr float kFp4SlackFactor = 1.0009765625f;     // 1 + 2^-10, quant.py:1294
 constexpr float kLowTieFactor = 0.99999904632568359375f;  // fp32(1 - 2^-20)
 constexpr float kE4m3MinNormal = 0.015625f;          // 2^-6
+constexpr float kFp4PlainLimit = 6.0000057220458984375f;  // fp32(6 * (1 + 2^-20)), exact
 
 __device__ __forceinline__ void check_add(unsigned long long* dst, unsigned v) {
 #pragma unroll
@@ -90,7 +91,7 @@ fp4_scale_check_kernel(const void* __restrict__ x, int64_t ldx, int64_t rows, in
   constexpr int BLOCK = FMT == 0 ? 16 : 32;
   const int64_t total = rows * nb;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  unsigned saturated = 0, underflow = 0, nonfinite = 0, not_repr = 0, coarser = 0;
+  unsigned saturated = 0, underflow = 0, nonfinite = 0, not_repr = 0, coarser = 0, plain = 0;
   float worst = 0.0f;
   for (int64_t base = blockIdx.x * static_cast<int64_t>(blockDim.x); base < total; base += stride) {
     const int64_t i = base + threadIdx.x;
@@ -134,6 +135,7 @@ fp4_scale_check_kernel(const void* __restrict__ x, int64_t ldx, int64_t rows, in
         coarser += (live && s > __double2float_rn(ldexp(1.0, c))) ? 1u : 0u;
       }
       saturated += (live && ratio > __fmul_rn(bound, kFp4SlackFactor)) ? 1u : 0u;
+      plain += ratio > kFp4PlainLimit ? 1u : 0u;  // quant.py:1290: ratio > 6 * (1 + 2^-20)
       nonfinite += finite ? 0u : 1u;
       not_repr += (finite && !representable) ? 1u : 0u;
       worst = (ratio > worst || ratio != ratio) ? ratio : worst;
@@ -144,7 +146,78 @@ fp4_scale_check_kernel(const void* __restrict__ x, int64_t ldx, int64_t rows, in
   check_add(&out->nonfinite, nonfinite);
   check_add(&out->not_representable, not_repr);
   check_add(&out->coarser, coarser);
+  check_add(&out->saturated_plain, plain);
   check_max(&out->worst_ratio_bits, worst);
+}
+
+// ------------------------------------------------------------------ error-report sums
+
+__device__ __forceinline__ float to_float(float v) { return v; }
+__device__ __forceinline__ float to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_float(__half v) { return __half2float(v); }
+
+// One CTA per row of a pair (x, y): float64 sums of x^2, y^2, (x - y)^2 and x * y, the NaN-
+// keeping maxima of |x| and |y|, and the counts of x != 0 and of x != 0 with y == 0
+// (quant.py:302-326 _error_metrics and the activation / output reports built on it).
+template <typename TX, typename TY>
+__global__ void __launch_bounds__(256)
+row_pair_stats_kernel(const TX* __restrict__ x, int64_t ldx, const TY* __restrict__ y, int64_t ldy, int64_t k,
+                      double* __restrict__ out) {
+  __shared__ double sred[8][6];
+  __shared__ uint32_t mred[8][2];
+  const int64_t row = blockIdx.x;
+  const TX* xr = x + row * ldx;
+  const TY* yr = y + row * ldy;
+  double sx = 0.0, sy = 0.0, sd = 0.0, sxy = 0.0, nz = 0.0, fl = 0.0;
+  uint32_t mx = 0, my = 0;
+  for (int64_t c = threadIdx.x; c < k; c += blockDim.x) {
+    const float a = to_float(xr[c]), bb = to_float(yr[c]);
+    const double da = a, db = bb;
+    sx += da * da;
+    sy += db * db;
+    sd += (da - db) * (da - db);
+    sxy += da * db;
+    nz += a != 0.0f ? 1.0 : 0.0;
+    fl += (a != 0.0f && bb == 0.0f) ? 1.0 : 0.0;
+    mx = max(mx, __float_as_uint(a) & 0x7FFFFFFFu);
+    my = max(my, __float_as_uint(bb) & 0x7FFFFFFFu);
+  }
+  double v[6] = {sx, sy, sd, sxy, nz, fl};
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int i = 0; i < 6; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], o);
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    my = max(my, __shfl_xor_sync(0xffffffffu, my, o));
+  }
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+    for (int i = 0; i < 6; ++i) sred[w][i] = v[i];
+    mred[w][0] = mx;
+    mred[w][1] = my;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int nw = blockDim.x >> 5;
+    double t[6] = {0, 0, 0, 0, 0, 0};
+    uint32_t ax = 0, ay = 0;
+    for (int i = 0; i < nw; ++i) {
+#pragma unroll
+      for (int j = 0; j < 6; ++j) t[j] += sred[i][j];
+      ax = max(ax, mred[i][0]);
+      ay = max(ay, mred[i][1]);
+    }
+    double* o = out + row * 8;
+    o[0] = t[0];
+    o[1] = t[1];
+    o[2] = t[2];
+    o[3] = t[3];
+    o[4] = __uint_as_float(ax);
+    o[5] = t[4];
+    o[6] = t[5];
+    o[7] = __uint_as_float(ay);
+  }
 }
 
 }  // namespace kab

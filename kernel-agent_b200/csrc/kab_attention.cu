@@ -119,7 +119,7 @@ void decode_split(const KabKvDecodeParams* p, int resident, int* splits, int* ch
   int64_t s = p->splits;
   if (s <= 0) {
     const int64_t pairs = p->batch * p->heads_kv;
-    s = (static_cast<int64_t>(resident) * sm_count() + pairs - 1) / pairs;
+    s = static_cast<int64_t>(resident) * sm_count() / pairs;  // at most one wave
   }
   s = std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(s, tiles), 256));  // the merge's weights fit in the ring
   const int64_t per = (p->length + s - 1) / s;

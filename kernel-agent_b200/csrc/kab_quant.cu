@@ -367,6 +367,32 @@ int kab_fp4_scale_check(const void* x, int dtype, int64_t rows, int64_t k, int64
   return check_launch("kab_fp4_scale_check");
 }
 
+int kab_row_pair_stats(const void* x, int x_dtype, int64_t ldx, const void* y, int y_dtype, int64_t ldy,
+                       int64_t rows, int64_t k, double* out, void* stream) {
+  KAB_REQUIRE(valid_dtype(x_dtype) && valid_dtype(y_dtype), "unknown dtype %d / %d", x_dtype, y_dtype);
+  KAB_REQUIRE(rows >= 0 && k >= 0, "negative shape");
+  if (rows == 0) return KAB_OK;
+  KAB_REQUIRE(out != nullptr && (k == 0 || (x != nullptr && y != nullptr)), "null pointer");
+  KAB_REQUIRE(ldx >= k && ldy >= k, "row strides %lld / %lld are below the width %lld", (long long)ldx,
+              (long long)ldy, (long long)k);
+  KAB_REQUIRE(rows < (int64_t(1) << 31), "too many rows");
+  const cudaStream_t s = as_stream(stream);
+  const dim3 grid(static_cast<unsigned>(rows));
+#define KAB_PAIR(TXX, TYY)                                                                                     \
+  row_pair_stats_kernel<TXX, TYY><<<grid, 256, 0, s>>>(static_cast<const TXX*>(x), ldx, static_cast<const TYY*>(y), \
+                                                       ldy, k, out)
+#define KAB_PAIR_Y(TXX)                                     \
+  if (y_dtype == KAB_F32) KAB_PAIR(TXX, float);             \
+  else if (y_dtype == KAB_BF16) KAB_PAIR(TXX, __nv_bfloat16); \
+  else KAB_PAIR(TXX, __half)
+  if (x_dtype == KAB_F32) { KAB_PAIR_Y(float); }
+  else if (x_dtype == KAB_BF16) { KAB_PAIR_Y(__nv_bfloat16); }
+  else { KAB_PAIR_Y(__half); }
+#undef KAB_PAIR_Y
+#undef KAB_PAIR
+  return check_launch("kab_row_pair_stats");
+}
+
 int kab_rmsnorm(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, const void* weight, float eps,
                 void* out, void* stream) {
   if (int e = check_matrix(x, dtype, rows, k, ldx, "x")) return e;

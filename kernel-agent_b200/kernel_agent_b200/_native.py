@@ -45,6 +45,7 @@ class KabScaleCheck(ctypes.Structure):
         ("not_pow2", ctypes.c_ulonglong),
         ("worst_ratio_bits", ctypes.c_uint),
         ("pad_", ctypes.c_uint),
+        ("saturated_plain", ctypes.c_ulonglong),
     ]
 
 
@@ -122,6 +123,8 @@ _SIGNATURES: dict[str, list] = {
                             c_void_p],
     "kab_attention_fp8": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                           c_int64, c_int64, c_int, ctypes.c_float, c_void_p, c_void_p],
+    "kab_row_pair_stats": [c_void_p, c_int, c_int64, c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p,
+                           c_void_p],
     "kab_quant_kv_fp8": [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64,
                          c_void_p, c_int64, c_int64, c_void_p],
     "kab_kv_decode_workspace": [POINTER(KabKvDecodeParams), POINTER(c_int), POINTER(c_size_t)],

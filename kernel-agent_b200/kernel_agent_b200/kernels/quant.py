@@ -701,7 +701,7 @@ def fp4_scale_values(scales: torch.Tensor, fmt: str) -> torch.Tensor:
 
 
 def fp4_scale_check(x: torch.Tensor, scales: torch.Tensor, outer: torch.Tensor | float | None = None,
-                    fmt: str | None = None) -> dict[str, Any]:
+                    fmt: str | None = None, *, _raw: bool = False) -> dict[str, Any]:
     """quant.py:1325-1416: how W4A4 activation block scales (unswizzled) fit the block maxima
     of ``x`` with the given outer scale: ``format``, ``blocks``, ``saturated``, ``share``,
     ``worst_ratio``, ``underflow``, ``nonfinite``, ``not_representable``, ``coarser`` (one
@@ -735,6 +735,8 @@ def fp4_scale_check(x: torch.Tensor, scales: torch.Tensor, outer: torch.Tensor |
              out.data_ptr(), _stream(x2))
     res = _check_result(out)
     blocks = rows * nb
+    if _raw:
+        return res, blocks
     return {
         "format": fmt,
         "blocks": blocks,
@@ -807,3 +809,373 @@ def fp4_stress_input(shape, fmt: str = "nvfp4", *, dtype: torch.dtype = torch.bf
     bmax = 64.0 * targets[index] / 448.0
     bmax[:, 0] = 64.0
     return (v * bmax[..., None]).reshape(*shape).to(dtype=dtype, device=device)
+
+
+# ------------------------------------------------------------------ error reports (GPU reductions)
+
+
+def _pair_stats(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """Per-row float64 sums of a pair ``x``, ``y`` ``[rows, k]`` in one GPU pass
+    (``kab_row_pair_stats``): columns sum x^2, sum y^2, sum (x - y)^2, sum x y, max |x|,
+    count x != 0, count (x != 0 and y == 0), max |y|."""
+    def two_d(t: torch.Tensor) -> torch.Tensor:
+        t = t if t.dtype in nat.DTYPES else t.float()
+        t = t.reshape(-1, t.shape[-1])
+        return t if t.stride(-1) == 1 else t.contiguous()
+
+    x2, y2 = two_d(x), two_d(y)
+    if x2.shape != y2.shape:
+        raise ValueError(f"shapes differ: {tuple(x2.shape)} and {tuple(y2.shape)}")
+    nat.require_cuda(x2, y2)
+    rows, k = x2.shape
+    out = torch.empty(rows, 8, dtype=torch.float64, device=x2.device)
+    if rows:
+        nat.call("kab_row_pair_stats", x2.data_ptr(), nat.dtype_code(x2), x2.stride(0) if k else 1, y2.data_ptr(),
+                 nat.dtype_code(y2), y2.stride(0) if k else 1, rows, k, out.data_ptr(), _stream(x2))
+    return out
+
+
+def _weight_fields(st: torch.Tensor, k: int) -> dict[str, Any]:
+    """quant.py:302-318: rel_l2, worst_channel_rel_l2, underflow and crest of a weight against
+    its dequantised values, from the rows' pair sums."""
+    tot = st.sum(dim=0)
+    row_norm = st[:, 0].sqrt()
+    live = row_norm > 0
+    row_err = st[:, 2].sqrt() / row_norm.clamp_min(1e-30)
+    crest = st[:, 4] / (row_norm / math.sqrt(max(k, 1))).clamp_min(1e-30)
+    neg = torch.tensor(float("-inf"), dtype=torch.float64, device=st.device)
+    vals = torch.stack([tot[0].sqrt(), tot[2].sqrt(), torch.where(live, row_err, neg).max() if st.shape[0] else neg,
+                        tot[6], tot[5], torch.where(live, crest, neg).max() if st.shape[0] else neg]).tolist()
+    norm, err, worst, flushed, nonzero, cr = vals
+    return {
+        "rel_l2": _sig(err / norm if norm > 0 else 0.0),
+        "worst_channel_rel_l2": _sig(worst if norm > 0 else 0.0),
+        "underflow": _sig(flushed / max(int(nonzero), 1)),
+        "crest": _sig(cr if norm > 0 else 0.0),
+    }
+
+
+def _output_fields(ref: torch.Tensor, new: torch.Tensor) -> dict[str, float]:
+    """quant.py:320-325 / 460-472: output_rel_l2, output_cosine, output_norm_ratio and
+    output_gain of ``new`` against ``ref`` (fp32 outputs), from one pass of pair sums."""
+    tot = _pair_stats(ref, new).sum(dim=0).tolist()
+    ref_norm, new_norm, dot = math.sqrt(tot[0]), math.sqrt(tot[1]), tot[3]
+    cos = dot / (ref_norm * new_norm) if ref_norm and new_norm else 1.0
+    return {
+        "output_rel_l2": _sig(math.sqrt(tot[2]) / ref_norm if ref_norm else 0.0),
+        "output_cosine": round(cos, 6),
+        "output_norm_ratio": round(new_norm / ref_norm, 5) if ref_norm else 1.0,
+        "output_gain": round(dot / ref_norm**2, 5) if ref_norm else 1.0,
+    }
+
+
+def _activation_fields(a: torch.Tensor, a_hat: torch.Tensor, k: int) -> dict[str, float]:
+    """quant.py:455-469: activation_rel_l2, activation_crest (largest amax / RMS of a token)
+    and activation_underflow of the quantised activations."""
+    st = _pair_stats(a, a_hat)
+    tot = st.sum(dim=0)
+    rms = (st[:, 0] / max(k, 1)).sqrt()
+    crest = st[:, 4] / rms.clamp_min(1e-30)
+    live = rms > 0
+    neg = torch.tensor(float("-inf"), dtype=torch.float64, device=st.device)
+    norm, err, cr, flushed, nonzero = torch.stack(
+        [tot[0].sqrt(), tot[2].sqrt(), torch.where(live, crest, neg).max() if st.shape[0] else neg, tot[6],
+         tot[5]]).tolist()
+    return {
+        "activation_rel_l2": _sig(err / norm if norm > 0 else 0.0),
+        "activation_crest": _sig(cr if cr != float("-inf") else 0.0),
+        "activation_underflow": _sig(flushed / max(int(nonzero), 1)),
+    }
+
+
+def _error_metrics(w: torch.Tensor, deq: torch.Tensor, x: torch.Tensor | None) -> dict[str, Any]:
+    """quant.py:302-326: the weight report of ``deq`` against ``w`` (fp32 ``[out, in]``) and,
+    with activations ``x``, the fp32 output error of ``x @ deqᵀ`` against ``x @ wᵀ``."""
+    report = _weight_fields(_pair_stats(w, deq), w.shape[1])
+    if x is not None:
+        a = x.detach().float().reshape(-1, w.shape[1]).to(w.device)
+        out = _output_fields(a @ w.T, a @ deq.T)
+        report["output_rel_l2"] = out["output_rel_l2"]
+        report["output_cosine"] = out["output_cosine"]
+    return report
+
+
+def fp8_error(weight: torch.Tensor, q: torch.Tensor, scale: torch.Tensor,
+              x: torch.Tensor | None = None) -> dict[str, Any]:
+    """quant.py:133-181: numerical error of ``weight`` stored as ``(q, scale)``: ``format``,
+    ``granularity``, ``rel_l2``, ``worst_channel_rel_l2``, ``underflow``, ``crest``,
+    ``bytes``; with ``x``: ``output_rel_l2`` and ``output_cosine`` (fp32 GEMMs)."""
+    nat.require_cuda(weight, q)
+    w = weight.detach().float()
+    deq = dequantize_fp8(q, scale, torch.float32).to(w.device)
+    return {
+        "format": str(q.dtype).removeprefix("torch."),
+        "granularity": "per output channel",
+        **_error_metrics(w, deq, x),
+        "bytes": {
+            "before": weight.numel() * weight.element_size(),
+            "after": q.numel() * q.element_size() + scale.numel() * scale.element_size(),
+        },
+    }
+
+
+def _one(scale: torch.Tensor | float) -> bool:
+    return not isinstance(scale, torch.Tensor) or scale.numel() == 1
+
+
+def fp4_error(weight: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor, tensor_scale: torch.Tensor | float,
+              x: torch.Tensor | None = None) -> dict[str, Any]:
+    """quant.py:328-359: :func:`fp8_error`'s report for ``weight`` stored as
+    :func:`quantize_fp4`'s ``(codes, scales, tensor_scale)``."""
+    nat.require_cuda(weight, codes)
+    w = weight.detach().float()
+    deq = dequantize_fp4(codes, scales, tensor_scale, torch.float32).to(w.device)
+    fmt = next((f for f, (_, dtype) in FP4_FORMATS.items() if dtype == scales.dtype), "fp4")
+    block = w.shape[1] // max(scales.shape[1], 1)
+    kind = "e4m3 scale per {} + fp32 tensor scale" if fmt == "nvfp4" else "e8m0 scale per {}"
+    tensor_scales = 1 if _one(tensor_scale) else torch.as_tensor(tensor_scale).numel()
+    if tensor_scales > 1:
+        kind += " x fp32 per channel (unbiased)"
+    return {
+        "format": fmt,
+        "granularity": kind.format(block),
+        **_error_metrics(w, deq, x),
+        "bytes": {
+            "before": weight.numel() * weight.element_size(),
+            "after": codes.numel() + scales.numel() * scales.element_size() + 4 * tensor_scales,
+        },
+    }
+
+
+def fp8_w8a8_error(weight: torch.Tensor, q: torch.Tensor, scale: torch.Tensor, x: torch.Tensor) -> dict[str, Any]:
+    """quant.py:420-476: :func:`fp8_error` of the weight plus the per-token activations'
+    ``activation_rel_l2`` / ``activation_crest`` / ``activation_underflow`` and the W8A8
+    output's ``output_rel_l2`` / ``output_cosine`` / ``output_norm_ratio`` against
+    ``x @ Wᵀ`` in fp32 (the W8A8 product on the tcgen05 kind::f8f6f4 GEMM, fp32 out)."""
+    report = fp8_error(weight, q, scale)
+    w = weight.detach().float()
+    a = x.detach().float().reshape(-1, w.shape[1]).to(w.device)
+    xq, xs = quantize_fp8_activations(a, q.dtype)
+    a_hat = dequantize_fp8(xq, xs, torch.float32)
+    out = _output_fields(a @ w.T, gemm.fp8(xq, q, xs, scale, None, out_dtype=torch.float32))
+    report.update(activations="e4m3 per token", **_activation_fields(a, a_hat, w.shape[1]),
+                  output_rel_l2=out["output_rel_l2"], output_cosine=out["output_cosine"],
+                  output_norm_ratio=out["output_norm_ratio"])
+    return report
+
+
+def mxfp8_error(weight: torch.Tensor, q: torch.Tensor, scales: torch.Tensor, x: torch.Tensor | None = None,
+                rule: str = "ceil") -> dict[str, Any]:
+    """quant.py:707-768: the weight report of an MXFP8 layer and, with ``x`` (quantised with
+    ``rule``), ``activation_rel_l2``, ``activation_saturation`` (share, worst_ratio) and the
+    output error of the block-scaled GEMM (tcgen05 kind::mxf8f6f4, fp32 out) against
+    ``x @ Wᵀ`` in fp32."""
+    nat.require_cuda(weight, q)
+    w = weight.detach().float()
+    deq = dequantize_mxfp8(q, scales, torch.float32).to(w.device)
+    report: dict[str, Any] = {
+        "format": "mxfp8",
+        "granularity": f"e4m3 + e8m0 scale per {MX_BLOCK} along K, both operands ({rule} rule)",
+        **_error_metrics(w, deq, None),
+        "bytes": {"before": weight.numel() * weight.element_size(), "after": q.numel() + scales.numel()},
+    }
+    if x is None:
+        return report
+    a = x.detach().float().reshape(-1, w.shape[1]).to(w.device)
+    xq, xs = quantize_mxfp8(a, rule)
+    a_hat = dequantize_mxfp8(xq, xs, torch.float32)
+    if w.shape[1] % 128 == 0 and q.shape[0] % 128 == 0:  # the block-scaled GEMM's shapes
+        new = gemm.mxf8(xq, _swizzle(xs.view(torch.uint8)), q,
+                        _swizzled(scales, q.shape[0], w.shape[1] // MX_BLOCK), None, out_dtype=torch.float32)
+    else:  # quant.py:745: the fp32 product of the dequantised operands
+        new = a_hat @ deq.T
+    out = _output_fields(a @ w.T, new)
+    saturation = mxfp8_saturation(a, xs)
+    return {
+        **report,
+        "activations": f"e4m3 + e8m0 per {MX_BLOCK} ({rule} rule)",
+        "activation_rel_l2": _activation_fields(a, a_hat, w.shape[1])["activation_rel_l2"],
+        "activation_saturation": {k: saturation[k] for k in ("share", "worst_ratio")},
+        "output_rel_l2": out["output_rel_l2"],
+        "output_cosine": out["output_cosine"],
+        "output_norm_ratio": out["output_norm_ratio"],
+    }
+
+
+def int8_error(weight: torch.Tensor, q: torch.Tensor, scale: torch.Tensor,
+               x: torch.Tensor | None = None) -> dict[str, Any]:
+    """quant.py:926-949: :func:`fp8_error`'s report for ``weight`` stored as
+    :func:`quantize_int8`'s ``(q, scale)``."""
+    nat.require_cuda(weight, q)
+    w = weight.detach().float()
+    deq = dequantize_int8(q, scale, torch.float32).to(w.device)
+    return {
+        "format": "int8",
+        "granularity": "per output channel, symmetric (amax / 127)",
+        **_error_metrics(w, deq, x),
+        "bytes": {
+            "before": weight.numel() * weight.element_size(),
+            "after": q.numel() + scale.numel() * scale.element_size(),
+        },
+    }
+
+
+def int8_w8a8_error(weight: torch.Tensor, q: torch.Tensor, scale: torch.Tensor, x: torch.Tensor, *,
+                    smooth: torch.Tensor | None = None) -> dict[str, Any]:
+    """quant.py:951-1000: the weight report of :func:`int8_error` (of ``weight * smooth`` with
+    SmoothQuant), the per-token activations' report and the INT8 W8A8 output (exact int32
+    products on the tcgen05 kind::i8 GEMM, both scales in fp32) against ``x @ Wᵀ`` in fp32."""
+    nat.require_cuda(weight, q)
+    w = weight.detach().float()
+    a = x.detach().float().reshape(-1, w.shape[1]).to(w.device)
+    s = _smooth_of(smooth, w.shape[1], w.device)
+    report = int8_error(w if s is None else w * s[None, :], q, scale)
+    xq, xs = quantize_int8_activations(a, s)
+    a_hat = xq.float() * xs[:, None]
+    if s is not None:
+        a_hat = a_hat * s[None, :]
+    new = gemm.int8(xq, q.to(xq.device), xs, scale.float().to(xq.device), None, out_dtype=torch.float32)
+    out = _output_fields(a @ w.T, new)
+    report.update(activations="int8 per token" + (" (SmoothQuant)" if s is not None else ""),
+                  **_activation_fields(a, a_hat, w.shape[1]), output_rel_l2=out["output_rel_l2"],
+                  output_cosine=out["output_cosine"], output_norm_ratio=out["output_norm_ratio"])
+    return report
+
+
+def int8_weights_linear(x: torch.Tensor, q: torch.Tensor, scale: torch.Tensor,
+                        bias: torch.Tensor | None = None) -> torch.Tensor:
+    """quant.py:888-899: ``x @ Wᵀ + bias`` with INT8 weight-only numerics: the activations as
+    they are, the int8 codes as values, fp32 accumulation (a plain fp32 GEMM), the
+    per-channel scale (and the bias) once per output, one rounding to ``x``'s dtype."""
+    nat.require_cuda(x, q)
+    a = x.reshape(-1, x.shape[-1]).float()
+    y = (a @ q.to(a.device).float().T) * scale.float().to(a.device)[None, :]
+    if bias is not None:
+        y = y + bias.float().to(a.device)
+    return y.to(x.dtype).reshape(*x.shape[:-1], q.shape[0])
+
+
+def smoothquant_factors(act_amax: torch.Tensor, weight: torch.Tensor, alpha: float = 0.5) -> torch.Tensor:
+    """quant.py:1002-1041: SmoothQuant's per-input-channel factors ``s_j = amax(|X_j|)^alpha /
+    amax(|W_j|)^(1 - alpha)`` (fp32 ``[in]``; 1 where either operand's channel is zero or the
+    activation maximum is not finite), clamped to [1e-5, 1e5]."""
+    a = act_amax.detach().float().reshape(-1)
+    nat.require_cuda(a)
+    w = weight.detach().float().abs().amax(dim=0).to(a.device)
+    if a.numel() != w.numel():
+        raise ValueError(f"{a.numel()} activation maxima for a weight with {w.numel()} inputs")
+    if not 0.0 <= alpha <= 1.0:
+        raise ValueError(f"alpha must be in [0, 1], got {alpha}")
+    ok = (a > 0) & (w > 0) & torch.isfinite(a)
+    s = a.clamp_min(1e-30).pow(alpha) / w.clamp_min(1e-30).pow(1.0 - alpha)
+    return torch.where(ok, s.clamp(1e-5, 1e5), torch.ones_like(s)).contiguous()
+
+
+def fp4_saturation(x: torch.Tensor, scales: torch.Tensor, outer: torch.Tensor, fmt: str = "nvfp4") -> dict[str, Any]:
+    """quant.py:1260-1297: how FP4 activation scales fit the block maxima of ``x`` (one GPU
+    pass of the scale check): ``blocks``, ``saturated`` (ratio above 6 x (1 + 2^-20)),
+    ``share`` and ``worst_ratio``."""
+    res, blocks = fp4_scale_check(x, scales, outer, fmt, _raw=True)
+    sat = int(res.saturated_plain)
+    return {
+        "blocks": blocks,
+        "saturated": sat,
+        "share": _sig(sat / blocks) if blocks else 0.0,
+        "worst_ratio": _sig(_worst(res)) if blocks else 0.0,
+    }
+
+
+def fp4_w4a4_error(weight: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor,
+                   tensor_scale: torch.Tensor | float, x: torch.Tensor, *, fmt: str = "nvfp4",
+                   granularity: str = "token", rotate: int | None = None, unbiased: bool = False) -> dict[str, Any]:
+    """quant.py:1511-1573: the weight report of :func:`fp4_error` (of the rotated weight), the
+    activations' ``activation_rel_l2`` / ``activation_crest`` / ``activation_saturation``, and
+    the W4A4 output (the block-scaled tcgen05 GEMM with its fp32 epilogue) against
+    ``x @ Wᵀ`` in fp32: ``output_rel_l2``, ``output_cosine``, ``output_norm_ratio``,
+    ``output_gain``."""
+    nat.require_cuda(weight, codes)
+    w = weight.detach().float()
+    a = x.detach().float().reshape(-1, w.shape[1]).to(w.device)
+    report = fp4_error(hadamard_rotate(w, rotate) if rotate else w, codes, scales, tensor_scale)
+    a_rot = hadamard_rotate(a, rotate) if rotate else a
+    xq, xs, outer = quantize_fp4_activations(a_rot, fmt, granularity)
+    saturation = fp4_saturation(a_rot, xs, outer, fmt)
+    if unbiased:
+        outer = outer * fp4_bias_correction(a_rot, xq, xs, outer)
+    a_hat = fp4_values(xq, xs) * outer[:, None]
+    act = _activation_fields(a_rot, a_hat, w.shape[1])
+    crest = _activation_fields(a, a, w.shape[1])["activation_crest"]  # before the rotation
+    new = fp4_w4a4_linear(a, codes, scales, tensor_scale, fmt=fmt, granularity=granularity, rotate=rotate,
+                          unbiased=unbiased)
+    out = _output_fields(a @ w.T, new)
+    block, kind = FP4_FORMATS[fmt][0], "e4m3" if fmt == "nvfp4" else "e8m0"
+    report.update(
+        activations=f"{fmt}: e2m1 + {kind} scale per {block}"
+        + (f" x fp32 per {granularity}" if fmt == "nvfp4" else "")
+        + (f", Hadamard {rotate}" if rotate else "")
+        + (", unbiased" if unbiased else ""),
+        activation_rel_l2=act["activation_rel_l2"],
+        activation_crest=crest,
+        activation_saturation={k: saturation[k] for k in ("share", "worst_ratio")},
+        **out,
+    )
+    return report
+
+
+def _same(a: torch.Tensor, b: torch.Tensor) -> bool:
+    """quant.py:1656-1658: whether two layers' kept inputs are the same values."""
+    return a.shape == b.shape and a.dtype == b.dtype and a.device == b.device and torch.equal(a, b)
+
+
+def fp4_w4a4_sensitivity(module: torch.nn.Module, run, *, fmt: str = "nvfp4", granularity: str = "token",
+                         rotate: int | None = None, calls: int = 4) -> list[dict[str, Any]]:
+    """quant.py:1575-1653: the W4A4 sensitivity probe: each ``nn.Linear`` of ``module``,
+    quantised alone to W4A4 (:func:`fp4_w4a4_error`) and to FP8 W8A8
+    (:func:`fp8_w8a8_error`) on its first ``calls`` inputs of ``run()``; one row per layer,
+    the most sensitive (largest W4A4 output relative L2 error) first."""
+    seen: dict[str, list[torch.Tensor]] = {}
+    layers = {n: m for n, m in module.named_modules() if isinstance(m, torch.nn.Linear)}
+
+    def keep(name: str):
+        def hook(_: torch.nn.Module, args: tuple[Any, ...]) -> None:
+            if len(seen.setdefault(name, [])) < calls and isinstance(args[0], torch.Tensor):
+                seen[name].append(args[0].detach().reshape(-1, args[0].shape[-1]))
+
+        return hook
+
+    hooks = [m.register_forward_pre_hook(keep(n)) for n, m in layers.items()]
+    try:
+        with torch.no_grad():
+            run()
+    finally:
+        for h in hooks:
+            h.remove()
+    found = []
+    kept = {n: torch.cat(seen[n]) for n in layers if n in seen}
+    group: dict[str, str] = {}
+    for name, x in kept.items():
+        group[name] = next((g for g, y in kept.items() if g in group and g == group[g] and _same(x, y)), name)
+    for name, x in kept.items():
+        w = layers[name].weight.detach()
+        x = x.to(w.device)
+        if w.shape[1] % (rotate or FP4_FORMATS[fmt][0]) or not x.numel():
+            continue
+        wq = hadamard_rotate(w, rotate) if rotate else w
+        e4 = fp4_w4a4_error(w, *quantize_fp4(wq, fmt), x, fmt=fmt, granularity=granularity, rotate=rotate)
+        e8 = fp8_w8a8_error(w, *quantize_fp8(w), x)
+        found.append({
+            "name": name,
+            "rows": int(x.shape[0]),
+            "in_features": int(w.shape[1]),
+            "out_features": int(w.shape[0]),
+            "flops": 2 * int(x.shape[0]) * int(w.shape[1]) * int(w.shape[0]),
+            "activation_crest": e4["activation_crest"],
+            "w4a4_rel_l2": e4["output_rel_l2"],
+            "w4a4_norm_change": _sig(e4["output_norm_ratio"] - 1.0),
+            "fp8_rel_l2": e8["output_rel_l2"],
+            "input_group": group[name],
+        })
+    total = sum(r["flops"] for r in found) or 1
+    for row in found:
+        row["flop_share"] = _sig(row.pop("flops") / total)
+    return sorted(found, key=lambda r: -r["w4a4_rel_l2"])

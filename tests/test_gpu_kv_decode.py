@@ -255,3 +255,15 @@ def test_module_against_sdpa(kv):
     assert out.shape == q.shape and rel(np_values(out), np_values(ref)) < 0.04
     with pytest.raises(NotImplementedError):
         mod(q[..., :96], k[..., :96], v[..., :96])
+
+
+def test_error_report_golden(kv, kvg):
+    """fp8_kv_error (one GPU pass of row sums per tensor) against the reference's report."""
+    import json
+
+    want = json.loads((GOLDEN / "kv_golden.json").read_text())["error"]
+    k = torch.from_numpy(kvg["err_k"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    got = kv.fp8_kv_error(k, k * 0.5)
+    assert got["bytes"] == want["bytes"] and got["format"] == want["format"]
+    for key in ("k_rel_l2", "k_worst_row_rel_l2", "v_rel_l2", "v_worst_row_rel_l2"):
+        assert got[key] == pytest.approx(want[key], abs=2e-5), key
