@@ -492,7 +492,7 @@ class KvDecode(Workload):
         qo = 2 * self.b * self.hq * self.d * 2
         self.bytes = 2 * rows * self.d + 2 * rows * 4 + qo
         self.units = self.bytes / 1e9
-        self.kernel = "kv_decode_kernel<128, 16, bf16>"
+        self.kernel = "kv_decode_kernel<128, 8, bf16>"
         self.kernel_bytes = self.bytes
         self.q_host = self.q.cpu().pin_memory()
         self.y_host = torch.empty(self.b, self.hq, self.d, dtype=torch.bfloat16).pin_memory()

@@ -21,13 +21,15 @@
 //    two e4m3 terms (one power-of-two scale per tile), about as fine as the reference's bf16
 //    P. The K scale multiplies the scores, the V scale is folded into P (the reference's
 //    split of the two scales, triton_fp8_kv_decode.py:142-155).
-//    Warp 0 issues the TMA loads (3-4 stage ring), warp 1 the MMAs, warps 2-5 (one token per
-//    thread) the per-tile softmax: scores, the tile max per query head, p = 2^(s - max), the
-//    row sums, P' split and written in the no-swizzle MN-major layout; warps 6-9 (one head-dim
-//    element per thread) merge each tile's O with its own max (no rescaling in TMEM) and write
+//    Warp 0 issues the TMA loads (5-7 stage ring); warp 1 owns the TMEM allocation; two groups
+//    of four softmax warps (warps 2-5 and 6-9, one token per thread) take the even and the odd
+//    tiles: scores, the tile max per query head, p = 2^(s - max), the row sums, P' split and
+//    written in the no-swizzle MN-major layout, after which one elected thread of the group
+//    issues the tile's P V and the group's next S; warps 10-13 (one head-dim element per
+//    thread) merge each tile's O with its own max in tile order (no rescaling in TMEM) and write
 //    the split's partial (max, sum, O) or, with one split, the output. The CTA that finishes a
 //    (sequence, KV head) last, by an atomic count, merges the splits' partials into the bf16
-//    output (triton_fp8_kv_decode.py:163-186).
+//    output with all its threads (triton_fp8_kv_decode.py:163-186).
 // No load uses cluster multicast; every wait is bounded and records kDevTimeout.
 #pragma once
 
@@ -110,7 +112,7 @@ struct DecodeLayout {
   static constexpr int kQinv = kStats + 2 * kStatsFloats * 4;   // [2][GP] term factors of the scores
   static constexpr int kLfin = kQinv + 2 * GP * 4;              // [GP] final row sums
   static constexpr int kBars = (kLfin + GP * 4 + 7) & ~7;
-  static constexpr int kNumBars = 2 * kStages + 2 * 6 + 1;
+  static constexpr int kNumBars = 2 * kStages + 2 * 5 + 2;
   static constexpr int kSmem = 1024 + kBars + kNumBars * 8 + 32;
   static constexpr int kThreads = 448;  // TMA, MMA, 2 x 4 softmax warps, 4 merge warps
   static constexpr int kTmemCols = 4 * kN <= 128 ? 128 : 256;  // S x 2 and O x 2, kN columns each
@@ -246,13 +248,12 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = kv_full + S;
   uint64_t* s_full = kv_empty + S;  // [2] MMA commit
-  uint64_t* s_free = s_full + 2;    // [2] 4 softmax warps
-  uint64_t* p_full = s_free + 2;    // [2] 4 softmax warps
+  uint64_t* p_full = s_full + 2;    // [2] 4 softmax warps
   uint64_t* p_free = p_full + 2;    // [2] MMA commit
   uint64_t* o_full = p_free + 2;    // [2] MMA commit
   uint64_t* o_free = o_full + 2;    // [2] 4 merge warps
-  uint64_t* drain = o_free + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* drain = o_free + 2;      // [2] one per softmax group
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   uint32_t* last_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -272,13 +273,13 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&s_full[i], 1);
-      tc::mbar_init(&s_free[i], 4);
       tc::mbar_init(&p_full[i], 4);
       tc::mbar_init(&p_free[i], 1);
       tc::mbar_init(&o_full[i], 1);
       tc::mbar_init(&o_free[i], 4);
     }
-    tc::mbar_init(drain, 1);
+    tc::mbar_init(&drain[0], 1);
+    tc::mbar_init(&drain[1], 1);
     tc::fence_barrier_init();
   }
   // The first tiles' loads go out at once (thread 0 initialised the barriers; the ring is
@@ -364,6 +365,39 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tO = tmem + 2 * N;
 
+  // The MMAs of tile i, issued by one elected thread of the softmax group that owns the tile
+  // (its tiles are i, i + 2, ...; S, P and O buffers i & 1 are the group's own), right after
+  // the group's barrier, so that no other warp's wake-up sits between a tile's softmax and the
+  // next tile's scores.
+  const uint32_t idesc_s = tc::idesc_f8(128, N);
+  const uint32_t idesc_pv = tc::idesc_f8(128, N) | (1u << 15) | (1u << 16);  // A and B MN-major
+  auto kdesc = [&](uint32_t a) { return D == 128 ? tc::desc_sw128(a) : tc::desc_sw64(a); };
+  auto issue_s = [&](int i) {  // S^T_i = K_i (Q_hi | Q_lo)^T, once K_i has landed
+    const int s = i % S;
+    const uint64_t kd = kdesc(tc::smem_u32(sRing + s * L::kStage));
+    const uint64_t qd = kdesc(tc::smem_u32(sQ));
+#pragma unroll
+    for (int kk = 0; kk < D / 32; ++kk)
+      tc::mma_f8(tS + (i & 1) * N, kd + static_cast<uint64_t>(2 * kk), qd + static_cast<uint64_t>(2 * kk), idesc_s,
+                 kk > 0 ? 1u : 0u);
+    tc::commit(&s_full[i & 1]);
+  };
+  auto issue_pv = [&](int i) {  // O^T_i = V_i^T (P_hi | P_lo)^T, then release V, P and K
+    const int s = i % S;
+    const uint32_t v_addr = tc::smem_u32(sRing + s * L::kStage + L::kTile);
+    const uint32_t p_addr = tc::smem_u32(sP + (i & 1) * L::kPBytes);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {  // 32 tokens per MMA
+      uint64_t vd;
+      if constexpr (D == 128) vd = tc::desc_sw128(v_addr + kk * 32 * L::kRow);
+      else vd = desc_vt64(v_addr + kk * 32 * L::kRow, static_cast<uint32_t>(L::kTile));
+      tc::mma_f8(tO + (i & 1) * N, vd, desc_p(p_addr + kk * 512), idesc_pv, kk > 0 ? 1u : 0u);
+    }
+    tc::commit(&o_full[i & 1]);
+    tc::commit(&p_free[i & 1]);
+    tc::commit(&kv_empty[s]);
+  };
+
   if (warp == 0) {
     if (lane == 0 && n_tiles > 0) {  // ---------------------------------------- TMA producer
       bool ok = true;
@@ -380,54 +414,7 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && n_tiles > 0) {  // ---------------------------------------- MMA issuer
-      bool ok = true;
-      const uint32_t idesc_s = tc::idesc_f8(128, N);
-      const uint32_t idesc_pv = tc::idesc_f8(128, N) | (1u << 15) | (1u << 16);  // A and B MN-major
-      const uint32_t q_addr = tc::smem_u32(sQ);
-      auto kdesc = [&](uint32_t a) { return D == 128 ? tc::desc_sw128(a) : tc::desc_sw64(a); };
-      auto issue_s = [&](int i) -> bool {
-        const int s = i % S;
-        if (!tc::mbar_wait(&kv_full[s], static_cast<uint32_t>((i / S) & 1))) return false;
-        if (!tc::mbar_wait(&s_free[i & 1], static_cast<uint32_t>(((i >> 1) & 1) ^ 1))) return false;
-        tc::fence_after_sync();
-        const uint64_t kd = kdesc(tc::smem_u32(sRing + s * L::kStage));
-        const uint64_t qd = kdesc(q_addr);
-#pragma unroll
-        for (int kk = 0; kk < D / 32; ++kk)
-          tc::mma_f8(tS + (i & 1) * N, kd + static_cast<uint64_t>(2 * kk), qd + static_cast<uint64_t>(2 * kk), idesc_s,
-                     kk > 0 ? 1u : 0u);
-        tc::commit(&s_full[i & 1]);
-        return true;
-      };
-      auto issue_pv = [&](int i) -> bool {
-        const int s = i % S;
-        if (!tc::mbar_wait(&p_full[i & 1], static_cast<uint32_t>((i >> 1) & 1))) return false;
-        if (!tc::mbar_wait(&o_free[i & 1], static_cast<uint32_t>(((i >> 1) & 1) ^ 1))) return false;
-        tc::fence_after_sync();
-        const uint32_t v_addr = tc::smem_u32(sRing + s * L::kStage + L::kTile);
-        const uint32_t p_addr = tc::smem_u32(sP + (i & 1) * L::kPBytes);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {  // 32 tokens per MMA
-          uint64_t vd;
-          if constexpr (D == 128) vd = tc::desc_sw128(v_addr + kk * 32 * L::kRow);
-          else vd = desc_vt64(v_addr + kk * 32 * L::kRow, static_cast<uint32_t>(L::kTile));
-          tc::mma_f8(tO + (i & 1) * N, vd, desc_p(p_addr + kk * 512), idesc_pv, kk > 0 ? 1u : 0u);
-        }
-        tc::commit(&o_full[i & 1]);
-        tc::commit(&p_free[i & 1]);
-        tc::commit(&kv_empty[s]);
-        return true;
-      };
-      if (!issue_s(0)) ok = false;
-      for (int i = 0; ok && i < n_tiles; ++i) {
-        if (i + 1 < n_tiles && !issue_s(i + 1)) { ok = false; break; }
-        if (!issue_pv(i)) { ok = false; break; }
-      }
-      tc::commit(drain);  // every MMA issued has completed once this arrives
-      if (!tc::mbar_wait(drain, 0)) ok = false;
-      if (!ok) atomicOr(&g_attention_status, kDevTimeout);
-    }
+    // warp 1 only owns the TMEM allocation: each softmax group issues its own MMAs
   } else if (warp < 10) {  // ------------------------------------------------ softmax warps
     // two groups of four warps take the even and the odd tiles; a warp's TMEM lane quarter
     // (warp % 4) holds 32 of a tile's tokens
@@ -453,6 +440,19 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
     float ks_a, vs_a, ks_b, vs_b;
     ld_scales(grp, ks_a, vs_a);
     ld_scales(grp + 2, ks_b, vs_b);
+    const bool elected = wi == 0 && lane == 0;
+    // the group's first scores
+    if (wi == 0) {
+      bool e_ok = true;
+      if (elected && grp < n_tiles) {
+        e_ok = tc::mbar_wait(&kv_full[grp % S], static_cast<uint32_t>((grp / S) & 1));
+        if (e_ok) {
+          tc::fence_after_sync();
+          issue_s(grp);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, e_ok ? 1 : 0, 0) != 0;
+    }
     for (int i = grp; i < n_tiles; i += 2) {
       const int t = t_begin + i * 128 + tok;
       const bool valid = t < t_end;
@@ -475,9 +475,6 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
           const float dot = __uint_as_float(raw[j]) * qinv[j] + __uint_as_float(raw[GP + j]) * qinv[GP + j];
           sl[j] = valid ? dot * kq : -INFINITY;  // scores in the log2 domain
         }
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&s_free[i & 1]);
       }
       // the tile's max per query head (and of the V scales): warp partials, then the 4 warps
       float part[GP];
@@ -524,51 +521,72 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
         lo[j / 4] = (a >> 16) | (c & 0xFFFF0000u);
       }
       const float wsum = warp_reduce_scatter<GP, false>(p, lane);
-      // P'_i into its buffer once P V_{i-2} has read it
+      // P'_i into its buffer once P V_{i-2} has read it (a failed wait skips the rest of the
+      // tile's work; the group leaves together at its next barrier)
       ok = warp_wait_d(&p_free[i & 1], static_cast<uint32_t>(((i >> 1) & 1) ^ 1));
-      if (!ok) continue;  // to the next barrier, where the warps leave together
-      uint8_t* pb = sP + (i & 1) * L::kPBytes + tok * 16;
-      {  // the token's row of P: the hi codes of its GP columns, then the lo codes
-        uint32_t w[GP / 2];
+      if (ok) {
+        uint8_t* pb = sP + (i & 1) * L::kPBytes + tok * 16;
+        {  // the token's row of P: the hi codes of its GP columns, then the lo codes
+          uint32_t w[GP / 2];
 #pragma unroll
-        for (int j = 0; j < GP / 4; ++j) { w[j] = hi[j]; w[GP / 4 + j] = lo[j]; }
+          for (int j = 0; j < GP / 4; ++j) { w[j] = hi[j]; w[GP / 4 + j] = lo[j]; }
 #pragma unroll
-        for (int blk = 0; blk < GP / 8; ++blk)
-          *reinterpret_cast<uint4*>(pb + blk * 2048) = make_uint4(w[4 * blk], w[4 * blk + 1], w[4 * blk + 2], w[4 * blk + 3]);
-      }
-      // tokens in [n_valid, L) of the last tile: zero their V rows (the codes there are not
-      // this sequence's; a NaN code times p = 0 would reach O)
-      bool landed = true;
-      if (t >= t_end && t < g.length) {
-        landed = tc::mbar_wait(&kv_full[i % S], static_cast<uint32_t>((i / S) & 1));
-        if (landed) {
-          uint4* vrow = reinterpret_cast<uint4*>(sRing + (i % S) * L::kStage + L::kTile + tok * L::kRow);
-#pragma unroll
-          for (int c = 0; c < L::kRow / 16; ++c) vrow[c] = make_uint4(0, 0, 0, 0);
+          for (int blk = 0; blk < GP / 8; ++blk)
+            *reinterpret_cast<uint4*>(pb + blk * 2048) = make_uint4(w[4 * blk], w[4 * blk + 1], w[4 * blk + 2], w[4 * blk + 3]);
         }
+        // tokens in [n_valid, L) of the last tile: zero their V rows (the codes there are not
+        // this sequence's; a NaN code times p = 0 would reach O)
+        bool landed = true;
+        if (t >= t_end && t < g.length) {
+          landed = tc::mbar_wait(&kv_full[i % S], static_cast<uint32_t>((i / S) & 1));
+          if (landed) {
+            uint4* vrow = reinterpret_cast<uint4*>(sRing + (i % S) * L::kStage + L::kTile + tok * L::kRow);
+#pragma unroll
+            for (int c = 0; c < L::kRow / 16; ++c) vrow[c] = make_uint4(0, 0, 0, 0);
+          }
+        }
+        ok = __all_sync(0xffffffffu, landed);
       }
-      ok = __all_sync(0xffffffffu, landed);
-      if (!ok) continue;
       // the stats of tile i into slot i & 1 once the merge warps have read those of tile i - 2
       // (they read them before releasing O of tile i - 2; that phase of o_free cannot have
-      // been overtaken, as the next one needs P V_i, which waits for this warp's p_full)
-      ok = warp_wait_d(&o_free[i & 1], static_cast<uint32_t>(((i >> 1) & 1) ^ 1));
-      if (!ok) continue;
-      float* st = stats + (i & 1) * L::kStatsFloats;
-      if ((lane & ((1 << kShift) - 1)) == 0) st[L::kSL + wi * GP + (lane >> kShift)] = wsum;
-      if (wi == 0) {
-        if (lane < GP) {  // the tile's max of row `lane`
-          float mi = -INFINITY;
+      // been overtaken, as the next one needs P V_i, issued after this group's barrier below)
+      if (ok) ok = warp_wait_d(&o_free[i & 1], static_cast<uint32_t>(((i >> 1) & 1) ^ 1));
+      if (ok) {
+        float* st = stats + (i & 1) * L::kStatsFloats;
+        if ((lane & ((1 << kShift) - 1)) == 0) st[L::kSL + wi * GP + (lane >> kShift)] = wsum;
+        if (wi == 0) {
+          if (lane < GP) {  // the tile's max of row `lane`
+            float mi = -INFINITY;
 #pragma unroll
-          for (int w = 0; w < 4; ++w) mi = fmaxf(mi, red[(slot * 4 + w) * (GP + 4) + lane]);
-          st[L::kSM + lane] = mi;
+            for (int w = 0; w < 4; ++w) mi = fmaxf(mi, red[(slot * 4 + w) * (GP + 4) + lane]);
+            st[L::kSM + lane] = mi;
+          }
+          if (lane == 0) st[L::kSF] = __int_as_float(f);
         }
-        if (lane == 0) st[L::kSF] = __int_as_float(f);
+        tc::fence_proxy_async();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&p_full[i & 1]);
       }
-      tc::fence_proxy_async();
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&p_full[i & 1]);
+      // every warp's P rows and TMEM reads are done: the elected thread issues P V_i and the
+      // group's next scores
+      if (named_sync_any(1 + grp, 128, !ok)) { ok = false; break; }
+      if (wi == 0) {
+        bool e_ok = true;
+        if (elected) {
+          tc::fence_after_sync();
+          issue_pv(i);
+          if (i + 2 < n_tiles) {
+            e_ok = tc::mbar_wait(&kv_full[(i + 2) % S], static_cast<uint32_t>(((i + 2) / S) & 1));
+            if (e_ok) issue_s(i + 2);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, e_ok ? 1 : 0, 0) != 0;
+      }
+    }
+    if (elected && grp < n_tiles) {  // every MMA this thread issued has completed
+      tc::commit(&drain[grp]);
+      if (!tc::mbar_wait(&drain[grp], 0)) ok = false;
     }
     if (!ok && lane == 0) atomicOr(&g_attention_status, kDevTimeout);
   } else {  // --------------------------------------------------------------- merge warps
