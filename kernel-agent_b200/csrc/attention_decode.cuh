@@ -27,9 +27,11 @@
 //    written in the no-swizzle MN-major layout, after which one elected thread of the group
 //    issues the tile's P V and the group's next S; warps 10-13 (one head-dim element per
 //    thread) merge each tile's O with its own max in tile order (no rescaling in TMEM) and write
-//    the split's partial (max, sum, O) or, with one split, the output. The CTA that finishes a
-//    (sequence, KV head) last, by an atomic count, merges the splits' partials into the bf16
-//    output with all its threads (triton_fp8_kv_decode.py:163-186).
+//    the split's partial (max, sum, O) or, with one split, the output. The splits' partials
+//    are merged into the bf16 output (triton_fp8_kv_decode.py:163-186) either within a thread-
+//    block cluster (the splits of a (sequence, KV head) as one cluster, each CTA merging a slice
+//    of the output from the others' shared memory) or through a global workspace, where the CTA
+//    that finishes a (sequence, KV head) last, by an atomic count, merges them all.
 // No load uses cluster multicast; every wait is bounded and records kDevTimeout.
 #pragma once
 
@@ -88,6 +90,8 @@ struct DecodeArgs {
   float* part_o;           // [batch * heads_kv, splits, GP, D]
   float* part_ml;          // [batch * heads_kv, splits, 2, GP]: max (log2 domain), sum
   unsigned* counters;      // [batch * heads_kv], zero between launches
+  int cluster;             // 1: the splits of a (sequence, KV head) are one thread-block cluster
+                           // and merge through distributed shared memory (no workspace)
 };
 
 template <int D, int GP>
@@ -183,6 +187,21 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
 #pragma unroll
     for (int c = 0; c < N / 32; ++c) tc::tmem_ld32(taddr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
   }
+}
+
+// Loads from the shared memory of a CTA of this cluster (a shared::cluster address from mapa).
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 
 __device__ __forceinline__ bool warp_wait_d(uint64_t* bar, uint32_t parity) {
@@ -643,6 +662,19 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
         for (int j = 0; j < GP; ++j)
           if (j < g.group) out[(orow + j) * D + d] = __float2bfloat16_rn(o_run[j] / lfin[j]);
       }
+    } else if (g.cluster) {
+      // this split's partial in this CTA's shared memory (the ring is free: every tile's P V
+      // has completed), read by the cluster's CTAs after the launch's last barrier
+      float* part = reinterpret_cast<float*>(sRing);  // [group][D], then max [GP], sum [GP]
+      if (d < D) {
+#pragma unroll
+        for (int j = 0; j < GP; ++j)
+          if (j < g.group) part[j * D + d] = o_run[j];
+      }
+      if (d < GP) {
+        part[GP * D + d] = m_fin;
+        part[GP * D + GP + d] = l_run;
+      }
     } else {
       // this split's partial, then the last CTA of (sequence, KV head) merges them all
       const int64_t pbase = static_cast<int64_t>(bh) * g.splits + sp;
@@ -674,9 +706,54 @@ kv_decode_kernel(const __grid_constant__ CUtensorMap tma_k, const __grid_constan
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, L::kTmemCols);
   }
+  // ---- the cluster's CTAs merge the splits' partials from each other's shared memory, each
+  // CTA a slice of the outputs; the second cluster barrier keeps every partial in place until
+  // all slices are read (every thread of every CTA of the cluster reaches both barriers)
+  if (g.splits > 1 && g.cluster) {
+    tc::cluster_sync();
+    const int cs = g.splits, rank = static_cast<int>(tc::cluster_ctarank());
+    const int quads = g.group * (D / 4);
+    const int per = (quads + cs - 1) / cs;
+    const float* part = reinterpret_cast<const float*>(sRing);
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(g.out);
+    const int64_t orow = static_cast<int64_t>(b) * g.heads_kv * g.group + static_cast<int64_t>(h) * g.group;
+    for (int o = rank * per + static_cast<int>(threadIdx.x); o < min(quads, (rank + 1) * per); o += L::kThreads) {
+      const int j = o / (D / 4), d4 = (o % (D / 4)) * 4;
+      float ms[16], w[16];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int s2 = 0; s2 < 16; ++s2) {
+        ms[s2] = s2 < cs ? ld_cluster_f32(tc::mapa(part + GP * D + j, s2)) : -INFINITY;
+        mx = fmaxf(mx, ms[s2]);
+      }
+      float den = 0.0f;
+#pragma unroll
+      for (int s2 = 0; s2 < 16; ++s2) {
+        w[s2] = ms[s2] == -INFINITY ? 0.0f : ex2(ms[s2] - mx);  // an empty split weighs 0
+        if (s2 < cs) den += w[s2] * ld_cluster_f32(tc::mapa(part + GP * D + GP + j, s2));
+      }
+      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+      for (int s2 = 0; s2 < 16; ++s2) {
+        if (s2 < cs) {
+          const float4 v = ld_cluster_f32x4(tc::mapa(part + j * D + d4, s2));
+          acc.x += w[s2] * v.x;
+          acc.y += w[s2] * v.y;
+          acc.z += w[s2] * v.z;
+          acc.w += w[s2] * v.w;
+        }
+      }
+      const float inv = 1.0f / den;
+      __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(out + (orow + j) * D + d4);
+      dst[0] = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+      dst[1] = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+    }
+    __syncwarp();
+    tc::cluster_sync();
+  }
   // ---- the last CTA of (sequence, KV head) merges the splits' partials (all threads; the
   // ring's shared memory is free: every load landed and every MMA completed)
-  if (g.splits > 1 && *last_flag != 0u) {
+  if (g.splits > 1 && !g.cluster && *last_flag != 0u) {
     __threadfence();
     const int tid = threadIdx.x;
     const int64_t first = static_cast<int64_t>(bh) * g.splits;

@@ -105,6 +105,47 @@ int decode_prepare(int qt) {
   return resident[ti][dev];
 }
 
+// How many clusters of `cs` CTAs of the kernel instance can be resident at once (0 when the
+// cluster cannot be formed); cached per device and size.
+template <int D, int GP>
+int decode_clusters(int qt, int cs) {
+  using L = DecodeLayout<D, GP>;
+  static int fits[3][64][17] = {};  // value + 1; 0: not asked yet
+  const int ti = qt == KAB_BF16 ? 0 : qt == KAB_F16 ? 1 : 2;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || cs < 2 || cs > 16) return 0;
+  if (fits[ti][dev][cs] == 0) {
+    auto kern = decode_kernel_for<D, GP>(qt);
+    int n = 0;
+    if (cs <= 8 || cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(cs));
+      cfg.blockDim = dim3(L::kThreads);
+      cfg.dynamicSmemBytes = L::kSmem;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = static_cast<unsigned>(cs);
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();  // a size the device refuses is not an error of the caller
+    fits[ti][dev][cs] = n + 1;
+  }
+  return fits[ti][dev][cs] - 1;
+}
+
+int decode_cluster_fit(int64_t d, int gp, int qt, int cs) {
+  if (d == 128)
+    return gp == 8 ? decode_clusters<128, 8>(qt, cs) : gp == 16 ? decode_clusters<128, 16>(qt, cs)
+                                                      : decode_clusters<128, 32>(qt, cs);
+  return gp == 8 ? decode_clusters<64, 8>(qt, cs) : gp == 16 ? decode_clusters<64, 16>(qt, cs)
+                                                  : decode_clusters<64, 32>(qt, cs);
+}
+
 int decode_resident(int64_t d, int gp, int qt) {
   if (d == 128)
     return gp == 8 ? decode_prepare<128, 8>(qt) : gp == 16 ? decode_prepare<128, 16>(qt) : decode_prepare<128, 32>(qt);
@@ -126,6 +167,27 @@ void decode_split(const KabKvDecodeParams* p, int resident, int* splits, int* ch
   const int64_t c = (per + 127) / 128 * 128;
   *chunk = static_cast<int>(c);
   *splits = static_cast<int>((p->length + c - 1) / c);
+}
+
+// The launch's splits, tokens per split and merge: the splits of a (sequence, KV head) form
+// one thread-block cluster and merge through distributed shared memory when a cluster of
+// that many CTAs fits and one wave of them runs at once; otherwise the partials go through
+// the global workspace and the last CTA merges them. (Fewer splits to make a cluster fit was
+// slower: at batch 4, 16 / 2 heads, 4096 tokens, 8 splits in clusters took 11.2 us per step
+// against 10.3 us for 16 splits merged through the workspace.)
+struct DecodePlan {
+  int splits = 1, chunk = 128, cluster = 0;
+};
+int decode_plan(const KabKvDecodeParams* p, int gp, DecodePlan* plan) {
+  const int qt = valid_dtype(p->q_dtype) ? p->q_dtype : KAB_BF16;
+  const int resident = decode_resident(p->head_dim, gp, qt);
+  if (resident < 0) return fail(KAB_ECUDA, "cannot configure the decode kernel");
+  decode_split(p, resident, &plan->splits, &plan->chunk);
+  const int64_t pairs = p->batch * p->heads_kv;
+  plan->cluster = 0;
+  if (plan->splits > 1 && plan->splits <= 16 && decode_cluster_fit(p->head_dim, gp, qt, plan->splits) >= pairs)
+    plan->cluster = 1;
+  return KAB_OK;
 }
 
 size_t decode_workspace_bytes(const KabKvDecodeParams* p, int splits, int gp) {
@@ -157,8 +219,24 @@ int launch_decode_t(const CUtensorMap& mk, const CUtensorMap& mv, const DecodeAr
   using L = DecodeLayout<D, GP>;
   auto kern = decode_kernel_for<D, GP>(qt);
   const dim3 grid(static_cast<unsigned>(g.splits), static_cast<unsigned>(pairs));
-  kern<<<grid, L::kThreads, L::kSmem, s>>>(mk, mv, g);
-  return check_launch("kab_kv_decode_fp8");
+  if (!g.cluster) {
+    kern<<<grid, L::kThreads, L::kSmem, s>>>(mk, mv, g);
+    return check_launch("kab_kv_decode_fp8");
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(L::kThreads);
+  cfg.dynamicSmemBytes = L::kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = static_cast<unsigned>(g.splits);
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, mk, mv, g) != cudaSuccess) return check_launch("kab_kv_decode_fp8 (cluster)");
+  return check_launch("kab_kv_decode_fp8 (cluster)");
 }
 
 }  // namespace
@@ -283,14 +361,11 @@ int kab_kv_decode_workspace(const KabKvDecodeParams* p, int* splits, size_t* byt
   int gp = 16;
   if (int e = decode_check(p, &gp)) return e;
   KAB_REQUIRE(bytes != nullptr, "null pointer");
-  int sp = 1, chunk = 128;
-  if (p->length > 0) {
-    const int resident = decode_resident(p->head_dim, gp, valid_dtype(p->q_dtype) ? p->q_dtype : KAB_BF16);
-    if (resident < 0) return fail(KAB_ECUDA, "cannot configure the decode kernel");
-    decode_split(p, resident, &sp, &chunk);
-  }
-  if (splits != nullptr) *splits = sp;
-  *bytes = decode_workspace_bytes(p, sp, gp);
+  DecodePlan plan;
+  if (p->length > 0)
+    if (int e = decode_plan(p, gp, &plan)) return e;
+  if (splits != nullptr) *splits = plan.splits;
+  *bytes = plan.cluster ? 0 : decode_workspace_bytes(p, plan.splits, gp);
   return KAB_OK;
 }
 
@@ -307,11 +382,10 @@ int kab_kv_decode_fp8(const KabKvDecodeParams* p, void* workspace, size_t worksp
                   p->vc_stride_l % 16 == 0 && p->vc_stride_h % 16 == 0 && p->vc_stride_b % 16 == 0,
               "code strides must be multiples of 16 bytes");
   KAB_REQUIRE(p->length < (int64_t(1) << 30) && p->batch * p->heads_kv < 65536, "problem too large");
-  const int resident = decode_resident(d, gp, p->q_dtype);
-  if (resident < 0) return fail(KAB_ECUDA, "cannot configure the decode kernel");
-  int splits = 1, chunk = 128;
-  decode_split(p, resident, &splits, &chunk);
-  const size_t need = decode_workspace_bytes(p, splits, gp);
+  DecodePlan plan;
+  if (int e = decode_plan(p, gp, &plan)) return e;
+  const int splits = plan.splits, chunk = plan.chunk;
+  const size_t need = plan.cluster ? 0 : decode_workspace_bytes(p, splits, gp);
   KAB_REQUIRE(need == 0 || (workspace != nullptr && workspace_bytes >= need && aligned(workspace, 256)),
               "the workspace needs %zu bytes, 256-byte aligned (kab_kv_decode_workspace)", need);
   CUtensorMap mk, mv;
@@ -339,6 +413,7 @@ int kab_kv_decode_fp8(const KabKvDecodeParams* p, void* workspace, size_t worksp
   g.lengths = p->lengths;
   g.scale_log2 = p->sm_scale * 1.4426950408889634f;
   g.out = p->out;
+  g.cluster = plan.cluster;
   const int64_t pairs = p->batch * p->heads_kv;
   if (need > 0) {
     uint8_t* w = static_cast<uint8_t*>(workspace);

@@ -239,6 +239,22 @@ def test_decode_split_edges(kv):
     status_clean()
 
 
+@pytest.mark.parametrize("splits", [4, 16, 32])
+def test_decode_split_merges(kv, splits):
+    """The splits' merge both ways: up to 16 splits of a (sequence, KV head) form one
+    thread-block cluster and merge through distributed shared memory; 32 go through the global
+    workspace and the last CTA. Each run twice (the workspace's counters return to zero)."""
+    q, k, v = _case(2, 8, 2, 4096, 128, seed=17)
+    kc, ks = kv.quantize_kv(k.to(DEV))
+    vc, vs = kv.quantize_kv(v.to(DEV))
+    lens = torch.tensor([4096, 1500], device=DEV)
+    want = _oracle(q, kc, ks, vc, vs, lengths=lens)
+    a = kv.fp8_kv_decode(q.to(DEV), kc, ks, vc, vs, lengths=lens, splits=splits)
+    b = kv.fp8_kv_decode(q.to(DEV), kc, ks, vc, vs, lengths=lens, splits=splits)
+    assert rel(np_values(a), want) < TOL and torch.equal(a, b)
+    status_clean()
+
+
 def test_module_against_sdpa(kv):
     """Fp8KVDecodeAttention (quantising K and V per call) against SDPA on the unquantised
     K / V: the quantisation error the reference test allows (kv_quant's < 0.04)."""
