@@ -202,6 +202,25 @@ def test_silu_mul_mxfp8_and_fp8(kp, kq, rows, k, golden):
     assert float((d == 0).mean()) >= 0.99 and int(d.max()) <= 1
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_silu_mul_matches_eager_on_gpu(kp, dtype):
+    """The producer's SiLU(g) * u (a fast exponential checked against the rounding boundaries,
+    the exact expf and IEEE division near them) against torch's own eager F.silu(g) * u on the
+    GPU, x / (1 + expf(-x)) with an IEEE division: 4M elements over |g| <= 20 and the small
+    values where the rounding boundaries are densest."""
+    gen_ = torch.Generator(device=DEV).manual_seed(7)
+    g = (torch.rand(1024, 4096, device=DEV, generator=gen_) * 40 - 20)
+    g[:256] = torch.randn(256, 4096, device=DEV, generator=gen_) * 0.05
+    g = g.to(dtype)
+    u = torch.randn(1024, 4096, device=DEV, generator=gen_).to(dtype)
+    h = torch.empty_like(g)
+    kp.silu_mul_fp8(g, u, mx=True, out=h)
+    eager = torch.nn.functional.silu(g) * u
+    same = (h.view(torch.int16) == eager.view(torch.int16)).float().mean().item()
+    assert same >= 0.9999, same
+    assert torch.allclose(h.float(), eager.float(), rtol=2 ** -7, atol=0)
+
+
 @pytest.mark.parametrize("gran", ["token", "tensor"])
 def test_nvfp4_golden(kq, golden, gran):
     g = golden
