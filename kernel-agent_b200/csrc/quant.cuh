@@ -25,9 +25,11 @@ constexpr float kNvfp4OuterStep = 0.00037202381645329297f;  // fp32(1 / 2688), q
 
 // F.silu(g) * u with the rounding points of eager (triton_fp8_producers.py:136-147): the
 // SiLU rounded to the input dtype, the product rounded to it again. `expf` is CUDA's.
+// (An intermediate value: the hardware conversion rounds to nearest even like the stored
+// outputs' f32_to_bf16_bits; only a NaN's payload can differ, and a NaN stays a NaN.)
 template <int T>
 __device__ __forceinline__ float round_to_input(float f) {
-  if constexpr (T == kBF16) return round_bf16(f);
+  if constexpr (T == kBF16) return __bfloat162float(__float2bfloat16_rn(f));
   else if constexpr (T == kF16) return __half2float(__float2half_rn(f));
   else return f;
 }
