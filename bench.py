@@ -14,6 +14,7 @@ Workloads (synthetic, seeded; BASELINE.json's configurations):
   fp8_blockwise  config 2: 1x128 FP8 producer + blockwise-scaled tcgen05 GEMM (M = 2048).
   fp8_attention  config 5: per-head e4m3 quantisation + causal tcgen05 FP8 attention.
   w8a8_decode    decode-size INT8 W8A8 linear (M = 16): per-token producer + skinny GEMM.
+  rmsnorm_fp8    fused RMSNorm -> FP8 per token (x [16384, 4096] bf16, one pass).
   kv_decode      FP8 KV-cache decode attention (16 / 2 heads, head_dim 128, batch 4, 4096
                  cached tokens): split-KV tcgen05 attention over e4m3 K / V.
 
@@ -171,6 +172,9 @@ def _cpu_worker(args):
     elif kind == "w8a8":
         x, q, sc, bias = payload
         oq.int8_w8a8_linear(x, q, sc, bias)
+    elif kind == "rmsnorm_fp8":
+        x, w = payload
+        oq.quantize_fp8_activations(oq.rmsnorm(x, w, 1e-6, "bf16"))
     elif kind == "kv":
         from oracle import kv_quant as okv
 
@@ -453,6 +457,85 @@ class W8a8Decode(Workload):
         rate, cores = cpu_rate("w8a8", chunks * procs, gb * procs, budget, procs)
         return {"value": rate, "unit": "GB/s", "cores": cores, "kind": "port",
                 "sample": f"oracle int8_w8a8_linear on X [16, 4096] x {cols} weight rows, repeated ~{budget:.0f} s"}
+
+    def reference(self, steps, warmup):
+        procs = os.cpu_count() or 1
+        r = self._cpu(2.0 * max(steps, 1), procs)
+        return r["value"], r["cores"], r["sample"] + f", {procs} processes"
+
+
+class RmsnormFp8(Workload):
+    """The fused RMSNorm -> FP8 producer (triton_fp8_producers.py:191-202, per-token e4m3):
+    x [16384, 4096] bf16, one pass over x (the norm kept in registers, then the codes)."""
+
+    name = "rmsnorm_fp8"
+    unit = "GB/s"
+    dtype = "bf16->e4m3"
+
+    def setup(self, dev, world, rank):
+        import torch
+
+        from kernel_agent_b200.kernels import producers
+
+        self.torch, self.producers = torch, producers
+        self.m, self.k = 16384, 4096
+        g = torch.Generator(device="cuda").manual_seed(0)
+        self.x = (torch.randn(self.m, self.k, device=dev, generator=g) * 3).to(torch.bfloat16)
+        self.w = (1.0 + 0.1 * torch.randn(self.k, device=dev, generator=g)).to(torch.bfloat16)
+        self.bytes = self.m * self.k * 2 + self.k * 2 + self.m * self.k + 4 * self.m
+        self.units = self.bytes / 1e9
+        self.kernel = "rmsnorm_quant_fp8_kernel"
+        self.kernel_bytes = self.bytes
+        self.x_host = self.x.cpu().pin_memory()
+        self.h2d = self.x.numel() * 2
+        self.d2h = self.m * self.k + 4 * self.m
+        self.out_host = [torch.empty(self.m, self.k, dtype=torch.uint8).pin_memory(),
+                         torch.empty(self.m, dtype=torch.float32).pin_memory()]
+        self.config = {"workload": "RMSNorm -> FP8 per token, x [16384, 4096] bf16, one pass",
+                       "rows": self.m, "k": self.k, "l2": "inputs larger than L2 (134 MB read, 67 MB written "
+                       "per step)"}
+
+    def step(self):
+        self.producers.rmsnorm_fp8(self.x, self.w, 1e-6)
+        return 1
+
+    def e2e_step(self):
+        x = self.x_host.to(self.x.device, non_blocking=True)
+        q, s = self.producers.rmsnorm_fp8(x, self.w, 1e-6)
+        self.out_host[0].copy_(q.view(self.torch.uint8), non_blocking=True)
+        self.out_host[1].copy_(s, non_blocking=True)
+        return 1
+
+    def library_bar(self):
+        """The same result in two passes (kab_rmsnorm into h, then the row quantiser)."""
+        torch = self.torch
+        try:
+            f = lambda: self.producers.quantize_rows(self.producers._rmsnorm(self.x, self.w, 1e-6, None))  # noqa: E731
+            for _ in range(3):
+                f()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+            a.record()
+            for _ in range(10):
+                f()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / 10
+            return {"two_pass_gbs": self.bytes / (ms / 1e3) / 1e9, "two_pass_ms": ms,
+                    "what": "kab_rmsnorm then kab_quant_rows_fp8, the same algorithmic bytes"}
+        except Exception as e:  # noqa: BLE001 - the bar is informational
+            return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+
+    def cpu_baseline(self):
+        return self._cpu(10.0, 1)
+
+    def _cpu(self, budget, procs):
+        rows = 64
+        chunk = (self.x[:rows].float().cpu().numpy(), self.w.float().cpu().numpy())
+        gb = rows * (self.k * 3 + 4) / 1e9
+        rate, cores = cpu_rate("rmsnorm_fp8", [chunk] * procs, gb * procs, budget, procs)
+        return {"value": rate, "unit": "GB/s", "cores": cores, "kind": "port",
+                "sample": f"oracle rmsnorm + quantize_fp8_activations on {rows} rows, repeated ~{budget:.0f} s"}
 
     def reference(self, steps, warmup):
         procs = os.cpu_count() or 1
@@ -1057,7 +1140,7 @@ class Fp8Attention(Workload):
 
 
 WORKLOADS = {w.name: w for w in (W4A4Linear, Nvfp4Producer, Mxfp8Producer, Compare, Fp8Blockwise, Fp8Attention,
-                                  W8a8Decode, KvDecode)}
+                                  W8a8Decode, KvDecode, RmsnormFp8)}
 DEFAULT = "w4a4"
 
 

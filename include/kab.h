@@ -299,6 +299,15 @@ int kab_hadamard_rotate(const void* x, int dtype, int64_t rows, int64_t k, int64
 int kab_rmsnorm(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, const void* weight, float eps,
                 void* out, void* stream);
 
+/* The same RMSNorm and its FP8 quantisation in one pass over x (the fused producers of
+ * triton_fp8_producers.py:120-133, 191-202): h (nullable: written when given) and the codes of
+ * h, bit for bit those of kab_rmsnorm followed by kab_quant_rows_fp8 (mx 0: fp32 scales
+ * [rows]) or kab_quant_mxfp8 with the ceil rule (mx 1: e8m0 bytes [rows, k / 32], in the
+ * 128 x 4 swizzled layout with `swizzle`). k <= 16384 (a multiple of 8, of 32 with mx). */
+int kab_rmsnorm_quant_fp8(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                          const void* weight, float eps, int mx, int swizzle, uint8_t* q,
+                          void* scales, void* h, void* stream);
+
 /* quant.py:1117-1148 fp4_bias_correction: per row of x [rows, k] quantised to (codes,
  * scales [rows, k / block] bytes, row-major or `swizzled`, outer [rows] / one value / null),
  * c = sum x^2 / sum x x^ in float64 (1 when sum x x^ <= 0 or c is not finite); fp32 out [rows]. */

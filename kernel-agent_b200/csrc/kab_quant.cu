@@ -409,6 +409,43 @@ int kab_rmsnorm(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, 
   return check_launch("kab_rmsnorm");
 }
 
+int kab_rmsnorm_quant_fp8(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, const void* weight,
+                          float eps, int mx, int swizzle, uint8_t* q, void* scales, void* h, void* stream) {
+  if (int e = check_matrix(x, dtype, rows, k, ldx, "x")) return e;
+  KAB_REQUIRE(k % (mx ? 32 : 8) == 0, "the last dimension %lld is not a multiple of %d", (long long)k, mx ? 32 : 8);
+  KAB_REQUIRE(k <= 16384, "rows of %lld elements exceed the fused kernel's 16384 (use kab_rmsnorm, then quantise)",
+              (long long)k);
+  KAB_REQUIRE(rows == 0 || (weight != nullptr && aligned(weight, 16) && q != nullptr && aligned(q, 8) &&
+                            scales != nullptr),
+              "weight, q or scales is null or misaligned");
+  KAB_REQUIRE(h == nullptr || aligned(h, 16), "h is not 16-byte aligned");
+  KAB_REQUIRE(eps >= 0.0f, "eps must be non-negative");
+  if (rows == 0 || k == 0) return KAB_OK;
+  KAB_REQUIRE(rows < (int64_t(1) << 31), "too many rows (%lld)", (long long)rows);
+  const int64_t per = (k / 8 + 255) / 256;
+  const int maxc = per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : 8;
+  const cudaStream_t s = as_stream(stream);
+  const unsigned grid = static_cast<unsigned>(rows);
+#define KAB_RQ(TT, MC, M) \
+  rmsnorm_quant_fp8_kernel<TT, MC, M><<<grid, 256, 0, s>>>(x, ldx, k, weight, eps, swizzle, q, scales, h)
+#define KAB_RQ_M(TT, MC) \
+  if (mx) KAB_RQ(TT, MC, 1); else KAB_RQ(TT, MC, 0)
+#define KAB_RQ_C(TT)                               \
+  switch (maxc) {                                  \
+    case 1: KAB_RQ_M(TT, 1); break;                \
+    case 2: KAB_RQ_M(TT, 2); break;                \
+    case 4: KAB_RQ_M(TT, 4); break;                \
+    default: KAB_RQ_M(TT, 8); break;               \
+  }
+  if (dtype == KAB_BF16) { KAB_RQ_C(kBF16) }
+  else if (dtype == KAB_F16) { KAB_RQ_C(kF16) }
+  else { KAB_RQ_C(kF32) }
+#undef KAB_RQ_C
+#undef KAB_RQ_M
+#undef KAB_RQ
+  return check_launch("kab_rmsnorm_quant_fp8");
+}
+
 int kab_hadamard_rotate(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, int block, float* out,
                         void* stream) {
   KAB_REQUIRE(valid_dtype(dtype), "unknown dtype %d", dtype);

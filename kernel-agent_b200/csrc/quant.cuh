@@ -660,6 +660,93 @@ rmsnorm_rows_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const vo
   }
 }
 
+// RMSNorm then FP8 in one pass over x (triton_fp8_producers.py:120-133, 191-202): one CTA of
+// 256 threads per row; the row's chunks stay in registers (MAXC per thread) from the sum of
+// squares, taken in rmsnorm_rows_kernel's order so that r and h are bit for bit the two-pass
+// ones, to the codes. MX 0: e4m3 per token (quant.py:361-377: scale amax / 448, 1 for a zero
+// row); MX 1: MXFP8 (quant.py:479-526: the ceil rule's e8m0 per 32, four lanes per block),
+// scales row-major or swizzled. h (nullable): the norm's output.
+template <int T, int MAXC, int MX>
+__global__ void __launch_bounds__(256)
+rmsnorm_quant_fp8_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const void* __restrict__ w, float eps,
+                         int swizzle, uint8_t* __restrict__ q, void* __restrict__ scales, void* __restrict__ h) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int64_t chunks = k >> 3;
+  float v[MAXC][8];
+  float ss = 0.0f;
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    const int64_t ci = threadIdx.x + static_cast<int64_t>(c) * 256;
+    if (ci < chunks) {
+      load8<T>(x, row * ldx + ci * 8, v[c]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = __fadd_rn(ss, __fmul_rn(v[c][j], v[c][j]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = lane < 8 ? red[lane] : 0.0f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot = __fadd_rn(tot, __shfl_xor_sync(0xffffffffu, tot, o));
+  const float r = rsqrtf(__fadd_rn(__fdiv_rn(tot, static_cast<float>(k)), eps));
+  __syncthreads();  // red is reused below
+  uint32_t abits = 0;
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    const int64_t ci = threadIdx.x + static_cast<int64_t>(c) * 256;
+    if (ci < chunks) {
+      float wv[8];
+      load8<T>(w, ci * 8, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        v[c][j] = round_to_input<T>(__fmul_rn(round_to_input<T>(__fmul_rn(v[c][j], r)), wv[j]));
+      if (h != nullptr) store_h8<T>(h, row * k + ci * 8, v[c]);
+      if constexpr (MX == 0) abits = abs_bits_max8(v[c], abits);
+    }
+  }
+  if constexpr (MX == 0) {
+    const float amax = block_amax(__uint_as_float(abits), red);
+    const float sc = amax > 0.0f ? __fdiv_rn(amax, kFp8Max) : 1.0f;  // quant.py:374-375
+    if (threadIdx.x == 0) reinterpret_cast<float*>(scales)[row] = sc;
+    const Divisor div(sc);
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) {
+      const int64_t ci = threadIdx.x + static_cast<int64_t>(c) * 256;
+      if (ci < chunks) {
+        float qv[8];
+        quotients<kLowE4m3>(v[c], div, qv);
+        *reinterpret_cast<uint2*>(q + row * k + ci * 8) = e4m3x8(qv);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) {  // every lane of a block of 32 runs the same iterations
+      const int64_t ci = threadIdx.x + static_cast<int64_t>(c) * 256;
+      const bool live = ci < chunks;
+      uint32_t b = live ? abs_bits_max8(v[c], 0u) : 0u;
+      b = max(b, __shfl_xor_sync(0xffffffffu, b, 1));
+      b = max(b, __shfl_xor_sync(0xffffffffu, b, 2));
+      if (live) {
+        const int e = mx_exponent(__uint_as_float(b), 0);
+        const float inv = pow2_neg(e);
+        float qv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) qv[i] = __fmul_rn(v[c][i], inv);
+        *reinterpret_cast<uint2*>(q + row * k + ci * 8) = e4m3x8(qv);
+        if ((ci & 3) == 0) {
+          const int64_t cols = k >> 5, col = ci >> 2;
+          const int64_t off = swizzle ? scale_offset_swizzled(row, col, cols) : row * cols + col;
+          reinterpret_cast<uint8_t*>(scales)[off] = static_cast<uint8_t>(e + 127);
+        }
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ global amax
 
 // NaN-keeping max |x| of a [rows, k] matrix into *out (which holds 0 before the launch):

@@ -140,8 +140,26 @@ def rmsnorm_fp8(x: torch.Tensor, weight: torch.Tensor, eps: float, mx: bool = Fa
     """``(codes, scales)`` of ``RMSNorm(x) * weight`` (triton_fp8_producers.py:191-202): per
     token e4m3 (fp32 scales ``[rows]``) or MXFP8 with ``mx`` (e8m0 bytes ``[rows, K / 32]``,
     swizzled with ``blocked``); ``out``: also the norm's output."""
-    h = _rmsnorm(x, weight, eps, out)
-    return quantize_rows(h, mx=mx, blocked=blocked)
+    nat.require_cuda(x, weight)
+    x2 = q._rows(q._input(x))
+    m, k = x2.shape
+    if k > 16384 or k % (q.MX_BLOCK if mx else 8):  # the two passes (the fused kernel's row limit)
+        h = _rmsnorm(x, weight, eps, out)
+        return quantize_rows(h, mx=mx, blocked=blocked)
+    w = weight.to(device=x2.device, dtype=x2.dtype).reshape(-1).contiguous()
+    if w.numel() != k:
+        raise ValueError(f"weight has {w.numel()} elements, expected {k}")
+    _check_out(out, x2)
+    if mx:
+        codes, scales = q._mx_outputs(m, k, x2.device, blocked)
+    else:
+        codes = torch.empty(m, k, dtype=torch.float8_e4m3fn, device=x2.device)
+        scales = torch.empty(m, dtype=torch.float32, device=x2.device)
+    if m:  # one pass: the norm kept in registers and quantised (kab_rmsnorm_quant_fp8)
+        nat.call("kab_rmsnorm_quant_fp8", x2.data_ptr(), nat.dtype_code(x2), m, k, x2.stride(0), w.data_ptr(),
+                 float(eps), int(mx), int(mx and blocked), codes.data_ptr(), scales.data_ptr(), nat.ptr(out),
+                 nat.stream_of(x2))
+    return codes, scales
 
 
 def rmsnorm_fp4(x: torch.Tensor, weight: torch.Tensor, eps: float, mx: bool = False, swizzle: bool = False,

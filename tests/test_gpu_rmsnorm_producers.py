@@ -78,6 +78,33 @@ def test_rmsnorm_fp8_codes_of_its_output(prod, m, k):
         assert np.array_equal(np_bytes(blocked), oq.swizzle_scales(rsm))
 
 
+@pytest.mark.parametrize("m,k", [(300, 1024), (7, 4096), (33, 16384), (2, 32)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_rmsnorm_fp8_one_pass_equals_two(prod, m, k, dtype):
+    """The fused producer (one pass over x: norm in registers, then the codes) gives the bytes
+    of the two passes (kab_rmsnorm into h, then the row / MXFP8 quantisers): h, codes and
+    scales, per token and MXFP8 (row-major and swizzled)."""
+    x, w = inputs(m, k, dtype, 5 * m + k)
+    h1 = torch.empty(m, k, dtype=dtype, device=DEV)
+    q1, s1 = prod.rmsnorm_fp8(x, w, 1e-5, out=h1)
+    h2 = prod._rmsnorm(x, w, 1e-5, None)
+    q2, s2 = prod.quantize_rows(h2)
+    assert torch.equal(h1, h2) and torch.equal(q1.view(torch.uint8), q2.view(torch.uint8)) and torch.equal(s1, s2)
+    for blocked in (False, True):
+        qm1, sm1 = prod.rmsnorm_fp8(x, w, 1e-5, mx=True, blocked=blocked)
+        qm2, sm2 = prod.quantize_rows(h2, mx=True, blocked=blocked)
+        assert torch.equal(qm1.view(torch.uint8), qm2.view(torch.uint8))
+        assert torch.equal(sm1.view(torch.uint8), sm2.view(torch.uint8))
+
+
+def test_rmsnorm_fp8_wide_rows_take_two_passes(prod):
+    x, w = inputs(3, 16384 + 64, torch.bfloat16, 9)
+    out = torch.empty_like(x)
+    q, s = prod.rmsnorm_fp8(x, w, 1e-6, out=out)
+    rq, rs = oq.quantize_fp8_activations(np_values(out))
+    assert np.array_equal(np_bytes(q), rq) and np.array_equal(np_values(s), rs)
+
+
 def test_unbiased_factor_of_the_other_fp4_producers(prod):
     x, _ = inputs(200, 2048, torch.bfloat16, 11)
     q, s, o, e = prod.quantize_rows_fp4(x, unbiased=True)
