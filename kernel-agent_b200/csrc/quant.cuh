@@ -667,7 +667,7 @@ rmsnorm_rows_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const vo
 // row); MX 1: MXFP8 (quant.py:479-526: the ceil rule's e8m0 per 32, four lanes per block),
 // scales row-major or swizzled. h (nullable): the norm's output.
 template <int T, int MAXC, int MX>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, MAXC <= 2 ? 8 : MAXC <= 4 ? 4 : 2)
 rmsnorm_quant_fp8_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const void* __restrict__ w, float eps,
                          int swizzle, uint8_t* __restrict__ q, void* __restrict__ scales, void* __restrict__ h) {
   __shared__ float red[32];
