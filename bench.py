@@ -15,6 +15,7 @@ Workloads (synthetic, seeded; BASELINE.json's configurations):
   fp8_attention  config 5: per-head e4m3 quantisation + causal tcgen05 FP8 attention.
   w8a8_decode    decode-size INT8 W8A8 linear (M = 16): per-token producer + skinny GEMM.
   rmsnorm_fp8    fused RMSNorm -> FP8 per token (x [16384, 4096] bf16, one pass).
+  rmsnorm_fp4    fused RMSNorm -> NVFP4 per token (x [16384, 4096] bf16, one pass).
   kv_decode      FP8 KV-cache decode attention (16 / 2 heads, head_dim 128, batch 4, 4096
                  cached tokens): split-KV tcgen05 attention over e4m3 K / V.
 
@@ -175,6 +176,9 @@ def _cpu_worker(args):
     elif kind == "rmsnorm_fp8":
         x, w = payload
         oq.quantize_fp8_activations(oq.rmsnorm(x, w, 1e-6, "bf16"))
+    elif kind == "rmsnorm_fp4":
+        x, w = payload
+        oq.quantize_fp4_activations(oq.rmsnorm(x, w, 1e-6, "bf16"), "nvfp4", "token")
     elif kind == "kv":
         from oracle import kv_quant as okv
 
@@ -541,6 +545,68 @@ class RmsnormFp8(Workload):
         procs = os.cpu_count() or 1
         r = self._cpu(2.0 * max(steps, 1), procs)
         return r["value"], r["cores"], r["sample"] + f", {procs} processes"
+
+
+class RmsnormFp4(RmsnormFp8):
+    """The fused RMSNorm -> NVFP4 producer (triton_fp4_producers.py:384-405, per-token outer
+    scale): x [16384, 4096] bf16, one pass over x (the norm kept in registers, then the codes,
+    block scales and outer scales)."""
+
+    name = "rmsnorm_fp4"
+    dtype = "bf16->e2m1"
+
+    def setup(self, dev, world, rank):
+        super().setup(dev, world, rank)
+        m, k = self.m, self.k
+        self.bytes = m * k * 2 + k * 2 + m * k // 2 + m * k // 16 + 4 * m
+        self.units = self.bytes / 1e9
+        self.kernel = "quant_fp4_fast_kernel<NORM>"
+        self.kernel_bytes = self.bytes
+        self.d2h = m * k // 2 + m * k // 16 + 4 * m
+        torch = self.torch
+        self.out_host = [torch.empty(m, k // 2, dtype=torch.uint8).pin_memory(),
+                         torch.empty(m, k // 16, dtype=torch.uint8).pin_memory(),
+                         torch.empty(m, dtype=torch.float32).pin_memory()]
+        self.config = {"workload": "RMSNorm -> NVFP4 per token, x [16384, 4096] bf16, one pass",
+                       "rows": m, "k": k, "l2": "inputs larger than L2 (134 MB read, 38 MB written per step)"}
+
+    def step(self):
+        self.producers.rmsnorm_fp4(self.x, self.w, 1e-6)
+        return 1
+
+    def e2e_step(self):
+        x = self.x_host.to(self.x.device, non_blocking=True)
+        for dst, src in zip(self.out_host, self.producers.rmsnorm_fp4(x, self.w, 1e-6)):
+            dst.copy_(src.view(self.torch.uint8) if src.dtype != self.torch.float32 else src, non_blocking=True)
+        return 1
+
+    def library_bar(self):
+        """The same result in two passes (kab_rmsnorm into h, then the NVFP4 producer)."""
+        torch = self.torch
+        try:
+            f = lambda: self.producers.quantize_rows_fp4(self.producers._rmsnorm(self.x, self.w, 1e-6, None))  # noqa: E731
+            for _ in range(3):
+                f()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+            a.record()
+            for _ in range(10):
+                f()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / 10
+            return {"two_pass_gbs": self.bytes / (ms / 1e3) / 1e9, "two_pass_ms": ms,
+                    "what": "kab_rmsnorm then kab_quant_fp4, the same algorithmic bytes"}
+        except Exception as e:  # noqa: BLE001 - the bar is informational
+            return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+
+    def _cpu(self, budget, procs):
+        rows = 64
+        chunk = (self.x[:rows].float().cpu().numpy(), self.w.float().cpu().numpy())
+        gb = rows * (self.k * 2 + self.k // 2 + self.k // 16 + 4) / 1e9
+        rate, cores = cpu_rate("rmsnorm_fp4", [chunk] * procs, gb * procs, budget, procs)
+        return {"value": rate, "unit": "GB/s", "cores": cores, "kind": "port",
+                "sample": f"oracle rmsnorm + quantize_fp4_activations on {rows} rows, repeated ~{budget:.0f} s"}
 
 
 class KvDecode(Workload):
@@ -1140,7 +1206,7 @@ class Fp8Attention(Workload):
 
 
 WORKLOADS = {w.name: w for w in (W4A4Linear, Nvfp4Producer, Mxfp8Producer, Compare, Fp8Blockwise, Fp8Attention,
-                                  W8a8Decode, KvDecode, RmsnormFp8)}
+                                  W8a8Decode, KvDecode, RmsnormFp8, RmsnormFp4)}
 DEFAULT = "w4a4"
 
 

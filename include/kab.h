@@ -308,6 +308,15 @@ int kab_rmsnorm_quant_fp8(const void* x, int dtype, int64_t rows, int64_t k, int
                           const void* weight, float eps, int mx, int swizzle, uint8_t* q,
                           void* scales, void* h, void* stream);
 
+/* The same RMSNorm and its FP4 quantisation in one pass over x (triton_fp4_producers.py:
+ * 261-294, 384-405): the codes, block scales and per-row outer scales of h, bit for bit those
+ * of kab_rmsnorm followed by kab_quant_fp4 with mode KAB_FP4_TOKEN (same outputs and layouts);
+ * h (nullable) receives the norm's output. x bf16 or fp16, k <= 32768 (a multiple of the
+ * format's block). */
+int kab_rmsnorm_quant_fp4(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                          const void* weight, float eps, int fmt, int swizzle, uint8_t* q,
+                          uint8_t* scales, float* outer, void* h, void* stream);
+
 /* quant.py:1117-1148 fp4_bias_correction: per row of x [rows, k] quantised to (codes,
  * scales [rows, k / block] bytes, row-major or `swizzled`, outer [rows] / one value / null),
  * c = sum x^2 / sum x x^ in float64 (1 when sum x x^ <= 0 or c is not finite); fp32 out [rows]. */

@@ -80,6 +80,24 @@ void launch_fp4_fast_nb(int maxc, unsigned rows, int threads, cudaStream_t s, co
   else if (maxc == 2) quant_fp4_fast_kernel<T, 2, F, M><<<rows, threads, 0, s>>>(x, ldx, k, amax, ts, swizzle, q, scales, outer);
   else quant_fp4_fast_kernel<T, kNbMax, F, M><<<rows, threads, 0, s>>>(x, ldx, k, amax, ts, swizzle, q, scales, outer);
 }
+template <int T, int F>
+void launch_rmsnorm_fp4(int maxc, unsigned rows, int threads, cudaStream_t s, const void* x, int64_t ldx, int64_t k,
+                        const void* w, float eps, int swizzle, uint8_t* q, uint8_t* scales, float* outer, void* h) {
+  constexpr int kNbMax = F == 0 ? 4 : 2;
+  const size_t smem = static_cast<size_t>(k) * 2 + static_cast<size_t>(k / (F == 0 ? 16 : 32)) * 4;  // row, fix list
+#define KAB_RF(NB)                                                                                          \
+  do {                                                                                                      \
+    static const bool attr = cudaFuncSetAttribute(quant_fp4_fast_kernel<T, NB, F, 0, true>,               \
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, 32768 * 2 + 2048 * 4) == cudaSuccess; \
+    (void)attr;                                                                                             \
+    quant_fp4_fast_kernel<T, NB, F, 0, true><<<rows, threads, smem, s>>>(x, ldx, k, nullptr, nullptr, swizzle, q, \
+                                                                        scales, outer, w, eps, h);         \
+  } while (0)
+  if (maxc == 1) KAB_RF(1);
+  else if (maxc == 2) KAB_RF(2);
+  else KAB_RF(kNbMax);
+#undef KAB_RF
+}
 template <int T>
 void launch_fp4_fast(int fmt, int mode, int maxc, unsigned rows, int threads, cudaStream_t s, const void* x,
                      int64_t ldx, int64_t k, const float* amax, const float* ts, int swizzle, uint8_t* q,
@@ -275,6 +293,40 @@ int kab_quant_fp4(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx
     else launch_fp4_fmt<kF32, false>(fmt, mode, maxc, grid, threads, s, x, ldx, nullptr, 0, rows, k, amax, tensor_scale, swizzle, q, scales, outer, nullptr);
   }
   return check_launch("kab_quant_fp4");
+}
+
+int kab_rmsnorm_quant_fp4(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, const void* weight,
+                          float eps, int fmt, int swizzle, uint8_t* q, uint8_t* scales, float* outer, void* h,
+                          void* stream) {
+  if (int e = check_matrix(x, dtype, rows, k, ldx, "x")) return e;
+  KAB_REQUIRE(dtype != KAB_F32, "the fused RMSNorm FP4 producer takes bf16 or fp16 (fp32: kab_rmsnorm, then kab_quant_fp4)");
+  KAB_REQUIRE(fmt == KAB_NVFP4 || fmt == KAB_MXFP4, "fmt %d is not NVFP4 (0) or MXFP4 (1)", fmt);
+  const int block = fmt == KAB_NVFP4 ? 16 : 32;
+  KAB_REQUIRE(k % block == 0, "width %lld is not a multiple of the block (%d)", (long long)k, block);
+  KAB_REQUIRE(k <= 32768, "width %lld exceeds the register-resident row (32768)", (long long)k);
+  KAB_REQUIRE(rows == 0 || (weight != nullptr && aligned(weight, 16)), "weight is null or not 16-byte aligned");
+  KAB_REQUIRE(h == nullptr || aligned(h, 16), "h is not 16-byte aligned");
+  KAB_REQUIRE(rows == 0 || (q != nullptr && scales != nullptr && outer != nullptr && aligned(q, block / 2)),
+              "outputs are null or misaligned");
+  KAB_REQUIRE(eps >= 0.0f, "eps must be non-negative");
+  if (rows == 0 || k == 0) return KAB_OK;
+  KAB_REQUIRE(rows < (int64_t(1) << 31), "too many rows (%lld)", (long long)rows);
+  // the fewest threads (a multiple of 32) that hold the row at 4 (NVFP4) or 2 (MXFP4) blocks
+  // each: more rows resident per SM, more of x in flight
+  const int64_t nblk = k / block;
+  const int nb_max = fmt == KAB_NVFP4 ? 4 : 2;
+  const int threads = static_cast<int>(((nblk + nb_max - 1) / nb_max + 31) / 32 * 32);
+  const int64_t per = (nblk + threads - 1) / threads;
+  const int maxc = per <= 1 ? 1 : per <= 2 ? 2 : 4;
+  const cudaStream_t s = as_stream(stream);
+  const unsigned grid = static_cast<unsigned>(rows);
+#define KAB_RF4(TT)                                                                                     \
+  if (fmt == KAB_NVFP4) launch_rmsnorm_fp4<TT, 0>(maxc, grid, threads, s, x, ldx, k, weight, eps, swizzle, q, scales, outer, h); \
+  else launch_rmsnorm_fp4<TT, 1>(maxc, grid, threads, s, x, ldx, k, weight, eps, swizzle, q, scales, outer, h)
+  if (dtype == KAB_BF16) { KAB_RF4(kBF16); }
+  else { KAB_RF4(kF16); }
+#undef KAB_RF4
+  return check_launch("kab_rmsnorm_quant_fp4");
 }
 
 int kab_amax(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, float* out,

@@ -493,17 +493,84 @@ __device__ __forceinline__ void fp4_block_pack(float (&t)[BLOCK], uint32_t bm, u
   }
 }
 
+// Two floats rounded to nearest even into one packed T word (low half: a): the hardware
+// conversion of round_to_input, two at a time. A NaN comes out as the hardware's NaN.
+template <int T>
+__device__ __forceinline__ uint32_t pack2_rn(float a, float b) {
+  uint32_t r;
+  if constexpr (T == kBF16) {
+    const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+    r = *reinterpret_cast<const uint32_t*>(&p);
+  } else {
+    const __half2 p = __floats2half2_rn(a, b);
+    r = *reinterpret_cast<const uint32_t*>(&p);
+  }
+  return r;
+}
+
+// h = T(T(x * r) * w) of W packed words of x (two T values each) in place; wr: the weight's
+// matching 16-byte chunks. The products are fp32 (two per mul.rn.f32x2), each rounded to T
+// as round_to_input does; a block holding a NaN gets the stored outputs' NaN (f32_to_bf16_bits
+// / f32_to_f16_bits of a NaN), so the words equal those kab_rmsnorm writes.
+template <int T, int W>
+__device__ __forceinline__ void norm_words(uint32_t (&v)[W], const uint4* __restrict__ wr, float r) {
+#pragma unroll
+  for (int c = 0; c < W / 4; ++c) {
+    const uint4 wq = __ldg(wr + c);
+    const uint32_t ww[4] = {wq.x, wq.y, wq.z, wq.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 a = mul2_rn(unpack2<T>(v[4 * c + i]), r);
+      const uint32_t xr = pack2_rn<T>(a.x, a.y);
+      const float2 b = unpack2<T>(xr), wv = unpack2<T>(ww[i]);
+      unsigned long long p;
+      const unsigned long long bv = (static_cast<unsigned long long>(__float_as_uint(b.y)) << 32) | __float_as_uint(b.x);
+      const unsigned long long wv2 = (static_cast<unsigned long long>(__float_as_uint(wv.y)) << 32) | __float_as_uint(wv.x);
+      asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(bv), "l"(wv2));
+      v[4 * c + i] = pack2_rn<T>(__uint_as_float(static_cast<uint32_t>(p)), __uint_as_float(static_cast<uint32_t>(p >> 32)));
+    }
+  }
+  uint32_t m = 0;
+#pragma unroll
+  for (int j = 0; j < W; ++j) m = __vmaxu2(m, v[j] & 0x7FFF7FFFu);
+  const uint32_t inf = T == kBF16 ? 0x7F80u : 0x7C00u;
+  if (max(m & 0xFFFFu, m >> 16) > inf) {  // a NaN: the stored outputs' pattern
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      uint32_t lo = v[j] & 0xFFFFu, hi = v[j] >> 16;
+      if constexpr (T == kBF16) {
+        if ((lo & 0x7FFFu) > inf) lo = f32_to_bf16_bits(__uint_as_float(0x7FC00000u));
+        if ((hi & 0x7FFFu) > inf) hi = f32_to_bf16_bits(__uint_as_float(0x7FC00000u));
+      } else {
+        if ((lo & 0x7FFFu) > inf) lo = f32_to_f16_bits(__uint_as_float(0x7FC00000u));
+        if ((hi & 0x7FFFu) > inf) hi = f32_to_f16_bits(__uint_as_float(0x7FC00000u));
+      }
+      v[j] = lo | (hi << 16);
+    }
+  }
+}
+
 // (NVFP4 with up to two blocks per thread: at most 42 registers, six 256-thread CTAs per SM)
-template <int T, int NB, int FMT, int MODE>
-__global__ void __launch_bounds__(512, FMT == 0 && NB <= 2 ? 3 : 1)
+// NORM: the row is first RMSNorm'd (triton_fp4_producers.py:261-294). The blocks are loaded
+// into registers and staged in shared memory, whence the sum of squares is taken in
+// rmsnorm_rows_kernel's order (its 256 threads, emulated by any multiple of 32), so r and
+// h = T(T(x * r) * w) are bit for bit the two-pass ones; h is quantised from registers (and
+// written to hout [rows, k] when given); blocks redone with the IEEE division recompute
+// their h from the staged x. Launched with k * 2 + (k / block) * 4 bytes of dynamic shared
+// memory.
+template <int T, int NB, int FMT, int MODE, bool NORM = false>
+__global__ void __launch_bounds__(512, !NORM && FMT == 0 && NB <= 2 ? 3 : 1)
 quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const float* __restrict__ amax_in,
                       const float* __restrict__ ts_in, int swizzle, uint8_t* __restrict__ q,
-                      uint8_t* __restrict__ scales, float* __restrict__ outer_out) {
+                      uint8_t* __restrict__ scales, float* __restrict__ outer_out,
+                      const void* __restrict__ nw = nullptr, float eps = 0.0f, void* __restrict__ hout = nullptr) {
   __shared__ float red[32];
   // blocks whose quotients need the IEEE division, redone by the whole CTA after the row
   __shared__ int fix[kFp4MaxRowBlocks];
   __shared__ int nfix;
+  extern __shared__ uint4 fp4_row_smem[];  // NORM: the row of x (k * 2 bytes), then its fix list
   constexpr int BLOCK = FMT == 0 ? 16 : 32;
+  int* const fixp = NORM ? reinterpret_cast<int*>(fp4_row_smem + (k >> 3)) : fix;
   if (threadIdx.x == 0) nfix = 0;
   __syncthreads();
   constexpr int W = BLOCK / 2;  // packed words per block
@@ -516,7 +583,6 @@ quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const 
 #pragma unroll
   for (int b = 0; b < NB; ++b) {
     const int bi = threadIdx.x + b * blockDim.x;
-    uint32_t m = 0;
     if (bi < nblk) {
 #pragma unroll
       for (int c = 0; c < W / 4; ++c) {
@@ -525,13 +591,61 @@ quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const 
         w[b][4 * c + 1] = r.y;
         w[b][4 * c + 2] = r.z;
         w[b][4 * c + 3] = r.w;
+        if constexpr (NORM) fp4_row_smem[bi * (W / 4) + c] = r;
       }
-#pragma unroll
-      for (int j = 0; j < W; ++j) m = __vmaxu2(m, w[b][j] & 0x7FFF7FFFu);
     } else {
 #pragma unroll
       for (int j = 0; j < W; ++j) w[b][j] = 0;
     }
+  }
+  float r_norm = 1.0f;
+  if constexpr (NORM) {
+    // the sum of squares of rmsnorm_rows_kernel's 256 threads, from the staged row: virtual
+    // thread v = tid + blockDim * u sums chunks v, v + 256, ... in turn; each warp's butterfly
+    // per u is that of virtual warp v / 32 (blockDim is a multiple of 32)
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int chunks = static_cast<int>(k >> 3);
+    for (int v0 = threadIdx.x - lane; v0 < 256; v0 += blockDim.x) {
+      float ss = 0.0f;
+      for (int c = v0 + lane; c < chunks; c += 256) {
+        const uint4 q4 = fp4_row_smem[c];
+        const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = unpack2<T>(qw[i]);
+          ss = __fadd_rn(ss, __fmul_rn(f.x, f.x));
+          ss = __fadd_rn(ss, __fmul_rn(f.y, f.y));
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      if (lane == 0) red[v0 >> 5] = ss;
+    }
+    __syncthreads();
+    float tot = lane < 8 ? red[lane] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tot = __fadd_rn(tot, __shfl_xor_sync(0xffffffffu, tot, o));
+    r_norm = rsqrtf(__fadd_rn(__fdiv_rn(tot, static_cast<float>(k)), eps));
+    __syncthreads();  // red is reused for the row's amax
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {  // h = T(T(x * r) * w) in place, and into hout when given
+      const int bi = threadIdx.x + b * blockDim.x;
+      if (bi >= nblk) continue;
+      norm_words<T, W>(w[b], reinterpret_cast<const uint4*>(nw) + static_cast<int64_t>(bi) * (W / 4), r_norm);
+      if (hout != nullptr) {
+        uint4* hr = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(hout) + row * k) +
+                    static_cast<int64_t>(bi) * (W / 4);
+#pragma unroll
+        for (int c = 0; c < W / 4; ++c) hr[c] = make_uint4(w[b][4 * c], w[b][4 * c + 1], w[b][4 * c + 2], w[b][4 * c + 3]);
+      }
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    uint32_t m = 0;
+#pragma unroll
+    for (int j = 0; j < W; ++j) m = __vmaxu2(m, w[b][j] & 0x7FFF7FFFu);
     bm[b] = max(m & 0xFFFFu, m >> 16);
     am = max(am, bm[b]);
   }
@@ -574,7 +688,7 @@ quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const 
       }
       // near an e2m1 decision point (or no fast reciprocal): these codes are provisional; the
       // block is redone with the IEEE division after the row, with all lanes busy
-      if (mn < 33u * 2048u) fix[atomicAdd(&nfix, 1)] = bi;
+      if (mn < 33u * 2048u) fixp[atomicAdd(&nfix, 1)] = bi;
       fp4_block_pack<T, BLOCK>(t, bm[b], packed);
     }
     uint8_t* dst = q + row * (k >> 1) + static_cast<int64_t>(bi) * (BLOCK / 2);
@@ -586,17 +700,18 @@ quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const 
   __syncthreads();  // every provisional code is written and the list is complete
   const int nf = nfix;
   for (int i = threadIdx.x; i < nf; i += blockDim.x) {
-    const int bi = fix[i];
+    const int bi = fixp[i];
     uint32_t wv[W];
     uint32_t m = 0;
 #pragma unroll
     for (int c = 0; c < W / 4; ++c) {
-      const uint4 r = __ldg(xr + static_cast<int64_t>(bi) * (W / 4) + c);
+      const uint4 r = NORM ? fp4_row_smem[bi * (W / 4) + c] : __ldg(xr + static_cast<int64_t>(bi) * (W / 4) + c);
       wv[4 * c] = r.x;
       wv[4 * c + 1] = r.y;
       wv[4 * c + 2] = r.z;
       wv[4 * c + 3] = r.w;
     }
+    if constexpr (NORM) norm_words<T, W>(wv, reinterpret_cast<const uint4*>(nw) + static_cast<int64_t>(bi) * (W / 4), r_norm);
 #pragma unroll
     for (int j = 0; j < W; ++j) m = __vmaxu2(m, wv[j] & 0x7FFF7FFFu);
     const uint32_t bmi = max(m & 0xFFFFu, m >> 16);

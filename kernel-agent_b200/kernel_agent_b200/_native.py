@@ -117,6 +117,8 @@ _SIGNATURES: dict[str, list] = {
     "kab_rmsnorm": [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_float, c_void_p, c_void_p],
     "kab_rmsnorm_quant_fp8": [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_float, c_int, c_int, c_void_p,
                               c_void_p, c_void_p, c_void_p],
+    "kab_rmsnorm_quant_fp4": [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_float, c_int, c_int, c_void_p,
+                              c_void_p, c_void_p, c_void_p, c_void_p],
     "kab_fp4_bias_correction": [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int,
                                 c_void_p, c_int, c_void_p, c_void_p],
     "kab_gemm_f8_blockwise": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p,

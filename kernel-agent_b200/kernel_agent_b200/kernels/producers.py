@@ -11,11 +11,13 @@ rounded again); codes and scales equal ``quant.quantize_*`` of those values bit 
 ``unbiased`` (FP4): also the epilogue's per-token scale ``outer * quant.fp4_bias_correction``
 of that output (a fourth result), as the reference's producers return it.
 
-The RMSNorm producers run the norm (``kab_rmsnorm``: ``r = rsqrt(sum(x^2) / K + eps)`` in
-fp32, ``h = dtype(dtype(x * r) * weight)``) into ``out`` (or a temporary) and quantise ``h``
-with the same quantisers: two passes over ``h`` where the reference's Triton kernel fuses
-them, codes exactly those of ``h``, and ``h`` eager's RMSNorm up to the order of the sum of
-squares and the last bit of ``rsqrt``.
+The RMSNorm producers (``r = rsqrt(sum(x^2) / K + eps)`` in fp32, ``h = dtype(dtype(x * r) *
+weight)``) norm and quantise each row in one pass over ``x`` (``kab_rmsnorm_quant_fp8``,
+``kab_rmsnorm_quant_fp4``), ``h`` kept in registers and written only to ``out``; FP8 rows
+wider than 16384 and fp32 FP4 rows take two passes (``kab_rmsnorm`` into ``out`` or a
+temporary, then the quantisers). Either way the codes are
+exactly those of ``h``, and ``h`` is eager's RMSNorm up to the order of the sum of squares
+and the last bit of ``rsqrt``.
 """
 
 from __future__ import annotations
@@ -168,5 +170,17 @@ def rmsnorm_fp4(x: torch.Tensor, weight: torch.Tensor, eps: float, mx: bool = Fa
     ``mx``) (triton_fp4_producers.py:384-405); ``out``: also the norm's output; ``unbiased``:
     and the epilogue's per-token scale (fourth)."""
     fmt = _fp4_block(x.shape[-1], mx)
-    h = _rmsnorm(x, weight, eps, out)
-    return _result_fp4(h, q._fp4(h, fmt, nat.KAB_FP4_TOKEN, swizzle=swizzle), fmt, swizzle, unbiased)
+    nat.require_cuda(x, weight)
+    x2 = q._rows(q._input(x))
+    m, k = x2.shape
+    if x2.dtype == torch.float32:  # the two passes (the fused kernel takes bf16 and fp16)
+        h = _rmsnorm(x, weight, eps, out)
+        return _result_fp4(h, q._fp4(h, fmt, nat.KAB_FP4_TOKEN, swizzle=swizzle), fmt, swizzle, unbiased)
+    w = weight.to(device=x2.device, dtype=x2.dtype).reshape(-1).contiguous()
+    if w.numel() != k:
+        raise ValueError(f"weight has {w.numel()} elements, expected {k}")
+    _check_out(out, x2)
+    # one pass (kab_rmsnorm_quant_fp4); the bias correction reads h, so it is then written
+    h = out if out is not None or not unbiased else torch.empty(m, k, dtype=x2.dtype, device=x2.device)
+    res = q._fp4(x2, fmt, nat.KAB_FP4_TOKEN, swizzle=swizzle, h=h, norm=(w, eps))
+    return _result_fp4(h, res, fmt, swizzle, unbiased) if unbiased else res

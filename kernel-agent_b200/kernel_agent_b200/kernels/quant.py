@@ -316,7 +316,9 @@ def fp4_values(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def _fp4(x2, fmt: str, mode: int, amax=None, ts=None, up=None, swizzle=False, h=None):
+def _fp4(x2, fmt: str, mode: int, amax=None, ts=None, up=None, swizzle=False, h=None, norm=None):
+    """codes, scales and outer of x2 (or, with ``norm = (weight, eps)``, of its RMSNorm, in one
+    pass by ``kab_rmsnorm_quant_fp4``; ``h`` then receives the norm's output)."""
     block, scale_dtype = FP4_FORMATS[fmt]
     m, k = x2.shape
     cols = k // block
@@ -328,7 +330,11 @@ def _fp4(x2, fmt: str, mode: int, amax=None, ts=None, up=None, swizzle=False, h=
     else:
         s = torch.empty(m, cols, dtype=torch.uint8, device=x2.device)
     outer = torch.empty(m, dtype=torch.float32, device=x2.device)
-    if m and k:
+    if m and k and norm is not None:
+        nat.call("kab_rmsnorm_quant_fp4", x2.data_ptr(), nat.dtype_code(x2), m, k, x2.stride(0),
+                 norm[0].data_ptr(), float(norm[1]), nat.KAB_NVFP4 if fmt == "nvfp4" else nat.KAB_MXFP4,
+                 int(swizzle), q.data_ptr(), s.data_ptr(), outer.data_ptr(), nat.ptr(h), _stream(x2))
+    elif m and k:
         nat.call("kab_quant_fp4", x2.data_ptr(), nat.dtype_code(x2), m, k, x2.stride(0), nat.ptr(up),
                  0 if up is None else up.stride(0), nat.KAB_NVFP4 if fmt == "nvfp4" else nat.KAB_MXFP4,
                  mode, nat.ptr(amax), nat.ptr(ts), q.data_ptr(), s.data_ptr(), int(swizzle),

@@ -97,6 +97,41 @@ def test_rmsnorm_fp8_one_pass_equals_two(prod, m, k, dtype):
         assert torch.equal(sm1.view(torch.uint8), sm2.view(torch.uint8))
 
 
+@pytest.mark.parametrize("m,k", [(300, 1024), (7, 4096), (5, 20480), (3, 32768), (2, 32)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_rmsnorm_fp4_one_pass_equals_two(prod, m, k, dtype):
+    """The fused FP4 producer (kab_rmsnorm_quant_fp4: norm in registers, then the codes; 256 to
+    512 threads and one to four blocks per thread across these widths) gives the bytes of the
+    two passes (kab_rmsnorm into h, then kab_quant_fp4): h, codes, scales (row-major and
+    swizzled) and outer scales, NVFP4 and MXFP4, with and without h written; a row holding
+    inf (r = 0, NaN codes) included."""
+    x, w = inputs(m, k, dtype, 3 * m + k)
+    x[m - 1, 5] = float("inf")
+    h2 = prod._rmsnorm(x, w, 1e-5, None)
+    for mx in (False, True):
+        for swizzle in (False, True):
+            h1 = torch.empty(m, k, dtype=dtype, device=DEV)
+            q1, s1, o1 = prod.rmsnorm_fp4(x, w, 1e-5, mx=mx, swizzle=swizzle, out=h1)
+            q2, s2, o2 = prod.quantize_rows_fp4(h2, mx=mx, swizzle=swizzle)
+            assert torch.equal(h1.view(torch.int16), h2.view(torch.int16))
+            assert torch.equal(q1, q2) and torch.equal(s1.view(torch.uint8), s2.view(torch.uint8))
+            assert torch.equal(o1.view(torch.int32), o2.view(torch.int32))
+            q3, s3, o3 = prod.rmsnorm_fp4(x, w, 1e-5, mx=mx, swizzle=swizzle)  # h not written
+            assert torch.equal(q3, q2) and torch.equal(s3.view(torch.uint8), s2.view(torch.uint8))
+    _, _, o4, e4 = prod.rmsnorm_fp4(x, w, 1e-5, unbiased=True)  # h into a temporary
+    _, _, _, e5 = prod.quantize_rows_fp4(h2, unbiased=True)
+    assert torch.equal(e4.view(torch.int32), e5.view(torch.int32))
+
+
+def test_rmsnorm_fp4_fp32_takes_two_passes(prod):
+    x, w = inputs(3, 1024, torch.float32, 13)
+    out = torch.empty_like(x)
+    q, s, o = prod.rmsnorm_fp4(x, w, 1e-6, out=out)
+    rq, rs, ro = oq.quantize_fp4_activations(np_values(out))
+    assert np.array_equal(np_bytes(q), rq) and np.array_equal(np_bytes(s), rs)
+    assert np.array_equal(np_values(o), ro)
+
+
 def test_rmsnorm_fp8_wide_rows_take_two_passes(prod):
     x, w = inputs(3, 16384 + 64, torch.bfloat16, 9)
     out = torch.empty_like(x)
