@@ -510,8 +510,7 @@ __device__ __forceinline__ uint32_t pack2_rn(float a, float b) {
 
 // h = T(T(x * r) * w) of W packed words of x (two T values each) in place; wr: the weight's
 // matching 16-byte chunks. The products are fp32 (two per mul.rn.f32x2), each rounded to T
-// as round_to_input does; a block holding a NaN gets the stored outputs' NaN (f32_to_bf16_bits
-// / f32_to_f16_bits of a NaN), so the words equal those kab_rmsnorm writes.
+// as round_to_input does (a NaN as the hardware's: block_absmax<NORM> then re-patterns it).
 template <int T, int W>
 __device__ __forceinline__ void norm_words(uint32_t (&v)[W], const uint4* __restrict__ wr, float r) {
 #pragma unroll
@@ -530,11 +529,19 @@ __device__ __forceinline__ void norm_words(uint32_t (&v)[W], const uint4* __rest
       v[4 * c + i] = pack2_rn<T>(__uint_as_float(static_cast<uint32_t>(p)), __uint_as_float(static_cast<uint32_t>(p >> 32)));
     }
   }
+}
+
+// |max| (16-bit pattern) of W packed words; with NORM, a block holding a NaN first gets the
+// stored outputs' NaN pattern (f32_to_bf16_bits / f32_to_f16_bits of a NaN) in place, so its
+// words equal those kab_rmsnorm writes.
+template <int T, int W, bool NORM>
+__device__ __forceinline__ uint32_t block_absmax(uint32_t (&v)[W]) {
   uint32_t m = 0;
 #pragma unroll
   for (int j = 0; j < W; ++j) m = __vmaxu2(m, v[j] & 0x7FFF7FFFu);
+  uint32_t bm = max(m & 0xFFFFu, m >> 16);
   const uint32_t inf = T == kBF16 ? 0x7F80u : 0x7C00u;
-  if (max(m & 0xFFFFu, m >> 16) > inf) {  // a NaN: the stored outputs' pattern
+  if (NORM && bm > inf) {
 #pragma unroll
     for (int j = 0; j < W; ++j) {
       uint32_t lo = v[j] & 0xFFFFu, hi = v[j] >> 16;
@@ -547,7 +554,12 @@ __device__ __forceinline__ void norm_words(uint32_t (&v)[W], const uint4* __rest
       }
       v[j] = lo | (hi << 16);
     }
+    m = 0;
+#pragma unroll
+    for (int j = 0; j < W; ++j) m = __vmaxu2(m, v[j] & 0x7FFF7FFFu);
+    bm = max(m & 0xFFFFu, m >> 16);
   }
+  return bm;
 }
 
 // (NVFP4 with up to two blocks per thread: at most 42 registers, six 256-thread CTAs per SM)
@@ -633,6 +645,7 @@ quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const 
       const int bi = threadIdx.x + b * blockDim.x;
       if (bi >= nblk) continue;
       norm_words<T, W>(w[b], reinterpret_cast<const uint4*>(nw) + static_cast<int64_t>(bi) * (W / 4), r_norm);
+      bm[b] = block_absmax<T, W, true>(w[b]);
       if (hout != nullptr) {
         uint4* hr = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(hout) + row * k) +
                     static_cast<int64_t>(bi) * (W / 4);
@@ -643,10 +656,11 @@ quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const 
   }
 #pragma unroll
   for (int b = 0; b < NB; ++b) {
-    uint32_t m = 0;
-#pragma unroll
-    for (int j = 0; j < W; ++j) m = __vmaxu2(m, w[b][j] & 0x7FFF7FFFu);
-    bm[b] = max(m & 0xFFFFu, m >> 16);
+    if constexpr (NORM) {
+      if (threadIdx.x + b * blockDim.x >= nblk) bm[b] = 0;  // zero words
+    } else {
+      bm[b] = block_absmax<T, W, false>(w[b]);
+    }
     am = max(am, bm[b]);
   }
   float s_outer = 1.0f;
@@ -702,7 +716,6 @@ quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const 
   for (int i = threadIdx.x; i < nf; i += blockDim.x) {
     const int bi = fixp[i];
     uint32_t wv[W];
-    uint32_t m = 0;
 #pragma unroll
     for (int c = 0; c < W / 4; ++c) {
       const uint4 r = NORM ? fp4_row_smem[bi * (W / 4) + c] : __ldg(xr + static_cast<int64_t>(bi) * (W / 4) + c);
@@ -712,9 +725,7 @@ quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const 
       wv[4 * c + 3] = r.w;
     }
     if constexpr (NORM) norm_words<T, W>(wv, reinterpret_cast<const uint4*>(nw) + static_cast<int64_t>(bi) * (W / 4), r_norm);
-#pragma unroll
-    for (int j = 0; j < W; ++j) m = __vmaxu2(m, wv[j] & 0x7FFF7FFFu);
-    const uint32_t bmi = max(m & 0xFFFFu, m >> 16);
+    const uint32_t bmi = block_absmax<T, W, NORM>(wv);
     uint32_t sbyte;
     float step;
     fp4_block_scale<T, FMT, MODE>(bmi, s_outer, by6, sbyte, step);
