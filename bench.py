@@ -488,7 +488,7 @@ class RmsnormFp8(Workload):
         self.w = (1.0 + 0.1 * torch.randn(self.k, device=dev, generator=g)).to(torch.bfloat16)
         self.bytes = self.m * self.k * 2 + self.k * 2 + self.m * self.k + 4 * self.m
         self.units = self.bytes / 1e9
-        self.kernel = "rmsnorm_quant_fp8_kernel"
+        self.kernel = "rmsnorm_quant_fp8_packed_kernel"
         self.kernel_bytes = self.bytes
         self.x_host = self.x.cpu().pin_memory()
         self.h2d = self.x.numel() * 2

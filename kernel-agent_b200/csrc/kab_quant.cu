@@ -489,9 +489,32 @@ int kab_rmsnorm_quant_fp8(const void* x, int dtype, int64_t rows, int64_t k, int
     case 4: KAB_RQ_M(TT, 4); break;                \
     default: KAB_RQ_M(TT, 8); break;               \
   }
-  if (dtype == KAB_BF16) { KAB_RQ_C(kBF16) }
-  else if (dtype == KAB_F16) { KAB_RQ_C(kF16) }
-  else { KAB_RQ_C(kF32) }
+  if (dtype != KAB_F32) {
+    // 2-byte rows: the packed kernel, the fewest threads (64, 128, 256) that hold the row at
+    // up to 8 chunks each
+    const int64_t chunks = k / 8;
+    const int nt = chunks <= 512 ? 64 : chunks <= 1024 ? 128 : 256;
+    const int64_t pc = (chunks + nt - 1) / nt;
+    const int nc = pc <= 1 ? 1 : pc <= 2 ? 2 : pc <= 4 ? 4 : 8;
+#define KAB_RP(TT, NC, NT)                                                                                     \
+  do {                                                                                                         \
+    if (mx) rmsnorm_quant_fp8_packed_kernel<TT, NC, 1, NT><<<grid, NT, 0, s>>>(x, ldx, k, weight, eps, swizzle, q, scales, h); \
+    else rmsnorm_quant_fp8_packed_kernel<TT, NC, 0, NT><<<grid, NT, 0, s>>>(x, ldx, k, weight, eps, swizzle, q, scales, h); \
+  } while (0)
+#define KAB_RP_T(TT)                          \
+  if (nt == 256) KAB_RP(TT, 8, 256);          \
+  else if (nt == 128) KAB_RP(TT, 8, 128);     \
+  else if (nc == 8) KAB_RP(TT, 8, 64);        \
+  else if (nc == 4) KAB_RP(TT, 4, 64);        \
+  else if (nc == 2) KAB_RP(TT, 2, 64);        \
+  else KAB_RP(TT, 1, 64)
+    if (dtype == KAB_BF16) { KAB_RP_T(kBF16); }
+    else { KAB_RP_T(kF16); }
+#undef KAB_RP_T
+#undef KAB_RP
+  } else {
+    KAB_RQ_C(kF32)
+  }
 #undef KAB_RQ_C
 #undef KAB_RQ_M
 #undef KAB_RQ

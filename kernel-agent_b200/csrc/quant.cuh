@@ -873,6 +873,122 @@ rmsnorm_quant_fp8_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, con
   }
 }
 
+// The same producer for bf16 / fp16 rows with NT threads per row (64, 128 or 256) and NC
+// 16-byte chunks each, kept packed (two values per register): more rows resident per SM.
+// Thread t holds chunks t + NT * c, which are exactly the chunks of rmsnorm_rows_kernel's
+// threads t + NT * u (u < 256 / NT, c = u + (256 / NT) * i), so the sum of squares is taken
+// per such virtual thread in its order and reduced per virtual warp: r and h are bit for bit
+// the two-pass ones. The norm is norm_words' packed arithmetic, a NaN re-patterned as stored.
+template <int T, int NC, int MX, int NT>
+__global__ void __launch_bounds__(NT)
+rmsnorm_quant_fp8_packed_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const void* __restrict__ w,
+                                float eps, int swizzle, uint8_t* __restrict__ q, void* __restrict__ scales,
+                                void* __restrict__ h) {
+  static_assert(T != kF32 && NT % 32 == 0 && 256 % NT == 0, "2-byte rows; NT divides 256");
+  constexpr int U = 256 / NT;  // virtual threads per thread
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int chunks = static_cast<int>(k >> 3);
+  const uint4* xr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + row * ldx);
+  uint32_t v[NC][4];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int ci = threadIdx.x + c * NT;
+    if (ci < chunks) {
+      const uint4 r = __ldg(xr + ci);
+      v[c][0] = r.x; v[c][1] = r.y; v[c][2] = r.z; v[c][3] = r.w;
+    } else {
+      v[c][0] = v[c][1] = v[c][2] = v[c][3] = 0u;
+    }
+  }
+  float ss[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) ss[u] = 0.0f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    if (threadIdx.x + c * NT < chunks) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack2<T>(v[c][i]);
+        ss[c % U] = __fadd_rn(ss[c % U], __fmul_rn(f.x, f.x));
+        ss[c % U] = __fadd_rn(ss[c % U], __fmul_rn(f.y, f.y));
+      }
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss[u] = __fadd_rn(ss[u], __shfl_xor_sync(0xffffffffu, ss[u], o));
+    if (lane == 0) red[warp + (NT / 32) * u] = ss[u];
+  }
+  __syncthreads();
+  float tot = lane < 8 ? red[lane] : 0.0f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot = __fadd_rn(tot, __shfl_xor_sync(0xffffffffu, tot, o));
+  const float r = rsqrtf(__fadd_rn(__fdiv_rn(tot, static_cast<float>(k)), eps));
+  uint32_t abits = 0;
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int ci = threadIdx.x + c * NT;
+    if (ci < chunks) {
+      norm_words<T, 4>(v[c], wr + ci, r);
+      const uint32_t bm = block_absmax<T, 4, true>(v[c]);
+      if (h != nullptr)
+        reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(h) + row * k)[ci] = make_uint4(v[c][0], v[c][1], v[c][2], v[c][3]);
+      if constexpr (MX == 0) abits = max(abits, __float_as_uint(half_bits_to_float<T>(bm)) & 0x7FFFFFFFu);
+    }
+  }
+  auto values = [&](int c, float (&f)[8]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 p = unpack2<T>(v[c][i]);
+      f[2 * i] = p.x;
+      f[2 * i + 1] = p.y;
+    }
+  };
+  if constexpr (MX == 0) {
+    const float amax = block_amax(__uint_as_float(abits), red);  // (syncs before reusing red)
+    const float sc = amax > 0.0f ? __fdiv_rn(amax, kFp8Max) : 1.0f;  // quant.py:374-375
+    if (threadIdx.x == 0) reinterpret_cast<float*>(scales)[row] = sc;
+    const Divisor div(sc);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int ci = threadIdx.x + c * NT;
+      if (ci < chunks) {
+        float f[8], qv[8];
+        values(c, f);
+        quotients<kLowE4m3>(f, div, qv);
+        *reinterpret_cast<uint2*>(q + row * k + static_cast<int64_t>(ci) * 8) = e4m3x8(qv);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {  // every lane of a block of 32 runs the same iterations
+      const int ci = threadIdx.x + c * NT;
+      const bool live = ci < chunks;
+      uint32_t b = live ? __float_as_uint(half_bits_to_float<T>(block_absmax<T, 4, false>(v[c]))) & 0x7FFFFFFFu : 0u;
+      b = max(b, __shfl_xor_sync(0xffffffffu, b, 1));
+      b = max(b, __shfl_xor_sync(0xffffffffu, b, 2));
+      if (live) {
+        const int e = mx_exponent(__uint_as_float(b), 0);
+        const float inv = pow2_neg(e);
+        float f[8], qv[8];
+        values(c, f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) qv[i] = __fmul_rn(f[i], inv);
+        *reinterpret_cast<uint2*>(q + row * k + static_cast<int64_t>(ci) * 8) = e4m3x8(qv);
+        if ((ci & 3) == 0) {
+          const int64_t cols = k >> 5, col = ci >> 2;
+          const int64_t off = swizzle ? scale_offset_swizzled(row, col, cols) : row * cols + col;
+          reinterpret_cast<uint8_t*>(scales)[off] = static_cast<uint8_t>(e + 127);
+        }
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ global amax
 
 // NaN-keeping max |x| of a [rows, k] matrix into *out (which holds 0 before the launch):

@@ -78,18 +78,24 @@ def test_rmsnorm_fp8_codes_of_its_output(prod, m, k):
         assert np.array_equal(np_bytes(blocked), oq.swizzle_scales(rsm))
 
 
-@pytest.mark.parametrize("m,k", [(300, 1024), (7, 4096), (33, 16384), (2, 32)])
+@pytest.mark.parametrize("m,k", [(300, 1024), (5, 2048), (7, 4096), (9, 8192), (33, 16384), (2, 32)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_rmsnorm_fp8_one_pass_equals_two(prod, m, k, dtype):
-    """The fused producer (one pass over x: norm in registers, then the codes) gives the bytes
-    of the two passes (kab_rmsnorm into h, then the row / MXFP8 quantisers): h, codes and
-    scales, per token and MXFP8 (row-major and swizzled)."""
+    """The fused producer (one pass over x: norm in registers, then the codes; for 2-byte rows
+    64 to 256 threads with 1 to 8 chunks each across these widths) gives the bytes of the two
+    passes (kab_rmsnorm into h, then the row / MXFP8 quantisers): h, codes and scales, per
+    token and MXFP8 (row-major and swizzled); a row holding inf (r = 0, a NaN in h) included."""
     x, w = inputs(m, k, dtype, 5 * m + k)
+    x[m - 1, 3] = float("inf")
+    bits = torch.int32 if dtype == torch.float32 else torch.int16
     h1 = torch.empty(m, k, dtype=dtype, device=DEV)
     q1, s1 = prod.rmsnorm_fp8(x, w, 1e-5, out=h1)
     h2 = prod._rmsnorm(x, w, 1e-5, None)
     q2, s2 = prod.quantize_rows(h2)
-    assert torch.equal(h1, h2) and torch.equal(q1.view(torch.uint8), q2.view(torch.uint8)) and torch.equal(s1, s2)
+    assert torch.equal(h1.view(bits), h2.view(bits))
+    assert torch.equal(q1.view(torch.uint8), q2.view(torch.uint8)) and torch.equal(s1.view(torch.int32), s2.view(torch.int32))
+    q3, s3 = prod.rmsnorm_fp8(x, w, 1e-5)  # h not written
+    assert torch.equal(q3.view(torch.uint8), q2.view(torch.uint8))
     for blocked in (False, True):
         qm1, sm1 = prod.rmsnorm_fp8(x, w, 1e-5, mx=True, blocked=blocked)
         qm2, sm2 = prod.quantize_rows(h2, mx=True, blocked=blocked)
