@@ -786,8 +786,9 @@ rmsnorm_rows_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const vo
   }
 }
 
-// RMSNorm then FP8 in one pass over x (triton_fp8_producers.py:120-133, 191-202): one CTA of
-// 256 threads per row; the row's chunks stay in registers (MAXC per thread) from the sum of
+// RMSNorm then FP8 in one pass over x (triton_fp8_producers.py:120-133, 191-202), launched
+// for fp32 rows (2-byte rows: rmsnorm_quant_fp8_packed_kernel below): one CTA of 256 threads
+// per row; the row's chunks stay in registers (MAXC per thread) from the sum of
 // squares, taken in rmsnorm_rows_kernel's order so that r and h are bit for bit the two-pass
 // ones, to the codes. MX 0: e4m3 per token (quant.py:361-377: scale amax / 448, 1 for a zero
 // row); MX 1: MXFP8 (quant.py:479-526: the ceil rule's e8m0 per 32, four lanes per block),
