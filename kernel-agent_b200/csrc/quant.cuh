@@ -874,7 +874,7 @@ rmsnorm_quant_fp8_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, con
   }
 }
 
-// The same producer for bf16 / fp16 rows with NT threads per row (64, 128 or 256) and NC
+// The same producer for bf16 / fp16 rows with NT threads per row (a divisor of 256) and NC
 // 16-byte chunks each, kept packed (two values per register): more rows resident per SM.
 // Thread t holds chunks t + NT * c, which are exactly the chunks of rmsnorm_rows_kernel's
 // threads t + NT * u (u < 256 / NT, c = u + (256 / NT) * i), so the sum of squares is taken

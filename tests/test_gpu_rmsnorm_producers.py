@@ -82,7 +82,7 @@ def test_rmsnorm_fp8_codes_of_its_output(prod, m, k):
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_rmsnorm_fp8_one_pass_equals_two(prod, m, k, dtype):
     """The fused producer (one pass over x: norm in registers, then the codes; for 2-byte rows
-    64 to 256 threads with 1 to 8 chunks each across these widths) gives the bytes of the two
+    128 or 256 threads with 1 to 8 chunks each across these widths) gives the bytes of the two
     passes (kab_rmsnorm into h, then the row / MXFP8 quantisers): h, codes and scales, per
     token and MXFP8 (row-major and swizzled); a row holding inf (r = 0, a NaN in h) included."""
     x, w = inputs(m, k, dtype, 5 * m + k)
@@ -106,7 +106,7 @@ def test_rmsnorm_fp8_one_pass_equals_two(prod, m, k, dtype):
 @pytest.mark.parametrize("m,k", [(300, 1024), (7, 4096), (5, 20480), (3, 32768), (2, 32)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_rmsnorm_fp4_one_pass_equals_two(prod, m, k, dtype):
-    """The fused FP4 producer (kab_rmsnorm_quant_fp4: norm in registers, then the codes; 256 to
+    """The fused FP4 producer (kab_rmsnorm_quant_fp4: norm in registers, then the codes; 128 to
     512 threads and one to four blocks per thread across these widths) gives the bytes of the
     two passes (kab_rmsnorm into h, then kab_quant_fp4): h, codes, scales (row-major and
     swizzled) and outer scales, NVFP4 and MXFP4, with and without h written; a row holding
