@@ -242,7 +242,7 @@ def test_mxfp4_and_fp4_weights_golden(kq, golden):
         assert float(ts) == float(g[f"w{fmt}_ts"])
 
 
-@pytest.mark.parametrize("rows,k", [(1, 16), (33, 64), (257, 1024), (64, 8192), (3, 32768)])
+@pytest.mark.parametrize("rows,k", [(1, 16), (33, 64), (257, 1024), (64, 8192), (5, 6144), (3, 32768)])
 @pytest.mark.parametrize("fmt", ["nvfp4", "mxfp4"])
 def test_fp4_random(kq, rows, k, fmt):
     if k % kq.FP4_FORMATS[fmt][0]:
