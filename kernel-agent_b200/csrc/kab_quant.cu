@@ -80,23 +80,38 @@ void launch_fp4_fast_nb(int maxc, unsigned rows, int threads, cudaStream_t s, co
   else if (maxc == 2) quant_fp4_fast_kernel<T, 2, F, M><<<rows, threads, 0, s>>>(x, ldx, k, amax, ts, swizzle, q, scales, outer);
   else quant_fp4_fast_kernel<T, kNbMax, F, M><<<rows, threads, 0, s>>>(x, ldx, k, amax, ts, swizzle, q, scales, outer);
 }
+// The kernel's dynamic shared memory (the staged row and the fix list) passes the default 48 KB
+// for rows above ~21.8K NVFP4 elements; the attribute is a per-device setting, so it is made
+// once on every device that launches the kernel.
+template <typename Kernel>
+int allow_row_smem(Kernel kernel, bool (&configured)[64]) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(KAB_ECUDA, "cudaGetDevice failed");
+  if (dev >= 64 || configured[dev]) return KAB_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 32768 * 2 + 2048 * 4) != cudaSuccess)
+    return fail(KAB_ECUDA, "cannot raise the RMSNorm FP4 producer's shared memory to %d bytes", 32768 * 2 + 2048 * 4);
+  configured[dev] = true;
+  return KAB_OK;
+}
+template <int T, int F, int NB>
+int launch_rmsnorm_fp4_nb(unsigned rows, int threads, size_t smem, cudaStream_t s, const void* x, int64_t ldx,
+                          int64_t k, const void* w, float eps, int swizzle, uint8_t* q, uint8_t* scales, float* outer,
+                          void* h) {
+  static bool configured[64] = {};
+  auto kernel = quant_fp4_fast_kernel<T, NB, F, 0, true>;
+  if (smem > 48 * 1024)
+    if (int e = allow_row_smem(kernel, configured)) return e;
+  kernel<<<rows, threads, smem, s>>>(x, ldx, k, nullptr, nullptr, swizzle, q, scales, outer, w, eps, h);
+  return KAB_OK;
+}
 template <int T, int F>
-void launch_rmsnorm_fp4(int maxc, unsigned rows, int threads, cudaStream_t s, const void* x, int64_t ldx, int64_t k,
-                        const void* w, float eps, int swizzle, uint8_t* q, uint8_t* scales, float* outer, void* h) {
+int launch_rmsnorm_fp4(int maxc, unsigned rows, int threads, cudaStream_t s, const void* x, int64_t ldx, int64_t k,
+                       const void* w, float eps, int swizzle, uint8_t* q, uint8_t* scales, float* outer, void* h) {
   constexpr int kNbMax = F == 0 ? 4 : 2;
   const size_t smem = static_cast<size_t>(k) * 2 + static_cast<size_t>(k / (F == 0 ? 16 : 32)) * 4;  // row, fix list
-#define KAB_RF(NB)                                                                                          \
-  do {                                                                                                      \
-    static const bool attr = cudaFuncSetAttribute(quant_fp4_fast_kernel<T, NB, F, 0, true>,               \
-                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, 32768 * 2 + 2048 * 4) == cudaSuccess; \
-    (void)attr;                                                                                             \
-    quant_fp4_fast_kernel<T, NB, F, 0, true><<<rows, threads, smem, s>>>(x, ldx, k, nullptr, nullptr, swizzle, q, \
-                                                                        scales, outer, w, eps, h);         \
-  } while (0)
-  if (maxc == 1) KAB_RF(1);
-  else if (maxc == 2) KAB_RF(2);
-  else KAB_RF(kNbMax);
-#undef KAB_RF
+  if (maxc == 1) return launch_rmsnorm_fp4_nb<T, F, 1>(rows, threads, smem, s, x, ldx, k, w, eps, swizzle, q, scales, outer, h);
+  if (maxc == 2) return launch_rmsnorm_fp4_nb<T, F, 2>(rows, threads, smem, s, x, ldx, k, w, eps, swizzle, q, scales, outer, h);
+  return launch_rmsnorm_fp4_nb<T, F, kNbMax>(rows, threads, smem, s, x, ldx, k, w, eps, swizzle, q, scales, outer, h);
 }
 template <int T>
 void launch_fp4_fast(int fmt, int mode, int maxc, unsigned rows, int threads, cudaStream_t s, const void* x,
@@ -266,6 +281,7 @@ int kab_quant_fp4(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx
   KAB_REQUIRE(!(fmt == KAB_NVFP4 && mode == KAB_FP4_TENSOR && amax == nullptr), "amax is null");
   KAB_REQUIRE(!(fmt == KAB_NVFP4 && mode == KAB_FP4_WEIGHT && tensor_scale == nullptr), "tensor_scale is null");
   KAB_REQUIRE(k / 8 <= 256 * 16, "width %lld exceeds the register-resident row (32768)", (long long)k);
+  KAB_REQUIRE(rows < (int64_t(1) << 31), "too many rows (%lld)", (long long)rows);
   if (up != nullptr) {
     if (int e = check_matrix(up, dtype, rows, k, ldu, "up")) return e;
     KAB_REQUIRE(dtype != KAB_F32, "the fused SiLU * up producer takes bf16 or fp16");
@@ -325,11 +341,11 @@ int kab_rmsnorm_quant_fp4(const void* x, int dtype, int64_t rows, int64_t k, int
   const cudaStream_t s = as_stream(stream);
   const unsigned grid = static_cast<unsigned>(rows);
 #define KAB_RF4(TT)                                                                                     \
-  if (fmt == KAB_NVFP4) launch_rmsnorm_fp4<TT, 0>(maxc, grid, threads, s, x, ldx, k, weight, eps, swizzle, q, scales, outer, h); \
-  else launch_rmsnorm_fp4<TT, 1>(maxc, grid, threads, s, x, ldx, k, weight, eps, swizzle, q, scales, outer, h)
-  if (dtype == KAB_BF16) { KAB_RF4(kBF16); }
-  else { KAB_RF4(kF16); }
+  (fmt == KAB_NVFP4 ? launch_rmsnorm_fp4<TT, 0>(maxc, grid, threads, s, x, ldx, k, weight, eps, swizzle, q, scales, outer, h) \
+                    : launch_rmsnorm_fp4<TT, 1>(maxc, grid, threads, s, x, ldx, k, weight, eps, swizzle, q, scales, outer, h))
+  const int e = dtype == KAB_BF16 ? KAB_RF4(kBF16) : KAB_RF4(kF16);
 #undef KAB_RF4
+  if (e) return e;
   return check_launch("kab_rmsnorm_quant_fp4");
 }
 

@@ -99,4 +99,6 @@ def main(src: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} <path to the reference's src directory>")
+    main(sys.argv[1])
