@@ -362,6 +362,12 @@ int kab_fp4_scale_check(const void* x, int dtype, int64_t rows, int64_t k, int64
                         const float* scale, const float* outer, int outer_per_row,
                         KabScaleCheck* result, void* stream);
 
+/* src/kernel_agent/kernels/scale_guard.py:103-118 outliers(): one pass over activations
+ * x [rows, k] with non-finite values as 0: row_sumsq [rows] (float64 sums of x^2), row_amax
+ * [rows] and col_amax [k] (largest |x| per row and per column). The outputs are reset here. */
+int kab_outlier_stats(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, double* row_sumsq,
+                      float* row_amax, float* col_amax, void* stream);
+
 /* Per-row sums of a pair of [rows, k] matrices x, y (x and y each fp32 / bf16 / fp16, rows
  * ldx / ldy elements apart), the reductions of the error reports (quant.py:133-181, 302-326,
  * 420-476, 707-768, 926-1000, 1511-1573; kv_quant.py:86-101): out[row * 8 + i] for
@@ -369,6 +375,42 @@ int kab_fp4_scale_check(const void* x, int dtype, int64_t rows, int64_t k, int64
  * count(x != 0 and y == 0), max |y|; float64, NaN propagating. */
 int kab_row_pair_stats(const void* x, int x_dtype, int64_t ldx, const void* y, int y_dtype, int64_t ldy,
                        int64_t rows, int64_t k, double* out, void* stream);
+
+/* ------------------------------------------------------------------ comparator routing */
+
+#define KAB_DIFF_MAXDIM 8
+
+/* The difference census of the comparator's routing (src/kernel_agent/kernels/compare.py:
+ * 806-1182: compare_grown, written_box, compare_written, compare_side_effects_flat). The
+ * compared region is [outer, len, inner] elements: element (o, i, n) of `a` (and of `b`,
+ * laid out like `a`) is a[(o * a_dim + a_off + i) * inner + n], of `base`
+ * base[(o * base_dim + base_off + i) * inner + n] (contiguous tensors sliced along one
+ * dimension; dtype KAB_F32 / KAB_BF16 / KAB_F16, 3 for float64, or 4 / 5 / 6 / 7 for integer
+ * or boolean elements of 1 / 2 / 4 / 8 bytes, compared by their bits). An element differs when
+ * a's (or, with `b` non-null, a's or b's) value differs
+ * from base's: `nan_equal` 1 takes NaN as equal to NaN (x == y or both NaN), 0 is IEEE `!=`.
+ * Optional outputs: `mask` (one byte per region element, row-major: 1 where it differs) and
+ * `hits` (per dimension k of the region's shape, shape[k] bytes laid end to end, set to 1 at
+ * each index where an element differs; the caller zeroes them). `box` (the same layout as
+ * `hits`): elements whose every index is flagged are not counted. */
+typedef struct KabDiffParams {
+  const void* a;
+  const void* b;
+  const void* base;
+  int dtype;
+  int nan_equal;
+  int64_t outer, len, inner;
+  int64_t a_dim, a_off, base_dim, base_off;
+  int ndim;
+  int64_t shape[KAB_DIFF_MAXDIM];
+  unsigned char* hits;
+  const unsigned char* box;
+  unsigned char* mask;
+} KabDiffParams;
+
+/* Runs the census; `count` (device, one 64-bit word) receives the number of differing
+ * elements (reset here). */
+int kab_diff_census(const KabDiffParams* params, unsigned long long* count, void* stream);
 
 /* ------------------------------------------------------------------ FP8 attention prefill */
 

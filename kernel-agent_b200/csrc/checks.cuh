@@ -221,3 +221,82 @@ row_pair_stats_kernel(const TX* __restrict__ x, int64_t ldx, const TY* __restric
 }
 
 }  // namespace kab
+
+namespace kab {
+
+// Outlier statistics of activations x [rows, k] (the scale guard's report,
+// src/kernel_agent/kernels/scale_guard.py:103-118), one pass over x with non-finite values
+// taken as 0: per row the sum of squares (float64) and the largest |x|; per column the
+// largest |x|. A CTA covers kOutlierRows rows x 2048 columns (256 threads x 8 columns): each
+// thread keeps the maxima of its 8 columns over the rows and adds them with one atomic max
+// per column; the row partials are reduced over the CTA (warp shuffles, then shared memory)
+// and added with one atomic per row. Maxima are non-negative floats, so their bit patterns
+// order like the values and an unsigned atomic max is the float max. The outputs start at 0.
+constexpr int kOutlierRows = 32;
+
+template <int T>
+__global__ void __launch_bounds__(256)
+outlier_stats_kernel(const void* __restrict__ x, int64_t ldx, int64_t rows, int64_t k,
+                     double* __restrict__ row_sumsq, unsigned* __restrict__ row_amax,
+                     unsigned* __restrict__ col_amax) {
+  __shared__ double s_sum[8][kOutlierRows];
+  __shared__ unsigned s_max[8][kOutlierRows];
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * kOutlierRows;
+  const int64_t c0 = (static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x) * 8;
+  const int nr = static_cast<int>(rows - r0 < kOutlierRows ? rows - r0 : kOutlierRows);
+  const bool live = c0 < k;
+  float sum[kOutlierRows];
+  unsigned rmax[kOutlierRows];
+  unsigned cmax[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int r = 0; r < kOutlierRows; ++r) {
+    sum[r] = 0.0f;
+    rmax[r] = 0u;
+    if (r < nr && live) {
+      float v[8];
+      load8<T>(x, (r0 + r) * ldx + c0, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float a = isfinite(v[j]) ? fabsf(v[j]) : 0.0f;
+        sum[r] = fmaf(a, a, sum[r]);
+        const unsigned b = __float_as_uint(a);
+        rmax[r] = max(rmax[r], b);
+        cmax[j] = max(cmax[j], b);
+      }
+    }
+  }
+  if (live) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (c0 + j < k && cmax[j] != 0u) atomicMax(col_amax + c0 + j, cmax[j]);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int r = 0; r < kOutlierRows; ++r) {
+    double s = sum[r];
+    unsigned m = rmax[r];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      s += __shfl_xor_sync(0xffffffffu, s, o);
+      m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    }
+    if (lane == 0) {
+      s_sum[warp][r] = s;
+      s_max[warp][r] = m;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < nr) {
+    double s = 0.0;
+    unsigned m = 0u;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      s += s_sum[w][threadIdx.x];
+      m = max(m, s_max[w][threadIdx.x]);
+    }
+    atomicAdd(row_sumsq + r0 + threadIdx.x, s);
+    if (m != 0u) atomicMax(row_amax + r0 + threadIdx.x, m);
+  }
+}
+
+}  // namespace kab

@@ -293,3 +293,81 @@ __global__ void channel_rms_kernel(const double* __restrict__ partial, int64_t c
 }
 
 }  // namespace kab
+
+namespace kab {
+
+// The difference census of the comparator's routing (src/kernel_agent/kernels/compare.py:
+// 806-1182: grown caches, rows written into an input, in-place updates): which elements of a
+// candidate tensor `a` (and, in union mode, of a second tensor `b` of the same layout) differ
+// from a base tensor, over a region that may be a slice of each along one dimension. One
+// pass; per differing element it sets its flag in `mask` and, per dimension, the flag of its
+// index in `hits`; elements inside a given box (all of their indices flagged in `box`) are
+// skipped. The count goes to `count` with one atomic per warp.
+constexpr int kDiffF64 = 3;  // the census also reads float64 tensors
+// ... and compares integer / boolean tensors by their bits (elements of 1, 2, 4 or 8 bytes)
+constexpr int kDiffBits8 = 4, kDiffBits16 = 5, kDiffBits32 = 6, kDiffBits64 = 7;
+
+template <int T>
+__device__ __forceinline__ bool differs_at(const void* x, int64_t ix, const void* y, int64_t iy, bool nan_equal) {
+  if constexpr (T == kDiffBits8) {
+    return __ldg(reinterpret_cast<const uint8_t*>(x) + ix) != __ldg(reinterpret_cast<const uint8_t*>(y) + iy);
+  } else if constexpr (T == kDiffBits16) {
+    return __ldg(reinterpret_cast<const uint16_t*>(x) + ix) != __ldg(reinterpret_cast<const uint16_t*>(y) + iy);
+  } else if constexpr (T == kDiffBits32) {
+    return __ldg(reinterpret_cast<const uint32_t*>(x) + ix) != __ldg(reinterpret_cast<const uint32_t*>(y) + iy);
+  } else if constexpr (T == kDiffBits64) {
+    return __ldg(reinterpret_cast<const unsigned long long*>(x) + ix) !=
+           __ldg(reinterpret_cast<const unsigned long long*>(y) + iy);
+  } else if constexpr (T == kDiffF64) {
+    const double a = __ldg(reinterpret_cast<const double*>(x) + ix), b = __ldg(reinterpret_cast<const double*>(y) + iy);
+    return nan_equal ? !(a == b || (a != a && b != b)) : a != b;
+  } else {
+    const float a = load_elem<T>(x, ix), b = load_elem<T>(y, iy);  // exact for 2-byte types
+    return nan_equal ? !(a == b || (a != a && b != b)) : a != b;
+  }
+}
+
+template <int T>
+__global__ void __launch_bounds__(256) diff_census_kernel(KabDiffParams P, unsigned long long* count) {
+  const int64_t total = P.outer * P.len * P.inner;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  unsigned found = 0;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < total; r += stride) {
+    const int64_t n = r % P.inner;
+    const int64_t oi = r / P.inner;
+    const int64_t i = oi % P.len, o = oi / P.len;
+    const int64_t ia = (o * P.a_dim + P.a_off + i) * P.inner + n;
+    const int64_t ib = (o * P.base_dim + P.base_off + i) * P.inner + n;
+    bool d = differs_at<T>(P.a, ia, P.base, ib, P.nan_equal != 0);
+    if (!d && P.b != nullptr) d = differs_at<T>(P.b, ia, P.base, ib, P.nan_equal != 0);
+    if (d && (P.box != nullptr || P.hits != nullptr)) {
+      // the element's index along each dimension of the region (row-major)
+      int64_t rest = r, off = 0;
+      int64_t idx[KAB_DIFF_MAXDIM];
+      for (int k = P.ndim - 1; k >= 0; --k) {
+        idx[k] = rest % P.shape[k];
+        rest /= P.shape[k];
+      }
+      bool inside = P.box != nullptr;
+      for (int k = 0; k < P.ndim; ++k) {
+        if (P.box != nullptr && !P.box[off + idx[k]]) inside = false;
+        off += P.shape[k];
+      }
+      if (inside) d = false;
+      if (d && P.hits != nullptr) {
+        off = 0;
+        for (int k = 0; k < P.ndim; ++k) {
+          P.hits[off + idx[k]] = 1;  // every writer stores the same byte
+          off += P.shape[k];
+        }
+      }
+    }
+    if (P.mask != nullptr) P.mask[r] = d ? 1 : 0;
+    found += d ? 1u : 0u;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) found += __shfl_xor_sync(0xffffffffu, found, o);
+  if ((threadIdx.x & 31) == 0 && found) atomicAdd(count, static_cast<unsigned long long>(found));
+}
+
+}  // namespace kab

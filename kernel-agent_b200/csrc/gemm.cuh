@@ -317,6 +317,80 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, const CUtensorM
   }
 }
 
+// The per-tile scale operands of one epilogue warp's share (rows row0 + lane, HC chunks of 32
+// columns from colh): the row scale and, lane i of chunk c, the column scale and bias of
+// column colh + 32 c + i. Loaded before the accumulator is ready.
+template <int KIND, int OUT, int HC>
+struct EpilogueOperands {
+  float sa;
+  float cs[HC], cb[HC];
+  __device__ __forceinline__ void load(const GemmArgs& g, int row0, int colh, int lane) {
+    const int64_t row = static_cast<int64_t>(row0) + lane;
+    sa = 0.0f;
+    if constexpr (KIND == 4) sa = g.a_scale == nullptr ? 1.0f : (row < g.m ? __ldg(g.a_scale + row) : 0.0f);
+    else if constexpr (KIND != 2 && OUT != kOutI32) sa = row < g.m ? __ldg(g.a_scale + row) : 0.0f;
+#pragma unroll
+    for (int c = 0; c < HC; ++c) {
+      const int64_t col = static_cast<int64_t>(colh) + c * 32 + lane;
+      cs[c] = 0.0f;
+      cb[c] = 0.0f;
+      if constexpr (OUT != kOutI32) {
+        if constexpr (KIND == 0 || KIND == 1) cs[c] = col < g.n ? __ldg(g.b_scale + col) : 0.0f;
+        if constexpr (KIND == 3 || KIND == 4) {
+          if (KIND == 4 && g.b_scale == nullptr) cs[c] = 1.0f;
+          else cs[c] = g.b_scale_per_col ? (col < g.n ? __ldg(g.b_scale + col) : 0.0f) : __ldg(g.b_scale);
+        }
+        if (g.bias != nullptr && col < g.n) cb[c] = load_bias(g.bias, g.bias_dtype, col);
+      }
+    }
+  }
+};
+
+// epilogue_tile for an accumulator that only one buffer holds: every column of the warp's
+// share is read from TMEM first (HC x 32 registers) and the accumulator is released before
+// any of the epilogue arithmetic, so the next tile's MMAs wait only for the TMEM reads.
+template <int KIND, int OUT, int HC, class Release>
+__device__ __forceinline__ void epilogue_tile_early(const GemmArgs& g, const EpilogueOperands<KIND, OUT, HC>& ops,
+                                                    const CUtensorMap* tma_out, const PeerMaps* peers, uint32_t tbase,
+                                                    int row0, int colh, uint8_t* stage0, int& chunk, int lane,
+                                                    Release release) {
+  constexpr int kStageOutBytes = 32 * 32 * out_bytes(OUT);
+  uint32_t r[HC][32];
+#pragma unroll
+  for (int c = 0; c < HC; ++c) tc::tmem_ld32(tbase + c * 32, r[c]);
+  tc::tmem_ld_wait();
+  tc::fence_before_sync();
+  __syncwarp();
+  if (lane == 0) release();
+#pragma unroll
+  for (int c = 0; c < HC; ++c) {
+    uint32_t y[32];
+    epilogue_math<KIND, OUT>(g, r[c], ops.sa, ops.cs[c], ops.cb[c], y);
+    uint8_t* buf = stage0 + (chunk & 1) * kStageOutBytes;
+    if (chunk >= 2) {  // the store two chunks ago has finished reading this buffer
+      if (lane == 0) tc::bulk_wait_read<1>();
+      __syncwarp();
+    }
+    uint32_t w[32];
+    pack_row<OUT>(y, w);
+    stage_packed<OUT>(buf, lane, w);
+    tc::fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+      tc::tma_store_2d(tma_out, buf, colh + c * 32, row0);
+      if (peers != nullptr) {
+#pragma unroll
+        for (int p = 0; p < kMaxPeers; ++p) {
+          if (p >= g.npeers) break;
+          tc::tma_store_2d(&peers->m[p], buf, colh + c * 32, row0);
+        }
+      }
+      tc::bulk_commit();
+    }
+    ++chunk;
+  }
+}
+
 template <int KIND, int BN, int BKB, int OUT>
 __global__ void __launch_bounds__(GemmLayout<KIND, BN, BKB, OUT>::kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,

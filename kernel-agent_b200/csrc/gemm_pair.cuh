@@ -59,7 +59,7 @@ struct PairLayout {
   static constexpr int kAccBufs = kScaled ? 1 : 2;
   static constexpr int kSfCol = kAccBufs * kBN;
   static constexpr int kSfSlotsFit = kScaled ? (512 - kSfCol) / kSfColsPerStage : 0;
-  static constexpr int kSfSlots = kSfSlotsFit > 4 ? 4 : kSfSlotsFit;
+  static constexpr int kSfSlots = kSfSlotsFit > 5 ? 5 : kSfSlotsFit;
   static constexpr int kStageOutBytes = 32 * 32 * out_bytes(OUT);
   static constexpr int kStagingBytes = kEpiWarps * 2 * kStageOutBytes;
   static_assert(kStagingBytes % 1024 == 0, "the operand tiles after the staging tiles need 1024-byte alignment");
@@ -67,10 +67,10 @@ struct PairLayout {
   static constexpr int kFixed = 1024 + kStagingBytes + 256;
   static constexpr int kStagesFit = (kSmemLimit - kFixed) / kStageBytes;
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
-  static constexpr int kBarriers = 2 * kStages + 2 * kAccBufs + 1;
+  static constexpr int kBarriers = 2 * kStages + 2 * kAccBufs + 1 + kSfSlots;
   static constexpr int kSmem = 1024 + kStagingBytes + kStages * kStageBytes + kBarriers * 8 + 16;
   static_assert(kStages >= 2, "shared memory does not fit two stages");
-  static_assert(!kScaled || kSfSlots >= 1, "TMEM does not fit a scale-factor slot");
+  static_assert(!kScaled || kSfSlots >= 2, "TMEM does not fit two scale-factor slots");
   static_assert(kSfCol + kSfSlots * kSfColsPerStage <= 512, "TMEM overflow");
   static_assert(kSmem <= kSmemLimit, "shared memory overflow");
 };
@@ -81,7 +81,7 @@ template <int KIND, int OUT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<KIND, OUT>::kThreads, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                  const __grid_constant__ CUtensorMap tma_sfa, const __grid_constant__ CUtensorMap tma_sfb,
-                 const __grid_constant__ CUtensorMap tma_out, GemmArgs g) {
+                 const __grid_constant__ CUtensorMap tma_out, GemmArgs g, const __grid_constant__ PeerMaps peers) {
   using L = PairLayout<KIND, OUT>;
   constexpr int STAGES = L::kStages;
   constexpr int KS = L::kKSteps;
@@ -101,7 +101,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + AB;
   uint64_t* drain = acc_empty + AB;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* sf_empty = drain + 1;  // leader: the MMAs that read scale-factor slot i completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_empty + L::kSfSlots);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = tc::cluster_ctarank();  // 0: the leader
@@ -116,6 +117,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
       tc::mbar_init(&acc_empty[b], 2 * L::kEpiWarps);
     }
     tc::mbar_init(drain, 1);
+    for (int i = 0; i < L::kSfSlots; ++i) tc::mbar_init(&sf_empty[i], 1);
     tc::fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -174,25 +176,39 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
       if (!ok) atomicOr(&g_gemm_status, kDevTimeout);
     }
   } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {  // ----------------------------------------- MMA issuer (leader)
-      const uint32_t empty_peer = tc::mapa(empty, 1), acc_full_peer = tc::mapa(acc_full, 1);
+    if (rank == 0) {  // ---------------------------------------------------- MMA issuer (leader)
+      // The whole warp walks the loop and waits; one elected lane issues the tcgen05
+      // instructions, and the warp reconverges after each group. Issued from a lone lane
+      // whose warp-mates wait elsewhere (at the final barrier), each tcgen05.cp took ~47
+      // cycles to issue and the twelve copies of a stage did not overlap the MMAs (B200,
+      // 256 x 256 x 64 NVFP4 pair MMAs: 819 vs 512 cycles per stage with the warp converged).
+      const bool leader = tc::elect_one();
       const uint32_t empty_own = tc::smem_u32(empty), acc_full_own = tc::smem_u32(acc_full);
-      int s = 0, ab = 0, slot = 0;
-      uint32_t ph = 0, aph = 0;
+      // The block scales of a stage go into a TMEM slot one k-step ahead of the MMAs that read
+      // them (the copies of step i + 1 are issued before the MMAs of step i); a slot is
+      // rewritten only after the MMAs that read it have completed (sf_empty).
+      const int my_tiles = pair0 < total ? (total - pair0 + npairs - 1) / npairs : 0;
+      const int64_t steps = static_cast<int64_t>(my_tiles) * g.k_stages;
+      int s = 0, ab = 0, slot = 0;        // the MMAs' stage, accumulator and scale slot
+      int cs = 0, cslot = 0;              // the next copies' stage and slot
+      uint32_t aph = 0, cph = 0, csph = 0;
       bool ok = true;
-      for (int t = pair0; ok && t < total; t += npairs) {
-        if (!tc::mbar_wait_cluster(&acc_empty[ab], aph ^ 1u)) { ok = false; break; }
-        tc::fence_after_sync();
-        const uint32_t d = tmem + ab * BN;
-        for (int kb = 0; kb < g.k_stages; ++kb) {
-          if (!tc::mbar_wait_cluster(&full[s], ph)) { ok = false; break; }
-          tc::fence_after_sync();
-          const uint64_t adesc = tc::desc_sw128(tc::smem_u32(sA + s * L::kABytes));
-          const uint64_t bdesc = tc::desc_sw128(tc::smem_u32(sB + s * L::kBBytes));
-          const uint32_t sf = tmem + L::kSfCol + slot * L::kSfColsPerStage;
-          if constexpr (L::kScaled) {  // set j: A's chunk j -> 4 columns, B's two chunks j -> 8
-            const uint32_t fa = tc::smem_u32(sSFA + s * L::kSfaBytes);
-            const uint32_t fb = tc::smem_u32(sSFB + s * L::kSfbBytes);
+      // every lane waits (the verdict is the warp's), the elected lane issues
+      auto wait_all = [&](uint64_t* bar, uint32_t parity, bool cluster) -> bool {
+        const bool done = cluster ? tc::mbar_wait_cluster(bar, parity) : tc::mbar_wait(bar, parity);
+        return __all_sync(0xffffffffu, done);
+      };
+      // waits for stage cs to land and slot cslot to be free, then copies the stage's scales
+      auto copy_next = [&]() -> bool {
+        if (!wait_all(&full[cs], cph, true)) return false;
+        if constexpr (L::kScaled) {
+          if (!wait_all(&sf_empty[cslot], csph ^ 1u, false)) return false;
+        }
+        if constexpr (L::kScaled) {  // set j: A's chunk j -> 4 columns, B's two chunks j -> 8
+          if (leader) {
+            const uint32_t sf = tmem + L::kSfCol + cslot * L::kSfColsPerStage;
+            const uint32_t fa = tc::smem_u32(sSFA + cs * L::kSfaBytes);
+            const uint32_t fb = tc::smem_u32(sSFB + cs * L::kSfbBytes);
 #pragma unroll
             for (int j = 0; j < L::kSfSets; ++j) {
               tc::cp_sf_pair(sf + 4 * j, tc::desc_sf(fa + j * 512));
@@ -201,39 +217,63 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
                 tc::cp_sf_pair(sf + L::kSfaCols + L::kGroups * j + 4 * c, tc::desc_sf(fb + c * L::kSfChunkBytes + j * 512));
             }
           }
+          __syncwarp();
+          if (++cslot == L::kSfSlots) { cslot = 0; csph ^= 1u; }
+        }
+        if (++cs == STAGES) { cs = 0; cph ^= 1u; }
+        return true;
+      };
+      int64_t step = 0;
+      if (steps > 0 && !copy_next()) ok = false;
+      for (int t = pair0; ok && t < total; t += npairs) {
+        if (!wait_all(&acc_empty[ab], aph ^ 1u, true)) { ok = false; break; }
+        tc::fence_after_sync();
+        const uint32_t d = tmem + ab * BN;
+        for (int kb = 0; kb < g.k_stages; ++kb, ++step) {
+          // stage s has landed (copy_next waited for it one step ago)
+          if (step + 1 < steps && !copy_next()) { ok = false; break; }
+          if (leader) {
+            const uint64_t adesc = tc::desc_sw128(tc::smem_u32(sA + s * L::kABytes));
+            const uint64_t bdesc = tc::desc_sw128(tc::smem_u32(sB + s * L::kBBytes));
+            const uint32_t sf = tmem + L::kSfCol + slot * L::kSfColsPerStage;
 #pragma unroll
-          for (int j = 0; j < KS; ++j) {
-            const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
-            const uint64_t a = adesc + static_cast<uint64_t>(2 * j);  // +32 bytes of K
-            const uint64_t b = bdesc + static_cast<uint64_t>(2 * j);
-            if constexpr (KIND == 0) {
-              tc::mma_i8_pair(d, a, b, tc::idesc_i8(256, BN), acc);
-            } else if constexpr (KIND == 1) {
-              tc::mma_f8_pair(d, a, b, tc::idesc_f8(256, BN), acc);
-            } else if constexpr (KIND == 2) {
-              tc::mma_mxf8_pair(d, a, b, tc::idesc_mxf8(256, BN, j), sf, sf + L::kSfaCols, acc);
-            } else if constexpr (KIND == 3) {
-              tc::mma_nvf4_pair(d, a, b, tc::idesc_nvf4(256, BN), sf + 4 * j, sf + L::kSfaCols + L::kGroups * j, acc);
-            } else {
-              tc::mma_mxf4_pair(d, a, b, tc::idesc_mxf4(256, BN, 2 * (j & 1)), sf + 4 * (j >> 1),
-                                sf + L::kSfaCols + L::kGroups * (j >> 1), acc);
+            for (int j = 0; j < KS; ++j) {
+              const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
+              const uint64_t a = adesc + static_cast<uint64_t>(2 * j);  // +32 bytes of K
+              const uint64_t b = bdesc + static_cast<uint64_t>(2 * j);
+              if constexpr (KIND == 0) {
+                tc::mma_i8_pair(d, a, b, tc::idesc_i8(256, BN), acc);
+              } else if constexpr (KIND == 1) {
+                tc::mma_f8_pair(d, a, b, tc::idesc_f8(256, BN), acc);
+              } else if constexpr (KIND == 2) {
+                tc::mma_mxf8_pair(d, a, b, tc::idesc_mxf8(256, BN, j), sf, sf + L::kSfaCols, acc);
+              } else if constexpr (KIND == 3) {
+                tc::mma_nvf4_pair(d, a, b, tc::idesc_nvf4(256, BN), sf + 4 * j, sf + L::kSfaCols + L::kGroups * j, acc);
+              } else {
+                tc::mma_mxf4_pair(d, a, b, tc::idesc_mxf4(256, BN, 2 * (j & 1)), sf + 4 * (j >> 1),
+                                  sf + L::kSfaCols + L::kGroups * (j >> 1), acc);
+              }
             }
+            tc::commit_pair_both(empty_own + 8 * s);  // stage s is free in both CTAs
+            if constexpr (L::kScaled) tc::commit_pair(tc::smem_u32(&sf_empty[slot]));
           }
-          tc::commit_pair(empty_own + 8 * s);
-          tc::commit_pair(empty_peer + 8 * s);
-          if (++s == STAGES) { s = 0; ph ^= 1u; }
+          __syncwarp();
+          if (++s == STAGES) s = 0;
           if constexpr (L::kScaled) {
             if (++slot == L::kSfSlots) slot = 0;
           }
         }
         if (!ok) break;
-        tc::commit_pair(acc_full_own + 8 * ab);
-        tc::commit_pair(acc_full_peer + 8 * ab);
+        if (leader) {
+          tc::commit_pair_both(acc_full_own + 8 * ab);
+        }
+        __syncwarp();
         if (++ab == AB) { ab = 0; aph ^= 1u; }
       }
-      tc::commit_pair(tc::smem_u32(drain));  // every MMA this thread issued has completed once this arrives
-      if (!tc::mbar_wait(drain, 0)) ok = false;
-      if (!ok) atomicOr(&g_gemm_status, kDevTimeout);
+      if (leader) tc::commit_pair(tc::smem_u32(drain));  // every MMA issued has completed once this arrives
+      __syncwarp();
+      if (!wait_all(drain, 0, false)) ok = false;
+      if (!ok && leader) atomicOr(&g_gemm_status, kDevTimeout);
     }
   } else {  // ------------------------------------------------------------- epilogue warps
     constexpr int HC = BN / 64;  // 32-column chunks per warp per tile
@@ -248,17 +288,20 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     for (int t = pair0; t < total; t += npairs) {
       int mt, nt;
       tile_coords(t, g.m_tiles, g.n_tiles, g.group_n, mt, nt);
+      const int row0 = mt * 256 + static_cast<int>(rank) * 128 + 32 * quarter;
+      const int colh = nt * BN + half * (BN / 2);
+      EpilogueOperands<KIND, OUT, HC> ops;
+      ops.load(g, row0, colh, lane);  // before the accumulator is ready
       if (!tc::mbar_wait_cluster(&acc_full[ab], aph)) {
         if (lane == 0) atomicOr(&g_gemm_status, kDevTimeout);
         break;
       }
       tc::fence_after_sync();
-      const int row0 = mt * 256 + static_cast<int>(rank) * 128 + 32 * quarter;
-      const int colh = nt * BN + half * (BN / 2);
       const uint32_t tbase = tmem + lane_base + ab * BN + half * (BN / 2);
       const uint32_t release_bar = acc_empty_leader + 8 * ab;
-      epilogue_tile<KIND, OUT, HC>(g, &tma_out, nullptr, tbase, row0, colh, stage0, chunk, lane,
-                                   [release_bar] { tc::mbar_arrive_cluster(release_bar); });
+      epilogue_tile_early<KIND, OUT, HC>(g, ops, &tma_out, g.npeers > 0 ? &peers : nullptr, tbase, row0, colh, stage0,
+                                         chunk, lane,
+                                         [release_bar] { tc::mbar_arrive_cluster(release_bar); });
       if (++ab == AB) { ab = 0; aph ^= 1u; }
     }
     if (lane == 0) tc::bulk_wait_all();

@@ -136,4 +136,41 @@ int kab_channel_rms(const void* x, const void* alt, int dtype, int64_t rows,
   return check_launch("kab_channel_rms finalize");
 }
 
+int kab_diff_census(const KabDiffParams* params, unsigned long long* count, void* stream) {
+  KAB_REQUIRE(params != nullptr && count != nullptr, "null pointer");
+  const KabDiffParams& P = *params;
+  KAB_REQUIRE(valid_dtype(P.dtype) || (P.dtype >= kDiffF64 && P.dtype <= kDiffBits64), "unknown dtype %d", P.dtype);
+  KAB_REQUIRE(P.outer >= 0 && P.len >= 0 && P.inner >= 0, "negative region");
+  KAB_REQUIRE(P.a_off >= 0 && P.base_off >= 0 && P.a_off + P.len <= P.a_dim && P.base_off + P.len <= P.base_dim,
+              "the slice [%lld, %lld) / [%lld, %lld) leaves the dimension (%lld / %lld)", (long long)P.a_off,
+              (long long)(P.a_off + P.len), (long long)P.base_off, (long long)(P.base_off + P.len),
+              (long long)P.a_dim, (long long)P.base_dim);
+  const int64_t total = P.outer * P.len * P.inner;
+  KAB_REQUIRE(total == 0 || (P.a != nullptr && P.base != nullptr), "null tensor");
+  if (P.hits != nullptr || P.box != nullptr) {
+    KAB_REQUIRE(P.ndim >= 1 && P.ndim <= KAB_DIFF_MAXDIM, "ndim %d not in 1..%d", P.ndim, KAB_DIFF_MAXDIM);
+    int64_t n = 1;
+    for (int k = 0; k < P.ndim; ++k) {
+      KAB_REQUIRE(P.shape[k] > 0, "empty dimension %d", k);
+      n *= P.shape[k];
+    }
+    KAB_REQUIRE(n == total, "the region's shape holds %lld elements, not %lld", (long long)n, (long long)total);
+  }
+  const cudaStream_t s = as_stream(stream);
+  if (cudaMemsetAsync(count, 0, sizeof(unsigned long long), s) != cudaSuccess) return check_launch("census reset");
+  if (total == 0) return KAB_OK;
+  const int64_t blocks = (total + 255) / 256;
+  const int cap = sm_count() * 8;
+  const int grid = static_cast<int>(blocks < cap ? blocks : cap);
+  if (P.dtype == KAB_BF16) diff_census_kernel<kBF16><<<grid, 256, 0, s>>>(P, count);
+  else if (P.dtype == KAB_F16) diff_census_kernel<kF16><<<grid, 256, 0, s>>>(P, count);
+  else if (P.dtype == kDiffF64) diff_census_kernel<kDiffF64><<<grid, 256, 0, s>>>(P, count);
+  else if (P.dtype == kDiffBits8) diff_census_kernel<kDiffBits8><<<grid, 256, 0, s>>>(P, count);
+  else if (P.dtype == kDiffBits16) diff_census_kernel<kDiffBits16><<<grid, 256, 0, s>>>(P, count);
+  else if (P.dtype == kDiffBits32) diff_census_kernel<kDiffBits32><<<grid, 256, 0, s>>>(P, count);
+  else if (P.dtype == kDiffBits64) diff_census_kernel<kDiffBits64><<<grid, 256, 0, s>>>(P, count);
+  else diff_census_kernel<kF32><<<grid, 256, 0, s>>>(P, count);
+  return check_launch("kab_diff_census");
+}
+
 }  // extern "C"

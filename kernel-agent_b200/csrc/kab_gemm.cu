@@ -131,7 +131,7 @@ int make_sf_map(CUtensorMap* map, const void* ptr, uint64_t bytes, uint32_t box_
 // resident at once (persistent), at most one per tile.
 template <int KIND, int OUT>
 int launch_pair_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& msa, const CUtensorMap& msb,
-                    const CUtensorMap& mo, const GemmArgs& g, cudaStream_t s) {
+                    const CUtensorMap& mo, const GemmArgs& g, const PeerMaps& pm, cudaStream_t s) {
   using L = PairLayout<KIND, OUT>;
   auto kernel = gemm_pair_kernel<KIND, OUT>;
   static int pairs_of[64] = {};
@@ -155,19 +155,19 @@ int launch_pair_one(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensor
   }
   const int tiles = g.m_tiles * g.n_tiles;
   const int grid = 2 * (tiles < pairs ? tiles : pairs);
-  kernel<<<grid, L::kThreads, L::kSmem, s>>>(ma, mb, msa, msb, mo, g);
+  kernel<<<grid, L::kThreads, L::kSmem, s>>>(ma, mb, msa, msb, mo, g, pm);
   return check_launch("gemm pair kernel");
 }
 
 template <int KIND>
 int launch_pair(int out, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& msa, const CUtensorMap& msb,
-                const CUtensorMap& mo, const GemmArgs& g, cudaStream_t s) {
+                const CUtensorMap& mo, const GemmArgs& g, const PeerMaps& pm, cudaStream_t s) {
   if constexpr (KIND == 0) {
-    if (out == kOutI32) return launch_pair_one<KIND, kOutI32>(ma, mb, msa, msb, mo, g, s);
+    if (out == kOutI32) return launch_pair_one<KIND, kOutI32>(ma, mb, msa, msb, mo, g, pm, s);
   }
-  if (out == KAB_BF16) return launch_pair_one<KIND, KAB_BF16>(ma, mb, msa, msb, mo, g, s);
-  if (out == KAB_F16) return launch_pair_one<KIND, KAB_F16>(ma, mb, msa, msb, mo, g, s);
-  return launch_pair_one<KIND, KAB_F32>(ma, mb, msa, msb, mo, g, s);
+  if (out == KAB_BF16) return launch_pair_one<KIND, KAB_BF16>(ma, mb, msa, msb, mo, g, pm, s);
+  if (out == KAB_F16) return launch_pair_one<KIND, KAB_F16>(ma, mb, msa, msb, mo, g, pm, s);
+  return launch_pair_one<KIND, KAB_F32>(ma, mb, msa, msb, mo, g, pm, s);
 }
 
 // The skinny kernel (gemm_skinny.cuh) for M <= 32: one CTA per 128-channel panel of W.
@@ -204,16 +204,31 @@ int launch_skinny_nt(int out, const CUtensorMap& mw, const CUtensorMap& mx, cons
   return launch_skinny_stages<KIND, NT, KAB_F32>(mw, mx, g, s);
 }
 
-// KAB_GEMM_PAIR=1 routes shapes with M > 128 and N >= 256 to the CTA-pair kernel. Off by
-// default: on B200 it measured 2.96 PFLOP/s on NVFP4 8192^3 against 3.66 for the one-CTA
-// kernel (its tcgen05.cp scale copies share the tensor pipe with the MMAs, ~44 cycles each,
-// 12 per stage, and without them the pair is still feed-limited at ~3.35).
-bool pair_enabled() {
-  static const bool on = [] {
+// Tile kernel choice. The CTA-pair kernel (256 x 256 tiles on two SMs) moves half the bytes
+// per FLOP through L2 and shared memory that the one-CTA kernel's 128 x 192 / 256 tiles do:
+// on B200 at 8192^3 it ran NVFP4 at 4.53 vs 3.82 PFLOP/s, MXFP4 4.89 vs 4.09, MXFP8 2.50 vs
+// 2.01, INT8 3.19 vs 2.85 POPS and FP8 2.87 vs 2.62, and the config-4 NVFP4 linear (8192 x
+// 28672 x 8192) at 4.73 vs 3.85. With fewer than two pair tiles per SM pair the one-CTA
+// kernel's smaller tiles fill the GPU better (2048 x 3072 x 1024: FP8 0.55 vs 0.49). So the
+// pair kernel takes shapes with M > 128, N >= 256 (padding N to 256 costing at most 1/16)
+// and at least two waves of pair tiles. KAB_GEMM_PAIR=0 / 1 (read once per process) forces
+// the one-CTA kernel / the pair kernel wherever its shape conditions hold.
+int pair_mode() {
+  static const int mode = [] {
     const char* v = std::getenv("KAB_GEMM_PAIR");
-    return v != nullptr && v[0] == '1';
+    if (v == nullptr || v[0] == 0) return -1;
+    return v[0] == '1' ? 1 : 0;
   }();
-  return on;
+  return mode;
+}
+
+bool use_pair(int64_t m, int64_t n) {
+  const int64_t pad256 = (n + 255) / 256 * 256 - n;
+  if (m <= 128 || n < 256 || pad256 * 16 > n) return false;
+  const int mode = pair_mode();
+  if (mode >= 0) return mode == 1;
+  const int64_t pair_tiles = ((m + 255) / 256) * ((n + 255) / 256);
+  return pair_tiles >= 2 * (sm_count() / 2);
 }
 
 // Common checks and launch: a [m, k_bytes] and b [n, k_bytes] K-major byte matrices.
@@ -250,10 +265,8 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
       return launch_skinny_nt<KIND, 32>(out_dtype, mw, mx, g, s);
     }
   }
-  // 256 x 256 tiles on SM pairs when there are at least two 128-row blocks of A and padding N
-  // to 256 costs at most 1/16 more columns
-  const int64_t pad256 = (n + 255) / 256 * 256 - n;
-  if (pair_enabled() && g.npeers == 0 && m > 128 && n >= 256 && pad256 * 16 <= n) {
+  // 256 x 256 tiles on SM pairs (use_pair: large shapes)
+  if (use_pair(m, n)) {
     g.m = m;
     g.n = n;
     g.k_stages = static_cast<int>(k_bytes / bkb);
@@ -275,7 +288,10 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
                               "B's block scales"))
         return e;
     }
-    return launch_pair<KIND>(out_dtype, ma, mb, msa, msb, mo, g, s);
+    PeerMaps pm{};
+    for (int p = 0; p < g.npeers; ++p)
+      if (int e = make_out_map(&pm.m[p], g.peer_out[p], out_dtype, m, n, g.ldo)) return e;
+    return launch_pair<KIND>(out_dtype, ma, mb, msa, msb, mo, g, pm, s);
   }
   // one-CTA tiles, width 256 (two 256-column accumulators) for int8 / fp8; the block-scaled
   // kinds keep room for their scale-factor ring next to two accumulators: 192 unless that pads

@@ -439,6 +439,28 @@ int kab_fp4_scale_check(const void* x, int dtype, int64_t rows, int64_t k, int64
   return check_launch("kab_fp4_scale_check");
 }
 
+int kab_outlier_stats(const void* x, int dtype, int64_t rows, int64_t k, int64_t ldx, double* row_sumsq,
+                      float* row_amax, float* col_amax, void* stream) {
+  if (int e = check_matrix(x, dtype, rows, k, ldx, "x")) return e;
+  KAB_REQUIRE(rows == 0 || k == 0 || (row_sumsq != nullptr && row_amax != nullptr && col_amax != nullptr),
+              "null output");
+  KAB_REQUIRE(rows <= static_cast<int64_t>(kOutlierRows) * 65535, "too many rows (%lld)", (long long)rows);
+  const cudaStream_t s = as_stream(stream);
+  if (rows > 0 && (cudaMemsetAsync(row_sumsq, 0, rows * sizeof(double), s) != cudaSuccess ||
+                   cudaMemsetAsync(row_amax, 0, rows * sizeof(float), s) != cudaSuccess))
+    return check_launch("outlier stats reset");
+  if (k > 0 && cudaMemsetAsync(col_amax, 0, k * sizeof(float), s) != cudaSuccess)
+    return check_launch("outlier stats reset");
+  if (rows == 0 || k == 0) return KAB_OK;
+  const dim3 grid(static_cast<unsigned>((k + 2047) / 2048), static_cast<unsigned>((rows + kOutlierRows - 1) / kOutlierRows));
+  auto* rm = reinterpret_cast<unsigned*>(row_amax);
+  auto* cm = reinterpret_cast<unsigned*>(col_amax);
+  if (dtype == KAB_BF16) outlier_stats_kernel<kBF16><<<grid, 256, 0, s>>>(x, ldx, rows, k, row_sumsq, rm, cm);
+  else if (dtype == KAB_F16) outlier_stats_kernel<kF16><<<grid, 256, 0, s>>>(x, ldx, rows, k, row_sumsq, rm, cm);
+  else outlier_stats_kernel<kF32><<<grid, 256, 0, s>>>(x, ldx, rows, k, row_sumsq, rm, cm);
+  return check_launch("kab_outlier_stats");
+}
+
 int kab_row_pair_stats(const void* x, int x_dtype, int64_t ldx, const void* y, int y_dtype, int64_t ldy,
                        int64_t rows, int64_t k, double* out, void* stream) {
   KAB_REQUIRE(valid_dtype(x_dtype) && valid_dtype(y_dtype), "unknown dtype %d / %d", x_dtype, y_dtype);

@@ -367,6 +367,13 @@ __device__ __forceinline__ void commit_pair(uint32_t bar) {
 }
 // cp_sf for CTA pairs: each CTA's 32-row x 128-bit chunk (the same shared-memory offset in
 // both) into its own TMEM, replicated into each warp quarter's 32 lanes.
+// commit_pair arriving on the barrier at the same shared-memory offset in both CTAs of the
+// pair (the leader's and the peer's) with one instruction.
+__device__ __forceinline__ void commit_pair_both(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+               ::"r"(bar), "h"(static_cast<unsigned short>(3))
+               : "memory");
+}
 __device__ __forceinline__ void cp_sf_pair(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }

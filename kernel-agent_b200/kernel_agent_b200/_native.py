@@ -61,6 +61,22 @@ class KabCompareParams(ctypes.Structure):
     ]
 
 
+KAB_DIFF_MAXDIM = 8
+KAB_DIFF_F64 = 3  # the difference census also reads float64 tensors
+KAB_DIFF_BITS = {1: 4, 2: 5, 4: 6, 8: 7}  # ... and compares integer / boolean tensors by their bits
+
+
+class KabDiffParams(ctypes.Structure):
+    _fields_ = [
+        ("a", c_void_p), ("b", c_void_p), ("base", c_void_p),
+        ("dtype", c_int), ("nan_equal", c_int),
+        ("outer", c_int64), ("len", c_int64), ("inner", c_int64),
+        ("a_dim", c_int64), ("a_off", c_int64), ("base_dim", c_int64), ("base_off", c_int64),
+        ("ndim", c_int), ("shape", c_int64 * KAB_DIFF_MAXDIM),
+        ("hits", c_void_p), ("box", c_void_p), ("mask", c_void_p),
+    ]
+
+
 class KabKvDecodeParams(ctypes.Structure):
     _fields_ = [
         ("q", c_void_p), ("q_dtype", c_int), ("q_stride_b", c_int64), ("q_stride_row", c_int64),
@@ -127,6 +143,8 @@ _SIGNATURES: dict[str, list] = {
                             c_void_p],
     "kab_attention_fp8": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                           c_int64, c_int64, c_int, ctypes.c_float, c_void_p, c_void_p],
+    "kab_diff_census": [c_void_p, c_void_p, c_void_p],
+    "kab_outlier_stats": [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
     "kab_row_pair_stats": [c_void_p, c_int, c_int64, c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p,
                            c_void_p],
     "kab_quant_kv_fp8": [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64,

@@ -470,99 +470,104 @@ def compare_tensors(
 
 
 def _like(rerounded: Any, ref: torch.Tensor) -> torch.Tensor | None:
-    """compare.py:793-803."""
-    if (
-        not isinstance(rerounded, torch.Tensor)
-        or type_error(rerounded) is not None
-        or rerounded.shape != ref.shape
-        or rerounded.dtype != ref.dtype
-    ):
-        return None
-    return rerounded.detach()
+    """compare.py:793-803: ``rerounded`` (detached) if it is a plain tensor of ``ref``'s shape
+    and dtype, else None."""
+    usable = (isinstance(rerounded, torch.Tensor) and type_error(rerounded) is None
+              and rerounded.shape == ref.shape and rerounded.dtype == ref.dtype)
+    return rerounded.detach() if usable else None
 
 
 # ------------------------------------------------------------------ caches and structures
+#
+# compare.py:806-1182. A tier judges part of an output when the call changed part of an
+# input: a cache grown along one dimension (the appended rows), rows written into an input
+# of the same shape (the box they span), or an argument updated in place (the elements either
+# side changed). The rest must be as the reference left it. Which elements differ from the
+# call's input is one GPU pass each (``kab_diff_census``: a count and, when asked, a mask of
+# the differing elements and, per dimension, the indices that hold one); the judged parts go
+# through :func:`compare_tensors`.
 
 
-def grown_dim(before: Any, after: Any) -> int | None:
-    """compare.py:806-825: the dimension along which ``after`` is ``before`` grown."""
-    if not (isinstance(before, torch.Tensor) and isinstance(after, torch.Tensor)):
-        return None
-    if (
-        not before.is_floating_point()
-        or before.dtype != after.dtype
-        or before.dim() != after.dim()
-        or before.layout != torch.strided
-        or after.layout != torch.strided
-        or before.numel() == 0
-    ):
-        return None
-    dims = [d for d in range(before.dim()) if before.shape[d] != after.shape[d]]
-    if len(dims) != 1 or after.shape[dims[0]] < before.shape[dims[0]]:
-        return None
-    return dims[0]
+@dataclasses.dataclass
+class _Census:
+    """The elements of a region that differ from the base tensor: how many, and (when asked)
+    a boolean mask of the region and per-dimension index flags."""
+
+    count: int
+    mask: torch.Tensor | None = None
+    hits: list[torch.Tensor] | None = None
 
 
-def _same(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """Elementwise equality with NaN equal to NaN."""
-    return (a == b) | (torch.isnan(a) & torch.isnan(b))
+def _census_dtype(t: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """The tensor as the census reads it and its type code: floats by value, integers and
+    booleans by their bits."""
+    if t.dtype in nat.DTYPES:
+        return t, nat.DTYPES[t.dtype]
+    if t.dtype == torch.float64:
+        return t, nat.KAB_DIFF_F64
+    if t.is_floating_point():
+        return t.float(), nat.KAB_F32  # 1-byte floats: their fp32 values are exact
+    if t.element_size() not in nat.KAB_DIFF_BITS:
+        raise ValueError(f"the difference census does not read {t.dtype} tensors")
+    return t, nat.KAB_DIFF_BITS[t.element_size()]
 
 
-def _mismatched(new, ref) -> bool:
-    return (
-        type_error(new) is not None
-        or new.shape != ref.shape
-        or new.dtype != ref.dtype
-        or new.layout != ref.layout
-        or new.device.type != ref.device.type
-    )
+def _census(a: torch.Tensor, base: torch.Tensor, *, also: torch.Tensor | None = None, nan_equal: bool = True,
+            dim: int = 0, length: int | None = None, a_off: int = 0, base_off: int = 0, mask: bool = False,
+            hits: bool = False, outside: list[torch.Tensor] | None = None) -> _Census:
+    """Which elements of ``a`` (or of ``a`` or ``also``, laid out like ``a``) differ from
+    ``base`` over ``length`` indices along ``dim`` (from ``a_off`` in ``a``, ``base_off`` in
+    ``base``; the whole dimension by default). ``nan_equal``: NaN equals NaN; else IEEE
+    ``!=``. ``outside``: per dimension the flags of a box whose elements are not counted."""
+    dev = nat.require_cuda(a)
+    shape0 = tuple(a.shape)
+    a, code = _census_dtype(a.detach().contiguous())
+    base = _census_dtype(base.detach().to(dev).contiguous())[0]
+    if also is not None:
+        also = _census_dtype(also.detach().to(dev).contiguous())[0]
+    shape = list(a.shape) or [1]
+    dim = dim % len(shape)
+    length = shape[dim] if length is None else length
+    region = shape[:dim] + [length] + shape[dim + 1:]
+    p = nat.KabDiffParams()
+    p.a, p.b, p.base = a.data_ptr(), nat.ptr(also), base.data_ptr()
+    p.dtype, p.nan_equal = code, int(nan_equal)
+    p.outer, p.len, p.inner = math.prod(shape[:dim]), length, math.prod(shape[dim + 1:])
+    p.a_dim, p.a_off = shape[dim], a_off
+    p.base_dim, p.base_off = (list(base.shape) or [1])[dim], base_off
+    flags = box = None
+    if hits or outside is not None:
+        if len(region) > nat.KAB_DIFF_MAXDIM:
+            raise ValueError(f"a census over {len(region)} dimensions (at most {nat.KAB_DIFF_MAXDIM})")
+        p.ndim = len(region)
+        for k, n in enumerate(region):
+            p.shape[k] = n
+        if hits:
+            flags = torch.zeros(sum(region), dtype=torch.uint8, device=dev)
+            p.hits = flags.data_ptr()
+        if outside is not None:
+            box = torch.cat([f.to(dev, torch.uint8).reshape(-1) for f in outside])
+            p.box = box.data_ptr()
+    marks = torch.empty(region, dtype=torch.uint8, device=dev) if mask else None
+    p.mask = nat.ptr(marks)
+    count = torch.empty(1, dtype=torch.int64, device=dev)
+    nat.call("kab_diff_census", ctypes.byref(p), count.data_ptr(), nat.stream_of(a))
+    found = _Census(int(count.item()))  # one device-to-host read
+    if marks is not None:
+        found.mask = marks.bool().reshape(shape0[:dim] + (length,) + shape0[dim + 1:]) if shape0 else marks.bool().reshape(())
+    if flags is not None:
+        found.hits = [f.bool() for f in flags.split(region)]
+    return found
 
 
-def compare_grown(name, before, ref, new, dim, *, tier=None, perturbed=False, input_scale=1.0,
-                  rerounded=None) -> dict[str, Any]:
-    """compare.py:833-915: a cache grown along ``dim``: the appended rows with the tier's
-    checks, the kept part bit for bit where the reference kept it."""
-    kw: dict[str, Any] = {"tier": tier, "perturbed": perturbed, "input_scale": input_scale}
-    if _mismatched(new, ref):
-        return compare_tensors(name, ref, new, rerounded=rerounded, **kw)
-    alt = _like(rerounded, ref)
-    kept, total = before.shape[dim], ref.shape[dim]
-    ref, before = ref.detach().to(new.device), before.detach().to(new.device)
-    new = new.detach()
-    appended = total - kept
-    channels = _channel_rms_of(ref.float().contiguous()) if perturbed else None
-    if channels is not None:
-        shape = [1] * ref.dim()
-        shape[-1] = ref.shape[-1]
-        channels = channels.reshape(shape)
-        if dim == ref.dim() - 1:
-            channels = channels.narrow(dim, kept, appended)
-    result = compare_tensors(
-        name, ref.narrow(dim, kept, appended), new.narrow(dim, kept, appended),
-        channel_rms=channels,
-        rerounded=None if alt is None else alt.to(new.device).narrow(dim, kept, appended), **kw,
-    )
-    result["grown"] = {"dim": dim, "kept": kept, "appended": appended}
-    rows = f"{appended} appended row{'s' if appended != 1 else ''} along dim {dim}"
-    problems = [f"the {rows} (after {kept} kept): {result['error']}"] if "error" in result else []
-    ref_old, new_old = ref.narrow(dim, 0, kept), new.narrow(dim, 0, kept)
-    unchanged = _same(ref_old, before)
-    if bool(unchanged.all()):
-        moved = int((~_same(new_old, before)).sum())
-        result["kept_changed"] = moved
-        if moved:
-            problems.append(
-                f"{moved} of the {before.numel()} elements of the {kept} kept rows along dim "
-                f"{dim} changed; the reference keeps them as they were (it only appends)"
-            )
-    else:
-        changed = ~unchanged | ~_same(new_old, before)
-        count = int(changed.sum())
-        old_alt = None if alt is None else alt.to(new.device).narrow(dim, 0, kept)[changed]
-        old = compare_tensors(name, ref_old[changed], new_old[changed], rerounded=old_alt, **kw)
-        result["changed_elements"] = count
-        if not old["ok"]:
-            problems.append(f"the {count} changed elements of the {kept} kept rows: {old['error']}")
+def _mismatched(new: Any, ref: torch.Tensor) -> bool:
+    """compare.py:860-867 / 980-987: a candidate compared whole (its error) rather than by part."""
+    return (type_error(new) is not None or new.shape != ref.shape or new.dtype != ref.dtype
+            or new.layout != ref.layout or new.device.type != ref.device.type)
+
+
+def _settle(result: dict[str, Any], problems: list[str]) -> dict[str, Any]:
+    """The verdict of a comparison by parts: its problems, or ok."""
     result.pop("error", None)
     if problems:
         result["error"] = "; ".join(problems)
@@ -570,124 +575,177 @@ def compare_grown(name, before, ref, new, dim, *, tier=None, perturbed=False, in
     return result
 
 
+def _channels_floor(ref: torch.Tensor, perturbed: bool) -> torch.Tensor | None:
+    """compare.py:582-589 on the whole reference, as a per-channel floor ``[C]`` for the part
+    a tier judges (on redrawn inputs only)."""
+    return _channel_rms_of(ref.float().contiguous()) if perturbed else None
+
+
+def grown_dim(before: Any, after: Any) -> int | None:
+    """compare.py:806-825: the one dimension along which ``after`` is ``before`` grown (both
+    floating-point, strided, one dtype and rank, ``before`` not empty), or None."""
+    if not isinstance(before, torch.Tensor) or not isinstance(after, torch.Tensor):
+        return None
+    comparable = (before.is_floating_point() and before.dtype == after.dtype and before.dim() == after.dim()
+                  and before.layout == torch.strided == after.layout and before.numel() > 0)
+    if not comparable:
+        return None
+    grew = [d for d, (b, a) in enumerate(zip(before.shape, after.shape)) if b != a]
+    return grew[0] if len(grew) == 1 and after.shape[grew[0]] > before.shape[grew[0]] else None
+
+
+def compare_grown(name, before, ref, new, dim, *, tier=None, perturbed=False, input_scale=1.0,
+                  rerounded=None) -> dict[str, Any]:
+    """compare.py:833-915: ``new`` against ``ref``, both ``before`` grown along ``dim``: the
+    appended rows on their own with the tier's checks, and the kept part: bit for bit where
+    the reference kept it, else the elements either side changed."""
+    options = {"tier": tier, "perturbed": perturbed, "input_scale": input_scale}
+    if _mismatched(new, ref):
+        return compare_tensors(name, ref, new, rerounded=rerounded, **options)
+    dev = new.device
+    spread = _like(rerounded, ref)
+    ref, before, new = ref.detach().to(dev), before.detach().to(dev), new.detach()
+    old = before.shape[dim]
+    grown = ref.shape[dim] - old
+
+    def appended(t: torch.Tensor) -> torch.Tensor:
+        return t.narrow(dim, old, grown)
+
+    floor = _channels_floor(ref, perturbed)
+    if floor is not None and dim == ref.dim() - 1:  # grown along the channels themselves
+        floor = floor.narrow(0, old, grown)
+    result = compare_tensors(name, appended(ref), appended(new), channel_rms=floor,
+                             rerounded=None if spread is None else appended(spread.to(dev)), **options)
+    result["grown"] = {"dim": dim, "kept": old, "appended": grown}
+    problems = []
+    if "error" in result:
+        plural = "s" if grown != 1 else ""
+        problems.append(f"the {grown} appended row{plural} along dim {dim} (after {old} kept): {result['error']}")
+    # the kept part: did the reference leave it as the input?
+    if _census(ref, before, dim=dim, length=old).count == 0:
+        drift = _census(new, before, dim=dim, length=old).count
+        result["kept_changed"] = drift
+        if drift:
+            problems.append(f"{drift} of the {before.numel()} elements of the {old} kept rows along dim {dim} "
+                            "changed; the reference keeps them as they were (it only appends)")
+    else:
+        either = _census(ref, before, also=new, dim=dim, length=old, mask=True)
+        pick = either.mask
+
+        def kept(t: torch.Tensor) -> torch.Tensor:
+            return t.narrow(dim, 0, old)[pick]
+
+        judged = compare_tensors(name, kept(ref), kept(new),
+                                 rerounded=None if spread is None else kept(spread.to(dev)), **options)
+        result["changed_elements"] = either.count
+        if not judged["ok"]:
+            problems.append(f"the {either.count} changed elements of the {old} kept rows: {judged['error']}")
+    return _settle(result, problems)
+
+
 def written_box(before: Any, after: Any) -> list[torch.Tensor] | None:
-    """compare.py:918-953: the indices per dimension of rows a call wrote into ``before``."""
-    if not (isinstance(before, torch.Tensor) and isinstance(after, torch.Tensor)):
+    """compare.py:918-953: per dimension, the indices of the box of rows a call wrote into
+    ``before`` to give ``after`` (same shape, floating-point, strided, not empty); None when
+    nothing differs, or the differences do not fill WRITTEN_MIN_DENSITY of a box that spans a
+    whole dimension of more than one element and at most WRITTEN_MAX_FRACTION of the tensor."""
+    if not isinstance(before, torch.Tensor) or not isinstance(after, torch.Tensor):
         return None
-    if (
-        not before.is_floating_point()
-        or before.dtype != after.dtype
-        or before.shape != after.shape
-        or before.layout != torch.strided
-        or after.layout != torch.strided
-        or before.dim() == 0
-        or before.numel() == 0
-    ):
+    comparable = (before.is_floating_point() and before.dtype == after.dtype and before.shape == after.shape
+                  and before.layout == torch.strided == after.layout and before.dim() > 0 and before.numel() > 0)
+    if not comparable or before.dim() > nat.KAB_DIFF_MAXDIM:  # more dimensions than the census takes:
+        return None                                                # compared whole
+    found = _census(after, before.to(after.device), hits=True)
+    if found.count == 0:  # the input itself: compared whole
         return None
-    changed = ~_same(after.detach(), before.detach().to(after.device))
-    count = int(changed.sum())
-    if count == 0:
+    extent = [int(h.sum()) for h in found.hits]
+    spans_a_row = any(e == n > 1 for e, n in zip(extent, after.shape))
+    area = math.prod(extent)
+    if area > WRITTEN_MAX_FRACTION * after.numel() or found.count < WRITTEN_MIN_DENSITY * area or not spans_a_row:
         return None
-    hits = [changed.movedim(d, 0).reshape(n, -1).any(1) for d, n in enumerate(changed.shape)]
-    sizes = [int(h.sum()) for h in hits]
-    box = math.prod(sizes)
-    if (
-        box > WRITTEN_MAX_FRACTION * changed.numel()
-        or count < WRITTEN_MIN_DENSITY * box
-        or not any(s == n > 1 for s, n in zip(sizes, changed.shape, strict=True))
-    ):
-        return None
-    return [h.nonzero().flatten() for h in hits]
+    return [h.nonzero().flatten() for h in found.hits]
 
 
 def compare_written(name, before, ref, new, box, *, tier=None, perturbed=False, input_scale=1.0,
                     rerounded=None) -> dict[str, Any]:
-    """compare.py:956-1034: rows written into an input: the box with the tier's checks, the
-    rest bit for bit."""
-    kw: dict[str, Any] = {"tier": tier, "perturbed": perturbed, "input_scale": input_scale}
+    """compare.py:956-1034: rows written into an input: the box (``box``: its indices per
+    dimension) with the tier's checks, every element outside it bit for bit as before."""
+    options = {"tier": tier, "perturbed": perturbed, "input_scale": input_scale}
     if _mismatched(new, ref):
-        return compare_tensors(name, ref, new, rerounded=rerounded, **kw)
-    alt = _like(rerounded, ref)
-    ref, before = ref.detach().to(new.device), before.detach().to(new.device)
-    new = new.detach()
-    box = [index.to(new.device) for index in box]
+        return compare_tensors(name, ref, new, rerounded=rerounded, **options)
+    dev = new.device
+    spread = _like(rerounded, ref)
+    ref, before, new = ref.detach().to(dev), before.detach().to(dev), new.detach()
+    box = [index.to(dev) for index in box]
 
-    def part(t: torch.Tensor) -> torch.Tensor:
+    def inside(t: torch.Tensor) -> torch.Tensor:
         for d, index in enumerate(box):
             if index.numel() < t.shape[d]:
                 t = t.index_select(d, index)
         return t
 
-    channels = _channel_rms_of(ref.float().contiguous()) if perturbed else None
-    if channels is not None:
-        if box[-1].numel() < ref.shape[-1]:
-            channels = channels.index_select(0, box[-1])
-        shape = [1] * ref.dim()
-        shape[-1] = channels.numel()
-        channels = channels.reshape(shape)
-    result = compare_tensors(
-        name, part(ref), part(new), channel_rms=channels,
-        rerounded=None if alt is None else part(alt.to(new.device)), **kw,
-    )
-    sizes = [int(index.numel()) for index in box]
-    result["written"] = {"box": sizes, "of": list(ref.shape)}
-    written = f"written {sizes} of {list(ref.shape)}"
-    where = f"the {written} (where the reference changed the input)"
-    problems = [f"{where}: {result['error']}"] if "error" in result else []
-    inside = torch.ones((), dtype=torch.bool, device=new.device)
+    floor = _channels_floor(ref, perturbed)
+    if floor is not None and box[-1].numel() < ref.shape[-1]:  # written along the channels
+        floor = floor.index_select(0, box[-1])
+    result = compare_tensors(name, inside(ref), inside(new), channel_rms=floor,
+                             rerounded=None if spread is None else inside(spread.to(dev)), **options)
+    extent = [int(index.numel()) for index in box]
+    written = f"written {extent} of {list(ref.shape)}"
+    result["written"] = {"box": extent, "of": list(ref.shape)}
+    problems = []
+    if "error" in result:
+        problems.append(f"the {written} (where the reference changed the input): {result['error']}")
+    member = []
     for d, index in enumerate(box):
-        hit = torch.zeros(ref.shape[d], dtype=torch.bool, device=new.device)
-        hit[index] = True
-        inside = inside & hit.view([-1 if i == d else 1 for i in range(ref.dim())])
-    moved = int((~_same(new, before) & ~inside).sum())
-    result["kept_changed"] = moved
-    if moved:
-        problems.append(
-            f"{moved} of the {ref.numel() - math.prod(sizes)} elements outside the {written} "
-            "changed; the reference keeps them as they were (it only writes the box)"
-        )
-    result.pop("error", None)
-    if problems:
-        result["error"] = "; ".join(problems)
-    result["ok"] = not problems
-    return result
+        flag = torch.zeros(ref.shape[d], dtype=torch.bool, device=dev)
+        flag[index] = True
+        member.append(flag)
+    drift = _census(new, before, outside=member).count
+    result["kept_changed"] = drift
+    if drift:
+        problems.append(f"{drift} of the {ref.numel() - math.prod(extent)} elements outside the {written} "
+                        "changed; the reference keeps them as they were (it only writes the box)")
+    return _settle(result, problems)
+
+
+def _grows_from(before: torch.Tensor, ref: torch.Tensor) -> int | None:
+    """The dimension along which ``ref`` grows ``before`` with its leading part there equal to
+    ``before`` (NaN as NaN), or None."""
+    dim = grown_dim(before, ref)
+    if dim is None:
+        return None
+    return dim if _census(ref, before, dim=dim, length=before.shape[dim]).count == 0 else None
 
 
 def compare_output(name, ref, new, inputs=(), *, tier=None, perturbed=False, input_scale=1.0,
                    rerounded=None) -> dict[str, Any]:
-    """compare.py:1037-1071: grown cache, written cache, or a plain tensor comparison."""
-    kw: dict[str, Any] = {"tier": tier, "perturbed": perturbed, "input_scale": input_scale,
-                          "rerounded": rerounded}
-    for before in inputs:
-        dim = grown_dim(before, ref)
-        if dim is None:
-            continue
-        lead = ref.detach().narrow(dim, 0, before.shape[dim])
-        if bool(_same(lead, before.detach().to(lead.device)).all()):
-            return compare_grown(name, before, ref, new, dim, **kw)
-    for before in inputs:
-        box = written_box(before, ref)
-        if box is not None:
-            return compare_written(name, before, ref, new, box, **kw)
-    return compare_tensors(name, ref, new, **kw)
+    """compare.py:1037-1071: an output that grows one of the call's inputs
+    (:func:`compare_grown`), one with rows written into one of them (:func:`compare_written`),
+    else the whole tensor (:func:`compare_tensors`)."""
+    options = {"tier": tier, "perturbed": perturbed, "input_scale": input_scale, "rerounded": rerounded}
+    grown = next(((src, dim) for src in inputs if (dim := _grows_from(src, ref)) is not None), None)
+    if grown is not None:
+        return compare_grown(name, grown[0], ref, new, grown[1], **options)
+    written = next(((src, box) for src in inputs if (box := written_box(src, ref)) is not None), None)
+    if written is not None:
+        return compare_written(name, written[0], ref, new, written[1], **options)
+    return compare_tensors(name, ref, new, **options)
 
 
 def compare_structures(ref, new, prefix: str = "out", *, inputs=None, tier=None, perturbed=False,
                        input_scale=1.0, rerounded=None) -> list[dict[str, Any]]:
-    """compare.py:1074-1103: the candidate's output against the reference's, tensor by tensor."""
-    ref_flat = flatten(ref, prefix)
-    new_flat = flatten(new, prefix)
-    alt_flat = flatten(rerounded, prefix)
+    """compare.py:1074-1103: the candidate's output against the reference's, tensor by
+    tensor (names from :func:`flatten`), each through :func:`compare_output`."""
+    candidate = flatten(new, prefix)
+    redrawn = flatten(rerounded, prefix)
     sources = list(flatten(inputs, "in").values())
-    kw: dict[str, Any] = {"tier": tier, "perturbed": perturbed, "input_scale": input_scale}
-    results = []
-    for name, tensor in ref_flat.items():
-        if name not in new_flat:
-            results.append({"name": name, "ok": False, "error": "missing in candidate output"})
-            continue
-        results.append(compare_output(name, tensor, new_flat[name], sources,
-                                      rerounded=alt_flat.get(name), **kw))
-    return results
+    options = {"tier": tier, "perturbed": perturbed, "input_scale": input_scale}
+
+    def one(name: str, tensor: torch.Tensor) -> dict[str, Any]:
+        if name not in candidate:
+            return {"name": name, "ok": False, "error": "missing in candidate output"}
+        return compare_output(name, tensor, candidate[name], sources, rerounded=redrawn.get(name), **options)
+
+    return [one(name, tensor) for name, tensor in flatten(ref, prefix).items()]
 
 
 def compare_side_effects(pre, ref_post, new_post, prefix: str = "args", *, tier=None,
@@ -699,38 +757,41 @@ def compare_side_effects(pre, ref_post, new_post, prefix: str = "args", *, tier=
     )
 
 
+def _updated_in_place(before: Any, ref: torch.Tensor, new: Any) -> bool:
+    """Whether an argument kept its shape and dtype on both sides (an in-place update)."""
+    return (before is not None and type_error(new) is None and before.shape == ref.shape == new.shape
+            and before.dtype == ref.dtype == new.dtype)
+
+
 def compare_side_effects_flat(pre_flat, ref_flat, new_flat, *, tier=None, perturbed=False,
                               input_scale=1.0, rerounded_flat=None) -> list[dict[str, Any]]:
-    """compare.py:1140-1182: in-place updates compared on the elements either side changed."""
-    kw: dict[str, Any] = {"tier": tier, "perturbed": perturbed, "input_scale": input_scale}
-    results: list[dict[str, Any]] = []
-    for name, ref in ref_flat.items():
+    """compare.py:1140-1182: each argument the reference's call left: grown (by
+    :func:`compare_grown`), updated in place (the elements either side changed, by IEEE
+    ``!=``, judged alone), or compared whole."""
+    options = {"tier": tier, "perturbed": perturbed, "input_scale": input_scale}
+    redrawn = rerounded_flat or {}
+
+    def one(name: str, ref: torch.Tensor) -> dict[str, Any]:
         new = new_flat.get(name)
         if new is None:
-            results.append({"name": name, "ok": False, "error": "missing in candidate arguments"})
-            continue
-        alt = (rerounded_flat or {}).get(name)
+            return {"name": name, "ok": False, "error": "missing in candidate arguments"}
+        spread = redrawn.get(name)
         before = pre_flat.get(name)
-        if before is not None and (dim := grown_dim(before, ref)) is not None:
-            results.append(compare_grown(name, before, ref, new, dim, rerounded=alt, **kw))
-            continue
-        if (
-            before is None
-            or type_error(new) is not None
-            or not (before.shape == ref.shape == new.shape)
-            or not (before.dtype == ref.dtype == new.dtype)
-        ):
-            results.append(compare_tensors(name, ref, new, rerounded=alt, **kw))
-            continue
-        before, ref = before.to(new.device), ref.to(new.device)
-        changed = (ref != before) | (new != before)
-        count = int(changed.sum())
-        if count == 0:
-            results.append({"name": name, "ok": True, "changed_elements": 0, "max_abs_err": 0.0})
-            continue
-        alt = _like(alt, ref)
-        alt = None if alt is None else alt.to(new.device)[changed]
-        result = compare_tensors(name, ref[changed], new[changed], rerounded=alt, **kw)
-        result["changed_elements"] = count
-        results.append(result)
-    return results
+        dim = grown_dim(before, ref) if before is not None else None
+        if dim is not None:
+            return compare_grown(name, before, ref, new, dim, rerounded=spread, **options)
+        if not _updated_in_place(before, ref, new):
+            return compare_tensors(name, ref, new, rerounded=spread, **options)
+        dev = new.device
+        ref_d, before_d = ref.to(dev), before.to(dev)
+        either = _census(ref_d, before_d, also=new, nan_equal=False, mask=True)
+        if either.count == 0:
+            return {"name": name, "ok": True, "changed_elements": 0, "max_abs_err": 0.0}
+        alt = _like(spread, ref)
+        pick = either.mask
+        result = compare_tensors(name, ref_d[pick], new[pick],
+                                 rerounded=None if alt is None else alt.to(dev)[pick], **options)
+        result["changed_elements"] = either.count
+        return result
+
+    return [one(name, ref) for name, ref in ref_flat.items()]

@@ -1128,60 +1128,100 @@ def fp4_w4a4_error(weight: torch.Tensor, codes: torch.Tensor, scales: torch.Tens
     return report
 
 
-def _same(a: torch.Tensor, b: torch.Tensor) -> bool:
-    """quant.py:1656-1658: whether two layers' kept inputs are the same values."""
+class _InputRecorder:
+    """Records the first ``calls`` inputs of every ``nn.Linear`` of a module while it runs
+    (forward pre-hooks, removed on exit), each as ``[rows, in_features]``."""
+
+    def __init__(self, module: torch.nn.Module, calls: int):
+        self.layers = {n: m for n, m in module.named_modules() if isinstance(m, torch.nn.Linear)}
+        self.calls = calls
+        self.inputs: dict[str, list[torch.Tensor]] = {}
+        self._hooks: list[Any] = []
+
+    def _hook_for(self, name: str):
+        def record(_: torch.nn.Module, args: tuple[Any, ...]) -> None:
+            got = self.inputs.setdefault(name, [])
+            if len(got) < self.calls and isinstance(args[0], torch.Tensor):
+                got.append(args[0].detach().reshape(-1, args[0].shape[-1]))
+        return record
+
+    def __enter__(self) -> "_InputRecorder":
+        self._hooks = [m.register_forward_pre_hook(self._hook_for(n)) for n, m in self.layers.items()]
+        return self
+
+    def __exit__(self, *exc) -> None:
+        for h in self._hooks:
+            h.remove()
+
+    def rows(self) -> dict[str, torch.Tensor]:
+        """The recorded inputs of each layer that ran, concatenated, in module order."""
+        return {n: torch.cat(self.inputs[n]) for n in self.layers if n in self.inputs}
+
+
+def _same_values(a: torch.Tensor, b: torch.Tensor) -> bool:
+    """quant.py:1656-1658: two layers read the same inputs (same shape, dtype, device and values)."""
     return a.shape == b.shape and a.dtype == b.dtype and a.device == b.device and torch.equal(a, b)
+
+
+def _input_groups(inputs: dict[str, torch.Tensor]) -> dict[str, str]:
+    """Each layer's group: the first layer (module order) that read the same inputs (q / k / v,
+    gate / up), itself when none did."""
+    leaders: list[tuple[str, torch.Tensor]] = []
+    groups: dict[str, str] = {}
+    for name, x in inputs.items():
+        leader = next((lead for lead, y in leaders if _same_values(x, y)), None)
+        if leader is None:
+            leaders.append((name, x))
+            leader = name
+        groups[name] = leader
+    return groups
+
+
+def _sensitivity_of(layer: torch.nn.Linear, x: torch.Tensor, fmt: str, granularity: str,
+                    rotate: int | None) -> dict[str, Any] | None:
+    """One layer quantised alone to W4A4 and to FP8 W8A8 on inputs ``x``: its row (without
+    name, group and FLOP share) and its GEMM FLOPs; None when W4A4 does not apply (K not a
+    multiple of the block or of the rotation, or no inputs)."""
+    w = layer.weight.detach()
+    out_f, in_f = w.shape
+    x = x.to(w.device)
+    if in_f % (rotate or FP4_FORMATS[fmt][0]) or x.numel() == 0:
+        return None
+    codes, scales, ts = quantize_fp4(hadamard_rotate(w, rotate) if rotate else w, fmt)
+    w4 = fp4_w4a4_error(w, codes, scales, ts, x, fmt=fmt, granularity=granularity, rotate=rotate)
+    w8 = fp8_w8a8_error(w, *quantize_fp8(w), x)
+    rows = int(x.shape[0])
+    return {
+        "rows": rows, "in_features": int(in_f), "out_features": int(out_f),
+        "activation_crest": w4["activation_crest"],
+        "w4a4_rel_l2": w4["output_rel_l2"],
+        "w4a4_norm_change": _sig(w4["output_norm_ratio"] - 1.0),
+        "fp8_rel_l2": w8["output_rel_l2"],
+        "_flops": 2 * rows * int(in_f) * int(out_f),
+    }
 
 
 def fp4_w4a4_sensitivity(module: torch.nn.Module, run, *, fmt: str = "nvfp4", granularity: str = "token",
                          rotate: int | None = None, calls: int = 4) -> list[dict[str, Any]]:
-    """quant.py:1575-1653: the W4A4 sensitivity probe: each ``nn.Linear`` of ``module``,
-    quantised alone to W4A4 (:func:`fp4_w4a4_error`) and to FP8 W8A8
-    (:func:`fp8_w8a8_error`) on its first ``calls`` inputs of ``run()``; one row per layer,
-    the most sensitive (largest W4A4 output relative L2 error) first."""
-    seen: dict[str, list[torch.Tensor]] = {}
-    layers = {n: m for n, m in module.named_modules() if isinstance(m, torch.nn.Linear)}
-
-    def keep(name: str):
-        def hook(_: torch.nn.Module, args: tuple[Any, ...]) -> None:
-            if len(seen.setdefault(name, [])) < calls and isinstance(args[0], torch.Tensor):
-                seen[name].append(args[0].detach().reshape(-1, args[0].shape[-1]))
-
-        return hook
-
-    hooks = [m.register_forward_pre_hook(keep(n)) for n, m in layers.items()]
-    try:
-        with torch.no_grad():
-            run()
-    finally:
-        for h in hooks:
-            h.remove()
-    found = []
-    kept = {n: torch.cat(seen[n]) for n in layers if n in seen}
-    group: dict[str, str] = {}
-    for name, x in kept.items():
-        group[name] = next((g for g, y in kept.items() if g in group and g == group[g] and _same(x, y)), name)
-    for name, x in kept.items():
-        w = layers[name].weight.detach()
-        x = x.to(w.device)
-        if w.shape[1] % (rotate or FP4_FORMATS[fmt][0]) or not x.numel():
-            continue
-        wq = hadamard_rotate(w, rotate) if rotate else w
-        e4 = fp4_w4a4_error(w, *quantize_fp4(wq, fmt), x, fmt=fmt, granularity=granularity, rotate=rotate)
-        e8 = fp8_w8a8_error(w, *quantize_fp8(w), x)
-        found.append({
-            "name": name,
-            "rows": int(x.shape[0]),
-            "in_features": int(w.shape[1]),
-            "out_features": int(w.shape[0]),
-            "flops": 2 * int(x.shape[0]) * int(w.shape[1]) * int(w.shape[0]),
-            "activation_crest": e4["activation_crest"],
-            "w4a4_rel_l2": e4["output_rel_l2"],
-            "w4a4_norm_change": _sig(e4["output_norm_ratio"] - 1.0),
-            "fp8_rel_l2": e8["output_rel_l2"],
-            "input_group": group[name],
-        })
-    total = sum(r["flops"] for r in found) or 1
-    for row in found:
-        row["flop_share"] = _sig(row.pop("flops") / total)
-    return sorted(found, key=lambda r: -r["w4a4_rel_l2"])
+    """quant.py:1575-1653: which ``nn.Linear`` layers of ``module`` to keep in FP8 W8A8. ``run()``
+    calls the module; each layer's first ``calls`` inputs (their rows together) are recorded,
+    and the layer is quantised alone to W4A4 (:func:`fp4_w4a4_error`) and to FP8 W8A8
+    (:func:`fp8_w8a8_error`) on them. One row per layer, most sensitive first (largest W4A4
+    output relative L2): ``name``, ``rows``, ``in_features``, ``out_features``,
+    ``activation_crest``, ``w4a4_rel_l2``, ``w4a4_norm_change``, ``fp8_rel_l2``, ``input_group``
+    (the first layer that read the same inputs) and ``flop_share`` (of the layers' GEMM
+    FLOPs). The quantised products run on this library's tcgen05 GEMMs."""
+    with _InputRecorder(module, calls) as recorder, torch.no_grad():
+        run()
+    inputs = recorder.rows()
+    groups = _input_groups(inputs)
+    table = []
+    for name, x in inputs.items():
+        found = _sensitivity_of(recorder.layers[name], x, fmt, granularity, rotate)
+        if found is not None:
+            table.append({"name": name, **found, "input_group": groups[name]})
+    total = sum(row["_flops"] for row in table) or 1
+    for row in table:
+        row["flop_share"] = _sig(row.pop("_flops") / total)
+    table.sort(key=lambda row: row["w4a4_rel_l2"], reverse=True)
+    return table

@@ -43,15 +43,25 @@ def test_scale_guard_unchecked_paths():
     from kernel_agent_b200.kernels import scale_guard
 
     x = torch.randn(4, 64)
+    tie = torch.randn(2, 32)
     cases = [{"count": 3, "args": (x,)}, {"count": 1, "args": (torch.randn(2, 32),)}]
     assert scale_guard.activation(cases, 32) is x
+    # equal counts keep the cases' order; keyword arguments come after positional ones
+    assert scale_guard.activation([{"count": 2, "args": (5, tie)}, {"count": 2, "args": (x,)}], 32) is tie
+    assert scale_guard.activation([{"args": (), "kwargs": {"x": x}}], 32) is x
     assert scale_guard.activation([{"args": (torch.randn(3, 5),)}], 32) is None
-    report = scale_guard.check(types.SimpleNamespace(), cases, "fp8_mx")
+    assert scale_guard.activation([{"args": (torch.zeros(0, 32),)}], 32) is None
+    # no quantisable input: neither outliers nor a check, only the note
+    none = [{"count": 1, "args": (torch.randn(3, 5),)}]
+    report = scale_guard.check(types.SimpleNamespace(), none, "fp8_mx")
     assert report["ok"] and not report["checked"] and "quantize_activations" in report["note"]
-    assert set(report["outliers"]) == {"crest", "channel_ratio"}
+    assert "outliers" not in report
     fake = types.SimpleNamespace(quantize_activations=lambda t: (t, t))
-    report = scale_guard.check(fake, [{"args": (torch.randn(3, 5),)}], "fp4_w4a4")
+    report = scale_guard.check(fake, none, "fp4_w4a4")
     assert report["ok"] and not report["checked"] and "nothing to quantise" in report["note"]
+    # the outlier statistics are a GPU reduction: a CPU tensor is refused, not computed on the CPU
+    with pytest.raises(ValueError, match="CUDA tensor required"):
+        scale_guard.outliers(x)
 
 
 def test_cpu_tensors_are_refused_by_the_checks(kq):
