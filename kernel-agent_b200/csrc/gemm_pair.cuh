@@ -141,7 +141,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
   const int total = g.m_tiles * g.n_tiles;
 
   if (warp == 0) {
-    if (lane == 0) {  // ---------------------------------------------------- TMA producer
+    {  // ------------------------------------------------------------------- TMA producer
+      // the whole warp walks the loop and waits (as the MMA warp does); one elected lane issues
+      const bool issuer = tc::elect_one();
       const uint32_t full_leader = tc::mapa(full, 0);
       int s = 0;
       uint32_t ph = 0;
@@ -152,28 +154,31 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
         const int arow = mt * 256 + static_cast<int>(rank) * 128;
         const int brow = nt * 256 + static_cast<int>(rank) * 128;
         for (int kb = 0; kb < g.k_stages; ++kb) {
-          if (!tc::mbar_wait_cluster(&empty[s], ph ^ 1u)) { ok = false; break; }
-          const uint32_t bar = full_leader + 8 * s;
-          if (rank == 0) tc::mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
-          tc::tma_load_2d_pair(&tma_a, bar, sA + s * L::kABytes, kb * BKB, arow);
-          tc::tma_load_2d_pair(&tma_b, bar, sB + s * L::kBBytes, kb * BKB, brow);
-          if constexpr (L::kScaled) {
-            // the stage's chunk of 128-row block r starts at byte (r * ncb + kc) * 512; a block
-            // past the end of the tensor reads as zeros (and counts its bytes)
-            const int64_t kc = KIND == 3 ? static_cast<int64_t>(KS) * kb : (KIND == 4 ? static_cast<int64_t>(KS / 2) * kb : kb);
-            const int64_t ra = static_cast<int64_t>(mt) * 2 + rank;
-            tc::tma_load_2d_pair(&tma_sfa, bar, sSFA + s * L::kSfaBytes, 0, static_cast<int>(2 * (ra * g.sfa_ncb + kc)));
+          if (!__all_sync(0xffffffffu, tc::mbar_wait_cluster(&empty[s], ph ^ 1u))) { ok = false; break; }
+          if (issuer) {
+            const uint32_t bar = full_leader + 8 * s;
+            if (rank == 0) tc::mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
+            tc::tma_load_2d_pair(&tma_a, bar, sA + s * L::kABytes, kb * BKB, arow);
+            tc::tma_load_2d_pair(&tma_b, bar, sB + s * L::kBBytes, kb * BKB, brow);
+            if constexpr (L::kScaled) {
+              // the stage's chunk of 128-row block r starts at byte (r * ncb + kc) * 512; a block
+              // past the end of the tensor reads as zeros (and counts its bytes)
+              const int64_t kc = KIND == 3 ? static_cast<int64_t>(KS) * kb : (KIND == 4 ? static_cast<int64_t>(KS / 2) * kb : kb);
+              const int64_t ra = static_cast<int64_t>(mt) * 2 + rank;
+              tc::tma_load_2d_pair(&tma_sfa, bar, sSFA + s * L::kSfaBytes, 0, static_cast<int>(2 * (ra * g.sfa_ncb + kc)));
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              const int64_t rb = static_cast<int64_t>(nt) * 2 + c;
-              tc::tma_load_2d_pair(&tma_sfb, bar, sSFB + s * L::kSfbBytes + c * L::kSfChunkBytes, 0,
-                                   static_cast<int>(2 * (rb * g.sfb_ncb + kc)));
+              for (int c = 0; c < 2; ++c) {
+                const int64_t rb = static_cast<int64_t>(nt) * 2 + c;
+                tc::tma_load_2d_pair(&tma_sfb, bar, sSFB + s * L::kSfbBytes + c * L::kSfChunkBytes, 0,
+                                     static_cast<int>(2 * (rb * g.sfb_ncb + kc)));
+              }
             }
           }
+          __syncwarp();
           if (++s == STAGES) { s = 0; ph ^= 1u; }
         }
       }
-      if (!ok) atomicOr(&g_gemm_status, kDevTimeout);
+      if (!ok && lane == 0) atomicOr(&g_gemm_status, kDevTimeout);
     }
   } else if (warp == 1) {
     if (rank == 0) {  // ---------------------------------------------------- MMA issuer (leader)

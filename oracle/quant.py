@@ -364,10 +364,12 @@ def quantize_fp4_activations(x, fmt="nvfp4", granularity="token"):
     return _fp4_codes(blocks, step), scales, outer
 
 
-def quantize_fp4(weight, fmt="nvfp4", unbiased=False):
+def quantize_fp4(weight, fmt="nvfp4", unbiased=False, amax=None):
     """quant.py:217-272: packed codes, block scale bytes and the fp32 tensor scale
     (``float(amax) / (6 * 448)`` in double, rounded to fp32; 1 for MXFP4); ``unbiased``: the
-    tensor scale times each output channel's :func:`fp4_bias_correction` (fp32 ``[out]``)."""
+    tensor scale times each output channel's :func:`fp4_bias_correction` (fp32 ``[out]``).
+    ``amax``: the whole weight's amax when ``weight`` is a slice of its rows (the tensor scale
+    is the whole weight's, quant.py:253-254)."""
     w = f32(weight)
     if w.ndim != 2:
         raise ValueError(f"expected a 2-D weight [out, in], got shape {tuple(w.shape)}")
@@ -383,7 +385,9 @@ def quantize_fp4(weight, fmt="nvfp4", unbiased=False):
     with np.errstate(**_ERRSTATE):
         bmax = np.abs(blocks).max(axis=-1).astype(F32)
         if fmt == "nvfp4":
-            amax = float(bmax.max()) if bmax.size else 0.0
+            if amax is None:
+                amax = float(bmax.max()) if bmax.size else 0.0
+            amax = float(amax)
             ts = F32(amax / (FP4_MAX * 448.0) if amax > 0 else 1.0)
             div = F32(FP4_MAX * float(ts))
             scales = e4m3_from_f32(np.minimum((bmax / div).astype(F32), F32(448.0)))
