@@ -443,12 +443,22 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t h) {
   if constexpr (T == kBF16) return __uint_as_float(h << 16);
   else return __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
 }
+// (the pairs are register pairs: mov.b64 {lo, hi} costs no instruction)
 __device__ __forceinline__ float2 mul2_rn(float2 a, float b) {
-  unsigned long long r;
-  const unsigned long long av = (static_cast<unsigned long long>(__float_as_uint(a.y)) << 32) | __float_as_uint(a.x);
-  const unsigned long long bv = (static_cast<unsigned long long>(__float_as_uint(b)) << 32) | __float_as_uint(b);
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(av), "l"(bv));
-  return make_float2(__uint_as_float(static_cast<uint32_t>(r)), __uint_as_float(static_cast<uint32_t>(r >> 32)));
+  float2 r;
+  asm("{\n .reg .b64 x, y, z;\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %4};\n mul.rn.f32x2 z, x, y;\n"
+      " mov.b64 {%0, %1}, z;\n}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  float2 r;
+  asm("{\n .reg .b64 x, y, z;\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %5};\n mul.rn.f32x2 z, x, y;\n"
+      " mov.b64 {%0, %1}, z;\n}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
 }
 template <int T>
 __device__ __forceinline__ float2 unpack2(uint32_t w) {
@@ -521,12 +531,8 @@ __device__ __forceinline__ void norm_words(uint32_t (&v)[W], const uint4* __rest
     for (int i = 0; i < 4; ++i) {
       const float2 a = mul2_rn(unpack2<T>(v[4 * c + i]), r);
       const uint32_t xr = pack2_rn<T>(a.x, a.y);
-      const float2 b = unpack2<T>(xr), wv = unpack2<T>(ww[i]);
-      unsigned long long p;
-      const unsigned long long bv = (static_cast<unsigned long long>(__float_as_uint(b.y)) << 32) | __float_as_uint(b.x);
-      const unsigned long long wv2 = (static_cast<unsigned long long>(__float_as_uint(wv.y)) << 32) | __float_as_uint(wv.x);
-      asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(bv), "l"(wv2));
-      v[4 * c + i] = pack2_rn<T>(__uint_as_float(static_cast<uint32_t>(p)), __uint_as_float(static_cast<uint32_t>(p >> 32)));
+      const float2 p = mul2_rn(unpack2<T>(xr), unpack2<T>(ww[i]));
+      v[4 * c + i] = pack2_rn<T>(p.x, p.y);
     }
   }
 }

@@ -706,12 +706,8 @@ def fp4_scale_values(scales: torch.Tensor, fmt: str) -> torch.Tensor:
     return scales.float()
 
 
-def fp4_scale_check(x: torch.Tensor, scales: torch.Tensor, outer: torch.Tensor | float | None = None,
-                    fmt: str | None = None, *, _raw: bool = False) -> dict[str, Any]:
-    """quant.py:1325-1416: how W4A4 activation block scales (unswizzled) fit the block maxima
-    of ``x`` with the given outer scale: ``format``, ``blocks``, ``saturated``, ``share``,
-    ``worst_ratio``, ``underflow``, ``nonfinite``, ``not_representable``, ``coarser`` (one
-    GPU pass)."""
+def _fp4_block_check(x: torch.Tensor, scales: torch.Tensor, outer, fmt: str | None):
+    """One GPU pass of the W4A4 scale-rule check: (its raw counts, the number of blocks, fmt)."""
     k = x.shape[-1]
     x2 = _rows(_input(x))
     rows = x2.shape[0]
@@ -739,10 +735,16 @@ def fp4_scale_check(x: torch.Tensor, scales: torch.Tensor, outer: torch.Tensor |
     nat.call("kab_fp4_scale_check", x2.data_ptr(), nat.dtype_code(x2), rows, k, x2.stride(0) if rows else k,
              nat.KAB_NVFP4 if fmt == "nvfp4" else nat.KAB_MXFP4, s.data_ptr(), nat.ptr(o), per_row,
              out.data_ptr(), _stream(x2))
-    res = _check_result(out)
-    blocks = rows * nb
-    if _raw:
-        return res, blocks
+    return _check_result(out), rows * nb, fmt
+
+
+def fp4_scale_check(x: torch.Tensor, scales: torch.Tensor, outer: torch.Tensor | float | None = None,
+                    fmt: str | None = None) -> dict[str, Any]:
+    """quant.py:1325-1416: how W4A4 activation block scales (unswizzled) fit the block maxima
+    of ``x`` with the given outer scale: ``format``, ``blocks``, ``saturated``, ``share``,
+    ``worst_ratio``, ``underflow``, ``nonfinite``, ``not_representable``, ``coarser`` (one
+    GPU pass)."""
+    res, blocks, fmt = _fp4_block_check(x, scales, outer, fmt)
     return {
         "format": fmt,
         "blocks": blocks,
@@ -1081,7 +1083,7 @@ def fp4_saturation(x: torch.Tensor, scales: torch.Tensor, outer: torch.Tensor, f
     """quant.py:1260-1297: how FP4 activation scales fit the block maxima of ``x`` (one GPU
     pass of the scale check): ``blocks``, ``saturated`` (ratio above 6 x (1 + 2^-20)),
     ``share`` and ``worst_ratio``."""
-    res, blocks = fp4_scale_check(x, scales, outer, fmt, _raw=True)
+    res, blocks, _ = _fp4_block_check(x, scales, outer, fmt)
     sat = int(res.saturated_plain)
     return {
         "blocks": blocks,

@@ -26,3 +26,13 @@ def test_w4a4_fused_peer_stores_match_one_gpu():
     for eq1, d1, eq2, d2 in run_ranks("w4a4_fused_body", world=2, backend="nccl", timeout=300):
         assert eq1, d1
         assert eq2, d2
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_w4a4_fused_peer_stores_with_the_pair_kernel(monkeypatch):
+    """The same with the CTA-pair GEMM forced on (the kernel the large shapes take): its
+    epilogue's TMA stores into the peer's IPC mapping, M = 200 inside one 256-row pair tile."""
+    monkeypatch.setenv("KAB_GEMM_PAIR", "1")  # the spawned ranks inherit it
+    for eq1, d1, eq2, d2 in run_ranks("w4a4_fused_body", world=2, backend="nccl", timeout=300):
+        assert eq1, d1
+        assert eq2, d2
