@@ -155,122 +155,6 @@ __device__ __forceinline__ void cmp_chunk_fast(const KabCompareParams& P, const 
   t.sum[KAB_CMP_SUM_D] += s_d;
 }
 
-// Two fp32 lanes in one 64-bit register (element 0 low) and the packed f32x2 operations of
-// sm_100, each lane rounded to nearest exactly like its scalar form.
-__device__ __forceinline__ unsigned long long pk2(float lo, float hi) {
-  unsigned long long r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void up2(unsigned long long v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ unsigned long long sub2(unsigned long long a, unsigned long long b) {
-  unsigned long long r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigned long long b) {
-  unsigned long long r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
-  unsigned long long r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
-  unsigned long long r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-
-// The fast step of the SIMPLE pass over U raw 16-byte chunks (8 elements each) of 2-byte
-// types, two elements per packed f32x2 instruction: the same arithmetic as cmp_chunk_fast
-// (diff = |a - b|, allowed = atol + rtol * |a| in two roundings, the largest diff / allowed
-// kept as its operands, float partial sums) for the group, speculatively. The group's sum of
-// |diff| is finite exactly when every element of a and b is (an infinite or NaN operand makes
-// its diff infinite or NaN; two finite ones whose difference overflows send the group the
-// slow way too), so one test per group decides: a finite group is added to the thread's
-// totals, any other is redone element by element by the general step. Returns whether the
-// group was taken. POS_ATOL: atol > 0, so allowed > 1e-30 and its clamp is skipped.
-template <int T, int U, bool POS_ATOL>
-__device__ __forceinline__ bool cmp_group_packed(const KabCompareParams& P, const uint4 (&ra)[U], const uint4 (&rb)[U],
-                                                 CmpThread& t) {
-  const unsigned long long atol2 = pk2(P.atol, P.atol), rtol2 = pk2(P.rtol, P.rtol);
-  unsigned long long saa = 0ull, sbb = 0ull, sab = 0ull, sdd = 0ull, sd = 0ull;  // +0.0f pairs
-  float mxd = 0.0f, gbd = 0.0f, gbal = 1.0f, gbds = 0.0f;  // gbds = gbd * (1 - 2^-20): the filter
-  int mism = 0;
-#pragma unroll
-  for (int u = 0; u < U; ++u) {
-    const uint32_t wa[4] = {ra[u].x, ra[u].y, ra[u].z, ra[u].w};
-    const uint32_t wb[4] = {rb[u].x, rb[u].y, rb[u].z, rb[u].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float a0, a1, b0, b1;
-      if constexpr (T == kBF16) {
-        a0 = __uint_as_float(wa[j] << 16);
-        a1 = __uint_as_float(wa[j] & 0xFFFF0000u);
-        b0 = __uint_as_float(wb[j] << 16);
-        b1 = __uint_as_float(wb[j] & 0xFFFF0000u);
-      } else {
-        const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&wa[j]));
-        const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&wb[j]));
-        a0 = fa.x; a1 = fa.y; b0 = fb.x; b1 = fb.y;
-      }
-      const unsigned long long a2 = pk2(a0, a1), b2 = pk2(b0, b1);
-      float d0, d1;
-      up2(sub2(a2, b2), d0, d1);
-      d0 = fabsf(d0);
-      d1 = fabsf(d1);
-      const unsigned long long d2 = pk2(d0, d1);
-      float al0, al1;
-      up2(add2(atol2, mul2(rtol2, pk2(fabsf(a0), fabsf(a1)))), al0, al1);
-      if constexpr (!POS_ATOL) {
-        al0 = fmaxf(al0, 1e-30f);
-        al1 = fmaxf(al1, 1e-30f);
-      }
-      mism += (d0 > al0) + (d1 > al1);
-      // ratio filter for both lanes at once: d * gbal >= gbds * allowed
-      float l0, l1, r0, r1;
-      up2(mul2(d2, pk2(gbal, gbal)), l0, l1);
-      up2(mul2(pk2(gbds, gbds), pk2(al0, al1)), r0, r1);
-      if (l0 >= r0 || l1 >= r1) {
-        if (static_cast<double>(d0) * gbal > static_cast<double>(gbd) * al0) { gbd = d0; gbal = al0; }
-        if (static_cast<double>(d1) * gbal > static_cast<double>(gbd) * al1) { gbd = d1; gbal = al1; }
-        gbds = gbd * 0.99999905f;
-      }
-      mxd = fmaxf(mxd, fmaxf(d0, d1));
-      saa = fma2(a2, a2, saa);
-      sbb = fma2(b2, b2, sbb);
-      sab = fma2(a2, b2, sab);
-      sdd = fma2(d2, d2, sdd);
-      sd = add2(sd, d2);
-    }
-  }
-  float x0, x1;
-  up2(sd, x0, x1);
-  if (!(fabsf(x0 + x1) < INFINITY)) return false;  // a non-finite element: the slow way
-  t.sum[KAB_CMP_SUM_D] += static_cast<double>(x0) + static_cast<double>(x1);
-  up2(saa, x0, x1);
-  t.sum[KAB_CMP_SUM_AA] += static_cast<double>(x0) + static_cast<double>(x1);
-  up2(sbb, x0, x1);
-  t.sum[KAB_CMP_SUM_BB] += static_cast<double>(x0) + static_cast<double>(x1);
-  up2(sab, x0, x1);
-  t.sum[KAB_CMP_SUM_AB] += static_cast<double>(x0) + static_cast<double>(x1);
-  up2(sdd, x0, x1);
-  t.sum[KAB_CMP_SUM_DD] += static_cast<double>(x0) + static_cast<double>(x1);
-  t.mx[KAB_CMP_MAX_D] = fmaxf(t.mx[KAB_CMP_MAX_D], mxd);
-  t.cnt[KAB_CMP_FINITE] += 8 * U;
-  t.cnt[KAB_CMP_MISMATCH] += mism;
-  if (static_cast<double>(gbd) * t.bal > static_cast<double>(t.bd) * gbal) {
-    t.bd = gbd;
-    t.bal = gbal;
-  }
-  return true;
-}
-
 __device__ __forceinline__ bool all_finite8(const float (&a)[8], const float (&b)[8]) {
   bool ok = true;
 #pragma unroll
@@ -280,7 +164,7 @@ __device__ __forceinline__ bool all_finite8(const float (&a)[8], const float (&b
 
 // SIMPLE: no rerounded tensor, alternative bound, widening or element ratio (the first pass
 // of every tier): chunks whose values are all finite take the fast step.
-template <int T, bool SIMPLE, bool POS_ATOL = false>
+template <int T, bool SIMPLE>
 __global__ void __launch_bounds__(256)
 compare_kernel(KabCompareParams P, CmpPartial* __restrict__ partials) {
   __shared__ CmpPartial sm[8];
@@ -301,13 +185,14 @@ compare_kernel(KabCompareParams P, CmpPartial* __restrict__ partials) {
           ra[u] = __ldg(reinterpret_cast<const uint4*>(P.ref) + (c + u * stride));
           rb[u] = __ldg(reinterpret_cast<const uint4*>(P.new_) + (c + u * stride));
         }
-        const bool taken = POS_ATOL ? cmp_group_packed<T, U, true>(P, ra, rb, t)
-                                    : cmp_group_packed<T, U, false>(P, ra, rb, t);
-        if (!taken) {
-          for (int u = 0; u < U; ++u) {
-            float a[8], b[8];
-            unpack8<T>(ra[u], a);
-            unpack8<T>(rb[u], b);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          float a[8], b[8];
+          unpack8<T>(ra[u], a);
+          unpack8<T>(rb[u], b);
+          if (all_finite8(a, b)) {
+            cmp_chunk_fast(P, a, b, t);
+          } else {
             for (int j = 0; j < 8; ++j) cmp_element(P, a[j], b[j], 0.0f, (c + u * stride) * 8 + j, t);
           }
         }

@@ -77,10 +77,8 @@ int kab_compare(const KabCompareParams* params, void* scratch, size_t scratch_by
   const cudaStream_t s = as_stream(stream);
   CmpPartial* partials = static_cast<CmpPartial*>(scratch);
   const bool simple = !P.has_rerounded && !P.alt_bound && P.widen_mode == 0 && P.element_mode == 0;
-  const bool pos_atol = P.atol > 0.0f;  // allowed > 0 everywhere: no clamp in the fast step
-#define KAB_CMP(TT)                                                                   \
-  if (simple && pos_atol) compare_kernel<TT, true, true><<<grid, 256, 0, s>>>(P, partials); \
-  else if (simple) compare_kernel<TT, true><<<grid, 256, 0, s>>>(P, partials);         \
+#define KAB_CMP(TT)                                                        \
+  if (simple) compare_kernel<TT, true><<<grid, 256, 0, s>>>(P, partials);  \
   else compare_kernel<TT, false><<<grid, 256, 0, s>>>(P, partials)
   if (P.dtype == KAB_BF16) { KAB_CMP(kBF16); }
   else if (P.dtype == KAB_F16) { KAB_CMP(kF16); }
