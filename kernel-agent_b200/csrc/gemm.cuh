@@ -391,6 +391,58 @@ __device__ __forceinline__ void epilogue_tile_early(const GemmArgs& g, const Epi
   }
 }
 
+// epilogue_tile_early with 128-byte staged rows: each store is [32 rows, 128 bytes] (64
+// columns of a 2-byte output, 32 of a 4-byte one) in the TMA store's 128-byte swizzle (16-byte
+// chunk i of row r at i ^ (r & 7)), so every row a store writes, to the local output and over
+// NVLink to each peer, is a full 128 bytes (B200: a probe of peer TMA stores moved 570 GB/s
+// with 64-byte rows and 698 GB/s with 128-byte ones). One 4 KB staging buffer per warp: before
+// it is rewritten, the previous store has finished reading it.
+template <int KIND, int OUT, int HC, class Release>
+__device__ __forceinline__ void epilogue_tile_wide(const GemmArgs& g, const EpilogueOperands<KIND, OUT, HC>& ops,
+                                                   const CUtensorMap* tma_out, const PeerMaps* peers, uint32_t tbase,
+                                                   int row0, int colh, uint8_t* stage, int lane, Release release) {
+  constexpr int kPer = out_bytes(OUT) == 2 ? 2 : 1;  // 32-column sub-chunks per 128-byte row
+  static_assert(HC % kPer == 0, "whole 128-byte rows");
+  uint32_t r[HC][32];
+#pragma unroll
+  for (int c = 0; c < HC; ++c) tc::tmem_ld32(tbase + c * 32, r[c]);
+  tc::tmem_ld_wait();
+  tc::fence_before_sync();
+  __syncwarp();
+  if (lane == 0) release();
+  const int sw = lane & 7;
+  uint4* row = reinterpret_cast<uint4*>(stage + lane * 128);
+#pragma unroll
+  for (int c = 0; c < HC; c += kPer) {
+    uint32_t w[32];  // the row's 128 bytes
+#pragma unroll
+    for (int h = 0; h < kPer; ++h) {
+      uint32_t y[32], p[32];
+      epilogue_math<KIND, OUT>(g, r[c + h], ops.sa, ops.cs[c + h], ops.cb[c + h], y);
+      pack_row<OUT>(y, p);
+#pragma unroll
+      for (int i = 0; i < 32 / kPer; ++i) w[h * (32 / kPer) + i] = p[i];
+    }
+    if (lane == 0) tc::bulk_wait_read<0>();  // the previous store has read the buffer
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) row[i ^ sw] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    tc::fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+      tc::tma_store_2d(tma_out, stage, colh + c * 32, row0);
+      if (peers != nullptr) {
+#pragma unroll
+        for (int p = 0; p < kMaxPeers; ++p) {
+          if (p >= g.npeers) break;
+          tc::tma_store_2d(&peers->m[p], stage, colh + c * 32, row0);
+        }
+      }
+      tc::bulk_commit();
+    }
+  }
+}
+
 template <int KIND, int BN, int BKB, int OUT>
 __global__ void __launch_bounds__(GemmLayout<KIND, BN, BKB, OUT>::kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,

@@ -60,8 +60,8 @@ struct PairLayout {
   static constexpr int kSfCol = kAccBufs * kBN;
   static constexpr int kSfSlotsFit = kScaled ? (512 - kSfCol) / kSfColsPerStage : 0;
   static constexpr int kSfSlots = kSfSlotsFit > 5 ? 5 : kSfSlotsFit;
-  static constexpr int kStageOutBytes = 32 * 32 * out_bytes(OUT);
-  static constexpr int kStagingBytes = kEpiWarps * 2 * kStageOutBytes;
+  static constexpr int kStageOutBytes = 32 * 128;  // one [32 rows, 128 bytes] store per warp
+  static constexpr int kStagingBytes = kEpiWarps * kStageOutBytes;
   static_assert(kStagingBytes % 1024 == 0, "the operand tiles after the staging tiles need 1024-byte alignment");
   static constexpr int kSmemLimit = 232448;
   static constexpr int kFixed = 1024 + kStagingBytes + 256;
@@ -286,10 +286,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     const int half = (warp - 2) >> 2;
     const uint32_t lane_base = static_cast<uint32_t>(32 * quarter) << 16;
     const uint32_t acc_empty_leader = tc::mapa(acc_empty, 0);
-    uint8_t* stage0 = sOut + (warp - 2) * 2 * L::kStageOutBytes;
+    uint8_t* stage0 = sOut + (warp - 2) * L::kStageOutBytes;
     int ab = 0;
     uint32_t aph = 0;
-    int chunk = 0;
     for (int t = pair0; t < total; t += npairs) {
       int mt, nt;
       tile_coords(t, g.m_tiles, g.n_tiles, g.group_n, mt, nt);
@@ -304,9 +303,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
       tc::fence_after_sync();
       const uint32_t tbase = tmem + lane_base + ab * BN + half * (BN / 2);
       const uint32_t release_bar = acc_empty_leader + 8 * ab;
-      epilogue_tile_early<KIND, OUT, HC>(g, ops, &tma_out, g.npeers > 0 ? &peers : nullptr, tbase, row0, colh, stage0,
-                                         chunk, lane,
-                                         [release_bar] { tc::mbar_arrive_cluster(release_bar); });
+      epilogue_tile_wide<KIND, OUT, HC>(g, ops, &tma_out, g.npeers > 0 ? &peers : nullptr, tbase, row0, colh, stage0,
+                                        lane, [release_bar] { tc::mbar_arrive_cluster(release_bar); });
       if (++ab == AB) { ab = 0; aph ^= 1u; }
     }
     if (lane == 0) tc::bulk_wait_all();

@@ -59,9 +59,10 @@ int make_map(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols_byt
   return KAB_OK;
 }
 
-// The output [m, n] (row stride ldo elements) written in [32, 32] boxes by TMA stores, from
-// staging tiles swizzled at the width of their rows (64 or 128 bytes).
-int make_out_map(CUtensorMap* map, void* ptr, int out, uint64_t m, uint64_t n, uint64_t ldo) {
+// The output [m, n] (row stride ldo elements) written by TMA stores from staging tiles swizzled
+// at the width of their rows: [32 rows, 32 columns] boxes (the one-CTA kernel's stores; 64- or
+// 128-byte rows), or with `wide` [32 rows, 128 bytes] boxes (the pair kernel's).
+int make_out_map(CUtensorMap* map, void* ptr, int out, uint64_t m, uint64_t n, uint64_t ldo, bool wide = false) {
   auto fn = encode_fn();
   if (fn == nullptr) return fail(KAB_EUNSUPPORTED, "cuTensorMapEncodeTiled is unavailable (driver too old?)");
   const CUtensorMapDataType dt = out == KAB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -70,10 +71,10 @@ int make_out_map(CUtensorMap* map, void* ptr, int out, uint64_t m, uint64_t n, u
                                                   : CU_TENSOR_MAP_DATA_TYPE_INT32;
   cuuint64_t dims[2] = {n, m};
   cuuint64_t strides[1] = {ldo * static_cast<uint64_t>(out_bytes(out))};
-  cuuint32_t box[2] = {32, 32};
+  cuuint32_t box[2] = {wide ? 128u / out_bytes(out) : 32u, 32};
   cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, dt, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        out_bytes(out) == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        (wide || out_bytes(out) == 4) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                         CU_TENSOR_MAP_L2_PROMOTION_NONE,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(KAB_EINVAL, "tensor map of the output failed (CUresult %d)", static_cast<int>(r));
@@ -277,7 +278,7 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
     CUtensorMap ma, mb, msa, msb, mo;
     if (int e = make_map(&ma, a, m, k_bytes, k_bytes, 128, bkb, "A")) return e;
     if (int e = make_map(&mb, b, n, k_bytes, k_bytes, 128, bkb, "B")) return e;
-    if (int e = make_out_map(&mo, out, out_dtype, m, n, g.ldo)) return e;
+    if (int e = make_out_map(&mo, out, out_dtype, m, n, g.ldo, true)) return e;
     msa = ma;
     msb = mb;
     if constexpr (GemmTraits<KIND>::kScaled) {
@@ -290,7 +291,7 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
     }
     PeerMaps pm{};
     for (int p = 0; p < g.npeers; ++p)
-      if (int e = make_out_map(&pm.m[p], g.peer_out[p], out_dtype, m, n, g.ldo)) return e;
+      if (int e = make_out_map(&pm.m[p], g.peer_out[p], out_dtype, m, n, g.ldo, true)) return e;
     return launch_pair<KIND>(out_dtype, ma, mb, msa, msb, mo, g, pm, s);
   }
   // one-CTA tiles, width 256 (two 256-column accumulators) for int8 / fp8; the block-scaled
