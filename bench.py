@@ -781,7 +781,7 @@ class Fp8Blockwise(Workload):
         self.ws_ = [(self.wq.clone(), self.ws.clone()) for _ in range(self.copies)]
         self.xq_ = [blockwise.quantize_fp8_groups(t) for t in self.xs_]
         self.units = 2.0 * m * n * k / 1e12
-        self.kernel = "gemm_blockwise_kernel" if m > 32 else "gemm_blockwise_kernel (decode size)"
+        self.kernel = "gemm_blockwise_kernel" if m > 32 else "gemm_blockwise_skinny_kernel (cluster split-K)"
         self.kernel_bytes = m * k + 4 * m * (k // 128) + n * k + 4 * (n // 128) * (k // 128) + m * n * 2
         self.kernel_units = self.kernel_bytes if self.bound == "hbm" else 2.0 * m * n * k
         self.h2d = m * k * 2

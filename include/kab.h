@@ -416,16 +416,18 @@ int kab_diff_census(const KabDiffParams* params, unsigned long long* count, void
 
 /* Per-head e4m3 quantisation of x [heads, seq, d] (docs/research-scripts/fp8-sm120/
  * fp8lib.py:173-176 _fq_last2: scale = amax / 448 per head, 0 -> 1; codes e4m3(x / scale)):
- * q [heads, seq, d], or [heads, d, seq] with `transpose` (the V^T operand of the attention),
- * scales fp32 [heads]. `amax`: [heads] words of device scratch (reset here). */
+ * q [heads, seq, d], or with `transpose` [heads, d, seq16] (the V^T operand of the attention;
+ * seq16 = seq rounded up to a multiple of 16, the columns past seq written as zeros), scales
+ * fp32 [heads]. `amax`: [heads] words of device scratch (reset here). */
 int kab_quant_heads_fp8(const void* x, int dtype, int64_t heads, int64_t seq, int64_t d,
                         int transpose, unsigned* amax, uint8_t* q, float* scales, void* stream);
 
 /* FP8 attention prefill (fp8lib.py:184-215 emulated_sdpa, mode "qkpv"): e4m3 Q [batch,
- * heads_q, seq, 128], K [batch, heads_kv, seq, 128], V^T [batch, heads_kv, 128, seq] with one
+ * heads_q, seq, 128], K [batch, heads_kv, seq, 128], V^T [batch, heads_kv, 128, seq16] with one
  * fp32 scale per (batch, head); S = Q K^T * scale, causal mask, online softmax with P as
  * e4m3(p * 448) / 448, out = (P V) / rowsum in bf16 [batch, heads_q, seq, 128]. GQA by head
- * index (heads_q % heads_kv == 0); seq % 128 == 0. */
+ * index (heads_q % heads_kv == 0); any seq (keys past it in the last 128-row tile are masked,
+ * V^T's row stride seq16 as kab_quant_heads_fp8 writes it). */
 int kab_attention_fp8(const uint8_t* q, const float* q_scale, const uint8_t* k, const float* k_scale,
                       const uint8_t* vt, const float* v_scale, int64_t batch, int64_t heads_q,
                       int64_t heads_kv, int64_t seq, int64_t head_dim, int causal, float sm_scale,

@@ -7,9 +7,11 @@
 //  * quant_heads kernels: the per-head amax (one atomic max of the bits per block) and the
 //    codes, row-major [S, D] for Q and K, transposed [D, S] for V so that V^T is the
 //    K-major B operand of the P V product.
-//  * attention_fp8_kernel: one CTA per 128-query tile. Warp 0 loads Q once and K / V^T tiles
-//    of 128 keys through a 3-stage TMA ring; warp 1 issues the tcgen05 MMAs (kind::f8f6f4):
-//    S_j = Q K_j^T into one of two 128-column TMEM buffers, then O += P_j V_j into a third;
+//  * attention_fp8_kernel: one CTA per 128-query tile, two CTAs per SM (256 TMEM columns and
+//    ~97 KB of shared memory each), so the softmax of one CTA runs while the other's MMAs do.
+//    Warp 0 loads Q once and K / V^T tiles of 128 keys through a 2-stage TMA ring; warp 1
+//    issues the tcgen05 MMAs (kind::f8f6f4): S_j = Q K_j^T into a 128-column TMEM buffer
+//    (released as soon as the softmax has read it), then O += P_j V_j into a second;
 //    warps 2-5 (one query row per thread) run the online softmax in the exp2 domain: a
 //    running row max m raised only when a tile's max exceeds it by more than 3 (so
 //    p = 2^(t - m) <= 8), the row sum of the unrounded codes' values, P as e4m3(p * 448 / 8)
@@ -59,8 +61,9 @@ __device__ __forceinline__ float head_scale(unsigned amax_bits) {
   return s > 0.0f ? s : 1.0f;
 }
 
-// Codes of a [64 rows, D] tile of one head: grid (S / 64, heads), 256 threads. TRANSPOSE
-// writes the tile into [D, S] (column block s0 .. s0 + 63 of each of the D rows).
+// Codes of a [64 rows, D] tile of one head: grid (ceil(S / 64), heads), 256 threads. TRANSPOSE
+// writes the tile into [D, S16] (S16 = S rounded up to 16, the columns past S zero: the row
+// stride a TMA map needs), column block s0 .. s0 + 63 of each of the D rows.
 template <int T, bool TRANSPOSE>
 __global__ void __launch_bounds__(256)
 quant_heads_kernel(const void* __restrict__ x, int64_t seq, int d, const unsigned* __restrict__ amax,
@@ -75,7 +78,10 @@ quant_heads_kernel(const void* __restrict__ x, int64_t seq, int d, const unsigne
   const int total = 64 * cpr;
   for (int c = threadIdx.x; c < total; c += blockDim.x) {
     const int r = c / cpr, col = (c % cpr) * 8;
-    if (s0 + r >= seq) continue;
+    if (s0 + r >= seq) {
+      if constexpr (TRANSPOSE) *reinterpret_cast<uint2*>(tile + r * d + col) = make_uint2(0u, 0u);
+      continue;
+    }
     float v[8], qv[8];
     load8<T>(x, (head * seq + s0 + r) * d + col, v);
     quotients<kLowE4m3>(v, div, qv);
@@ -85,7 +91,8 @@ quant_heads_kernel(const void* __restrict__ x, int64_t seq, int d, const unsigne
   }
   if constexpr (TRANSPOSE) {
     __syncthreads();
-    // [D, S]: row dd gets the tile's 64 codes of column dd, 16 at a time
+    // [D, S16]: row dd gets the tile's 64 codes of column dd, 16 at a time
+    const int64_t ld = (seq + 15) / 16 * 16;
     for (int c = threadIdx.x; c < d * 4; c += blockDim.x) {
       const int dd = c >> 2, part = c & 3;
       uint32_t w[4];
@@ -97,8 +104,7 @@ quant_heads_kernel(const void* __restrict__ x, int64_t seq, int d, const unsigne
         w[i] = word;
       }
       const int64_t col = s0 + part * 16;
-      if (col + 16 <= seq)
-        *reinterpret_cast<uint4*>(q + (head * d + dd) * seq + col) = make_uint4(w[0], w[1], w[2], w[3]);
+      if (col < ld) *reinterpret_cast<uint4*>(q + (head * d + dd) * ld + col) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 }
@@ -106,27 +112,35 @@ quant_heads_kernel(const void* __restrict__ x, int64_t seq, int d, const unsigne
 // ------------------------------------------------------------------ attention
 
 struct AttnArgs {
-  int seq;            // keys = queries, a multiple of 128
+  int seq;            // keys = queries (any length: the last tile's keys past it are masked)
   int heads_q, heads_kv;
-  int q_tiles;        // seq / 128
+  int q_tiles;        // ceil(seq / 128)
   int causal;
   const float* q_scale;  // [batch * heads_q]
   const float* k_scale;  // [batch * heads_kv]
   const float* v_scale;
   float sm_scale_log2;   // softmax scale * log2(e)
-  void* out;             // [batch, heads_q, seq, 128] bf16
+  void* out;             // [batch, heads_q, seq, D] bf16
 };
 
+// Shared memory of one CTA for head dimension D (128 or 64): Q and the K ring hold
+// [128 tokens, D] tiles (rows of D bytes, swizzled at D bytes), the V^T ring [D, 128 keys]
+// tiles and P one [128, 128] tile (rows of 128 bytes, the 128-byte swizzle).
+template <int D>
 struct AttnLayout {
-  static constexpr int kTile = 128 * 128;  // bytes of a 128 x 128 e4m3 tile
-  static constexpr int kStages = 3;
+  static_assert(D == 128 || D == 64, "head_dim 128 or 64");
+  static constexpr int kQKTile = 128 * D;
+  static constexpr int kVTile = D * 128;
+  static constexpr int kPTile = 128 * 128;
+  static constexpr int kStages = 2;
   static constexpr int kThreads = 192;
   static constexpr int kQ = 0;
-  static constexpr int kK = kQ + kTile;
-  static constexpr int kV = kK + kStages * kTile;
-  static constexpr int kP = kV + kStages * kTile;
-  static constexpr int kBars = kP + 2 * kTile;
-  static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 2 + 1;
+  static constexpr int kK = kQ + kQKTile;
+  static constexpr int kV = kK + kStages * kQKTile;
+  static constexpr int kP = kV + kStages * kVTile;
+  static constexpr int kBars = kP + kPTile;
+  static constexpr int kNumBars = 1 + 4 * kStages + 4 + 1;
+  static constexpr int kTmemCols = 256;  // S at column 0, O (D columns) at 128
   static constexpr int kSmem = 1024 + kBars + kNumBars * 8 + 16;
 };
 
@@ -142,10 +156,13 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity));
 }
 
-__global__ void __launch_bounds__(AttnLayout::kThreads, 1)
+template <int D>
+__global__ void __launch_bounds__(AttnLayout<D>::kThreads, 2)
 attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_constant__ CUtensorMap tma_k,
                      const __grid_constant__ CUtensorMap tma_vt, AttnArgs g) {
-  using L = AttnLayout;
+  using L = AttnLayout<D>;
+  constexpr int kChunks = D / 32;  // 32-column TMEM loads of O
+  auto qk_desc = [](uint32_t a) { return D == 128 ? tc::desc_sw128(a) : tc::desc_sw64(a); };
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + L::kQ;
@@ -154,13 +171,18 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
   uint8_t* sP = smem + L::kP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBars);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + L::kStages;
-  uint64_t* s_full = kv_empty + L::kStages;  // [2]
-  uint64_t* s_empty = s_full + 2;            // [2], 4 softmax warps
-  uint64_t* p_full = s_empty + 2;            // [2], 4 softmax warps
-  uint64_t* p_empty = p_full + 2;            // [2]
-  uint64_t* drain = p_empty + 2;
+  // K and V tiles have their own ring barriers: K_j's slot is free once S_j is computed, so the
+  // next K loads while the softmax of tile j runs, V's once P_j V_j is
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + L::kStages;
+  uint64_t* v_full = k_empty + L::kStages;
+  uint64_t* v_empty = v_full + L::kStages;
+  // one S buffer and one P buffer; use j of each completes phase j (parity j & 1)
+  uint64_t* s_full = v_empty + L::kStages;
+  uint64_t* s_empty = s_full + 1;  // 4 softmax warps
+  uint64_t* p_full = s_empty + 1;  // 4 softmax warps
+  uint64_t* p_empty = p_full + 1;
+  uint64_t* drain = p_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   // heavy (long causal) tiles first
@@ -175,15 +197,15 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
   if (threadIdx.x == 0) {
     tc::mbar_init(q_full, 1);
     for (int s = 0; s < L::kStages; ++s) {
-      tc::mbar_init(&kv_full[s], 1);
-      tc::mbar_init(&kv_empty[s], 1);
+      tc::mbar_init(&k_full[s], 1);
+      tc::mbar_init(&k_empty[s], 1);
+      tc::mbar_init(&v_full[s], 1);
+      tc::mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(&s_full[i], 1);
-      tc::mbar_init(&s_empty[i], 4);
-      tc::mbar_init(&p_full[i], 4);
-      tc::mbar_init(&p_empty[i], 1);
-    }
+    tc::mbar_init(s_full, 1);
+    tc::mbar_init(s_empty, 4);
+    tc::mbar_init(p_full, 4);
+    tc::mbar_init(p_empty, 1);
     tc::mbar_init(drain, 1);
     tc::fence_barrier_init();
   }
@@ -192,65 +214,75 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
     tc::prefetch_tensormap(&tma_k);
     tc::prefetch_tensormap(&tma_vt);
   }
-  if (warp == 1) { tc::tmem_alloc(tmem_slot, 512); tc::tmem_relinquish(); }
+  if (warp == 1) { tc::tmem_alloc(tmem_slot, L::kTmemCols); tc::tmem_relinquish(); }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 256;  // S buffers at columns 0 and 128, O at 256
+  const uint32_t tS = tmem, tO = tmem + 128;  // S at column 0, O at 128
 
   if (warp == 0) {
-    if (lane == 0) {  // ---------------------------------------------------- TMA producer
+    if (lane < 2) {  // --------------------------- TMA producers: lane 0 Q and K tiles, lane 1 V^T tiles
       bool ok = true;
-      tc::mbar_arrive_expect_tx(q_full, L::kTile);
-      tc::tma_load_2d(&tma_q, q_full, sQ, 0, bh * g.seq + qt * 128);
+      const bool is_k = lane == 0;
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      uint8_t* dst = is_k ? sK : sV;
+      const int tile = is_k ? L::kQKTile : L::kVTile;
+      if (is_k) {
+        tc::mbar_arrive_expect_tx(q_full, L::kQKTile);
+        tc::tma_load_2d(&tma_q, q_full, sQ, 0, bh * g.seq + qt * 128);
+      }
       int issued = 0;
       for (int j = 0; j < n_kv; ++j) {
         const int s = j % L::kStages;
         const uint32_t ph = static_cast<uint32_t>((j / L::kStages) & 1);
-        if (!tc::mbar_wait(&kv_empty[s], ph ^ 1u)) { ok = false; break; }
-        tc::mbar_arrive_expect_tx(&kv_full[s], 2 * L::kTile);
-        tc::tma_load_2d(&tma_k, &kv_full[s], sK + s * L::kTile, 0, bhk * g.seq + j * 128);
-        tc::tma_load_2d(&tma_vt, &kv_full[s], sV + s * L::kTile, j * 128, bhk * 128);
+        if (!tc::mbar_wait(&empty[s], ph ^ 1u)) { ok = false; break; }
+        tc::mbar_arrive_expect_tx(&full[s], tile);
+        if (is_k) tc::tma_load_2d(&tma_k, &full[s], dst + s * tile, 0, bhk * g.seq + j * 128);
+        else tc::tma_load_2d(&tma_vt, &full[s], dst + s * tile, j * 128, bhk * D);
         issued = j + 1;
       }
       if (!ok) {
         atomicOr(&g_attention_status, kDevTimeout);
-        tc::mbar_wait(q_full, 0);
+        if (is_k) tc::mbar_wait(q_full, 0);
         for (int j = (issued > L::kStages ? issued - L::kStages : 0); j < issued; ++j)
-          tc::mbar_wait(&kv_full[j % L::kStages], static_cast<uint32_t>((j / L::kStages) & 1));
+          tc::mbar_wait(&full[j % L::kStages], static_cast<uint32_t>((j / L::kStages) & 1));
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---------------------------------------------------- MMA issuer
       bool ok = tc::mbar_wait(q_full, 0);
-      const uint32_t idesc = tc::idesc_f8(128, 128);
-      const uint64_t qdesc = tc::desc_sw128(tc::smem_u32(sQ));
+      const uint32_t idesc = tc::idesc_f8(128, 128);  // S = Q K^T: 128 x 128, K = D
+      const uint32_t idesc_pv = tc::idesc_f8(128, D);  // O += P V: 128 x D, K = 128 keys
+      const uint64_t qdesc = qk_desc(tc::smem_u32(sQ));
       auto issue_pv = [&](int t) -> bool {
-        if (!tc::mbar_wait(&p_full[t & 1], static_cast<uint32_t>((t >> 1) & 1))) return false;
-        tc::fence_after_sync();
+        if (!tc::mbar_wait(p_full, static_cast<uint32_t>(t & 1))) return false;
         const int s = t % L::kStages;
-        const uint64_t pdesc = tc::desc_sw128(tc::smem_u32(sP + (t & 1) * L::kTile));
-        const uint64_t vdesc = tc::desc_sw128(tc::smem_u32(sV + s * L::kTile));
+        if (!tc::mbar_wait(&v_full[s], static_cast<uint32_t>((t / L::kStages) & 1))) return false;
+        tc::fence_after_sync();
+        const uint64_t pdesc = tc::desc_sw128(tc::smem_u32(sP));
+        const uint64_t vdesc = tc::desc_sw128(tc::smem_u32(sV + s * L::kVTile));
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          tc::mma_f8(tO, pdesc + static_cast<uint64_t>(2 * kk), vdesc + static_cast<uint64_t>(2 * kk), idesc,
+          tc::mma_f8(tO, pdesc + static_cast<uint64_t>(2 * kk), vdesc + static_cast<uint64_t>(2 * kk), idesc_pv,
                      (t > 0 || kk > 0) ? 1u : 0u);
-        tc::commit(&p_empty[t & 1]);
-        tc::commit(&kv_empty[s]);
+        tc::commit(p_empty);
+        tc::commit(&v_empty[s]);
         return true;
       };
       for (int j = 0; ok && j < n_kv; ++j) {
         const int s = j % L::kStages;
-        if (!tc::mbar_wait(&kv_full[s], static_cast<uint32_t>((j / L::kStages) & 1))) { ok = false; break; }
-        if (!tc::mbar_wait(&s_empty[j & 1], static_cast<uint32_t>(((j >> 1) & 1) ^ 1))) { ok = false; break; }
+        if (!tc::mbar_wait(&k_full[s], static_cast<uint32_t>((j / L::kStages) & 1))) { ok = false; break; }
+        if (!tc::mbar_wait(s_empty, static_cast<uint32_t>((j & 1) ^ 1))) { ok = false; break; }
         tc::fence_after_sync();
-        const uint64_t kdesc = tc::desc_sw128(tc::smem_u32(sK + s * L::kTile));
+        const uint64_t kdesc = qk_desc(tc::smem_u32(sK + s * L::kQKTile));
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          tc::mma_f8(tS + (j & 1) * 128, qdesc + static_cast<uint64_t>(2 * kk), kdesc + static_cast<uint64_t>(2 * kk),
-                     idesc, kk > 0 ? 1u : 0u);
-        tc::commit(&s_full[j & 1]);
+        for (int kk = 0; kk < D / 32; ++kk)
+          tc::mma_f8(tS, qdesc + static_cast<uint64_t>(2 * kk), kdesc + static_cast<uint64_t>(2 * kk), idesc,
+                     kk > 0 ? 1u : 0u);
+        tc::commit(s_full);
+        tc::commit(&k_empty[s]);
         if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
       }
       if (ok && !issue_pv(n_kv - 1)) ok = false;
@@ -273,13 +305,13 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!warp_wait(&s_full[j & 1], static_cast<uint32_t>((j >> 1) & 1))) { ok = false; break; }
+      if (!warp_wait(s_full, static_cast<uint32_t>(j & 1))) { ok = false; break; }
       tc::fence_after_sync();
       float sv[128];
       {  // the four loads in flight together, one wait
         uint32_t raw[4][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tc::tmem_ld32(tS + lane_base + (j & 1) * 128 + c * 32, raw[c]);
+        for (int c = 0; c < 4; ++c) tc::tmem_ld32(tS + lane_base + c * 32, raw[c]);
         tc::tmem_ld_wait();
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -288,10 +320,15 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
       }
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&s_empty[j & 1]);
+      if (lane == 0) tc::mbar_arrive(s_empty);
       if (g.causal && j == qt) {  // keys after the query: -inf
 #pragma unroll
         for (int i = 0; i < 128; ++i) sv[i] = i > r ? -INFINITY : sv[i];
+      }
+      if (j == g.q_tiles - 1 && (g.seq & 127)) {  // keys past the sequence (a ragged last tile): -inf
+        const int valid = g.seq - j * 128;
+#pragma unroll
+        for (int i = 0; i < 128; ++i) sv[i] = i >= valid ? -INFINITY : sv[i];
       }
       float mxs[8];  // eight independent chains, then a tree
 #pragma unroll
@@ -317,23 +354,22 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
       const float rowsum = (sums[0] + sums[1]) + (sums[2] + sums[3]);
       l_run = l_run * alpha + rowsum;
       m_run = m_new;
-      // P_j into its buffer once P V_{j-2} has read it: row r, 16-byte chunk c at c ^ (r % 8)
-      if (!warp_wait(&p_empty[j & 1], static_cast<uint32_t>(((j >> 1) & 1) ^ 1))) { ok = false; break; }
-      uint8_t* prow = sP + (j & 1) * L::kTile + r * 128;
+      // P_j into the buffer once P V_{j-1} has read it (and landed in O): row r, 16-byte chunk
+      // c at c ^ (r % 8)
+      if (!warp_wait(p_empty, static_cast<uint32_t>((j & 1) ^ 1))) { ok = false; break; }
+      uint8_t* prow = sP + r * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c)
         *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
             make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
       tc::fence_proxy_async();
-      // O holds P V up to tile j - 1: rescale it when a row's max moved. P V_{j-1} has landed
-      // once p_empty[(j - 1) & 1] completes its phase (j - 1) >> 1; this warp waited for the
-      // phase before it at tile j - 1, so the parity wait is exact.
+      // O holds P V up to tile j - 1 (landed: the wait for the P buffer above): rescale it when
+      // a row's max moved
       if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-        if (!warp_wait(&p_empty[(j - 1) & 1], static_cast<uint32_t>(((j - 1) >> 1) & 1))) { ok = false; break; }
         tc::fence_after_sync();
         {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < kChunks; ++c) {
             uint32_t o[32];
             tc::tmem_ld32(tO + lane_base + c * 32, o);
             tc::tmem_ld_wait();
@@ -350,17 +386,18 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
       }
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&p_full[j & 1]);
+      if (lane == 0) tc::mbar_arrive(p_full);
     }
-    // the last P V (the same exact wait as the rescale's), then O / rowsum * v_scale in bf16
-    // (the code scale cancels)
-    if (ok && !warp_wait(&p_empty[(n_kv - 1) & 1], static_cast<uint32_t>(((n_kv - 1) >> 1) & 1))) ok = false;
-    if (ok) {
+    // the last P V, then O / rowsum * v_scale in bf16 (the code scale cancels)
+    if (ok && !warp_wait(p_empty, static_cast<uint32_t>((n_kv - 1) & 1))) ok = false;
+    if (ok) {  // (every lane loads: the TMEM loads are warp-wide; rows past a ragged sequence
+               // are not stored)
       tc::fence_after_sync();
+      const bool store = qrow < g.seq;
       const float f = g.v_scale[bhk] / l_run;
-      __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(g.out) + (static_cast<int64_t>(bh) * g.seq + qrow) * 128;
+      __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(g.out) + (static_cast<int64_t>(bh) * g.seq + qrow) * D;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < kChunks; ++c) {
         uint32_t o[32];
         tc::tmem_ld32(tO + lane_base + c * 32, o);
         tc::tmem_ld_wait();
@@ -370,9 +407,11 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
           const __nv_bfloat162 hv = __floats2bfloat162_rn(__uint_as_float(o[2 * i]) * f, __uint_as_float(o[2 * i + 1]) * f);
           w[i] = *reinterpret_cast<const uint32_t*>(&hv);
         }
+        if (store) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          reinterpret_cast<uint4*>(orow + c * 32)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          for (int i = 0; i < 4; ++i)
+            reinterpret_cast<uint4*>(orow + c * 32)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
       }
     } else if (lane == 0) {
       atomicOr(&g_attention_status, kDevTimeout);
@@ -383,7 +422,7 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
   if (warp == 1) {
     __syncwarp();
     tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, 512);
+    tc::tmem_dealloc(tmem, L::kTmemCols);
   }
 }
 

@@ -44,17 +44,20 @@ PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
   return fn;
 }
 
-// A [rows, cols] byte matrix read in 128 x 128-byte boxes with the 128-byte swizzle.
-int byte_map(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, const char* name) {
+// A [rows, cols] byte matrix read in boxes of box_rows x box_cols bytes (box_cols 128 or 64),
+// swizzled at the box's row length like the MMA operands.
+int byte_map(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, const char* name,
+             uint32_t box_cols = 128, uint32_t box_rows = 128) {
   auto fn = attn_encode_fn();
   if (fn == nullptr) return fail(KAB_EUNSUPPORTED, "cuTensorMapEncodeTiled is unavailable (driver too old?)");
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {cols};
-  cuuint32_t box[2] = {128, 128};
+  cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        box_cols == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(KAB_EINVAL, "tensor map of %s failed (CUresult %d)", name, static_cast<int>(r));
   return KAB_OK;
 }
@@ -239,6 +242,23 @@ int launch_decode_t(const CUtensorMap& mk, const CUtensorMap& mv, const DecodeAr
   return check_launch("kab_kv_decode_fp8 (cluster)");
 }
 
+template <int D>
+int launch_attention(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnArgs& g,
+                     int64_t ctas, void* stream) {
+  using L = AttnLayout<D>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(attention_fp8_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem) !=
+        cudaSuccess)
+      return fail(KAB_ECUDA, "cannot set %d bytes of shared memory", L::kSmem);
+    configured[dev] = true;
+  }
+  attention_fp8_kernel<D><<<static_cast<unsigned>(ctas), L::kThreads, L::kSmem, as_stream(stream)>>>(mq, mk, mv, g);
+  return check_launch("kab_attention_fp8");
+}
+
 }  // namespace
 }  // namespace kab
 
@@ -254,7 +274,6 @@ int kab_quant_heads_fp8(const void* x, int dtype, int64_t heads, int64_t seq, in
   KAB_REQUIRE(x != nullptr && amax != nullptr && q != nullptr && scales != nullptr, "null pointer");
   KAB_REQUIRE(aligned(x, 16) && aligned(q, 16), "x and q must be 16-byte aligned");
   KAB_REQUIRE(d % 8 == 0 && d <= 256, "head_dim %lld must be a multiple of 8, at most 256", (long long)d);
-  KAB_REQUIRE(!transpose || seq % 64 == 0, "the transposed layout needs seq a multiple of 64");
   KAB_REQUIRE(heads < 65536, "too many heads (%lld)", (long long)heads);
   const cudaStream_t s = as_stream(stream);
   if (cudaMemsetAsync(amax, 0, heads * sizeof(unsigned), s) != cudaSuccess) return check_launch("amax reset");
@@ -285,40 +304,33 @@ int kab_attention_fp8(const uint8_t* q, const float* q_scale, const uint8_t* k, 
   if (batch == 0 || heads_q == 0 || seq == 0) return KAB_OK;
   KAB_REQUIRE(q && k && vt && q_scale && k_scale && v_scale && out, "null pointer");
   KAB_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(vt, 16) && aligned(out, 16), "pointers must be 16-byte aligned");
-  KAB_REQUIRE(head_dim == 128, "head_dim %lld: the kernel takes 128", (long long)head_dim);
-  KAB_REQUIRE(seq % 128 == 0, "seq %lld must be a multiple of 128", (long long)seq);
+  KAB_REQUIRE(head_dim == 128 || head_dim == 64, "head_dim %lld: the kernel takes 128 or 64", (long long)head_dim);
   KAB_REQUIRE(heads_kv > 0 && heads_q % heads_kv == 0, "heads_q %lld is not a multiple of heads_kv %lld",
               (long long)heads_q, (long long)heads_kv);
-  const int64_t ctas = batch * heads_q * (seq / 128);
+  const int64_t q_tiles = (seq + 127) / 128;
+  const int64_t ld_vt = (seq + 15) / 16 * 16;  // V^T rows: seq rounded up to 16 (kab_quant_heads_fp8)
+  const int64_t ctas = batch * heads_q * q_tiles;
   KAB_REQUIRE(ctas < (int64_t(1) << 31) && batch * heads_q * seq < (int64_t(1) << 31), "problem too large");
+  const uint32_t d = static_cast<uint32_t>(head_dim);
   CUtensorMap mq, mk, mv;
-  if (int e = byte_map(&mq, q, static_cast<uint64_t>(batch * heads_q * seq), 128, "Q")) return e;
-  if (int e = byte_map(&mk, k, static_cast<uint64_t>(batch * heads_kv * seq), 128, "K")) return e;
-  if (int e = byte_map(&mv, vt, static_cast<uint64_t>(batch * heads_kv * 128), static_cast<uint64_t>(seq), "V^T"))
+  if (int e = byte_map(&mq, q, static_cast<uint64_t>(batch * heads_q * seq), d, "Q", d, 128)) return e;
+  if (int e = byte_map(&mk, k, static_cast<uint64_t>(batch * heads_kv * seq), d, "K", d, 128)) return e;
+  if (int e = byte_map(&mv, vt, static_cast<uint64_t>(batch * heads_kv * head_dim), static_cast<uint64_t>(ld_vt),
+                       "V^T", 128, d))
     return e;
   AttnArgs g{};
   g.seq = static_cast<int>(seq);
   g.heads_q = static_cast<int>(heads_q);
   g.heads_kv = static_cast<int>(heads_kv);
-  g.q_tiles = static_cast<int>(seq / 128);
+  g.q_tiles = static_cast<int>(q_tiles);
   g.causal = causal;
   g.q_scale = q_scale;
   g.k_scale = k_scale;
   g.v_scale = v_scale;
   g.sm_scale_log2 = sm_scale * 1.4426950408889634f;
   g.out = out;
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(attention_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnLayout::kSmem) !=
-        cudaSuccess)
-      return fail(KAB_ECUDA, "cannot set %d bytes of shared memory", AttnLayout::kSmem);
-    configured[dev] = true;
-  }
-  attention_fp8_kernel<<<static_cast<unsigned>(ctas), AttnLayout::kThreads, AttnLayout::kSmem, as_stream(stream)>>>(
-      mq, mk, mv, g);
-  return check_launch("kab_attention_fp8");
+  return head_dim == 128 ? launch_attention<128>(mq, mk, mv, g, ctas, stream)
+                          : launch_attention<64>(mq, mk, mv, g, ctas, stream);
 }
 
 int kab_quant_kv_fp8(const void* x, int dtype, int64_t outer, int64_t inner, int64_t d, int64_t xs_o, int64_t xs_i,

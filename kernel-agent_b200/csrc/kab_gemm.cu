@@ -327,6 +327,50 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
   return launch_out<KIND, 128>(out_dtype, ma, mb, mo, g, pm, s);
 }
 
+// Whether the decode-size blockwise GEMM's CTAs, as many as fit an SM by shared memory and
+// threads, can all hold their TMEM at once (a CTA that waited for TMEM held by a cluster peer
+// on the same SM would wait forever).
+bool blockwise_skinny_fits(int64_t m, int per) {
+  const bool small = m <= 16;
+  const int smem = small ? BlockwiseSkinnyLayout<16>::smem(per) : BlockwiseSkinnyLayout<32>::smem(per);
+  const uint32_t cols = small ? BlockwiseSkinnyLayout<16>::tmem_cols(per) : BlockwiseSkinnyLayout<32>::tmem_cols(per);
+  const int by_smem = (228 * 1024) / (smem + 1024);
+  const int by_threads = 2048 / BlockwiseSkinnyLayout<16>::kThreads;
+  const int resident = by_smem < by_threads ? by_smem : by_threads;
+  return resident >= 1 && static_cast<uint32_t>(resident) * cols <= 512u;
+}
+
+// The decode-size blockwise GEMM (M <= 32): one cluster of `csize` CTAs per 128-channel panel.
+template <int NT, int OUT>
+int launch_blockwise_skinny(const CUtensorMap& mw, const CUtensorMap& mx, const BlockwiseSkinnyArgs& g, int csize,
+                            cudaStream_t s) {
+  using L = BlockwiseSkinnyLayout<NT>;
+  auto kernel = gemm_blockwise_skinny_kernel<NT, OUT>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int max_smem = L::smem(L::kMaxPer);
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) != cudaSuccess)
+      return fail(KAB_ECUDA, "cannot set %d bytes of shared memory", max_smem);
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(g.n / 128 * csize));
+  cfg.blockDim = dim3(L::kThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(L::smem(g.per));
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = static_cast<unsigned>(csize);
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kernel, mw, mx, g) != cudaSuccess) return check_launch("blockwise gemm (decode size)");
+  return check_launch("blockwise gemm (decode size)");
+}
+
 template <int OUT>
 int launch_blockwise(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const BlockwiseArgs& g,
                      cudaStream_t s) {
@@ -479,10 +523,43 @@ int kab_gemm_f8_blockwise(const uint8_t* a, const float* a_scale, const uint8_t*
   KAB_REQUIRE(out != nullptr && aligned(out, 16), "output is null or not 16-byte aligned");
   KAB_REQUIRE(ldo >= n && ldo % 8 == 0, "ldo %lld must be >= n and a multiple of 8", (long long)ldo);
   KAB_REQUIRE(m <= (int64_t(1) << 30) && n <= (int64_t(1) << 30), "shape too large");
+  const int k_blocks = static_cast<int>(k / 128);
+  const cudaStream_t s = as_stream(stream);
+  // decode sizes: the K steps of each 128-channel panel split over a cluster of up to 8 CTAs,
+  // as many as keep the grid within one CTA per SM (the weight stream needs no more)
+  const int64_t panels = n / 128;
+  int want = static_cast<int>(sm_count() / (panels > 0 ? panels : 1));
+  want = want < 1 ? 1 : (want > 8 ? 8 : want);
+  const int per = (k_blocks + want - 1) / want;
+  if (m <= 32 && per <= BlockwiseSkinnyLayout<16>::kMaxPer && blockwise_skinny_fits(m, per)) {
+    BlockwiseSkinnyArgs q{};
+    q.m = m;
+    q.n = n;
+    q.ldo = ldo;
+    q.k_blocks = k_blocks;
+    q.per = per;
+    const int csize = (k_blocks + per - 1) / per;
+    q.sa = a_scale;
+    q.sb = b_scale;
+    q.bias = bias;
+    q.bias_dtype = bias_dtype;
+    q.out = out;
+    const uint32_t nt = m <= 16 ? 16 : 32;
+    CUtensorMap mw, mx;
+    if (int e = make_map(&mw, b, n, k, k, 128, 128, "B")) return e;
+    if (int e = make_map(&mx, a, m, k, k, nt, 128, "A")) return e;
+#define KAB_SKINNY(NT)                                                                    \
+  if (out_dtype == KAB_BF16) return launch_blockwise_skinny<NT, KAB_BF16>(mw, mx, q, csize, s); \
+  if (out_dtype == KAB_F16) return launch_blockwise_skinny<NT, KAB_F16>(mw, mx, q, csize, s);   \
+  return launch_blockwise_skinny<NT, KAB_F32>(mw, mx, q, csize, s)
+    if (nt == 16) { KAB_SKINNY(16); }
+    KAB_SKINNY(32);
+#undef KAB_SKINNY
+  }
   BlockwiseArgs g{};
   g.m = m;
   g.n = n;
-  g.k_blocks = static_cast<int>(k / 128);
+  g.k_blocks = k_blocks;
   g.m_tiles = static_cast<int>((m + 127) / 128);
   g.n_tiles = static_cast<int>(n / 128);
   g.sa = a_scale;
@@ -493,7 +570,6 @@ int kab_gemm_f8_blockwise(const uint8_t* a, const float* a_scale, const uint8_t*
   if (int e = make_map(&ma, a, m, k, k, 128, 128, "A")) return e;
   if (int e = make_map(&mb, b, n, k, k, 128, 128, "B")) return e;
   if (int e = make_out_map(&mo, out, out_dtype, m, n, ldo)) return e;
-  const cudaStream_t s = as_stream(stream);
   if (out_dtype == KAB_BF16) return launch_blockwise<KAB_BF16>(ma, mb, mo, g, s);
   if (out_dtype == KAB_F16) return launch_blockwise<KAB_F16>(ma, mb, mo, g, s);
   return launch_blockwise<KAB_F32>(ma, mb, mo, g, s);

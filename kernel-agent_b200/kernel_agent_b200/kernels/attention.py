@@ -24,7 +24,9 @@ _E4M3 = torch.float8_e4m3fn
 
 def quantize_fp8_heads(t: torch.Tensor, transpose: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
     """``(codes e4m3 [..., S, D], scales fp32 [...])`` with one scale ``amax / 448`` per leading
-    index (fp8lib.py:173-176). ``transpose``: codes as ``[..., D, S]`` (the ``Vᵀ`` operand)."""
+    index (fp8lib.py:173-176). ``transpose``: codes as ``[..., D, S]`` (the ``Vᵀ`` operand), a
+    view of a ``[..., D, S16]`` buffer whose rows are padded with zero codes to a multiple of 16
+    (the row stride the attention kernel's tensor map needs)."""
     if t.dim() < 2:
         raise ValueError(f"expected [..., S, D], got shape {tuple(t.shape)}")
     nat.require_cuda(t)
@@ -34,20 +36,20 @@ def quantize_fp8_heads(t: torch.Tensor, transpose: bool = False) -> tuple[torch.
     *lead, s, d = x.shape
     heads = math.prod(lead)
     amax = torch.empty(max(heads, 1), dtype=torch.int32, device=x.device)
-    codes = torch.empty(*lead, d, s, dtype=_E4M3, device=x.device) if transpose else \
+    codes = torch.empty(*lead, d, (s + 15) // 16 * 16, dtype=_E4M3, device=x.device) if transpose else \
         torch.empty(*lead, s, d, dtype=_E4M3, device=x.device)
     scales = torch.empty(lead, dtype=torch.float32, device=x.device)
     if heads and s and d:
         nat.call("kab_quant_heads_fp8", x.data_ptr(), nat.dtype_code(x), heads, s, d, int(transpose),
                  amax.data_ptr(), codes.data_ptr(), scales.data_ptr(), nat.stream_of(x))
-    return codes, scales
+    return (codes[..., :s] if transpose else codes), scales
 
 
 def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, is_causal: bool = False,
                   enable_gqa: bool = False, scale: float | None = None) -> torch.Tensor:
-    """FP8 ``softmax(Q Kᵀ · scale) V`` over ``q [B, Hq, S, 128]``, ``k`` / ``v [B, Hkv, S, 128]``
-    (``Hq`` a multiple of ``Hkv`` with ``enable_gqa``), the qkpv emulation's arithmetic on the
-    tensor cores; returns ``q.dtype`` (bf16) ``[B, Hq, S, 128]``."""
+    """FP8 ``softmax(Q Kᵀ · scale) V`` over ``q [B, Hq, S, D]``, ``k`` / ``v [B, Hkv, S, D]``
+    (``D`` 128 or 64; ``Hq`` a multiple of ``Hkv`` with ``enable_gqa``; any ``S``), the qkpv
+    emulation's arithmetic on the tensor cores; returns ``q.dtype`` (bf16) ``[B, Hq, S, D]``."""
     if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
         raise ValueError("expected 4-D q, k, v [batch, heads, seq, head_dim]")
     b, hq, s, d = q.shape
@@ -56,10 +58,8 @@ def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, is_causal: 
     hkv = k.shape[1]
     if hkv != hq and not (enable_gqa and hq % hkv == 0):
         raise ValueError(f"{hq} query heads and {hkv} key / value heads need enable_gqa=True and a multiple")
-    if d != 128:
-        raise ValueError(f"head_dim {d}: the FP8 attention kernel takes 128")
-    if s % 128:
-        raise ValueError(f"sequence length {s} is not a multiple of 128")
+    if d not in (128, 64):
+        raise ValueError(f"head_dim {d}: the FP8 attention kernel takes 128 or 64")
     nat.require_cuda(q, k, v)
     qc, qs = quantize_fp8_heads(q)
     kc, ks = quantize_fp8_heads(k)

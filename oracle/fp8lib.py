@@ -61,7 +61,12 @@ def quantize_fp8_blocks(w, block: int = 128) -> tuple[np.ndarray, np.ndarray]:
 def fp8_blockwise_gemm(xq, xs, wq, ws, bias=None, out_dtype="bf16", group: int = 128) -> np.ndarray:
     """gemm_bench.py:39-68 ``_bw_gemm``: for each 128-wide K step a partial product of the
     e4m3 codes (exact in float64, rounded to fp32), then ``acc += part * sa[m, kb] * sb[nb,
-    kb]`` in fp32; ``+ bias``; one rounding to the output dtype."""
+    kb]`` as the Triton kernel compiles it (default fp fusion: ``t = part * sa`` rounded to
+    fp32, then ``acc = fma(t, sb, acc)``); ``+ bias``; one rounding to the output dtype.
+
+    The fused multiply-add is taken in float64 (``t * sb`` is exact there, 48 significant
+    bits) and rounded to fp32; that double rounding can differ from a single one by one fp32
+    unit in the last place in rare ties, far below the tests' bf16 tolerance."""
     a = e4m3_to_f32(xq).astype(np.float64)
     b = e4m3_to_f32(wq).astype(np.float64)
     m, k = a.shape
@@ -73,8 +78,7 @@ def fp8_blockwise_gemm(xq, xs, wq, ws, bias=None, out_dtype="bf16", group: int =
         sl = slice(kb * group, (kb + 1) * group)
         part = (a[:, sl] @ b[:, sl].T).astype(F32)
         t = (part * f32(xs)[:, kb : kb + 1]).astype(F32)
-        t = (t * sb_full[None, :, kb]).astype(F32)
-        acc = (acc + t).astype(F32)
+        acc = (t.astype(np.float64) * sb_full[None, :, kb].astype(np.float64) + acc.astype(np.float64)).astype(F32)
     if bias is not None:
         acc = (acc + f32(bias)[None, :]).astype(F32)
     return f32_to_bf16(acc) if out_dtype == "bf16" else acc

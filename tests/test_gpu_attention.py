@@ -33,7 +33,8 @@ def bf(g, key):
     return torch.from_numpy(g[key].view(np.int16)).view(torch.bfloat16)
 
 
-@pytest.mark.parametrize("shape", [(2, 3, 256, 128), (1, 1, 128, 64), (4, 2, 192, 128)])
+@pytest.mark.parametrize("shape", [(2, 3, 256, 128), (1, 1, 128, 64), (4, 2, 192, 128), (1, 2, 100, 128),
+                                   (2, 2, 37, 64)])
 @pytest.mark.parametrize("transpose", [False, True])
 def test_quantize_heads_bit_exact(ka, shape, transpose):
     g = torch.Generator().manual_seed(sum(shape))
@@ -88,9 +89,34 @@ def test_attention_config5_heads(ka):
         assert rel < max(0.05, 1.25 * rel_emu) and cos > 0.998, ((b, h), rel, rel_emu, cos)
 
 
+@pytest.mark.parametrize("b,hq,hkv,s,d", [(1, 2, 2, 100, 128), (2, 4, 2, 300, 128), (1, 2, 1, 17, 128),
+                                          (1, 1, 1, 129, 128), (1, 2, 2, 256, 64), (2, 4, 2, 300, 64),
+                                          (1, 3, 1, 70, 64)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_attention_ragged_sequences(ka, b, hq, hkv, s, d, causal):
+    """Sequences that are not a multiple of the 128-row tile, and head_dim 64: the keys past S
+    in the last tile are masked and its rows past S are not stored (they would land on the
+    next head's first rows); every head against the qkpv emulation and fp32 attention."""
+    g = torch.Generator().manual_seed(b * 1000 + s + d)
+    q, k, v = (torch.randn(b, h, s, d, generator=g).to(torch.bfloat16) for h in (hq, hkv, hkv))
+    y = ka.attention_fp8(q.to(DEV), k.to(DEV), v.to(DEV), is_causal=causal, enable_gqa=hq != hkv)
+    assert y.shape == q.shape
+    got_all = y.float().cpu().numpy()
+    for bi in range(b):
+        for h in range(hq):
+            hk = h // (hq // hkv)
+            qh, kh, vh = (t.float().numpy() for t in (q[bi, h], k[bi, hk], v[bi, hk]))
+            emu = ofp8.attention_fp8_head(qh, kh, vh, causal=causal)
+            ref = ofp8.sdpa_fp32(qh[None, None], kh[None, None], vh[None, None], causal=causal)[0, 0]
+            got = got_all[bi, h]
+            rel, cos = rel_cos(got, ref)
+            rel_emu, _ = rel_cos(emu, ref)
+            assert rel < max(0.05, 1.25 * rel_emu) and cos > 0.998, ((bi, h), rel, rel_emu, cos)
+
+
 def test_attention_rejects_bad_shapes(ka):
-    q = torch.zeros(1, 2, 100, 128, device=DEV, dtype=torch.bfloat16)
-    with pytest.raises(ValueError, match="multiple of 128"):
+    q = torch.zeros(1, 2, 128, 96, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="head_dim"):
         ka.attention_fp8(q, q, q)
     q = torch.zeros(1, 4, 128, 128, device=DEV, dtype=torch.bfloat16)
     kv = torch.zeros(1, 2, 128, 128, device=DEV, dtype=torch.bfloat16)

@@ -224,7 +224,7 @@ def kb():
     return blockwise
 
 
-@pytest.mark.parametrize("m", [1, 16, 2048, 200])
+@pytest.mark.parametrize("m", [1, 16, 2048, 200, 5, 17, 32])
 def test_fp8_blockwise_linear_config2(kb, m):
     """Config 2 (K = 1024, N = 3072, M in {1, 16, 2048}, plus a ragged M): against the oracle's
     per-128-K promotion of the same codes, and against the fp32 fake-quant matmul."""
@@ -246,6 +246,35 @@ def test_fp8_blockwise_linear_config2(kb, m):
     wfq = fp8lib.e4m3_to_f32(np_bytes(wq)).astype(np.float64) * np.repeat(np.repeat(ws.cpu().numpy(), 128, 0), 128, 1)
     dq = (fq @ wfq.T + np_values(bias)[None, :]).astype(np.float32)
     close_bf16_tol(y[rows], dq, "blockwise vs dequant-matmul")
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 128, 128), (3, 1152, 384), (16, 8192, 256), (32, 2048, 640),
+                                   (24, 640, 128), (9, 9216, 256)])
+@pytest.mark.parametrize("out", ["bf16", "f16", "f32"])
+def test_fp8_blockwise_decode_sizes(kb, m, k, n, out):
+    """The decode-size path (M <= 32: the K steps of each 128-channel panel split over a cluster
+    of up to 8 CTAs, reduced in K order through distributed shared memory) at K from one step
+    to 64 steps, a step count that does not divide by 8, and each output dtype, with bias,
+    against the oracle's promotion of the same codes; K = 9216 (72 steps) takes the tiled
+    kernel."""
+    from oracle import fp8lib
+
+    g = torch.Generator().manual_seed(m * 7 + k + n)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    bias = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16)
+    wq, ws = kb.quantize_fp8_blocks(w.to(DEV))
+    dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[out]
+    y = kb.fp8_blockwise_linear(x.to(DEV), wq, ws, bias.to(DEV), out_dtype=dt)
+    assert y.shape == (m, n) and y.dtype == dt
+    xq, xs = fp8lib.quantize_fp8_groups(np_values(x), 128)
+    want = fp8lib.fp8_blockwise_gemm(xq, xs, np_bytes(wq), ws.cpu().numpy(), np_values(bias), out_dtype="f32")
+    if out == "bf16":
+        close_bf16(y, want, f"blockwise decode m={m} k={k} n={n}")
+    else:
+        got = y.float().cpu().numpy().astype(np.float64)
+        rel = np.linalg.norm(got - want) / np.linalg.norm(want)
+        assert rel < (1e-3 if out == "f16" else 1e-5), (m, k, n, out, rel)
 
 
 def test_fp8_blockwise_golden(kb, golden):
