@@ -150,6 +150,60 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Two fp32 lanes per instruction (packed f32x2 arithmetic of sm_100), each lane rounded to
+// nearest like its scalar form.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n .reg .b64 a, b, c, d;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %5};\n mov.b64 c, {%6, %7};\n"
+      " fma.rn.f32x2 d, a, b, c;\n mov.b64 {%0, %1}, d;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 a, b, d;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %5};\n add.rn.f32x2 d, a, b;\n"
+      " mov.b64 {%0, %1}, d;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 a, b, d;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %5};\n sub.rn.f32x2 d, a, b;\n"
+      " mov.b64 {%0, %1}, d;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// 2^t for two lanes on the FMA pipe instead of the MUFU unit (which the softmax saturates with
+// exp2 and the e4m3 conversions). Range reduction: t is clamped to >= -120 (so 2^t stays a
+// normal float; masked -inf scores give ~1e-36, which rounds to the e4m3 code 0 and is nothing
+// in a row sum >= 1), n = round(t) by adding and subtracting 1.5 * 2^23 (fp32 addition rounds
+// to an integer there), r = t - n in [-1/2, 1/2]; 2^r by a degree-3 polynomial, the minimax
+// fit of 2^r in relative error on [-1/2, 1/2] (coefficients computed for this kernel by linear
+// programming on a dense grid; maximum relative error 7.5e-5 in fp32 Horner form, against
+// e4m3's relative step of 1/16); then n is added to the exponent field: the bits of
+// 1.5 * 2^23 + n shifted left by 23 are n << 23, modulo 2^32.
+__device__ __forceinline__ float2 exp2_poly2(float2 t) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  t.x = fmaxf(t.x, -120.0f);
+  t.y = fmaxf(t.y, -120.0f);
+  const float2 f = add2(t, make_float2(kShift, kShift));
+  const float2 r = sub2(t, sub2(f, make_float2(kShift, kShift)));
+  float2 q = fma2(r, make_float2(0.0551716685295105f, 0.0551716685295105f),
+                  make_float2(0.2426111251115799f, 0.2426111251115799f));
+  q = fma2(q, r, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  q = fma2(q, r, make_float2(0.9999280571937561f, 0.9999280571937561f));
+  return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(f.x) << 23)),
+                     __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(f.y) << 23)));
+}
+
+// Which element pairs of the softmax take exp2_poly2 rather than the MUFU: of every group of
+// eight scores, kPolyPairs of the four pairs (the MUFU also carries the e4m3 conversions).
+constexpr int kPolyPairs = 1;
+
 // A bounded wait whose outcome the whole warp shares (the softmax warps follow it with
 // .sync.aligned TMEM accesses, which need every lane).
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
@@ -342,26 +396,35 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
       const float m_new = raise ? tmax : m_run;
       const float alpha = m_run == -INFINITY ? 0.0f : (raise ? ex2(m_run - m_new) : 1.0f);
       const float bias = kCodeLog2 - m_new;
-      float sums[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // four independent chains
-      uint32_t pw[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float p0 = ex2(fmaf(sv[4 * i], scale_log2, bias)), p1 = ex2(fmaf(sv[4 * i + 1], scale_log2, bias));
-        const float p2 = ex2(fmaf(sv[4 * i + 2], scale_log2, bias)), p3 = ex2(fmaf(sv[4 * i + 3], scale_log2, bias));
-        sums[i & 3] += (p0 + p1) + (p2 + p3);
-        pw[i] = static_cast<uint32_t>(e4m3_pair(p0, p1)) | (static_cast<uint32_t>(e4m3_pair(p2, p3)) << 16);
-      }
-      const float rowsum = (sums[0] + sums[1]) + (sums[2] + sums[3]);
-      l_run = l_run * alpha + rowsum;
-      m_run = m_new;
-      // P_j into the buffer once P V_{j-1} has read it (and landed in O): row r, 16-byte chunk
-      // c at c ^ (r % 8)
+      // P_j goes into the buffer once P V_{j-1} has read it (and landed in O); that MMA was
+      // issued when P_{j-1} was written and is done by now, so waiting here costs little and
+      // each 16-byte chunk of codes is stored as soon as it is made: the row's 128 scores are
+      // the only long-lived registers, which leaves room for the conversions of several chunks
+      // to be in flight at once. Row r's chunk c sits at c ^ (r % 8).
       if (!warp_wait(p_empty, static_cast<uint32_t>((j & 1) ^ 1))) { ok = false; break; }
+      float2 sums[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};  // four independent chains
+      const float2 sc2 = make_float2(scale_log2, scale_log2), bias2 = make_float2(bias, bias);
       uint8_t* prow = sP + r * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
-            make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
+      for (int c = 0; c < 8; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int i = 4 * c + q;
+          const float2 t01 = fma2(make_float2(sv[4 * i], sv[4 * i + 1]), sc2, bias2);
+          const float2 t23 = fma2(make_float2(sv[4 * i + 2], sv[4 * i + 3]), sc2, bias2);
+          // pair 2i of the row's 64 pairs, pair 2i + 1: the first kPolyPairs of each four on
+          // the FMA pipe, the rest on the MUFU
+          const float2 p01 = ((2 * i) & 3) < kPolyPairs ? exp2_poly2(t01) : make_float2(ex2(t01.x), ex2(t01.y));
+          const float2 p23 = ((2 * i + 1) & 3) < kPolyPairs ? exp2_poly2(t23) : make_float2(ex2(t23.x), ex2(t23.y));
+          sums[i & 1] = add2(sums[i & 1], add2(p01, p23));
+          w[q] = static_cast<uint32_t>(e4m3_pair(p01.x, p01.y)) | (static_cast<uint32_t>(e4m3_pair(p23.x, p23.y)) << 16);
+        }
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      const float rowsum = (sums[0].x + sums[0].y) + (sums[1].x + sums[1].y);
+      l_run = l_run * alpha + rowsum;
+      m_run = m_new;
       tc::fence_proxy_async();
       // O holds P V up to tile j - 1 (landed: the wait for the P buffer above): rescale it when
       // a row's max moved
