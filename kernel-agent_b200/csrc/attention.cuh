@@ -150,6 +150,14 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// max(a, b, c) in one instruction (the three-input form of sm_100; a NaN input is ignored,
+// as by fmaxf).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // Two fp32 lanes per instruction (packed f32x2 arithmetic of sm_100), each lane rounded to
 // nearest like its scalar form.
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
@@ -384,13 +392,16 @@ attention_fp8_kernel(const __grid_constant__ CUtensorMap tma_q, const __grid_con
 #pragma unroll
         for (int i = 0; i < 128; ++i) sv[i] = i >= valid ? -INFINITY : sv[i];
       }
-      float mxs[8];  // eight independent chains, then a tree
+      float mxs[8];  // eight independent chains of three-input maxima, then a tree
 #pragma unroll
       for (int a = 0; a < 8; ++a) mxs[a] = sv[a];
 #pragma unroll
-      for (int i = 8; i < 128; ++i) mxs[i & 7] = fmaxf(mxs[i & 7], sv[i]);
-      const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
-                             fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
+      for (int i = 8; i < 120; i += 2) mxs[(i >> 1) & 7] = fmax3(mxs[(i >> 1) & 7], sv[i], sv[i + 1]);
+      mxs[4] = fmax3(mxs[4], sv[120], sv[121]);
+      mxs[5] = fmax3(mxs[5], sv[122], sv[123]);
+      mxs[6] = fmax3(mxs[6], sv[124], sv[125]);
+      mxs[7] = fmax3(mxs[7], sv[126], sv[127]);
+      const float mx = fmax3(fmax3(mxs[0], mxs[1], mxs[2]), fmax3(mxs[3], mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7]));
       const float tmax = mx * scale_log2;  // the scale is positive: the max of the scaled scores
       const bool raise = !(tmax <= m_run + kHeadroom);
       const float m_new = raise ? tmax : m_run;
