@@ -432,12 +432,14 @@ constexpr int kFp4MaxRowBlocks = 32768 / 16;  // scale blocks of the longest row
 //  * the row is kept as packed 16-bit pairs; block maxima come from __vmaxu2 on |pairs|
 //    (non-negative bf16 / fp16 values order like their bit patterns, NaN above inf);
 //  * two quotients per mul.rn.f32x2;
-//  * the window test "(bits + 16) mod 2^21 <= 32" is bits * 2^11 + 2^15 (mod 2^32) < 33 * 2^11,
-//    one IMAD, folded over the block with a running unsigned min;
-//  * a block that trips it (6.7 % of them on config 4's activations: ratios of bf16 values
-//    often land exactly on short floats) goes on a shared-memory list and is recomputed with
-//    the IEEE division after the row by the whole CTA, instead of one lane dividing while its
-//    warp waits.
+//  * instead of the exactness window (which trips on any quotient near a float with three
+//    significant bits: 6.7 % of the blocks of config 4's activations, ratios of bf16 values
+//    often being exact), each block's codes are taken twice, from the products with the
+//    reciprocal nudged up and down by 2^-19; agreeing codes are the quotient's codes (only a
+//    quotient within about 2^-19 of an actual e2m1 midpoint makes them differ);
+//  * a block whose codes differ goes on a shared-memory list and is recomputed with the IEEE
+//    division after the row by the whole CTA, instead of one lane dividing while its warp
+//    waits.
 template <int T>
 __device__ __forceinline__ float half_bits_to_float(uint32_t h) {
   if constexpr (T == kBF16) return __uint_as_float(h << 16);
@@ -695,21 +697,41 @@ quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const 
 #pragma unroll
     for (int c = 0; c < BLOCK / 8; ++c) packed[c] = 0;
     if (step > 0.0f) {
+      // The codes of v * y(1 + 2^-19) and of v * y(1 - 2^-19) bracket those of the IEEE
+      // quotient RN(v / step): y, the hardware reciprocal, is within 2^-22 of 1 / step, so the
+      // two products lie on either side of v / step and of its rounding, and the e2m1 rounding
+      // is monotonic. Where both give the same codes, those are the quotient's codes; a block
+      // where they differ (a quotient within about 2^-19 of an e2m1 midpoint), or whose
+      // divisor has no normal reciprocal, keeps provisional codes and is redone with the IEEE
+      // division after the row, with all lanes busy.
       const Divisor d(div);
-      float t[BLOCK];
-      uint32_t mn = d.fast ? 0xFFFFFFFFu : 0u;
+      const float y_hi = __fmul_rn(d.y, 1.0f + 0x1p-19f), y_lo = __fmul_rn(d.y, 1.0f - 0x1p-19f);
+      constexpr uint32_t kHalfInf = T == kBF16 ? 0x7F80u : 0x7C00u;
+      const bool has_nan = bm[b] > kHalfInf;  // its NaN quotients become 0
+      bool agree = d.fast;
 #pragma unroll
-      for (int j = 0; j < W; ++j) {
-        const float2 p = mul2_rn(unpack2<T>(w[b][j]), d.y);
-        t[2 * j] = p.x;
-        t[2 * j + 1] = p.y;
-        mn = min(mn, __float_as_uint(p.x) * 2048u + 32768u);
-        mn = min(mn, __float_as_uint(p.y) * 2048u + 32768u);
+      for (int c = 0; c < BLOCK / 8; ++c) {
+        float eh[8], el[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 v = unpack2<T>(w[b][4 * c + j]);
+          const float2 ph = mul2_rn(v, y_hi), pl = mul2_rn(v, y_lo);
+          eh[2 * j] = ph.x;
+          eh[2 * j + 1] = ph.y;
+          el[2 * j] = pl.x;
+          el[2 * j + 1] = pl.y;
+        }
+        if (has_nan) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            eh[j] = eh[j] == eh[j] ? eh[j] : 0.0f;
+            el[j] = el[j] == el[j] ? el[j] : 0.0f;
+          }
+        }
+        packed[c] = e2m1x8(eh);
+        agree = agree && packed[c] == e2m1x8(el);
       }
-      // near an e2m1 decision point (or no fast reciprocal): these codes are provisional; the
-      // block is redone with the IEEE division after the row, with all lanes busy
-      if (mn < 33u * 2048u) fixp[atomicAdd(&nfix, 1)] = bi;
-      fp4_block_pack<T, BLOCK>(t, bm[b], packed);
+      if (!agree) fixp[atomicAdd(&nfix, 1)] = bi;
     }
     uint8_t* dst = q + row * (k >> 1) + static_cast<int64_t>(bi) * (BLOCK / 2);
     if constexpr (BLOCK == 16) *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
