@@ -129,6 +129,21 @@ def test_rmsnorm_fp4_one_pass_equals_two(prod, m, k, dtype):
     assert torch.equal(e4.view(torch.int32), e5.view(torch.int32))
 
 
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_rmsnorm_fp4_wide_rows_on_a_second_device(prod):
+    """Rows of 32768 elements need more than 48 KB of shared memory, a per-device function
+    attribute: the first launch on the second GPU sets it there too (the first device's
+    setting does not carry over)."""
+    x0, w0 = inputs(3, 32768, torch.bfloat16, 11)
+    prod.rmsnorm_fp4(x0, w0, 1e-5)  # device 0 first
+    with torch.cuda.device(1):
+        x, w = x0.to("cuda:1"), w0.to("cuda:1")
+        q1, s1, o1 = prod.rmsnorm_fp4(x, w, 1e-5)
+        q2, s2, o2 = prod.quantize_rows_fp4(prod._rmsnorm(x, w, 1e-5, None))
+        assert torch.equal(q1, q2) and torch.equal(s1.view(torch.uint8), s2.view(torch.uint8))
+        assert torch.equal(o1.view(torch.int32), o2.view(torch.int32))
+
+
 def test_rmsnorm_fp4_fp32_takes_two_passes(prod):
     x, w = inputs(3, 1024, torch.float32, 13)
     out = torch.empty_like(x)
