@@ -60,6 +60,7 @@ struct CmpThread {
   double sum[KAB_CMP_NSUM];
   float mx[KAB_CMP_NMAX];
   float bd, bal;
+  float rb;  // the largest approximate ratio d * rcp(allowed) seen by the fast step
 };
 
 __device__ __forceinline__ void cmp_init(CmpThread& t) {
@@ -71,6 +72,14 @@ __device__ __forceinline__ void cmp_init(CmpThread& t) {
   for (int i = 0; i < KAB_CMP_NMAX; ++i) t.mx[i] = 0.0f;
   t.bd = 0.0f;
   t.bal = 1.0f;
+  t.rb = 0.0f;
+}
+
+// The hardware reciprocal (rcp.approx: within about one unit in the last place).
+__device__ __forceinline__ float cmp_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // (bd, bal) <- (d, al) when d / al > bd / bal exactly (finite d >= 0, al > 0): a float filter
@@ -126,18 +135,23 @@ __device__ __forceinline__ void cmp_element(const KabCompareParams& P, float a, 
 
 // The common case of 8 elements (no rerounded / alternative bound / widening / element
 // ratio; every a and b finite): the same counts and maxima with float partial sums over the
-// 8 products added to the float64 totals, and the ratio kept as its operands.
+// 8 products added to the float64 totals, and the ratio kept as its operands. The exact
+// ratio comparison runs only for a chunk that may hold a new largest ratio: its largest
+// approximate ratio d * rcp(allowed) (within 2^-21 of the exact one) is at least 1 - 2^-20
+// of the largest approximation seen before, which any chunk holding a larger exact ratio
+// satisfies. That is a handful of chunks per thread, instead of a branch per element.
 __device__ __forceinline__ void cmp_chunk_fast(const KabCompareParams& P, const float (&a)[8], const float (&b)[8],
                                                CmpThread& t) {
   float s_aa = 0.0f, s_bb = 0.0f, s_ab = 0.0f, s_dd = 0.0f, s_d = 0.0f;
   float mxd = t.mx[KAB_CMP_MAX_D];
+  float rc = 0.0f;
   int mism = 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float d = fabsf(__fsub_rn(a[j], b[j]));
     const float allowed = __fadd_rn(P.atol, __fmul_rn(P.rtol, fabsf(a[j])));
     mism += d > allowed;
-    ratio_max(d, fmaxf(allowed, 1e-30f), t.bd, t.bal);
+    rc = fmaxf(rc, d * cmp_rcp(fmaxf(allowed, 1e-30f)));
     mxd = fmaxf(mxd, d);
     s_aa = fmaf(a[j], a[j], s_aa);
     s_bb = fmaf(b[j], b[j], s_bb);
@@ -145,6 +159,15 @@ __device__ __forceinline__ void cmp_chunk_fast(const KabCompareParams& P, const 
     s_dd = fmaf(d, d, s_dd);
     s_d += d;
   }
+  if (rc >= t.rb * 0.99999905f) {  // 1 - 2^-20: this chunk may hold a new largest ratio
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float d = fabsf(__fsub_rn(a[j], b[j]));
+      const float allowed = __fadd_rn(P.atol, __fmul_rn(P.rtol, fabsf(a[j])));
+      ratio_max(d, fmaxf(allowed, 1e-30f), t.bd, t.bal);
+    }
+  }
+  t.rb = fmaxf(t.rb, rc);
   t.mx[KAB_CMP_MAX_D] = mxd;
   t.cnt[KAB_CMP_FINITE] += 8;
   t.cnt[KAB_CMP_MISMATCH] += mism;
