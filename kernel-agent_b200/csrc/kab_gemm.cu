@@ -300,6 +300,9 @@ int run(const void* a, const void* b, int64_t m, int64_t n, int64_t k_bytes, Gem
   int bn;
   if (!GemmTraits<KIND>::kScaled) {
     bn = n >= 256 ? 256 : 128;
+    // a small problem (config 1: 128 x 1024 x 1024 is 4 tiles of 128 x 256) is bound by each
+    // CTA's serial operand stream: twice the tiles at half the width halve that stream
+    if (bn == 256 && ((m + 127) / 128) * ((n + 255) / 256) * 2 <= sm_count()) bn = 128;
   } else {
     const int64_t pad192 = (n + 191) / 192 * 192 - n;
     bn = (n >= 192 && pad192 * 16 <= n) ? 192 : 128;
