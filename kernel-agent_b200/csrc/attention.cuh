@@ -82,10 +82,9 @@ quant_heads_kernel(const void* __restrict__ x, int64_t seq, int d, const unsigne
       if constexpr (TRANSPOSE) *reinterpret_cast<uint2*>(tile + r * d + col) = make_uint2(0u, 0u);
       continue;
     }
-    float v[8], qv[8];
+    float v[8];
     load8<T>(x, (head * seq + s0 + r) * d + col, v);
-    quotients<kLowE4m3>(v, div, qv);
-    const uint2 codes = e4m3x8(qv);
+    const uint2 codes = e4m3x8_quotients(v, div);
     if constexpr (TRANSPOSE) *reinterpret_cast<uint2*>(tile + r * d + col) = codes;
     else *reinterpret_cast<uint2*>(q + (head * seq + s0 + r) * d + col) = codes;
   }

@@ -67,9 +67,7 @@ quant_kv_kernel(const void* __restrict__ x, int64_t rows, int64_t inner, int64_t
   // kv_quant.py:44: torch.where(amax > 0, amax / 448, 1) (NaN -> 1; a positive amax whose
   // quotient underflows keeps the zero scale, as the reference does)
   const float s = amax > 0.0f ? __fdiv_rn(amax, kFp8Max) : 1.0f;
-  float qv[8];
-  quotients<kLowE4m3>(v, Divisor(s), qv);
-  *reinterpret_cast<uint2*>(codes + o * cs_o + t * cs_i + j * 8) = e4m3x8(qv);
+  *reinterpret_cast<uint2*>(codes + o * cs_o + t * cs_i + j * 8) = e4m3x8_quotients(v, Divisor(s));
   if (j == 0) scales[o * ss_o + t * ss_i] = s;
 }
 

@@ -65,6 +65,43 @@ __device__ __forceinline__ uint2 e4m3x8(const float (&q)[8]) {
   const uint32_t w1 = e4m3_pair(q[4], q[5]) | (static_cast<uint32_t>(e4m3_pair(q[6], q[7])) << 16);
   return make_uint2(w0, w1);
 }
+// e4m3 codes of the eight IEEE quotients RN(v / s) (d = Divisor(s)), element 0 in the low
+// byte. The codes of v * y(1 + 2^-19) and of v * y(1 - 2^-19) bracket those of the quotient: y
+// is within 2^-22 of 1 / s, so the two products lie on either side of v / s and of its
+// rounding, and the e4m3 rounding is monotonic. Where both give the same codes, those are the
+// quotient's; otherwise (a quotient within about 2^-19 of an e4m3 midpoint) and where s has
+// no normal reciprocal, the eight quotients are divided. Unlike the short-float window of
+// `quotients`, quotients that land on or near representable e4m3 values (frequent for ratios
+// of bf16 values) do not divide.
+__device__ __forceinline__ float2 fmul2_rn(float a, float b, float c) {  // (a * c, b * c)
+  float2 r;
+  asm("{\n .reg .b64 x, y, z;\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %4};\n mul.rn.f32x2 z, x, y;\n"
+      " mov.b64 {%0, %1}, z;\n}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ uint2 e4m3x8_quotients(const float (&v)[8], const Divisor& d) {
+  if (d.fast) {
+    const float yh = __fmul_rn(d.y, 1.0f + 0x1p-19f), yl = __fmul_rn(d.y, 1.0f - 0x1p-19f);
+    float h[8], l[8];
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      const float2 ph = fmul2_rn(v[i], v[i + 1], yh), pl = fmul2_rn(v[i], v[i + 1], yl);
+      h[i] = ph.x;
+      h[i + 1] = ph.y;
+      l[i] = pl.x;
+      l[i + 1] = pl.y;
+    }
+    const uint2 ch = e4m3x8(h), cl = e4m3x8(l);
+    if (ch.x == cl.x && ch.y == cl.y) return ch;
+  }
+  float t[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t[i] = __fdiv_rn(v[i], d.s);
+  return e4m3x8(t);
+}
+
 // Eight int8 codes: rint(q) to nearest even, clamped to +-127 (NaN -> 0), element 0 low.
 __device__ __forceinline__ uint2 int8x8(const float (&q)[8]) {
   uint32_t w[2] = {0, 0};

@@ -206,8 +206,7 @@ quant_rows_kernel(const void* __restrict__ x, int64_t ldx, const void* __restric
       quotients<kLowInt8>(v, div, qv);
       *reinterpret_cast<uint2*>(reinterpret_cast<int8_t*>(q) + row * k + ci * 8) = int8x8(qv);
     } else {  // quant.py:376: (v / scale).clamp(±448) to e4m3
-      quotients<kLowE4m3>(v, div, qv);
-      *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(q) + row * k + ci * 8) = e4m3x8(qv);
+      *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(q) + row * k + ci * 8) = e4m3x8_quotients(v, div);
     }
   };
   if constexpr (MAXC > 0) {
@@ -244,9 +243,7 @@ quant_groups_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, uint8_t*
   if (!live) return;
   float s = __fdiv_rn(__uint_as_float(abits), kFp8Max);
   s = s > 0.0f ? s : 1.0f;  // fp8lib.py:17-18 _safe
-  float qv[8];
-  quotients<kLowE4m3>(v, Divisor(s), qv);
-  *reinterpret_cast<uint2*>(q + row * k + j * 8) = e4m3x8(qv);
+  *reinterpret_cast<uint2*>(q + row * k + j * 8) = e4m3x8_quotients(v, Divisor(s));
   if ((j % LANES) == 0) scales[row * (k / (LANES * 8)) + j / LANES] = s;
 }
 
@@ -278,9 +275,7 @@ quant_blocks128_kernel(const void* __restrict__ w, int64_t ldw, int64_t k,
   for (int c = 0; c < 8; ++c) {
     const int idx = threadIdx.x + c * 256;
     const int64_t r = nb * 128 + (idx >> 4), col = kb * 128 + (idx & 15) * 8;
-    float qv[8];
-    quotients<kLowE4m3>(v[c], div, qv);
-    *reinterpret_cast<uint2*>(q + r * k + col) = e4m3x8(qv);
+    *reinterpret_cast<uint2*>(q + r * k + col) = e4m3x8_quotients(v[c], div);
   }
 }
 
@@ -872,9 +867,7 @@ rmsnorm_quant_fp8_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, con
     for (int c = 0; c < MAXC; ++c) {
       const int64_t ci = threadIdx.x + static_cast<int64_t>(c) * 256;
       if (ci < chunks) {
-        float qv[8];
-        quotients<kLowE4m3>(v[c], div, qv);
-        *reinterpret_cast<uint2*>(q + row * k + ci * 8) = e4m3x8(qv);
+        *reinterpret_cast<uint2*>(q + row * k + ci * 8) = e4m3x8_quotients(v[c], div);
       }
     }
   } else {
@@ -986,10 +979,9 @@ rmsnorm_quant_fp8_packed_kernel(const void* __restrict__ x, int64_t ldx, int64_t
     for (int c = 0; c < NC; ++c) {
       const int ci = threadIdx.x + c * NT;
       if (ci < chunks) {
-        float f[8], qv[8];
+        float f[8];
         values(c, f);
-        quotients<kLowE4m3>(f, div, qv);
-        *reinterpret_cast<uint2*>(q + row * k + static_cast<int64_t>(ci) * 8) = e4m3x8(qv);
+        *reinterpret_cast<uint2*>(q + row * k + static_cast<int64_t>(ci) * 8) = e4m3x8_quotients(f, div);
       }
     }
   } else {
