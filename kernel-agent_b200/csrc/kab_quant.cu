@@ -7,8 +7,6 @@
 namespace kab {
 namespace {
 
-constexpr int64_t kMaxRegChunks = 16;  // chunks of 8 a thread keeps in registers
-
 // Threads per row and chunks per thread for a row of `nchunks` chunks of 8.
 void row_shape(int64_t nchunks, int& threads, int& maxc) {
   threads = nchunks <= 128 ? 128 : 256;
