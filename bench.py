@@ -292,6 +292,55 @@ class Workload:
     def e2e_step(self):
         raise NotImplementedError
 
+    def pipelined_e2e(self, hosts, run, out_host):
+        """One end-to-end step through the public API, pipelined as a serving loop runs it:
+        this step's input copies (pinned `hosts` -> device, on their own stream) and the
+        previous step's output copy (device -> pinned host, on another stream) overlap this
+        step's kernels. Every step still copies all of its own inputs and its whole output:
+        two device input slots and two pinned output buffers alternate. `run(*device_inputs)`
+        returns the step's output tensor."""
+        torch = self.torch
+        if not hasattr(self, "_pipe"):
+            dev = torch.device("cuda", torch.cuda.current_device())
+            self._pipe = {
+                "in": torch.cuda.Stream(), "out": torch.cuda.Stream(), "i": 0,
+                "dev": [[torch.empty(h.shape, dtype=h.dtype, device=dev) for h in hosts] for _ in range(2)],
+                "host": [out_host, torch.empty_like(out_host).pin_memory()],
+                "ev_in": [torch.cuda.Event() for _ in range(2)], "ev_done": [None, None], "ev_out": [None, None],
+                "y": [None, None],
+            }
+        p = self._pipe
+        slot = p["i"] % 2
+        cur = torch.cuda.current_stream()
+        if p["ev_done"][slot] is not None:
+            p["in"].wait_event(p["ev_done"][slot])  # step i - 2's kernels have read this input slot
+        with torch.cuda.stream(p["in"]):
+            for d, h in zip(p["dev"][slot], hosts):
+                d.copy_(h, non_blocking=True)
+        p["ev_in"][slot].record(p["in"])
+        cur.wait_event(p["ev_in"][slot])
+        if p["ev_out"][slot] is not None:
+            cur.wait_event(p["ev_out"][slot])  # step i - 2's output copy has read its slot
+        y = run(*p["dev"][slot])
+        done = torch.cuda.Event()
+        done.record(cur)
+        p["ev_done"][slot] = done
+        p["out"].wait_event(done)
+        with torch.cuda.stream(p["out"]):
+            p["host"][slot].copy_(y, non_blocking=True)
+        ev_out = torch.cuda.Event()
+        ev_out.record(p["out"])
+        p["ev_out"][slot] = ev_out
+        p["y"][slot] = y  # alive until its copy is done: step i + 2 waits for ev_out first
+        p["i"] += 1
+
+    def e2e_drain(self):
+        """Makes the current stream wait for the output copies a pipelined e2e step left."""
+        if hasattr(self, "_pipe"):
+            for ev in self._pipe["ev_out"]:
+                if ev is not None:
+                    self.torch.cuda.current_stream().wait_event(ev)
+
     def cpu_case(self, dev) -> CpuCase:
         raise NotImplementedError
 
@@ -399,11 +448,8 @@ class W4A4Linear(Workload):
         return kernel_ms(self.dominant, steps, self.torch)
 
     def e2e_step(self):
-        """One step through the public API with host buffers. On one GPU the steps are pipelined
-        as a serving loop would run them: step i's input copy (its own stream) and step i - 1's
-        output copy (another stream) overlap step i's kernels; every step still copies its own
-        134 MB in and its own 470 MB out (two device input / output slots, two pinned output
-        buffers)."""
+        """One step through the public API with host buffers: on one GPU pipelined over three
+        streams (`pipelined_e2e`), every step copying its own 134 MB in and 470 MB out."""
         if self.world > 1:
             x = self.x_host.to(self.x.device, non_blocking=True)
             y = self.sharded.fp4_w4a4_linear_sharded(x, self.wq, self.ws, self.ts, self.bias,
@@ -411,45 +457,9 @@ class W4A4Linear(Workload):
                                                      peers=self.peers)
             self.y_host.copy_(y, non_blocking=True)
             return 2
-        torch = self.torch
-        if not hasattr(self, "_pipe"):
-            self._pipe = {
-                "in": torch.cuda.Stream(), "out": torch.cuda.Stream(), "i": 0,
-                "x": [torch.empty_like(self.x) for _ in range(2)], "y": [None, None],
-                "host": [self.y_host, torch.empty_like(self.y_host).pin_memory()],
-                "ev_in": [torch.cuda.Event() for _ in range(2)], "ev_done": [None, None],
-                "ev_out": [None, None],
-            }
-        p = self._pipe
-        slot = p["i"] % 2
-        cur = torch.cuda.current_stream()
-        if p["ev_done"][slot] is not None:
-            p["in"].wait_event(p["ev_done"][slot])  # step i - 2's kernels have read this input slot
-        with torch.cuda.stream(p["in"]):
-            p["x"][slot].copy_(self.x_host, non_blocking=True)
-        p["ev_in"][slot].record(p["in"])
-        cur.wait_event(p["ev_in"][slot])
-        if p["ev_out"][slot] is not None:
-            cur.wait_event(p["ev_out"][slot])  # step i - 2's output copy has read its slot
-        y = self.quant.fp4_w4a4_linear(p["x"][slot], self.wq, self.ws, self.ts, self.bias)
-        done = torch.cuda.Event()
-        done.record(cur)
-        p["ev_done"][slot] = done
-        p["out"].wait_event(done)
-        with torch.cuda.stream(p["out"]):
-            p["host"][slot].copy_(y, non_blocking=True)
-        ev_out = torch.cuda.Event()
-        ev_out.record(p["out"])
-        p["ev_out"][slot] = ev_out
-        p["y"][slot] = y  # alive until its copy is done: step i + 2 waits for ev_out first
-        p["i"] += 1
+        self.pipelined_e2e([self.x_host], lambda x: self.quant.fp4_w4a4_linear(x, self.wq, self.ws, self.ts, self.bias),
+                           self.y_host)
         return 2
-
-    def e2e_drain(self):
-        if hasattr(self, "_pipe"):
-            for ev in self._pipe["ev_out"]:
-                if ev is not None:
-                    self.torch.cuda.current_stream().wait_event(ev)
 
     def close(self):
         if self.peers is not None:
@@ -668,10 +678,11 @@ class Mxfp8Mlp(Workload):
         return {"producer_kernel_ms": ms, "producer_gbs": self.producer_bytes / (ms / 1e3) / 1e9}
 
     def e2e_step(self):
-        g = self.g_host.to(self.g.device, non_blocking=True)
-        u = self.u_host.to(self.g.device, non_blocking=True)
-        xq, xs = self.producers.silu_mul_fp8(g, u, mx=True, blocked=True)
-        self.y_host.copy_(self._gemm(xq, xs), non_blocking=True)
+        def run(g, u):
+            xq, xs = self.producers.silu_mul_fp8(g, u, mx=True, blocked=True)
+            return self._gemm(xq, xs)
+
+        self.pipelined_e2e([self.g_host, self.u_host], run, self.y_host)
         return 2
 
     def library_bar(self):
@@ -965,9 +976,9 @@ class Fp8Attention(Workload):
         return 1
 
     def e2e_step(self):
-        q, k, v = (h.to(self.q.device, non_blocking=True) for h in self.hosts)
-        y = self.attention.attention_fp8(q, k, v, is_causal=True, enable_gqa=True)
-        self.y_host.copy_(y, non_blocking=True)
+        self.pipelined_e2e(list(self.hosts),
+                           lambda q, k, v: self.attention.attention_fp8(q, k, v, is_causal=True, enable_gqa=True),
+                           self.y_host)
         return 7
 
     def library_bar(self):
