@@ -574,10 +574,11 @@ __device__ __forceinline__ uint32_t block_absmax(uint32_t (&v)[W]) {
 // their h from the staged x. Launched with k * 2 + (k / block) * 4 bytes of dynamic shared
 // memory.
 template <int T, int NB, int FMT, int MODE, bool NORM = false>
-// (NVFP4 with four blocks per thread runs at 128 threads: capped at 64 registers, eight CTAs fit
-// an SM instead of seven, which keeps more rows' loads in flight: 46.4 vs 50.1 us on x [8192,
-// 8192] bf16, one B200)
-__global__ void __launch_bounds__(512, FMT == 0 ? (NB <= 2 ? (NORM ? 1 : 3) : 2) : 1)
+// (NVFP4 runs at 128 threads per row for most widths: capped at 64 registers with four blocks
+// per thread and at 40 with one or two, more CTAs (rows) fit an SM, which keeps more rows'
+// loads in flight: 46.4 vs 50.1 us on x [8192, 8192] bf16, and the fused RMSNorm producer 77.5
+// vs 79.3 us on x [16384, 4096] bf16, one B200)
+__global__ void __launch_bounds__(512, FMT == 0 ? (NB <= 2 ? 3 : 2) : 1)
 quant_fp4_fast_kernel(const void* __restrict__ x, int64_t ldx, int64_t k, const float* __restrict__ amax_in,
                       const float* __restrict__ ts_in, int swizzle, uint8_t* __restrict__ q,
                       uint8_t* __restrict__ scales, float* __restrict__ outer_out,
